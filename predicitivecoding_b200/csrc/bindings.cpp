@@ -1,0 +1,286 @@
+// Python bindings for the sm_100a kernels (torch extension, built in-tree).
+//
+// Every entry takes torch tensors, launches on the current CUDA stream (so the
+// calls compose with torch streams and CUDA-graph capture) and raises on a bad
+// argument or a launch error.  No entry point allocates device memory except
+// where the docstring says so.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <atomic>
+
+#include "gemm_api.h"
+
+// launchers defined in the .cu files
+int pcb_embed_fwd(const int* tok, const void* W, float* x, int M, int D, int V, cudaStream_t s);
+int pcb_embed_bwd(const int* tok, const float* dx, float* dW, int M, int D, int V, cudaStream_t s);
+int pcb_rmsnorm_fwd(const float* x, const void* g, void* y, float* inv, int M, int D, float eps, cudaStream_t s);
+int pcb_rmsnorm_bwd(const float* dy, const float* x, const void* g, const float* inv, float* dx, void* dx16,
+                    float* dg, int M, int D, int accumulate, int num_sms, cudaStream_t s);
+int pcb_rope(void* buf, long long ld, const float* cs, int M, int S, int D, int hd, int nparts, float sign,
+             cudaStream_t s);
+int pcb_ce(void* logits, long long ld, const int* tgt, float* loss, int M, int V, float scale, int write_grad,
+           cudaStream_t s);
+int pcb_sumsq(const float* x, long long n, float* out, int square, cudaStream_t s);
+int pcb_colsum(const void* x, int is_bf16, long long ld, float* out, int M, int N, float scale, cudaStream_t s);
+int pcb_adamw(float* w, const float* g, float* m, float* v, void* w16, long long n, long long n_decay,
+              const float* hyper, float b1, float b2, float eps, const float* clip_sumsq, float max_norm,
+              cudaStream_t s);
+int pcb_f32_to_bf16(const float* x, void* y, long long n, cudaStream_t s);
+int pcb_attn_fwd(const void* qkv, long long ld, void* out, long long ld_o, float* lse, int B, int S, int H, int HD,
+                 float scale, cudaStream_t s);
+int pcb_attn_bwd(const void* qkv, long long ld, const void* out, const void* dout, long long ld_o, const float* lse,
+                 float* dvec, float* dq_acc, void* dqkv, long long ld_d, int B, int S, int H, int HD, float scale,
+                 cudaStream_t s);
+
+namespace {
+
+std::atomic<long long> g_launches{0};
+
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+void check(int rc, const char* what, int kernels = 1) {
+  g_launches.fetch_add(kernels, std::memory_order_relaxed);
+  TORCH_CHECK(rc == 0, "pcb kernel '", what, "' failed with code ", rc, " (",
+              cudaGetErrorString(cudaGetLastError()), ")");
+}
+
+void req(const at::Tensor& t, at::ScalarType dt, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.scalar_type() == dt, name, " has dtype ", t.scalar_type(), ", expected ", dt);
+}
+
+// row stride (elements) of a 2-D view whose inner dimension is contiguous
+long long row_stride(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.dim() == 2, name, " must be 2-D");
+  TORCH_CHECK(t.stride(1) == 1, name, " must have a contiguous inner dimension");
+  return t.stride(0);
+}
+
+int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+void* ptr_or_null(const c10::optional<at::Tensor>& t) { return t.has_value() ? t->data_ptr() : nullptr; }
+
+// ---------------------------------------------------------------- GEMM
+// a: [M,K] (a_mn=0) or [K,M] (a_mn=1);  b: [N,K] (b_mn=0) or [K,N] (b_mn=1).
+void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, int64_t epi,
+          const c10::optional<at::Tensor>& c, const c10::optional<at::Tensor>& d,
+          const c10::optional<at::Tensor>& aux, const c10::optional<at::Tensor>& bias, double alpha,
+          int64_t force_bn, int64_t force_splits, const c10::optional<at::Tensor>& err) {
+  req(a, at::kBFloat16, "a");
+  req(b, at::kBFloat16, "b");
+  const long long lda = row_stride(a, "a"), ldb = row_stride(b, "b");
+  pcb::GemmArgs args{};
+  args.M = a_mn ? a.size(1) : a.size(0);
+  args.K = a_mn ? a.size(0) : a.size(1);
+  args.N = b_mn ? b.size(1) : b.size(0);
+  const int kb = b_mn ? b.size(0) : b.size(1);
+  TORCH_CHECK(kb == args.K, "gemm: K mismatch (", args.K, " vs ", kb, ")");
+  args.alpha = static_cast<float>(alpha);
+  if (c) { args.C = c->data_ptr(); args.ldc = row_stride(*c, "c"); }
+  if (d) { args.D = d->data_ptr(); args.ldd = row_stride(*d, "d"); }
+  if (aux) { args.aux = aux->data_ptr(); args.ldaux = row_stride(*aux, "aux"); }
+  if (bias) {
+    TORCH_CHECK(bias->scalar_type() == at::kFloat || bias->scalar_type() == at::kBFloat16, "bias: fp32 or bf16");
+    args.bias = bias->data_ptr();
+    args.bias_bf16 = bias->scalar_type() == at::kBFloat16 ? 1 : 0;
+  }
+  if (err) args.err = err->data_ptr<int>();
+  if (epi == pcb::EPI_SWIGLU) TORCH_CHECK(args.N % 128 == 0, "swiglu gemm needs N % 128 == 0");
+  if (epi == pcb::EPI_SWIGLU_BWD) TORCH_CHECK(args.N % 64 == 0, "swiglu bwd gemm needs N % 64 == 0");
+  const at::cuda::CUDAGuard guard(a.device());
+  check(pcb_gemm_launch(a.data_ptr(), a_mn, lda, b.data_ptr(), b_mn, ldb, (int)epi, args, (int)force_bn,
+                        (int)force_splits, num_sms(), cur_stream()),
+        "gemm");
+}
+
+// PC-specific GEMM entry (epilogues 8..10), scalar knobs passed explicitly.
+void gemm_pc(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, int64_t epi,
+             const c10::optional<at::Tensor>& c, const c10::optional<at::Tensor>& d,
+             const c10::optional<at::Tensor>& aux, const c10::optional<at::Tensor>& bias, double alpha, int64_t act,
+             double pi, double eta, double actreg, double decay, const c10::optional<at::Tensor>& energy,
+             const c10::optional<at::Tensor>& pred_out, const c10::optional<at::Tensor>& pred_bf16,
+             const c10::optional<at::Tensor>& err) {
+  req(a, at::kBFloat16, "a");
+  req(b, at::kBFloat16, "b");
+  const long long lda = row_stride(a, "a"), ldb = row_stride(b, "b");
+  pcb::GemmArgs args{};
+  args.M = a_mn ? a.size(1) : a.size(0);
+  args.K = a_mn ? a.size(0) : a.size(1);
+  args.N = b_mn ? b.size(1) : b.size(0);
+  const int kb = b_mn ? b.size(0) : b.size(1);
+  TORCH_CHECK(kb == args.K, "gemm_pc: K mismatch");
+  args.alpha = static_cast<float>(alpha);
+  if (c) { args.C = c->data_ptr(); args.ldc = row_stride(*c, "c"); }
+  if (d) { args.D = d->data_ptr(); args.ldd = row_stride(*d, "d"); }
+  if (aux) { args.aux = aux->data_ptr(); args.ldaux = row_stride(*aux, "aux"); }
+  if (bias) { req(*bias, at::kFloat, "bias"); args.bias = bias->data_ptr(); }
+  if (err) args.err = err->data_ptr<int>();
+  args.act = (int)act;
+  args.pc_pi = (float)pi;
+  args.pc_eta = (float)eta;
+  args.pc_actreg = (float)actreg;
+  args.pc_decay = (float)decay;
+  if (energy) args.pc_energy = energy->data_ptr<float>();
+  if (pred_out) { args.pc_pred_out = pred_out->data_ptr(); args.ld_pred = row_stride(*pred_out, "pred_out"); }
+  if (pred_bf16) {
+    args.pc_pred_bf16 = pred_bf16->data_ptr();
+    args.ld_pred = row_stride(*pred_bf16, "pred_bf16");
+  }
+  const at::cuda::CUDAGuard guard(a.device());
+  check(pcb_gemm_launch(a.data_ptr(), a_mn, lda, b.data_ptr(), b_mn, ldb, (int)epi, args, 0, 1, num_sms(),
+                        cur_stream()),
+        "gemm_pc");
+}
+
+// ---------------------------------------------------------------- elementwise
+void embed_fwd(const at::Tensor& tok, const at::Tensor& W, at::Tensor& x) {
+  req(tok, at::kInt, "tok");
+  req(W, at::kBFloat16, "W");
+  req(x, at::kFloat, "x");
+  check(pcb_embed_fwd(tok.data_ptr<int>(), W.data_ptr(), x.data_ptr<float>(), tok.numel(), W.size(1),
+                      W.size(0), cur_stream()),
+        "embed_fwd");
+}
+void embed_bwd(const at::Tensor& tok, const at::Tensor& dx, at::Tensor& dW) {
+  req(tok, at::kInt, "tok");
+  req(dx, at::kFloat, "dx");
+  req(dW, at::kFloat, "dW");
+  check(pcb_embed_bwd(tok.data_ptr<int>(), dx.data_ptr<float>(), dW.data_ptr<float>(), tok.numel(), dW.size(1),
+                      dW.size(0), cur_stream()),
+        "embed_bwd");
+}
+void rmsnorm_fwd(const at::Tensor& x, const at::Tensor& g, at::Tensor& y, const c10::optional<at::Tensor>& inv,
+                 double eps) {
+  req(x, at::kFloat, "x");
+  req(g, at::kBFloat16, "g");
+  req(y, at::kBFloat16, "y");
+  TORCH_CHECK(x.is_contiguous() && y.is_contiguous(), "rmsnorm_fwd: contiguous tensors required");
+  const int D = x.size(-1);
+  const int M = x.numel() / D;
+  check(pcb_rmsnorm_fwd(x.data_ptr<float>(), g.data_ptr(), y.data_ptr(),
+                        inv ? inv->data_ptr<float>() : nullptr, M, D, (float)eps, cur_stream()),
+        "rmsnorm_fwd");
+}
+void rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& g, const at::Tensor& inv, at::Tensor& dx,
+                 const c10::optional<at::Tensor>& dx16, at::Tensor& dg, bool accumulate) {
+  req(dy, at::kFloat, "dy");
+  req(x, at::kFloat, "x");
+  req(g, at::kBFloat16, "g");
+  req(dx, at::kFloat, "dx");
+  req(dg, at::kFloat, "dg");
+  if (dx16) req(*dx16, at::kBFloat16, "dx16");
+  const int D = x.size(-1);
+  const int M = x.numel() / D;
+  check(pcb_rmsnorm_bwd(dy.data_ptr<float>(), x.data_ptr<float>(), g.data_ptr(), inv.data_ptr<float>(),
+                        dx.data_ptr<float>(), ptr_or_null(dx16), dg.data_ptr<float>(), M, D, accumulate ? 1 : 0,
+                        num_sms(), cur_stream()),
+        "rmsnorm_bwd");
+}
+void rope(at::Tensor& buf, const at::Tensor& cs, int64_t S, int64_t D, int64_t hd, int64_t nparts, double sign) {
+  req(buf, at::kBFloat16, "buf");
+  req(cs, at::kFloat, "cs");
+  const long long ld = row_stride(buf, "buf");
+  check(pcb_rope(buf.data_ptr(), ld, cs.data_ptr<float>(), buf.size(0), S, D, hd, nparts, (float)sign, cur_stream()),
+        "rope");
+}
+void cross_entropy(at::Tensor& logits, const at::Tensor& tgt, at::Tensor& loss, double scale, bool write_grad) {
+  req(logits, at::kBFloat16, "logits");
+  req(tgt, at::kInt, "tgt");
+  req(loss, at::kFloat, "loss");
+  const long long ld = row_stride(logits, "logits");
+  check(pcb_ce(logits.data_ptr(), ld, tgt.data_ptr<int>(), loss.data_ptr<float>(), logits.size(0), logits.size(1),
+               (float)scale, write_grad ? 1 : 0, cur_stream()),
+        "cross_entropy");
+}
+void sumsq(const at::Tensor& x, at::Tensor& out, bool square) {
+  req(x, at::kFloat, "x");
+  req(out, at::kFloat, "out");
+  check(pcb_sumsq(x.data_ptr<float>(), x.numel(), out.data_ptr<float>(), square ? 1 : 0, cur_stream()), "sumsq");
+}
+void colsum(const at::Tensor& x, at::Tensor& out, double scale) {
+  TORCH_CHECK(x.is_cuda(), "x must be CUDA");
+  req(out, at::kFloat, "out");
+  const long long ld = row_stride(x, "x");
+  const bool bf = x.scalar_type() == at::kBFloat16;
+  TORCH_CHECK(bf || x.scalar_type() == at::kFloat, "colsum: bf16 or fp32 input");
+  check(pcb_colsum(x.data_ptr(), bf ? 1 : 0, ld, out.data_ptr<float>(), x.size(0), x.size(1), (float)scale,
+                   cur_stream()),
+        "colsum");
+}
+// hyper: device fp32 [5] = [lr, wd, bias_correction1, bias_correction2, grad_scale]
+void adamw(at::Tensor& w, const at::Tensor& g, at::Tensor& m, at::Tensor& v, const c10::optional<at::Tensor>& w16,
+           int64_t n_decay, const at::Tensor& hyper, double b1, double b2, double eps,
+           const c10::optional<at::Tensor>& clip_sumsq, double max_norm) {
+  req(w, at::kFloat, "w");
+  req(g, at::kFloat, "g");
+  req(m, at::kFloat, "m");
+  req(v, at::kFloat, "v");
+  if (w16) req(*w16, at::kBFloat16, "w16");
+  req(hyper, at::kFloat, "hyper");
+  TORCH_CHECK(hyper.numel() >= 5, "adamw: hyper needs 5 values");
+  check(pcb_adamw(w.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
+                  ptr_or_null(w16), w.numel(), n_decay, hyper.data_ptr<float>(), (float)b1, (float)b2, (float)eps,
+                  clip_sumsq ? clip_sumsq->data_ptr<float>() : nullptr, (float)max_norm, cur_stream()),
+        "adamw");
+}
+void f32_to_bf16(const at::Tensor& x, at::Tensor& y) {
+  req(x, at::kFloat, "x");
+  req(y, at::kBFloat16, "y");
+  TORCH_CHECK(x.numel() == y.numel(), "f32_to_bf16: size mismatch");
+  check(pcb_f32_to_bf16(x.data_ptr<float>(), y.data_ptr(), x.numel(), cur_stream()), "f32_to_bf16");
+}
+void attn_fwd(const at::Tensor& qkv, at::Tensor& out, at::Tensor& lse, int64_t B, int64_t S, int64_t H, int64_t HD,
+              double scale) {
+  req(qkv, at::kBFloat16, "qkv");
+  req(out, at::kBFloat16, "out");
+  req(lse, at::kFloat, "lse");
+  check(pcb_attn_fwd(qkv.data_ptr(), row_stride(qkv, "qkv"), out.data_ptr(), row_stride(out, "out"),
+                     lse.data_ptr<float>(), B, S, H, HD, (float)scale, cur_stream()),
+        "attn_fwd");
+}
+void attn_bwd(const at::Tensor& qkv, const at::Tensor& out, const at::Tensor& dout, const at::Tensor& lse,
+              at::Tensor& dvec, at::Tensor& dq_acc, at::Tensor& dqkv, int64_t B, int64_t S, int64_t H, int64_t HD,
+              double scale) {
+  req(qkv, at::kBFloat16, "qkv");
+  req(dout, at::kBFloat16, "dout");
+  req(dqkv, at::kBFloat16, "dqkv");
+  req(dq_acc, at::kFloat, "dq_acc");
+  TORCH_CHECK(row_stride(out, "out") == row_stride(dout, "dout"), "attn_bwd: out/dout strides differ");
+  check(pcb_attn_bwd(qkv.data_ptr(), row_stride(qkv, "qkv"), out.data_ptr(), dout.data_ptr(), row_stride(dout, "dout"),
+                     lse.data_ptr<float>(), dvec.data_ptr<float>(), dq_acc.data_ptr<float>(), dqkv.data_ptr(),
+                     row_stride(dqkv, "dqkv"), B, S, H, HD, (float)scale, cur_stream()),
+        "attn_bwd", 3);
+}
+
+int64_t launch_count() { return g_launches.load(); }
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "predicitivecoding_b200 sm_100a kernels";
+  m.def("gemm", &gemm);
+  m.def("gemm_pc", &gemm_pc);
+  m.def("embed_fwd", &embed_fwd);
+  m.def("embed_bwd", &embed_bwd);
+  m.def("rmsnorm_fwd", &rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("rope", &rope);
+  m.def("cross_entropy", &cross_entropy);
+  m.def("sumsq", &sumsq);
+  m.def("colsum", &colsum);
+  m.def("adamw", &adamw);
+  m.def("f32_to_bf16", &f32_to_bf16);
+  m.def("attn_fwd", &attn_fwd);
+  m.def("attn_bwd", &attn_bwd);
+  m.def("launch_count", &launch_count);
+}

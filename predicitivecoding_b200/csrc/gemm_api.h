@@ -1,0 +1,58 @@
+// Host-safe GEMM API shared by the CUDA sources and the C++ bindings.
+#pragma once
+#include <cuda_runtime.h>
+
+namespace pcb {
+
+enum GemmEpi : int {
+  EPI_BF16 = 0,        // C(bf16)  = alpha*acc + bias
+  EPI_F32 = 1,         // C(f32)   = alpha*acc + bias
+  EPI_ACC_F32 = 2,     // C(f32)  += alpha*acc + bias          (plain read-modify-write)
+  EPI_RED_F32 = 3,     // C(f32)  += alpha*acc                 (atomic: split-K / accumulate)
+  EPI_GELU = 4,        // C(bf16)  = pre = acc + bias ; D(bf16) = gelu(pre)
+  EPI_SWIGLU = 5,      // C(bf16)  = pre [M,2F] (64-col gate/up interleave) ; D(bf16) = silu(g)*u [M,F]
+  EPI_SWIGLU_BWD = 6,  // acc = d(act)[M,F], aux = pre[M,2F] ; C(bf16) = d(pre)[M,2F]
+  EPI_GELU_BWD = 7,    // acc = d(act), aux = pre(bf16) ; C(bf16) = d(act)*gelu'(pre)
+  EPI_PC_PRED = 8,     // PC prediction + error + delta (see gemm_epilogue_pc)
+  EPI_PC_STATE = 9,    // PC state update
+  EPI_PC_WUPD = 10,    // PC Hebbian weight update (single rank)
+  EPI_BF16_ACC = 11,   // C(bf16) = alpha*acc + aux(bf16)      (bf16 residual add)
+  EPI_RESID_F32 = 12,  // C(f32)  = aux(f32) + alpha*acc + bias (residual stream: x_out = x_in + f(x))
+  EPI_COUNT = 13,
+};
+
+struct GemmArgs {
+  int M, N, K;
+  int a_mn, b_mn;
+  int splits;           // K splits (>= 1)
+  int kb_per_split;     // k-blocks (of 64) per split
+  float alpha;
+  void* C;              // primary output (see epilogue)
+  long long ldc;
+  void* D;              // secondary output
+  long long ldd;
+  const void* aux;      // auxiliary input
+  long long ldaux;
+  const void* bias;     // [N] or nullptr (fp32, or bf16 when bias_bf16)
+  int bias_bf16;
+  int* err;             // device error word (may be nullptr)
+  // predictive-coding epilogue parameters
+  int act;              // 0 linear, 1 tanh, 2 relu, 3 sigmoid
+  float pc_pi;          // precision of the layer below (EPI_PC_PRED)
+  float pc_eta;         // state lr (EPI_PC_STATE) / weight lr / batch (EPI_PC_WUPD)
+  float pc_actreg;      // L1 activity regularisation (EPI_PC_STATE)
+  float pc_decay;       // multiplicative decay (EPI_PC_WUPD): W <- (W + eta*acc) * decay
+  float* pc_energy;     // sum of squared errors accumulator (EPI_PC_PRED), may be nullptr
+  void* pc_pred_out;    // optional prediction output fp32 (EPI_PC_PRED, FFG warm start)
+  long long ld_pred;
+  void* pc_pred_bf16;   // optional bf16 copy of the prediction (FFG warm start)
+};
+
+}  // namespace pcb
+
+// Host entry: launches the kernel for the given operands.  Returns 0 on success.
+// `A`/`B` are bf16 device pointers.  lda/ldb are row strides in elements of the
+// operand as stored (K-major: stride between M/N rows; MN-major: stride between K rows).
+int pcb_gemm_launch(const void* A, int a_mn, long long lda, const void* B, int b_mn, long long ldb,
+                    int epi, pcb::GemmArgs args, int force_bn, int force_splits, int num_sms,
+                    cudaStream_t stream);

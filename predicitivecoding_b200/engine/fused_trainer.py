@@ -1,0 +1,418 @@
+"""Device-resident decoder trainer on the hand-written sm_100a kernels.
+
+The B200 counterpart of the reference's ``DeviceDecoderTrainer``
+(PredictiveCoding.Device/Training/DeviceDecoderTrainer.cs:40-575): weights, Adam
+state and every activation live in preallocated device buffers; a step is one
+forward, one fused cross-entropy, one backward and one AdamW, with the loss as
+the only value read back.  Differences by design:
+
+* true batches: the reference trains one sequence per launch chain and
+  accumulates windows; here one step processes ``batch`` sequences at once;
+* bf16 tensor-core GEMMs (tcgen05) with fused epilogues (residual add, GELU /
+  SwiGLU, their backward), fp32 residual stream and fp32 master weights;
+* one flat parameter arena (fp32 master, grads, moments, bf16 working copy),
+  sharded over data-parallel ranks (ZeRO-1): gradients are reduce-scattered,
+  each rank runs AdamW on its shard, bf16 weights are all-gathered;
+* the whole step is captured into one CUDA graph (single rank) so the ~280
+  launches of a 12-layer step cost one graph launch on the host.
+
+Supported family: RMSNorm + RoPE dense decoders (GELU FFN with biases, as the
+reference trains, or SwiGLU without biases), head_dim 64/128, seq % 128 == 0 —
+the same restriction as the reference's ``Supports`` (DeviceDecoderTrainer.cs:104-110)
+plus the SwiGLU extension.
+"""
+from __future__ import annotations
+
+import math
+import time
+from typing import Dict, List, Optional, Sequence
+
+import torch
+
+from .. import ops
+from ..models.config import DecoderLmConfig
+from ..models.decoder_lm import DecoderLM, rope_tables
+from .arena import ParamArena, ParamSpec
+
+
+def supports(cfg: DecoderLmConfig, seq: Optional[int] = None) -> bool:
+    """True when ``cfg`` can run on the fused device path."""
+    s = seq or cfg.max_seq
+    return (cfg.use_rms_norm and cfg.use_rope and cfg.block_pattern is None and cfg.num_experts == 0
+            and cfg.num_loops == 1 and cfg.mtp_weight == 0 and not cfg.use_plan and cfg.dropout == 0
+            and cfg.head_dim in (64, 128) and s % 128 == 0 and cfg.dim % 64 == 0 and cfg.ff_dim % 64 == 0
+            and cfg.vocab % 8 == 0)
+
+
+def _interleave_gate_up(gate_t: torch.Tensor, up_t: torch.Tensor) -> torch.Tensor:
+    """[F, D] gate and up rows -> [2F, D] with 64-row groups [gate_g | up_g] (the SwiGLU epilogue layout)."""
+    F_, D = gate_t.shape
+    g = gate_t.reshape(F_ // 64, 64, D)
+    u = up_t.reshape(F_ // 64, 64, D)
+    return torch.stack((g, u), dim=1).reshape(2 * F_, D)
+
+
+def _split_gate_up(w13: torch.Tensor):
+    F2, D = w13.shape
+    x = w13.reshape(F2 // 128, 2, 64, D)
+    return x[:, 0].reshape(F2 // 2, D), x[:, 1].reshape(F2 // 2, D)
+
+
+class FusedDecoderTrainer:
+    """One data-parallel rank of the fused decoder training step."""
+
+    def __init__(self, cfg: DecoderLmConfig, batch: int, seq: Optional[int] = None, *, device="cuda",
+                 lr: float = 3e-4, weight_decay: float = 0.1, betas=(0.9, 0.999), eps: float = 1e-8,
+                 clip_norm: float = 0.0, seed: int = 42, model: Optional[DecoderLM] = None,
+                 decay_all: bool = True, process_group=None, grad_sync: str = "auto", use_graph: bool = True):
+        seq = seq or cfg.max_seq
+        if not supports(cfg, seq):
+            raise NotImplementedError("FusedDecoderTrainer needs a dense RMSNorm+RoPE config "
+                                      "(head_dim 64/128, seq % 128 == 0); use the autograd path.")
+        self.cfg, self.B, self.S = cfg, batch, seq
+        self.M = batch * seq
+        self.device = torch.device(device)
+        self.lr, self.wd, self.betas, self.eps, self.clip_norm = lr, weight_decay, betas, eps, clip_norm
+        self.t = 0
+        self.use_graph = use_graph
+        self.graph: Optional[torch.cuda.CUDAGraph] = None
+        self.tokens_seen = 0
+
+        # ---------------- data parallel
+        self.pg = process_group
+        if self.pg is not None:
+            import torch.distributed as dist
+            self.world, self.rank = dist.get_world_size(self.pg), dist.get_rank(self.pg)
+        else:
+            self.world, self.rank = 1, 0
+        if grad_sync == "auto":
+            grad_sync = "zero" if self.world > 1 else "none"
+        self.grad_sync = grad_sync
+        self.peer = None  # fused peer-memory reducer, set by enable_fused_dp()
+
+        # ---------------- parameters
+        D, F_, V, L = cfg.dim, cfg.ff_dim, cfg.vocab, cfg.num_blocks
+        specs = [ParamSpec("wemb", (V, D))]
+        for l in range(L):
+            specs.append(ParamSpec(f"b{l}.wqkv", (3 * D, D)))
+            specs.append(ParamSpec(f"b{l}.wo", (D, D)))
+            if cfg.ffn == "swiglu":
+                specs.append(ParamSpec(f"b{l}.w13", (2 * F_, D)))
+            else:
+                specs.append(ParamSpec(f"b{l}.w1", (F_, D)))
+            specs.append(ParamSpec(f"b{l}.w2", (D, F_)))
+        specs.append(ParamSpec("wout", (V, D)))
+        for l in range(L):
+            specs.append(ParamSpec(f"b{l}.ln1", (D,), decay_all))
+            specs.append(ParamSpec(f"b{l}.ln2", (D,), decay_all))
+            if cfg.ffn == "gelu":
+                specs.append(ParamSpec(f"b{l}.b1", (F_,), decay_all))
+                specs.append(ParamSpec(f"b{l}.b2", (D,), decay_all))
+        specs.append(ParamSpec("lnf", (D,), decay_all))
+        self.arena = ParamArena(specs, self.world)
+        A = self.arena
+        dev = self.device
+        f32, bf16 = torch.float32, torch.bfloat16
+        self.w16 = torch.zeros(A.total, device=dev, dtype=bf16)      # full bf16 working copy (replicated)
+        self.grad = torch.zeros(A.total, device=dev, dtype=f32)      # full gradient (local, then reduced)
+        lo, hi = self.rank * A.shard, (self.rank + 1) * A.shard
+        self.shard_lo, self.shard_hi = lo, hi
+        self.w32 = torch.zeros(A.shard, device=dev, dtype=f32)       # fp32 master shard
+        self.m = torch.zeros(A.shard, device=dev, dtype=f32)
+        self.v = torch.zeros(A.shard, device=dev, dtype=f32)
+        self.grad_shard = self.grad[lo:hi] if self.world == 1 else torch.zeros(A.shard, device=dev, dtype=f32)
+        self.n_decay_local = max(0, min(A.n_decay - lo, A.shard))
+        self.hyper_host = torch.zeros(8, dtype=f32).pin_memory()
+        self.hyper = torch.zeros(8, device=dev, dtype=f32)
+        self.clip_buf = torch.zeros(1, device=dev, dtype=f32)
+        self.W = A.views(self.w16)   # bf16 views by name
+        self.G = A.views(self.grad)  # fp32 grad views by name
+
+        if model is None:
+            model = DecoderLM(cfg, seed=seed)
+        self.import_model(model)
+
+        # ---------------- activations
+        M, S, H, hd = self.M, seq, cfg.num_heads, cfg.head_dim
+        z = lambda *shape, dt=bf16: torch.empty(*shape, device=dev, dtype=dt)
+        self.tok = torch.zeros(M, device=dev, dtype=torch.int32)
+        self.tgt = torch.zeros(M, device=dev, dtype=torch.int32)
+        self.tok_pin = torch.zeros(M, dtype=torch.int32).pin_memory()
+        self.tgt_pin = torch.zeros(M, dtype=torch.int32).pin_memory()
+        self.loss_pin = torch.zeros(1, dtype=f32).pin_memory()
+        self.x = [z(M, D, dt=f32) for _ in range(L + 1)]
+        self.xmid = [z(M, D, dt=f32) for _ in range(L)]
+        self.n1 = [z(M, D) for _ in range(L)]
+        self.n2 = [z(M, D) for _ in range(L)]
+        self.inv1 = [z(M, dt=f32) for _ in range(L)]
+        self.inv2 = [z(M, dt=f32) for _ in range(L)]
+        self.qkv = [z(M, 3 * D) for _ in range(L)]
+        self.ao = [z(M, D) for _ in range(L)]
+        self.lse = [z(batch * H, S, dt=f32) for _ in range(L)]
+        fpre = 2 * F_ if cfg.ffn == "swiglu" else F_
+        self.pre = [z(M, fpre) for _ in range(L)]
+        self.act = [z(M, F_) for _ in range(L)]
+        self.nf = z(M, D)
+        self.invf = z(M, dt=f32)
+        self.logits = z(M, V)
+        self.loss_rows = z(M, dt=f32)
+        self.loss_sum = z(1, dt=f32)
+        # backward scratch
+        self.dx = z(M, D, dt=f32)
+        self.dx16 = z(M, D)
+        self.dn = z(M, D, dt=f32)
+        self.dpre = z(M, fpre)
+        self.dao = z(M, D)
+        self.dqkv = z(M, 3 * D)
+        self.dq_acc = z(M, D, dt=f32)
+        self.dvec = z(batch * H, S, dt=f32)
+        cos, sin = rope_tables(S, hd, 0, device=dev)
+        self.rope_cs = torch.stack((cos, sin), dim=-1).contiguous()  # [S, hd/2, 2]
+        self.attn_scale = 1.0 / math.sqrt(hd)
+        self.launches_per_step = None
+
+    # ------------------------------------------------------------------ weights in/out
+    @torch.no_grad()
+    def import_model(self, model: DecoderLM) -> None:
+        """Copy a DecoderLM's weights (reference [in,out] layout) into the arena."""
+        cfg = self.cfg
+        full = torch.zeros(self.arena.total, dtype=torch.float32)
+        V = self.arena.views(full)
+        V["wemb"].copy_(model.wemb.detach().float().cpu())
+        for l, blk in enumerate(model.blocks):
+            V[f"b{l}.wqkv"].copy_(torch.cat([blk.wq.T, blk.wk.T, blk.wv.T], 0).cpu())
+            V[f"b{l}.wo"].copy_(blk.wo.T.cpu())
+            V[f"b{l}.ln1"].copy_(blk.ln1_g.cpu())
+            V[f"b{l}.ln2"].copy_(blk.ln2_g.cpu())
+            if cfg.ffn == "swiglu":
+                V[f"b{l}.w13"].copy_(_interleave_gate_up(blk.w1.T.cpu(), blk.w3.T.cpu()))
+            else:
+                V[f"b{l}.w1"].copy_(blk.w1.T.cpu())
+                V[f"b{l}.b1"].copy_(blk.b1.cpu())
+                V[f"b{l}.b2"].copy_(blk.b2.cpu())
+            V[f"b{l}.w2"].copy_(blk.w2.T.cpu())
+        V["lnf"].copy_(model.lnf_g.cpu())
+        V["wout"].copy_(model.wout.T.cpu())
+        full_d = full.to(self.device)
+        self.w32.copy_(full_d[self.shard_lo:self.shard_hi])
+        self.w16.copy_(full_d.to(torch.bfloat16))
+        self.m.zero_()
+        self.v.zero_()
+        self.t = 0
+
+    @torch.no_grad()
+    def master_weights(self) -> torch.Tensor:
+        """Full fp32 master buffer (all-gathered across ranks)."""
+        if self.world == 1:
+            return self.w32.clone()
+        import torch.distributed as dist
+        out = torch.empty(self.arena.total, device=self.device, dtype=torch.float32)
+        dist.all_gather_into_tensor(out, self.w32, group=self.pg)
+        return out
+
+    @torch.no_grad()
+    def export_model(self, model: Optional[DecoderLM] = None) -> DecoderLM:
+        """Write the fp32 master weights back into a DecoderLM (reference layout)."""
+        cfg = self.cfg
+        if model is None:
+            model = DecoderLM(cfg)
+        V = self.arena.views(self.master_weights().cpu())
+        model.wemb.copy_(V["wemb"])
+        D = cfg.dim
+        for l, blk in enumerate(model.blocks):
+            wqkv = V[f"b{l}.wqkv"]
+            blk.wq.copy_(wqkv[:D].T)
+            blk.wk.copy_(wqkv[D:2 * D].T)
+            blk.wv.copy_(wqkv[2 * D:].T)
+            blk.wo.copy_(V[f"b{l}.wo"].T)
+            blk.ln1_g.copy_(V[f"b{l}.ln1"])
+            blk.ln2_g.copy_(V[f"b{l}.ln2"])
+            if cfg.ffn == "swiglu":
+                g, u = _split_gate_up(V[f"b{l}.w13"])
+                blk.w1.copy_(g.T)
+                blk.w3.copy_(u.T)
+            else:
+                blk.w1.copy_(V[f"b{l}.w1"].T)
+                blk.b1.copy_(V[f"b{l}.b1"])
+                blk.b2.copy_(V[f"b{l}.b2"])
+            blk.w2.copy_(V[f"b{l}.w2"].T)
+        model.lnf_g.copy_(V["lnf"])
+        model.wout.copy_(V["wout"].T)
+        return model
+
+    # ------------------------------------------------------------------ the step
+    def _forward(self, write_grad: bool = True) -> None:
+        cfg = self.cfg
+        W = self.W
+        B, S, M, D, H, hd = self.B, self.S, self.M, cfg.dim, cfg.num_heads, cfg.head_dim
+        ops.embed_fwd(self.tok, W["wemb"], self.x[0])
+        for l in range(cfg.num_blocks):
+            ops.rmsnorm_fwd(self.x[l], W[f"b{l}.ln1"], self.n1[l], self.inv1[l], cfg.eps)
+            ops.gemm(self.n1[l], W[f"b{l}.wqkv"], epi=ops.EPI_BF16, c=self.qkv[l])
+            ops.rope(self.qkv[l], self.rope_cs, S, D, hd, 2, 1.0)
+            ops.attn_fwd(self.qkv[l], self.ao[l], self.lse[l], B, S, H, hd, self.attn_scale)
+            ops.gemm(self.ao[l], W[f"b{l}.wo"], epi=ops.EPI_RESID_F32, c=self.xmid[l], aux=self.x[l])
+            ops.rmsnorm_fwd(self.xmid[l], W[f"b{l}.ln2"], self.n2[l], self.inv2[l], cfg.eps)
+            if cfg.ffn == "swiglu":
+                ops.gemm(self.n2[l], W[f"b{l}.w13"], epi=ops.EPI_SWIGLU, c=self.pre[l], d=self.act[l])
+                ops.gemm(self.act[l], W[f"b{l}.w2"], epi=ops.EPI_RESID_F32, c=self.x[l + 1], aux=self.xmid[l])
+            else:
+                ops.gemm(self.n2[l], W[f"b{l}.w1"], epi=ops.EPI_GELU, c=self.pre[l], d=self.act[l],
+                         bias=W[f"b{l}.b1"])
+                ops.gemm(self.act[l], W[f"b{l}.w2"], epi=ops.EPI_RESID_F32, c=self.x[l + 1], aux=self.xmid[l],
+                         bias=W[f"b{l}.b2"])
+        L = cfg.num_blocks
+        ops.rmsnorm_fwd(self.x[L], W["lnf"], self.nf, self.invf, cfg.eps)
+        ops.gemm(self.nf, W["wout"], epi=ops.EPI_BF16, c=self.logits)
+        ops.cross_entropy(self.logits, self.tgt, self.loss_rows, 1.0 / M, write_grad)
+        self.loss_sum.zero_()
+        ops.sumsq(self.loss_rows, self.loss_sum, square=False)
+
+    def _backward(self) -> None:
+        cfg = self.cfg
+        W, G = self.W, self.G
+        B, S, D, H, hd = self.B, self.S, cfg.dim, cfg.num_heads, cfg.head_dim
+        L = cfg.num_blocks
+        RED = ops.EPI_RED_F32
+        dl = self.logits  # holds dlogits after the fused CE
+        ops.gemm(dl, self.nf, a_mn=True, b_mn=True, epi=RED, c=G["wout"])           # dWout = dL^T nf
+        ops.gemm(dl, W["wout"], b_mn=True, epi=ops.EPI_F32, c=self.dn)              # dnf = dL Wout
+        ops.rmsnorm_bwd(self.dn, self.x[L], W["lnf"], self.invf, self.dx, G["lnf"], False, self.dx16)
+        for l in reversed(range(L)):
+            # ---- FFN: x_{l+1} = xmid + ffn(norm2(xmid))
+            ops.gemm(self.dx16, self.act[l], a_mn=True, b_mn=True, epi=RED, c=G[f"b{l}.w2"])
+            if cfg.ffn == "swiglu":
+                ops.gemm(self.dx16, W[f"b{l}.w2"], b_mn=True, epi=ops.EPI_SWIGLU_BWD, c=self.dpre, aux=self.pre[l])
+                ops.gemm(self.dpre, self.n2[l], a_mn=True, b_mn=True, epi=RED, c=G[f"b{l}.w13"])
+                ops.gemm(self.dpre, W[f"b{l}.w13"], b_mn=True, epi=ops.EPI_F32, c=self.dn)
+            else:
+                ops.colsum(self.dx16, G[f"b{l}.b2"])
+                ops.gemm(self.dx16, W[f"b{l}.w2"], b_mn=True, epi=ops.EPI_GELU_BWD, c=self.dpre, aux=self.pre[l])
+                ops.colsum(self.dpre, G[f"b{l}.b1"])
+                ops.gemm(self.dpre, self.n2[l], a_mn=True, b_mn=True, epi=RED, c=G[f"b{l}.w1"])
+                ops.gemm(self.dpre, W[f"b{l}.w1"], b_mn=True, epi=ops.EPI_F32, c=self.dn)
+            ops.rmsnorm_bwd(self.dn, self.xmid[l], W[f"b{l}.ln2"], self.inv2[l], self.dx, G[f"b{l}.ln2"], True,
+                            self.dx16)
+            # ---- attention: xmid = x + attn(norm1(x)) Wo
+            ops.gemm(self.dx16, self.ao[l], a_mn=True, b_mn=True, epi=RED, c=G[f"b{l}.wo"])
+            ops.gemm(self.dx16, W[f"b{l}.wo"], b_mn=True, epi=ops.EPI_BF16, c=self.dao)
+            ops.attn_bwd(self.qkv[l], self.ao[l], self.dao, self.lse[l], self.dvec, self.dq_acc, self.dqkv,
+                         B, S, H, hd, self.attn_scale)
+            ops.rope(self.dqkv, self.rope_cs, S, D, hd, 2, -1.0)
+            ops.gemm(self.dqkv, self.n1[l], a_mn=True, b_mn=True, epi=RED, c=G[f"b{l}.wqkv"])
+            ops.gemm(self.dqkv, W[f"b{l}.wqkv"], b_mn=True, epi=ops.EPI_F32, c=self.dn)
+            ops.rmsnorm_bwd(self.dn, self.x[l], W[f"b{l}.ln1"], self.inv1[l], self.dx, G[f"b{l}.ln1"], True,
+                            self.dx16)
+        ops.embed_bwd(self.tok, self.dx, G["wemb"])
+
+    def _optimizer(self) -> None:
+        """Gradient sync (data parallel) + AdamW on this rank's shard + bf16 weight refresh."""
+        self.hyper.copy_(self.hyper_host, non_blocking=True)
+        if self.world > 1:
+            if self.peer is not None:
+                self.peer.reduce_scatter_adamw(self)
+                return
+            import torch.distributed as dist
+            dist.reduce_scatter_tensor(self.grad_shard, self.grad, group=self.pg)
+        clip = None
+        if self.clip_norm > 0:
+            self.clip_buf.zero_()
+            ops.sumsq(self.grad_shard, self.clip_buf, square=True)
+            if self.world > 1:
+                import torch.distributed as dist
+                dist.all_reduce(self.clip_buf, group=self.pg)
+            clip = self.clip_buf
+        w16_shard = self.w16[self.shard_lo:self.shard_hi]
+        ops.adamw(self.w32, self.grad_shard, self.m, self.v, w16_shard, self.n_decay_local, self.hyper,
+                  self.betas[0], self.betas[1], self.eps, clip, self.clip_norm)
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.all_gather_into_tensor(self.w16, w16_shard, group=self.pg)
+
+    def _step_body(self) -> None:
+        self.tok.copy_(self.tok_pin, non_blocking=True)
+        self.tgt.copy_(self.tgt_pin, non_blocking=True)
+        self.grad.zero_()
+        self._forward(True)
+        self._backward()
+        self._optimizer()
+        self.loss_pin.copy_(self.loss_sum, non_blocking=True)
+
+    def _set_hyper(self, lr: float) -> None:
+        self.t += 1
+        b1, b2 = self.betas
+        self.hyper_host[0] = lr
+        self.hyper_host[1] = self.wd
+        self.hyper_host[2] = 1.0 - b1 ** self.t
+        self.hyper_host[3] = 1.0 - b2 ** self.t
+        # gradients are sums over ranks of per-rank means: fold the 1/world mean here
+        self.hyper_host[4] = 1.0 / self.world
+
+    def stage(self, tokens: torch.Tensor, targets: torch.Tensor) -> None:
+        """Copy one step's [B, S] int tokens/targets into the pinned staging buffers."""
+        self.tok_pin.copy_(tokens.reshape(-1).to(torch.int32))
+        self.tgt_pin.copy_(targets.reshape(-1).to(torch.int32))
+
+    def launch(self, lr: Optional[float] = None) -> None:
+        """Enqueue one full training step on the current stream (no host sync)."""
+        self._set_hyper(self.lr if lr is None else lr)
+        if self.use_graph and self.world == 1:
+            if self.graph is None:
+                self._capture()
+            self.graph.replay()
+        else:
+            self._step_body()
+        self.tokens_seen += self.M
+
+    def _capture(self) -> None:
+        # one eager step first: sets kernel attributes and driver entry points outside capture,
+        # then restore the state it touched so the captured step starts from the same place
+        w32, w16, m, v = self.w32.clone(), self.w16.clone(), self.m.clone(), self.v.clone()
+        before = ops.launch_count()
+        self._step_body()
+        torch.cuda.synchronize(self.device)
+        self.launches_per_step = ops.launch_count() - before
+        self.w32.copy_(w32); self.w16.copy_(w16); self.m.copy_(m); self.v.copy_(v)
+        del w32, w16, m, v
+        self.graph = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(self.graph, stream=s):
+                self._step_body()
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        torch.cuda.synchronize(self.device)
+
+    def read_loss(self) -> float:
+        """Synchronise and return the mean loss of the last launched step."""
+        torch.cuda.current_stream(self.device).synchronize()
+        return float(self.loss_pin[0]) / self.M
+
+    def step(self, tokens: torch.Tensor, targets: torch.Tensor, lr: Optional[float] = None) -> float:
+        """Public API: one training step on host tokens/targets [B, S]; returns the mean loss."""
+        self.stage(tokens, targets)
+        self.launch(lr)
+        return self.read_loss()
+
+    @torch.no_grad()
+    def evaluate_loss(self, tokens: torch.Tensor, targets: torch.Tensor) -> float:
+        """Mean CE without touching gradients or weights (DeviceDecoderTrainer.EvaluateLoss)."""
+        self.stage(tokens, targets)
+        self.tok.copy_(self.tok_pin, non_blocking=True)
+        self.tgt.copy_(self.tgt_pin, non_blocking=True)
+        self._forward(write_grad=False)
+        self.loss_pin.copy_(self.loss_sum, non_blocking=True)
+        return self.read_loss()
+
+    # ------------------------------------------------------------------ optimizer state
+    def adam_state(self):
+        return self.t, self.m, self.v
+
+    def flops_per_step(self) -> float:
+        """Model FLOPs of one step (6*N*T for the matmuls + causal attention fwd/bwd)."""
+        cfg = self.cfg
+        D, F_, V, L = cfg.dim, cfg.ff_dim, cfg.vocab, cfg.num_blocks
+        ffn = (3 if cfg.ffn == "swiglu" else 2) * D * F_
+        mat = L * (4 * D * D + ffn) + V * D
+        attn = L * 2 * 2 * self.S * D / 2  # QK^T and PV, causal half, per token
+        return 6.0 * mat * self.M + 3.0 * attn * self.M

@@ -1,0 +1,138 @@
+"""Python entry points of the sm_100a kernels.
+
+The compiled extension ``predicitivecoding_b200._C`` is built in-tree by
+``python setup.py build_ext --inplace`` (or ``__graft_entry__.build()``).  On a
+machine with a CUDA device the extension is mandatory: :func:`ext` raises if it
+cannot be imported, so no GPU code path silently falls back to PyTorch.
+"""
+from __future__ import annotations
+
+import importlib
+from typing import Optional
+
+import torch
+
+_EXT = None
+_EXT_ERR: Optional[BaseException] = None
+
+# GEMM epilogues (must match csrc/gemm_api.h)
+EPI_BF16 = 0
+EPI_F32 = 1
+EPI_ACC_F32 = 2
+EPI_RED_F32 = 3
+EPI_GELU = 4
+EPI_SWIGLU = 5
+EPI_SWIGLU_BWD = 6
+EPI_GELU_BWD = 7
+EPI_PC_PRED = 8
+EPI_PC_STATE = 9
+EPI_PC_WUPD = 10
+EPI_BF16_ACC = 11
+EPI_RESID_F32 = 12
+
+ACT_CODES = {"linear": 0, "tanh": 1, "relu": 2, "sigmoid": 3}
+
+
+def ext():
+    """Return the compiled kernel module, raising a clear error when it is missing."""
+    global _EXT, _EXT_ERR
+    if _EXT is None:
+        try:
+            _EXT = importlib.import_module("predicitivecoding_b200._C")
+        except Exception as e:  # pragma: no cover - depends on the build
+            _EXT_ERR = e
+            raise RuntimeError(
+                "predicitivecoding_b200._C is not built; run `python setup.py build_ext --inplace` "
+                f"(import error: {e})"
+            ) from e
+    return _EXT
+
+
+def available() -> bool:
+    try:
+        ext()
+        return True
+    except RuntimeError:
+        return False
+
+
+def launch_count() -> int:
+    """Number of kernel launches issued through the bindings since import."""
+    return int(ext().launch_count())
+
+
+# --------------------------------------------------------------------------- GEMM
+def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = False, epi: int = EPI_BF16,
+         c: Optional[torch.Tensor] = None, d: Optional[torch.Tensor] = None, aux: Optional[torch.Tensor] = None,
+         bias: Optional[torch.Tensor] = None, alpha: float = 1.0, bn: int = 0, splits: int = 0,
+         err: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:
+    """C = epilogue(op(a) @ op(b)) on the tcgen05 tensor cores.
+
+    ``a`` is [M, K] (``a_mn=False``) or [K, M] (``a_mn=True``); ``b`` is [N, K]
+    (``b_mn=False``, the nn.Linear weight layout) or [K, N] (``b_mn=True``).
+    With ``epi=EPI_BF16`` and ``c=None`` a new bf16 output is allocated.
+    """
+    if c is None and epi in (EPI_BF16, EPI_F32):
+        M = a.shape[1] if a_mn else a.shape[0]
+        N = b.shape[1] if b_mn else b.shape[0]
+        c = torch.empty(M, N, device=a.device, dtype=torch.bfloat16 if epi == EPI_BF16 else torch.float32)
+    ext().gemm(a, a_mn, b, b_mn, epi, c, d, aux, bias, float(alpha), int(bn), int(splits), err)
+    return c
+
+
+def gemm_pc(a, b, *, a_mn=False, b_mn=False, epi, c=None, d=None, aux=None, bias=None, alpha=1.0, act="tanh",
+            pi=1.0, eta=0.1, actreg=0.0, decay=1.0, energy=None, pred_out=None, pred_bf16=None, err=None):
+    """GEMM with a predictive-coding epilogue (prediction/error, state update or weight update)."""
+    ext().gemm_pc(a, a_mn, b, b_mn, epi, c, d, aux, bias, float(alpha), ACT_CODES[act] if isinstance(act, str) else int(act),
+                  float(pi), float(eta), float(actreg), float(decay), energy, pred_out, pred_bf16, err)
+
+
+# --------------------------------------------------------------------------- elementwise
+def embed_fwd(tok, W, x):
+    ext().embed_fwd(tok, W, x)
+
+
+def embed_bwd(tok, dx, dW):
+    ext().embed_bwd(tok, dx, dW)
+
+
+def rmsnorm_fwd(x, g, y, inv, eps):
+    ext().rmsnorm_fwd(x, g, y, inv, float(eps))
+
+
+def rmsnorm_bwd(dy, x, g, inv, dx, dg, accumulate=False, dx16=None):
+    ext().rmsnorm_bwd(dy, x, g, inv, dx, dx16, dg, bool(accumulate))
+
+
+def rope(buf, cs, S, D, hd, nparts=2, sign=1.0):
+    ext().rope(buf, cs, int(S), int(D), int(hd), int(nparts), float(sign))
+
+
+def cross_entropy(logits, tgt, loss, scale, write_grad=True):
+    ext().cross_entropy(logits, tgt, loss, float(scale), bool(write_grad))
+
+
+def sumsq(x, out, square=True):
+    """out[0] += sum(x**2) (square=True, non-finite entries count as 0) or sum(x)."""
+    ext().sumsq(x, out, bool(square))
+
+
+def colsum(x, out, scale=1.0):
+    ext().colsum(x, out, float(scale))
+
+
+def adamw(w, g, m, v, w16, n_decay, hyper, b1=0.9, b2=0.999, eps=1e-8, clip_sumsq=None, max_norm=0.0):
+    """Flat AdamW; ``hyper`` is a device fp32 tensor [lr, wd, bc1, bc2, grad_scale]."""
+    ext().adamw(w, g, m, v, w16, int(n_decay), hyper, float(b1), float(b2), float(eps), clip_sumsq, float(max_norm))
+
+
+def f32_to_bf16(x, y):
+    ext().f32_to_bf16(x, y)
+
+
+def attn_fwd(qkv, out, lse, B, S, H, HD, scale):
+    ext().attn_fwd(qkv, out, lse, int(B), int(S), int(H), int(HD), float(scale))
+
+
+def attn_bwd(qkv, out, dout, lse, dvec, dq_acc, dqkv, B, S, H, HD, scale):
+    ext().attn_bwd(qkv, out, dout, lse, dvec, dq_acc, dqkv, int(B), int(S), int(H), int(HD), float(scale))

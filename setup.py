@@ -1,0 +1,40 @@
+"""Build the sm_100a kernels of predicitivecoding_b200 in-tree.
+
+    python setup.py build_ext --inplace
+
+produces predicitivecoding_b200/_C*.so next to the Python sources.
+"""
+import os
+
+from setuptools import setup
+from torch.utils.cpp_extension import BuildExtension, CUDAExtension
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+CSRC = os.path.join("predicitivecoding_b200", "csrc")
+
+NVCC_FLAGS = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-O3", "-lineinfo", "-std=c++17",
+    "--expt-relaxed-constexpr",
+    "-Xptxas", "-warn-spills",
+]
+
+setup(
+    name="predicitivecoding_b200",
+    version="0.1.0",
+    packages=["predicitivecoding_b200"],
+    ext_modules=[
+        CUDAExtension(
+            name="predicitivecoding_b200._C",
+            sources=[
+                os.path.join(CSRC, "bindings.cpp"),
+                os.path.join(CSRC, "gemm_tcgen05.cu"),
+                os.path.join(CSRC, "ops_llm.cu"),
+                os.path.join(CSRC, "attention.cu"),
+            ],
+            include_dirs=[os.path.join(HERE, CSRC)],
+            extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
+        )
+    ],
+    cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
+)

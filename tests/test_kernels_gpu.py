@@ -1,0 +1,257 @@
+"""Numerics of every sm_100a kernel against a plain PyTorch fp32 reference of the same op.
+
+Tolerances follow the reference's own GPU parity tests: bf16 GEMM within 0.02
+relative (TEST/PredicitiveCoding.UnitTests/LlmDeviceTrainTests.cs:302-335), fused
+attention forward/backward vs autograd (:90-182, loosened from 1e-4 for bf16 operands).
+"""
+import math
+
+import pytest
+import torch
+
+from predicitivecoding_b200 import ops
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def rel_err(a, b):
+    a, b = a.float(), b.float()
+    return float((a - b).norm() / (b.norm() + 1e-12))
+
+
+def _operands(M, N, K, a_mn, b_mn, seed=0):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    A = torch.randn(M, K, generator=g).to(DEV, torch.bfloat16)       # logical [M, K]
+    B = torch.randn(K, N, generator=g).to(DEV, torch.bfloat16)       # logical [K, N]
+    a_st = A.t().contiguous() if a_mn else A.contiguous()            # stored [K,M] or [M,K]
+    b_st = B.contiguous() if b_mn else B.t().contiguous()            # stored [K,N] or [N,K]
+    ref = A.float() @ B.float()
+    return a_st, b_st, ref
+
+
+@pytest.mark.parametrize("a_mn", [False, True])
+@pytest.mark.parametrize("b_mn", [False, True])
+@pytest.mark.parametrize("shape", [(256, 256, 128), (384, 512, 320), (200, 136, 72), (1024, 768, 2048)])
+def test_gemm_layouts(a_mn, b_mn, shape):
+    M, N, K = shape
+    a, b, ref = _operands(M, N, K, a_mn, b_mn)
+    out = torch.empty(M, N, device=DEV, dtype=torch.float32)
+    ops.gemm(a, b, a_mn=a_mn, b_mn=b_mn, epi=ops.EPI_F32, c=out)
+    torch.cuda.synchronize()
+    assert rel_err(out, ref) < 1e-3, rel_err(out, ref)
+
+
+@pytest.mark.parametrize("bn", [128, 256])
+def test_gemm_bf16_out_and_bias(bn):
+    M, N, K = 512, 512, 256
+    a, b, ref = _operands(M, N, K, False, False, seed=1)
+    bias = torch.randn(N, device=DEV)
+    out = ops.gemm(a, b, epi=ops.EPI_BF16, bias=bias, alpha=0.5, bn=bn)
+    torch.cuda.synchronize()
+    assert rel_err(out, 0.5 * ref + bias) < 0.02
+
+
+def test_gemm_split_k_red():
+    M, N, K = 256, 384, 4096
+    a, b, ref = _operands(M, N, K, True, True, seed=2)
+    out = torch.ones(M, N, device=DEV)
+    ops.gemm(a, b, a_mn=True, b_mn=True, epi=ops.EPI_RED_F32, c=out, splits=8)
+    torch.cuda.synchronize()
+    assert rel_err(out, ref + 1.0) < 1e-3
+
+
+def test_gemm_resid():
+    M, N, K = 512, 256, 192
+    a, b, ref = _operands(M, N, K, False, False, seed=3)
+    x = torch.randn(M, N, device=DEV)
+    out = torch.empty_like(x)
+    ops.gemm(a, b, epi=ops.EPI_RESID_F32, c=out, aux=x)
+    torch.cuda.synchronize()
+    assert rel_err(out, ref + x) < 1e-3
+
+
+def _gelu(x):
+    return 0.5 * x * (1 + torch.tanh(0.7978845608 * (x + 0.044715 * x ** 3)))
+
+
+def test_gemm_gelu_and_bwd():
+    M, N, K = 512, 512, 256
+    a, b, ref = _operands(M, N, K, False, False, seed=4)
+    ref = ref / 16
+    bias = torch.randn(N, device=DEV) * 0.1
+    pre = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    act = torch.empty_like(pre)
+    ops.gemm(a, b, epi=ops.EPI_GELU, c=pre, d=act, bias=bias, alpha=1 / 16)
+    torch.cuda.synchronize()
+    assert rel_err(pre, ref + bias) < 0.02
+    assert rel_err(act, _gelu(pre.float())) < 0.02
+    # backward: d(pre) = (dact) * gelu'(pre), dact = a2 @ b2
+    a2, b2, dact = _operands(M, N, K, False, True, seed=5)
+    dpre = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    ops.gemm(a2, b2, b_mn=True, epi=ops.EPI_GELU_BWD, c=dpre, aux=pre)
+    x = pre.float().requires_grad_()
+    _gelu(x).backward(dact)
+    torch.cuda.synchronize()
+    assert rel_err(dpre, x.grad) < 0.02
+
+
+def test_gemm_swiglu_and_bwd():
+    M, F, D = 512, 256, 192
+    g = torch.Generator().manual_seed(6)
+    x = torch.randn(M, D, generator=g).to(DEV, torch.bfloat16)
+    wg = (torch.randn(F, D, generator=g) / 8).to(DEV, torch.bfloat16)
+    wu = (torch.randn(F, D, generator=g) / 8).to(DEV, torch.bfloat16)
+    from predicitivecoding_b200.engine.fused_trainer import _interleave_gate_up
+    w13 = _interleave_gate_up(wg, wu).contiguous()
+    pre = torch.empty(M, 2 * F, device=DEV, dtype=torch.bfloat16)
+    act = torch.empty(M, F, device=DEV, dtype=torch.bfloat16)
+    ops.gemm(x, w13, epi=ops.EPI_SWIGLU, c=pre, d=act)
+    gr = x.float() @ wg.float().t()
+    ur = x.float() @ wu.float().t()
+    ref = torch.nn.functional.silu(gr) * ur
+    torch.cuda.synchronize()
+    assert rel_err(act, ref) < 0.02
+    # backward through the interleaved layout
+    dh = torch.randn(M, F, device=DEV)
+    w2 = torch.randn(D, F, device=DEV).to(torch.bfloat16)  # stored [K=D? no] -> use dact = y @ w2
+    y = torch.randn(M, D, device=DEV).to(torch.bfloat16)
+    dact = y.float() @ w2.float()
+    dpre = torch.empty_like(pre)
+    ops.gemm(y, w2, b_mn=True, epi=ops.EPI_SWIGLU_BWD, c=dpre, aux=pre)
+    pre_f = pre.float().view(M, F // 64, 2, 64)
+    gg = pre_f[:, :, 0].reshape(M, F).requires_grad_()
+    uu = pre_f[:, :, 1].reshape(M, F).requires_grad_()
+    (torch.nn.functional.silu(gg) * uu).backward(dact)
+    torch.cuda.synchronize()
+    d = dpre.float().view(M, F // 64, 2, 64)
+    assert rel_err(d[:, :, 0].reshape(M, F), gg.grad) < 0.02
+    assert rel_err(d[:, :, 1].reshape(M, F), uu.grad) < 0.02
+
+
+def test_rmsnorm_fwd_bwd():
+    M, D = 1000, 768
+    x = torch.randn(M, D, device=DEV)
+    g = (1 + 0.1 * torch.randn(D, device=DEV)).to(torch.bfloat16)
+    y = torch.empty(M, D, device=DEV, dtype=torch.bfloat16)
+    inv = torch.empty(M, device=DEV)
+    ops.rmsnorm_fwd(x, g, y, inv, 1e-5)
+    xr = x.clone().requires_grad_()
+    gr = g.float().clone().requires_grad_()
+    ref = xr * torch.rsqrt(xr.pow(2).mean(-1, keepdim=True) + 1e-5) * gr
+    assert rel_err(y, ref) < 0.01
+    dy = torch.randn(M, D, device=DEV)
+    ref.backward(dy)
+    dx = torch.ones(M, D, device=DEV)
+    dx16 = torch.empty(M, D, device=DEV, dtype=torch.bfloat16)
+    dg = torch.zeros(D, device=DEV)
+    ops.rmsnorm_bwd(dy, x, g, inv, dx, dg, accumulate=True, dx16=dx16)
+    torch.cuda.synchronize()
+    assert rel_err(dx, xr.grad + 1) < 1e-4
+    assert rel_err(dx16, xr.grad + 1) < 0.01
+    assert rel_err(dg, gr.grad) < 1e-4
+
+
+def test_rope_roundtrip_and_values():
+    from predicitivecoding_b200.models.decoder_lm import apply_rope, rope_tables
+    B, S, H, hd = 2, 128, 4, 64
+    D = H * hd
+    qkv = torch.randn(B * S, 3 * D, device=DEV).to(torch.bfloat16)
+    cos, sin = rope_tables(S, hd, device=DEV)
+    cs = torch.stack((cos, sin), -1).contiguous()
+    out = qkv.clone()
+    ops.rope(out, cs, S, D, hd, 2, 1.0)
+    q = qkv[:, :D].float().view(B, S, H, hd).transpose(1, 2)
+    ref = apply_rope(q, cos, sin).transpose(1, 2).reshape(B * S, D)
+    torch.cuda.synchronize()
+    assert rel_err(out[:, :D], ref) < 0.01
+    assert torch.equal(out[:, 2 * D:], qkv[:, 2 * D:])
+    ops.rope(out, cs, S, D, hd, 2, -1.0)
+    torch.cuda.synchronize()
+    assert rel_err(out, qkv) < 0.02
+
+
+def test_cross_entropy_fused():
+    M, V = 300, 32000
+    logits = (torch.randn(M, V, device=DEV) * 2).to(torch.bfloat16)
+    tgt = torch.randint(0, V, (M,), device=DEV, dtype=torch.int32)
+    tgt[5] = -1
+    loss = torch.empty(M, device=DEV)
+    lg = logits.float().clone().requires_grad_()
+    keep = tgt >= 0
+    ref_rows = torch.nn.functional.cross_entropy(lg, tgt.long().clamp(min=0), reduction="none") * keep
+    (ref_rows.sum() / M).backward()
+    buf = logits.clone()
+    ops.cross_entropy(buf, tgt, loss, 1.0 / M, True)
+    torch.cuda.synchronize()
+    assert rel_err(loss, ref_rows) < 1e-3
+    assert rel_err(buf, lg.grad) < 0.02
+    assert float(buf[5].float().abs().max()) == 0.0
+
+
+def test_adamw_matches_reference_order():
+    n = 10000
+    w = torch.randn(n, device=DEV)
+    g = torch.randn(n, device=DEV)
+    m = torch.zeros(n, device=DEV)
+    v = torch.zeros(n, device=DEV)
+    w16 = torch.empty(n, device=DEV, dtype=torch.bfloat16)
+    lr, wd, b1, b2, eps = 1e-2, 0.1, 0.9, 0.999, 1e-8
+    wr, mr, vr = w.clone(), m.clone(), v.clone()
+    for t in range(1, 4):
+        hyper = torch.tensor([lr, wd, 1 - b1 ** t, 1 - b2 ** t, 1.0, 0, 0, 0], device=DEV)
+        ops.adamw(w, g, m, v, w16, n // 2, hyper, b1, b2, eps)
+        mr = b1 * mr + (1 - b1) * g
+        vr = b2 * vr + (1 - b2) * g * g
+        wr = wr - lr * (mr / (1 - b1 ** t)) / ((vr / (1 - b2 ** t)).sqrt() + eps)
+        wr[: n // 2] = wr[: n // 2] - lr * wd * wr[: n // 2]
+    torch.cuda.synchronize()
+    assert rel_err(w, wr) < 1e-6
+    assert rel_err(w16, wr) < 0.01
+
+
+@pytest.mark.parametrize("hd", [64, 128])
+def test_attention_fwd_bwd(hd):
+    B, S, H = 2, 256, 2
+    D = H * hd
+    qkv = (torch.randn(B * S, 3 * D, device=DEV)).to(torch.bfloat16)
+    out = torch.empty(B * S, D, device=DEV, dtype=torch.bfloat16)
+    lse = torch.empty(B * H, S, device=DEV)
+    scale = 1 / math.sqrt(hd)
+    ops.attn_fwd(qkv, out, lse, B, S, H, hd, scale)
+    q, k, v = (qkv.float()[:, i * D:(i + 1) * D].view(B, S, H, hd).transpose(1, 2).clone().requires_grad_()
+               for i in range(3))
+    s = (q @ k.transpose(-1, -2)) * scale
+    mask = torch.ones(S, S, dtype=torch.bool, device=DEV).triu(1)
+    s = s.masked_fill(mask, float("-inf"))
+    p = torch.softmax(s, -1)
+    o = (p @ v)
+    ref = o.transpose(1, 2).reshape(B * S, D)
+    torch.cuda.synchronize()
+    assert rel_err(out, ref) < 0.02
+    assert rel_err(lse.view(B, H, S), torch.logsumexp(s, -1)) < 1e-3
+    do = torch.randn(B * S, D, device=DEV).to(torch.bfloat16)
+    o.backward(do.float().view(B, S, H, hd).transpose(1, 2))
+    dqkv = torch.zeros(B * S, 3 * D, device=DEV, dtype=torch.bfloat16)
+    dvec = torch.empty(B * H, S, device=DEV)
+    dq_acc = torch.empty(B * S, D, device=DEV)
+    ops.attn_bwd(qkv, out, do, lse, dvec, dq_acc, dqkv, B, S, H, hd, scale)
+    torch.cuda.synchronize()
+    for i, t in enumerate((q, k, v)):
+        ref_g = t.grad.transpose(1, 2).reshape(B * S, D)
+        assert rel_err(dqkv[:, i * D:(i + 1) * D], ref_g) < 0.03, ("qkv"[i], rel_err(dqkv[:, i * D:(i + 1) * D], ref_g))
+
+
+def test_embed_fwd_bwd():
+    V, D, M = 500, 256, 1000
+    W = torch.randn(V, D, device=DEV).to(torch.bfloat16)
+    tok = torch.randint(0, V, (M,), device=DEV, dtype=torch.int32)
+    x = torch.empty(M, D, device=DEV)
+    ops.embed_fwd(tok, W, x)
+    dx = torch.randn(M, D, device=DEV)
+    dW = torch.zeros(V, D, device=DEV)
+    ops.embed_bwd(tok, dx, dW)
+    ref = torch.zeros(V, D, device=DEV).index_add_(0, tok.long(), dx)
+    torch.cuda.synchronize()
+    assert torch.equal(x, W.float()[tok.long()])
+    assert rel_err(dW, ref) < 1e-5
