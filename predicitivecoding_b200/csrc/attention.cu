@@ -556,3 +556,67 @@ int pcb_attn_bwd(const void* qkv, long long ld, const void* out, const void* dou
                                                           (long long)B * S, H * HD);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
+
+// ------------------------------------------------------------------------------------------
+// Allocation-free variant (see attention_noalloc.h for who needs it and the contract).
+// Same kernels as pcb_attn_bwd; the two fp32 scratch buffers come from a file-scope device
+// array instead of the caller.
+// ------------------------------------------------------------------------------------------
+#include <cstdio>
+#include <mutex>
+
+#include "attention_noalloc.h"
+
+namespace {
+
+constexpr size_t kNoAllocFloats = PCB_ATTN_NOALLOC_SCRATCH_BYTES / sizeof(float);
+static __device__ __align__(256) float g_attn_bwd_scratch[kNoAllocFloats];
+
+constexpr int kMaxDevices = 128;
+std::mutex g_noalloc_mu;
+float* g_noalloc_base[kMaxDevices] = {};
+
+// Device address of g_attn_bwd_scratch on the current device, looked up once per device.
+// The symbol name is only a host-side handle; the address must come from the runtime.
+int noalloc_scratch(float** base) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return -8;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_base[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_attn_bwd_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      fprintf(stderr, "pcb_attn_bwd_noalloc: cudaGetSymbolAddress failed on device %d: %s\n", dev,
+              cudaGetErrorString(e));
+      return -9;
+    }
+    g_noalloc_base[dev] = static_cast<float*>(p);
+  }
+  *base = g_noalloc_base[dev];
+  return 0;
+}
+
+}  // namespace
+
+extern "C" int pcb_attn_bwd_noalloc(const void* qkv, long long ld, const void* out, const void* dout, long long ld_o,
+                                    const float* lse, void* dqkv, long long ld_d, int B, int S, int H, int HD,
+                                    float scale, cudaStream_t s) {
+  if (B <= 0 || H <= 0 || S <= 0 || S % 128 != 0 || ld % 8 || ld_o % 8 || ld_d % 8) return -1;
+  if (HD != 64 && HD != 128) return -1;
+  const size_t dq_floats = ((size_t)B * S * H * HD + 63) / 64 * 64;
+  const size_t need = dq_floats + (size_t)B * H * S;
+  if (need > kNoAllocFloats) {
+    fprintf(stderr,
+            "pcb_attn_bwd_noalloc: problem needs %zu scratch floats (B=%d S=%d H=%d HD=%d) but the built-in "
+            "scratch holds %zu (%u bytes); use pcb_attn_bwd with caller-provided buffers\n",
+            need, B, S, H, HD, kNoAllocFloats, (unsigned)PCB_ATTN_NOALLOC_SCRATCH_BYTES);
+    return PCB_ATTN_NOALLOC_E_TOO_LARGE;
+  }
+  float* base = nullptr;
+  const int rc = noalloc_scratch(&base);
+  if (rc != 0) return rc;
+  float* dq_acc = base;
+  float* dvec = base + dq_floats;
+  // the preprocess kernel zeroes dq_acc, so stale contents of an earlier call never leak in
+  return pcb_attn_bwd(qkv, ld, out, dout, ld_o, lse, dvec, dq_acc, dqkv, ld_d, B, S, H, HD, scale, s);
+}
