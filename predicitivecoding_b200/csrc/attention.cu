@@ -267,7 +267,7 @@ __global__ void __launch_bounds__(128)
     attn_bwd_kernel(const __nv_bfloat16* __restrict__ qkv, long long ld, const __nv_bfloat16* __restrict__ dout,
                     long long ld_o, const float* __restrict__ lse, const float* __restrict__ dvec,
                     float* __restrict__ dq_acc, __nv_bfloat16* __restrict__ dqkv, long long ld_d, int S, int H,
-                    float scale) {
+                    float scale, const float2* __restrict__ rope_cs) {
   constexpr int BKV = 64, BQ = 64, NT = 128;
   constexpr int KSTEPS = HD / 16;
   constexpr int DT = HD / 8;
@@ -467,21 +467,34 @@ __global__ void __launch_bounds__(128)
 #pragma unroll
   for (int dt = 0; dt < DT; ++dt) {
     const int c = dt * 8 + 2 * t;
-    *reinterpret_cast<uint32_t*>(dk0 + c) = pack_bf16x2(dk[dt][0] * scale, dk[dt][1] * scale);
-    *reinterpret_cast<uint32_t*>(dk1 + c) = pack_bf16x2(dk[dt][2] * scale, dk[dt][3] * scale);
+    float a0 = dk[dt][0] * scale, a1 = dk[dt][1] * scale, a2 = dk[dt][2] * scale, a3 = dk[dt][3] * scale;
+    if (rope_cs != nullptr) {  // k was rotated by +theta in the forward: rotate its gradient by -theta
+      const float2 r0 = rope_cs[kr0 * (HD / 2) + (c >> 1)];
+      const float2 r1 = rope_cs[(kr0 + 8) * (HD / 2) + (c >> 1)];
+      const float b0 = a0 * r0.x + a1 * r0.y, b1 = -a0 * r0.y + a1 * r0.x;
+      const float b2 = a2 * r1.x + a3 * r1.y, b3 = -a2 * r1.y + a3 * r1.x;
+      a0 = b0; a1 = b1; a2 = b2; a3 = b3;
+    }
+    *reinterpret_cast<uint32_t*>(dk0 + c) = pack_bf16x2(a0, a1);
+    *reinterpret_cast<uint32_t*>(dk1 + c) = pack_bf16x2(a2, a3);
     *reinterpret_cast<uint32_t*>(dv0 + c) = pack_bf16x2(dv[dt][0], dv[dt][1]);
     *reinterpret_cast<uint32_t*>(dv1 + c) = pack_bf16x2(dv[dt][2], dv[dt][3]);
   }
 }
 
-// dqkv[:, 0:D] = bf16(dq_acc)
+// dqkv[:, 0:D] = bf16(dq_acc), optionally rotated by -theta (RoPE backward of q)
 __global__ void attn_dq_convert_kernel(const float* __restrict__ dq_acc, __nv_bfloat16* __restrict__ dqkv,
-                                       long long ld_d, long long M, int D) {
+                                       long long ld_d, long long M, int D, int S, int HD,
+                                       const float2* __restrict__ rope_cs) {
   const long long total = M * (D / 2);
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
     const long long r = i / (D / 2);
     const int c = (int)(i % (D / 2)) * 2;
-    const float2 v = *reinterpret_cast<const float2*>(dq_acc + r * D + c);
+    float2 v = *reinterpret_cast<const float2*>(dq_acc + r * D + c);
+    if (rope_cs != nullptr) {
+      const float2 cs = rope_cs[(int)(r % S) * (HD / 2) + ((c % HD) >> 1)];
+      v = make_float2(v.x * cs.x + v.y * cs.y, -v.x * cs.y + v.y * cs.x);
+    }
     *reinterpret_cast<uint32_t*>(dqkv + r * ld_d + c) = pack_bf16x2(v.x, v.y);
   }
 }
@@ -519,7 +532,7 @@ int pcb_attn_fwd(const void* qkv, long long ld, void* out, long long ld_o, float
 template <int HD>
 static int bwd_launch(const void* qkv, long long ld, const void* dout, long long ld_o, const float* lse,
                       const float* dvec, float* dq_acc, void* dqkv, long long ld_d, int B, int S, int H, float scale,
-                      cudaStream_t s) {
+                      const float* rope_cs, cudaStream_t s) {
   const size_t smem = (size_t)(2 * 64 * HD * 2 + 4 * 64 * HD * 2 + 64 * 64 * 2 + 4 * 64 * 4);
   static bool attr = false;
   if (!attr) {
@@ -529,15 +542,18 @@ static int bwd_launch(const void* qkv, long long ld, const void* dout, long long
   dim3 grid(S / 64, B * H);
   attn_bwd_kernel<HD><<<grid, 128, smem, s>>>(reinterpret_cast<const __nv_bfloat16*>(qkv), ld,
                                               reinterpret_cast<const __nv_bfloat16*>(dout), ld_o, lse, dvec, dq_acc,
-                                              reinterpret_cast<__nv_bfloat16*>(dqkv), ld_d, S, H, scale);
+                                              reinterpret_cast<__nv_bfloat16*>(dqkv), ld_d, S, H, scale,
+                                              reinterpret_cast<const float2*>(rope_cs));
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
 // Full attention backward: preprocess, main kernel, dQ conversion.  dq_acc [B*S, D] fp32 and
 // dvec [B*H, S] fp32 are scratch.
-int pcb_attn_bwd(const void* qkv, long long ld, const void* out, const void* dout, long long ld_o, const float* lse,
-                 float* dvec, float* dq_acc, void* dqkv, long long ld_d, int B, int S, int H, int HD, float scale,
-                 cudaStream_t s) {
+// Same as pcb_attn_bwd, and when rope_cs is given (cos/sin table [S][HD/2]) the dq and dk it writes are
+// already rotated back by -theta, i.e. they are gradients w.r.t. the pre-RoPE q and k.
+int pcb_attn_bwd_rope(const void* qkv, long long ld, const void* out, const void* dout, long long ld_o,
+                      const float* lse, float* dvec, float* dq_acc, void* dqkv, long long ld_d, int B, int S, int H,
+                      int HD, float scale, const float* rope_cs, cudaStream_t s) {
   if (S % 128 != 0 || ld % 8 || ld_o % 8 || ld_d % 8) return -1;
   const long long rows = (long long)B * S * H;
   attn_bwd_pre_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(out),
@@ -545,16 +561,24 @@ int pcb_attn_bwd(const void* qkv, long long ld, const void* out, const void* dou
                                                                   dvec, dq_acc, B, S, H, HD);
   if (cudaGetLastError() != cudaSuccess) return -3;
   int r;
-  if (HD == 64) r = bwd_launch<64>(qkv, ld, dout, ld_o, lse, dvec, dq_acc, dqkv, ld_d, B, S, H, scale, s);
-  else if (HD == 128) r = bwd_launch<128>(qkv, ld, dout, ld_o, lse, dvec, dq_acc, dqkv, ld_d, B, S, H, scale, s);
+  if (HD == 64) r = bwd_launch<64>(qkv, ld, dout, ld_o, lse, dvec, dq_acc, dqkv, ld_d, B, S, H, scale, rope_cs, s);
+  else if (HD == 128)
+    r = bwd_launch<128>(qkv, ld, dout, ld_o, lse, dvec, dq_acc, dqkv, ld_d, B, S, H, scale, rope_cs, s);
   else return -1;
   if (r) return r;
   const long long total = (long long)B * S * (H * HD / 2);
   long long blocks = (total + 255) / 256;
   if (blocks > 148 * 16) blocks = 148 * 16;
   attn_dq_convert_kernel<<<(unsigned)blocks, 256, 0, s>>>(dq_acc, reinterpret_cast<__nv_bfloat16*>(dqkv), ld_d,
-                                                          (long long)B * S, H * HD);
+                                                          (long long)B * S, H * HD, S, HD,
+                                                          reinterpret_cast<const float2*>(rope_cs));
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+int pcb_attn_bwd(const void* qkv, long long ld, const void* out, const void* dout, long long ld_o, const float* lse,
+                 float* dvec, float* dq_acc, void* dqkv, long long ld_d, int B, int S, int H, int HD, float scale,
+                 cudaStream_t s) {
+  return pcb_attn_bwd_rope(qkv, ld, out, dout, ld_o, lse, dvec, dq_acc, dqkv, ld_d, B, S, H, HD, scale, nullptr, s);
 }
 
 // ------------------------------------------------------------------------------------------

@@ -30,9 +30,23 @@ int pcb_adamw(float* w, const float* g, float* m, float* v, void* w16, long long
 int pcb_f32_to_bf16(const float* x, void* y, long long n, cudaStream_t s);
 int pcb_attn_fwd(const void* qkv, long long ld, void* out, long long ld_o, float* lse, int B, int S, int H, int HD,
                  float scale, cudaStream_t s);
-int pcb_attn_bwd(const void* qkv, long long ld, const void* out, const void* dout, long long ld_o, const float* lse,
-                 float* dvec, float* dq_acc, void* dqkv, long long ld_d, int B, int S, int H, int HD, float scale,
-                 cudaStream_t s);
+int pcb_attn_bwd_rope(const void* qkv, long long ld, const void* out, const void* dout, long long ld_o,
+                      const float* lse, float* dvec, float* dq_acc, void* dqkv, long long ld_d, int B, int S, int H,
+                      int HD, float scale, const float* rope_cs, cudaStream_t s);
+
+int pcb_peer_alloc(size_t bytes, void** ptr);
+int pcb_peer_free(void* ptr);
+int pcb_ipc_handle(void* ptr, void* out64);
+int pcb_ipc_open(const void* in64, void** ptr);
+int pcb_ipc_close(void* ptr);
+int pcb_peer_barrier(void* const* peer_flags_dev, unsigned int* ctr, int rank, int world, int* err, cudaStream_t s);
+int pcb_rs_adamw_ag(void* const* grad_peers, void* const* w16_peers, float* w32, float* m, float* v, long long lo,
+                    long long hi, long long n_decay, const float* hyper, float b1, float b2, float eps, int world,
+                    int num_sms, cudaStream_t s);
+int pcb_pc_allreduce_update(void* const* delta_peers, void* const* w_peers, void* const* w16_peers, long long lo,
+                            long long hi, float alpha, float decay, int world, int num_sms, cudaStream_t s);
+int pcb_peer_reduce(void* const* in_peers, void* const* out_peers, long long lo, long long hi, float scale, int world,
+                    int num_sms, cudaStream_t s);
 
 namespace {
 
@@ -75,7 +89,8 @@ void* ptr_or_null(const c10::optional<at::Tensor>& t) { return t.has_value() ? t
 void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, int64_t epi,
           const c10::optional<at::Tensor>& c, const c10::optional<at::Tensor>& d,
           const c10::optional<at::Tensor>& aux, const c10::optional<at::Tensor>& bias, double alpha,
-          int64_t force_bn, int64_t force_splits, const c10::optional<at::Tensor>& err) {
+          int64_t force_bn, int64_t force_splits, const c10::optional<at::Tensor>& err,
+          const c10::optional<at::Tensor>& rope_cs, int64_t rope_S, int64_t rope_hd, int64_t rope_cols) {
   req(a, at::kBFloat16, "a");
   req(b, at::kBFloat16, "b");
   const long long lda = row_stride(a, "a"), ldb = row_stride(b, "b");
@@ -95,6 +110,14 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, int64_
     args.bias_bf16 = bias->scalar_type() == at::kBFloat16 ? 1 : 0;
   }
   if (err) args.err = err->data_ptr<int>();
+  if (rope_cs) {
+    req(*rope_cs, at::kFloat, "rope_cs");
+    TORCH_CHECK(epi == pcb::EPI_BF16 && rope_hd % 2 == 0 && rope_S > 0, "gemm: rope needs EPI_BF16, even hd");
+    args.rope_cs = rope_cs->data_ptr<float>();
+    args.rope_S = (int)rope_S;
+    args.rope_hd = (int)rope_hd;
+    args.rope_cols = (int)rope_cols;
+  }
   if (epi == pcb::EPI_SWIGLU) TORCH_CHECK(args.N % 128 == 0, "swiglu gemm needs N % 128 == 0");
   if (epi == pcb::EPI_SWIGLU_BWD) TORCH_CHECK(args.N % 64 == 0, "swiglu bwd gemm needs N % 64 == 0");
   const at::cuda::CUDAGuard guard(a.device());
@@ -250,19 +273,80 @@ void attn_fwd(const at::Tensor& qkv, at::Tensor& out, at::Tensor& lse, int64_t B
 }
 void attn_bwd(const at::Tensor& qkv, const at::Tensor& out, const at::Tensor& dout, const at::Tensor& lse,
               at::Tensor& dvec, at::Tensor& dq_acc, at::Tensor& dqkv, int64_t B, int64_t S, int64_t H, int64_t HD,
-              double scale) {
+              double scale, const c10::optional<at::Tensor>& rope_cs) {
   req(qkv, at::kBFloat16, "qkv");
   req(dout, at::kBFloat16, "dout");
   req(dqkv, at::kBFloat16, "dqkv");
   req(dq_acc, at::kFloat, "dq_acc");
   TORCH_CHECK(row_stride(out, "out") == row_stride(dout, "dout"), "attn_bwd: out/dout strides differ");
-  check(pcb_attn_bwd(qkv.data_ptr(), row_stride(qkv, "qkv"), out.data_ptr(), dout.data_ptr(), row_stride(dout, "dout"),
-                     lse.data_ptr<float>(), dvec.data_ptr<float>(), dq_acc.data_ptr<float>(), dqkv.data_ptr(),
-                     row_stride(dqkv, "dqkv"), B, S, H, HD, (float)scale, cur_stream()),
+  if (rope_cs) req(*rope_cs, at::kFloat, "rope_cs");
+  check(pcb_attn_bwd_rope(qkv.data_ptr(), row_stride(qkv, "qkv"), out.data_ptr(), dout.data_ptr(),
+                          row_stride(dout, "dout"), lse.data_ptr<float>(), dvec.data_ptr<float>(),
+                          dq_acc.data_ptr<float>(), dqkv.data_ptr(), row_stride(dqkv, "dqkv"), B, S, H, HD,
+                          (float)scale, rope_cs ? rope_cs->data_ptr<float>() : nullptr, cur_stream()),
         "attn_bwd", 3);
 }
 
 int64_t launch_count() { return g_launches.load(); }
+
+// ---------------------------------------------------------------- peer memory (CUDA IPC)
+// Allocate `bytes` with cudaMalloc (an IPC-exportable allocation base), zeroed, as a uint8 tensor.
+at::Tensor peer_alloc(int64_t bytes, int64_t device) {
+  const c10::cuda::CUDAGuard guard((c10::DeviceIndex)device);
+  void* p = nullptr;
+  TORCH_CHECK(pcb_peer_alloc((size_t)bytes, &p) == 0, "peer_alloc: cudaMalloc failed");
+  auto opts = at::TensorOptions().dtype(at::kByte).device(at::kCUDA, device);
+  return torch::from_blob(p, {bytes}, [](void* q) { pcb_peer_free(q); }, opts);
+}
+py::bytes ipc_handle(const at::Tensor& t) {
+  char buf[64];
+  TORCH_CHECK(pcb_ipc_handle(t.data_ptr(), buf) == 0, "ipc_handle: cudaIpcGetMemHandle failed");
+  return py::bytes(buf, 64);
+}
+int64_t ipc_open(py::bytes h) {
+  std::string s = h;
+  TORCH_CHECK(s.size() == 64, "ipc_open: handle must be 64 bytes");
+  void* p = nullptr;
+  TORCH_CHECK(pcb_ipc_open(s.data(), &p) == 0, "ipc_open: cudaIpcOpenMemHandle failed");
+  return reinterpret_cast<int64_t>(p);
+}
+void ipc_close(int64_t p) { pcb_ipc_close(reinterpret_cast<void*>(p)); }
+
+void* const* ptr_table(const at::Tensor& t, int world, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kLong && t.numel() >= world, name,
+              ": device int64 pointer table of size >= world required");
+  return reinterpret_cast<void* const*>(t.data_ptr<int64_t>());
+}
+
+void peer_barrier(const at::Tensor& flag_ptrs, at::Tensor& ctr, int64_t rank, int64_t world,
+                  const c10::optional<at::Tensor>& err) {
+  check(pcb_peer_barrier(ptr_table(flag_ptrs, world, "flag_ptrs"), reinterpret_cast<unsigned int*>(ctr.data_ptr()),
+                         (int)rank, (int)world, err ? err->data_ptr<int>() : nullptr, cur_stream()),
+        "peer_barrier");
+}
+void rs_adamw_ag(const at::Tensor& grad_ptrs, const at::Tensor& w16_ptrs, at::Tensor& w32, at::Tensor& m, at::Tensor& v,
+                 int64_t lo, int64_t hi, int64_t n_decay, const at::Tensor& hyper, double b1, double b2, double eps,
+                 int64_t world) {
+  req(w32, at::kFloat, "w32");
+  TORCH_CHECK(w32.numel() >= hi - lo && m.numel() >= hi - lo && v.numel() >= hi - lo, "rs_adamw_ag: state too small");
+  check(pcb_rs_adamw_ag(ptr_table(grad_ptrs, world, "grad_ptrs"), ptr_table(w16_ptrs, world, "w16_ptrs"),
+                        w32.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), lo, hi, n_decay,
+                        hyper.data_ptr<float>(), (float)b1, (float)b2, (float)eps, (int)world, num_sms(), cur_stream()),
+        "rs_adamw_ag");
+}
+void pc_allreduce_update(const at::Tensor& delta_ptrs, const at::Tensor& w_ptrs, const c10::optional<at::Tensor>& w16_ptrs,
+                         int64_t lo, int64_t hi, double alpha, double decay, int64_t world) {
+  check(pcb_pc_allreduce_update(ptr_table(delta_ptrs, world, "delta_ptrs"), ptr_table(w_ptrs, world, "w_ptrs"),
+                                w16_ptrs ? ptr_table(*w16_ptrs, world, "w16_ptrs") : nullptr, lo, hi, (float)alpha,
+                                (float)decay, (int)world, num_sms(), cur_stream()),
+        "pc_allreduce_update");
+}
+void peer_reduce(const at::Tensor& in_ptrs, const at::Tensor& out_ptrs, int64_t lo, int64_t hi, double scale,
+                 int64_t world) {
+  check(pcb_peer_reduce(ptr_table(in_ptrs, world, "in_ptrs"), ptr_table(out_ptrs, world, "out_ptrs"), lo, hi,
+                        (float)scale, (int)world, num_sms(), cur_stream()),
+        "peer_reduce");
+}
 
 }  // namespace
 
@@ -283,4 +367,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_fwd", &attn_fwd);
   m.def("attn_bwd", &attn_bwd);
   m.def("launch_count", &launch_count);
+  m.def("peer_alloc", &peer_alloc);
+  m.def("ipc_handle", &ipc_handle);
+  m.def("ipc_open", &ipc_open);
+  m.def("ipc_close", &ipc_close);
+  m.def("peer_barrier", &peer_barrier);
+  m.def("rs_adamw_ag", &rs_adamw_ag);
+  m.def("pc_allreduce_update", &pc_allreduce_update);
+  m.def("peer_reduce", &peer_reduce);
 }

@@ -259,4 +259,22 @@ PCB_DEVICE float gelu_tanh_grad(float x) {
 }
 PCB_DEVICE float sigmoidf_(float x) { return 1.f / (1.f + __expf(-x)); }
 
+// Hardware tanh approximation (PTX tanh.approx.f32, |rel err| ~ 2^-11): for epilogues whose
+// results are rounded to bf16 (8 mantissa bits) anyway.
+PCB_DEVICE float tanh_approx(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+PCB_DEVICE float gelu_tanh_fast(float x) {
+  const float u = 0.7978845608f * (x + 0.044715f * x * x * x);
+  return 0.5f * x * (1.f + tanh_approx(u));
+}
+PCB_DEVICE float gelu_tanh_grad_fast(float x) {
+  const float u = 0.7978845608f * (x + 0.044715f * x * x * x);
+  const float t = tanh_approx(u);
+  const float du = 0.7978845608f * (1.f + 3.f * 0.044715f * x * x);
+  return 0.5f * (1.f + t) + 0.5f * x * (1.f - t * t) * du;
+}
+
 }  // namespace pcb

@@ -46,6 +46,12 @@ struct GemmArgs {
   void* pc_pred_out;    // optional prediction output fp32 (EPI_PC_PRED, FFG warm start)
   long long ld_pred;
   void* pc_pred_bf16;   // optional bf16 copy of the prediction (FFG warm start)
+  // fused RoPE (EPI_BF16): rotate interleaved pairs of columns [0, rope_cols) by the angle table
+  // cs[pos][hd/2] = (cos, sin), pos = row % rope_S, pair = (col % rope_hd) / 2
+  const float* rope_cs;
+  int rope_S;
+  int rope_hd;
+  int rope_cols;
 };
 
 }  // namespace pcb

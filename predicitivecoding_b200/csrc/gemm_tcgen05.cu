@@ -10,7 +10,8 @@ namespace pcb {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;                 // two per TMEM lane quadrant, splitting columns
+constexpr int kThreads = 64 + 32 * kEpiWarps;  // producer warp + MMA warp + epilogue warps
 
 template <int BN>
 struct GemmCfg {
@@ -139,6 +140,16 @@ PCB_DEVICE void epilogue_chunk(const GemmArgs& a, int m, int n, float (&v)[32], 
     }
   }
   if (EPI == EPI_BF16) {
+    if (a.rope_cs != nullptr && n < a.rope_cols) {
+      const float2* cs = reinterpret_cast<const float2*>(a.rope_cs) + (long long)(m % a.rope_S) * (a.rope_hd >> 1);
+#pragma unroll
+      for (int j = 0; j < 32; j += 2) {
+        const float2 c = cs[((n + j) % a.rope_hd) >> 1];
+        const float x0 = v[j], x1 = v[j + 1];
+        v[j] = x0 * c.x - x1 * c.y;
+        v[j + 1] = x0 * c.y + x1 * c.x;
+      }
+    }
     store_bf16x32(reinterpret_cast<__nv_bfloat16*>(a.C) + (long long)m * a.ldc + n, v, nvalid);
   } else if (EPI == EPI_F32) {
     store_f32x32(reinterpret_cast<float*>(a.C) + (long long)m * a.ldc + n, v, nvalid);
@@ -163,13 +174,13 @@ PCB_DEVICE void epilogue_chunk(const GemmArgs& a, int m, int n, float (&v)[32], 
     store_bf16x32(reinterpret_cast<__nv_bfloat16*>(a.C) + (long long)m * a.ldc + n, v, nvalid);
     float g[32];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) g[j] = gelu_tanh(__bfloat162float(__float2bfloat16_rn(v[j])));
+    for (int j = 0; j < 32; ++j) g[j] = gelu_tanh_fast(__bfloat162float(__float2bfloat16_rn(v[j])));
     store_bf16x32(reinterpret_cast<__nv_bfloat16*>(a.D) + (long long)m * a.ldd + n, g, nvalid);
   } else if (EPI == EPI_GELU_BWD) {
     float p[32];
     load_bf16x32(reinterpret_cast<const __nv_bfloat16*>(a.aux) + (long long)m * a.ldaux + n, p, nvalid);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = a.alpha * v[j] * gelu_tanh_grad(p[j]);
+    for (int j = 0; j < 32; ++j) v[j] = a.alpha * v[j] * gelu_tanh_grad_fast(p[j]);
     store_bf16x32(reinterpret_cast<__nv_bfloat16*>(a.C) + (long long)m * a.ldc + n, v, nvalid);
   } else if (EPI == EPI_SWIGLU_BWD) {
     // n indexes the activation columns f; 32 | 64 so a chunk stays inside one group
@@ -183,7 +194,7 @@ PCB_DEVICE void epilogue_chunk(const GemmArgs& a, int m, int n, float (&v)[32], 
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       const float dh = a.alpha * v[j];
-      const float s = 1.f / (1.f + __expf(-g[j]));
+      const float s = __fdividef(1.f, 1.f + __expf(-g[j]));
       const float silu = g[j] * s;
       du[j] = dh * silu;
       dg[j] = dh * u[j] * s * (1.f + g[j] * (1.f - s));
@@ -289,7 +300,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&tfull[s], 1);
-      mbar_init(&tempty[s], 4);
+      mbar_init(&tempty[s], kEpiWarps);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -391,7 +402,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---------------- epilogue warps ----------------
-    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int q = warp & 3;             // TMEM lane quadrant this warp may access
+    const int half = (warp - 2) >> 2;   // which of the two warps of this quadrant (column split)
     const int row = q * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -408,8 +420,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // 128-column groups: [64 gate | 64 up]; output 64 activation columns per group
 #pragma unroll 1
         for (int g = 0; g < BN / 128; ++g) {
-#pragma unroll 1
-          for (int h = 0; h < 2; ++h) {
+          {
+            const int h = half;
             float gv[32], uv[32];
             tmem_load_f32x32(tbase + g * 128 + h * 32, gv);
             tmem_load_f32x32(tbase + g * 128 + 64 + h * 32, uv);
@@ -431,7 +443,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // (which reads them back) sees exactly what the forward used
                 const float gg = __bfloat162float(__float2bfloat16_rn(gv[j]));
                 const float uu = __bfloat162float(__float2bfloat16_rn(uv[j]));
-                o[j] = gg / (1.f + __expf(-gg)) * uu;
+                o[j] = __fdividef(gg, 1.f + __expf(-gg)) * uu;
               }
               const int fcol = (n0 >> 1) + g * 64 + h * 32;
               store_bf16x32(reinterpret_cast<__nv_bfloat16*>(args.D) + (long long)m * args.ldd + fcol, o, nvalid);
@@ -440,7 +452,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       } else {
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = half; c < BN / 32; c += 2) {
           float v[32];
           tmem_load_f32x32(tbase + c * 32, v);
           epilogue_chunk<EPI>(args, m, n0 + c * 32, v, row_ok);

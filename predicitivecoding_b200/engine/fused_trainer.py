@@ -86,9 +86,13 @@ class FusedDecoderTrainer:
         else:
             self.world, self.rank = 1, 0
         if grad_sync == "auto":
-            grad_sync = "zero" if self.world > 1 else "none"
+            grad_sync = "fused" if self.world > 1 else "none"
+        if self.world == 1:
+            grad_sync = "none"
+        if grad_sync not in ("none", "zero", "fused"):
+            raise ValueError(f"grad_sync must be 'none', 'zero' (NCCL) or 'fused' (peer memory), got {grad_sync!r}")
         self.grad_sync = grad_sync
-        self.peer = None  # fused peer-memory reducer, set by enable_fused_dp()
+        self.peer = None
 
         # ---------------- parameters
         D, F_, V, L = cfg.dim, cfg.ff_dim, cfg.vocab, cfg.num_blocks
@@ -113,8 +117,17 @@ class FusedDecoderTrainer:
         A = self.arena
         dev = self.device
         f32, bf16 = torch.float32, torch.bfloat16
-        self.w16 = torch.zeros(A.total, device=dev, dtype=bf16)      # full bf16 working copy (replicated)
-        self.grad = torch.zeros(A.total, device=dev, dtype=f32)      # full gradient (local, then reduced)
+        if grad_sync == "fused":
+            # gradients and bf16 weights live in IPC-shared buffers: the fused optimizer kernel
+            # reduce-scatters gradients and all-gathers weights by loading/storing peer memory
+            from ..parallel.peer import PeerGroup
+            self.peer = PeerGroup(self.pg, dev)
+            self._w16_sym = self.peer.symmetric(A.total, bf16)
+            self._grad_sym = self.peer.symmetric(A.total, f32)
+            self.w16, self.grad = self._w16_sym.local, self._grad_sym.local
+        else:
+            self.w16 = torch.zeros(A.total, device=dev, dtype=bf16)      # full bf16 working copy (replicated)
+            self.grad = torch.zeros(A.total, device=dev, dtype=f32)      # full gradient (local, then reduced)
         lo, hi = self.rank * A.shard, (self.rank + 1) * A.shard
         self.shard_lo, self.shard_hi = lo, hi
         self.w32 = torch.zeros(A.shard, device=dev, dtype=f32)       # fp32 master shard
@@ -248,8 +261,8 @@ class FusedDecoderTrainer:
         ops.embed_fwd(self.tok, W["wemb"], self.x[0])
         for l in range(cfg.num_blocks):
             ops.rmsnorm_fwd(self.x[l], W[f"b{l}.ln1"], self.n1[l], self.inv1[l], cfg.eps)
-            ops.gemm(self.n1[l], W[f"b{l}.wqkv"], epi=ops.EPI_BF16, c=self.qkv[l])
-            ops.rope(self.qkv[l], self.rope_cs, S, D, hd, 2, 1.0)
+            ops.gemm(self.n1[l], W[f"b{l}.wqkv"], epi=ops.EPI_BF16, c=self.qkv[l],
+                     rope=(self.rope_cs, S, hd, 2 * D))
             ops.attn_fwd(self.qkv[l], self.ao[l], self.lse[l], B, S, H, hd, self.attn_scale)
             ops.gemm(self.ao[l], W[f"b{l}.wo"], epi=ops.EPI_RESID_F32, c=self.xmid[l], aux=self.x[l])
             ops.rmsnorm_fwd(self.xmid[l], W[f"b{l}.ln2"], self.n2[l], self.inv2[l], cfg.eps)
@@ -297,8 +310,7 @@ class FusedDecoderTrainer:
             ops.gemm(self.dx16, self.ao[l], a_mn=True, b_mn=True, epi=RED, c=G[f"b{l}.wo"])
             ops.gemm(self.dx16, W[f"b{l}.wo"], b_mn=True, epi=ops.EPI_BF16, c=self.dao)
             ops.attn_bwd(self.qkv[l], self.ao[l], self.dao, self.lse[l], self.dvec, self.dq_acc, self.dqkv,
-                         B, S, H, hd, self.attn_scale)
-            ops.rope(self.dqkv, self.rope_cs, S, D, hd, 2, -1.0)
+                         B, S, H, hd, self.attn_scale, self.rope_cs)
             ops.gemm(self.dqkv, self.n1[l], a_mn=True, b_mn=True, epi=RED, c=G[f"b{l}.wqkv"])
             ops.gemm(self.dqkv, W[f"b{l}.wqkv"], b_mn=True, epi=ops.EPI_F32, c=self.dn)
             ops.rmsnorm_bwd(self.dn, self.x[l], W[f"b{l}.ln1"], self.inv1[l], self.dx, G[f"b{l}.ln1"], True,
@@ -308,10 +320,17 @@ class FusedDecoderTrainer:
     def _optimizer(self) -> None:
         """Gradient sync (data parallel) + AdamW on this rank's shard + bf16 weight refresh."""
         self.hyper.copy_(self.hyper_host, non_blocking=True)
+        if self.grad_sync == "fused":
+            if self.clip_norm > 0:
+                raise NotImplementedError("global-norm clipping is not fused into the peer optimizer; "
+                                          "use grad_sync='zero' with clip_norm")
+            self.peer.barrier()   # every rank's gradients are complete
+            ops.ext().rs_adamw_ag(self._grad_sym.ptrs, self._w16_sym.ptrs, self.w32, self.m, self.v,
+                                  self.shard_lo, self.shard_hi, self.arena.n_decay, self.hyper,
+                                  self.betas[0], self.betas[1], self.eps, self.world)
+            self.peer.barrier()   # every rank's weights are written before anyone's next forward
+            return
         if self.world > 1:
-            if self.peer is not None:
-                self.peer.reduce_scatter_adamw(self)
-                return
             import torch.distributed as dist
             dist.reduce_scatter_tensor(self.grad_shard, self.grad, group=self.pg)
         clip = None
@@ -356,7 +375,7 @@ class FusedDecoderTrainer:
     def launch(self, lr: Optional[float] = None) -> None:
         """Enqueue one full training step on the current stream (no host sync)."""
         self._set_hyper(self.lr if lr is None else lr)
-        if self.use_graph and self.world == 1:
+        if self.use_graph and self.grad_sync in ("none", "fused"):
             if self.graph is None:
                 self._capture()
             self.graph.replay()

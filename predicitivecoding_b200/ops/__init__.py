@@ -65,18 +65,22 @@ def launch_count() -> int:
 def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = False, epi: int = EPI_BF16,
          c: Optional[torch.Tensor] = None, d: Optional[torch.Tensor] = None, aux: Optional[torch.Tensor] = None,
          bias: Optional[torch.Tensor] = None, alpha: float = 1.0, bn: int = 0, splits: int = 0,
-         err: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:
+         err: Optional[torch.Tensor] = None, rope: Optional[tuple] = None) -> Optional[torch.Tensor]:
     """C = epilogue(op(a) @ op(b)) on the tcgen05 tensor cores.
 
     ``a`` is [M, K] (``a_mn=False``) or [K, M] (``a_mn=True``); ``b`` is [N, K]
     (``b_mn=False``, the nn.Linear weight layout) or [K, N] (``b_mn=True``).
     With ``epi=EPI_BF16`` and ``c=None`` a new bf16 output is allocated.
+    ``rope=(cs, S, hd, cols)`` rotates interleaved column pairs < cols by the RoPE angle of
+    position ``row % S`` (``cs`` is the [S, hd/2, 2] cos/sin table); only with EPI_BF16.
     """
     if c is None and epi in (EPI_BF16, EPI_F32):
         M = a.shape[1] if a_mn else a.shape[0]
         N = b.shape[1] if b_mn else b.shape[0]
         c = torch.empty(M, N, device=a.device, dtype=torch.bfloat16 if epi == EPI_BF16 else torch.float32)
-    ext().gemm(a, a_mn, b, b_mn, epi, c, d, aux, bias, float(alpha), int(bn), int(splits), err)
+    rc, rS, rhd, rcols = rope if rope is not None else (None, 0, 0, 0)
+    ext().gemm(a, a_mn, b, b_mn, epi, c, d, aux, bias, float(alpha), int(bn), int(splits), err, rc, int(rS), int(rhd),
+               int(rcols))
     return c
 
 
@@ -134,5 +138,6 @@ def attn_fwd(qkv, out, lse, B, S, H, HD, scale):
     ext().attn_fwd(qkv, out, lse, int(B), int(S), int(H), int(HD), float(scale))
 
 
-def attn_bwd(qkv, out, dout, lse, dvec, dq_acc, dqkv, B, S, H, HD, scale):
-    ext().attn_bwd(qkv, out, dout, lse, dvec, dq_acc, dqkv, int(B), int(S), int(H), int(HD), float(scale))
+def attn_bwd(qkv, out, dout, lse, dvec, dq_acc, dqkv, B, S, H, HD, scale, rope_cs=None):
+    """Attention backward; with ``rope_cs`` the dq/dk written are w.r.t. the pre-RoPE q/k."""
+    ext().attn_bwd(qkv, out, dout, lse, dvec, dq_acc, dqkv, int(B), int(S), int(H), int(HD), float(scale), rope_cs)
