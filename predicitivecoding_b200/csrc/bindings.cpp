@@ -44,7 +44,7 @@ int pcb_rs_adamw_ag(void* const* grad_peers, void* const* w16_peers, float* w32,
                     long long hi, long long n_decay, const float* hyper, float b1, float b2, float eps, int world,
                     int num_sms, cudaStream_t s);
 int pcb_pc_allreduce_update(void* const* delta_peers, void* const* w_peers, void* const* w16_peers, long long lo,
-                            long long hi, float alpha, float decay, int world, int num_sms, cudaStream_t s);
+                            long long hi, float alpha, float decay, int world, int rank, int num_sms, cudaStream_t s);
 int pcb_peer_reduce(void* const* in_peers, void* const* out_peers, long long lo, long long hi, float scale, int world,
                     int num_sms, cudaStream_t s);
 
@@ -335,10 +335,10 @@ void rs_adamw_ag(const at::Tensor& grad_ptrs, const at::Tensor& w16_ptrs, at::Te
         "rs_adamw_ag");
 }
 void pc_allreduce_update(const at::Tensor& delta_ptrs, const at::Tensor& w_ptrs, const c10::optional<at::Tensor>& w16_ptrs,
-                         int64_t lo, int64_t hi, double alpha, double decay, int64_t world) {
+                         int64_t lo, int64_t hi, double alpha, double decay, int64_t world, int64_t rank) {
   check(pcb_pc_allreduce_update(ptr_table(delta_ptrs, world, "delta_ptrs"), ptr_table(w_ptrs, world, "w_ptrs"),
                                 w16_ptrs ? ptr_table(*w16_ptrs, world, "w16_ptrs") : nullptr, lo, hi, (float)alpha,
-                                (float)decay, (int)world, num_sms(), cur_stream()),
+                                (float)decay, (int)world, (int)rank, num_sms(), cur_stream()),
         "pc_allreduce_update");
 }
 void peer_reduce(const at::Tensor& in_ptrs, const at::Tensor& out_ptrs, int64_t lo, int64_t hi, double scale,

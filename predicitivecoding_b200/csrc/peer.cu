@@ -108,7 +108,7 @@ __global__ void __launch_bounds__(256)
 __global__ void __launch_bounds__(256)
     pc_allreduce_update_kernel(const float* const* __restrict__ delta_peers, float* const* __restrict__ w_peers,
                                __nv_bfloat16* const* __restrict__ w16_peers, long long lo, long long hi, float alpha,
-                               float decay, int world) {
+                               float decay, int world, int rank) {
   const long long n4 = (hi - lo) / 4;
   for (long long q = blockIdx.x * (long long)blockDim.x + threadIdx.x; q < n4; q += (long long)gridDim.x * blockDim.x) {
     const long long i = lo + 4 * q;
@@ -117,8 +117,8 @@ __global__ void __launch_bounds__(256)
       const float4 x = __ldcg(reinterpret_cast<const float4*>(delta_peers[p] + i));
       d.x += x.x; d.y += x.y; d.z += x.z; d.w += x.w;
     }
-    // every rank's W is identical; read the local (first-listed owner) copy
-    float4 w = __ldcg(reinterpret_cast<const float4*>(w_peers[0] + i));
+    // every rank's W is identical; read the local copy
+    float4 w = __ldcg(reinterpret_cast<const float4*>(w_peers[rank] + i));
     w.x = (w.x + alpha * d.x) * decay;
     w.y = (w.y + alpha * d.y) * decay;
     w.z = (w.z + alpha * d.z) * decay;
@@ -206,13 +206,13 @@ int pcb_rs_adamw_ag(void* const* grad_peers, void* const* w16_peers, float* w32,
 }
 
 int pcb_pc_allreduce_update(void* const* delta_peers, void* const* w_peers, void* const* w16_peers, long long lo,
-                            long long hi, float alpha, float decay, int world, int num_sms, cudaStream_t s) {
+                            long long hi, float alpha, float decay, int world, int rank, int num_sms, cudaStream_t s) {
   if ((lo % 4) || ((hi - lo) % 4)) return -1;
   const int grid = grid_for_n4((hi - lo) / 4, num_sms);
   pc_allreduce_update_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const float* const*>(delta_peers),
                                                   reinterpret_cast<float* const*>(w_peers),
                                                   reinterpret_cast<__nv_bfloat16* const*>(w16_peers), lo, hi, alpha,
-                                                  decay, world);
+                                                  decay, world, rank);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
