@@ -48,6 +48,8 @@ int pcb_pc_allreduce_update(void* const* delta_peers, void* const* w_peers, void
 int pcb_peer_reduce(void* const* in_peers, void* const* out_peers, long long lo, long long hi, float scale, int world,
                     int num_sms, cudaStream_t s);
 
+extern "C" void pcb_set_gemm_mode(int mode);
+
 namespace {
 
 std::atomic<long long> g_launches{0};
@@ -367,6 +369,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_fwd", &attn_fwd);
   m.def("attn_bwd", &attn_bwd);
   m.def("launch_count", &launch_count);
+  m.def("set_gemm_mode", [](int64_t m) { pcb_set_gemm_mode((int)m); },
+        "GEMM kernel choice: -1 env/auto, 0 auto, 1 single-CTA only, 2 CTA pairs when legal");
   m.def("peer_alloc", &peer_alloc);
   m.def("ipc_handle", &ipc_handle);
   m.def("ipc_open", &ipc_open);

@@ -1,0 +1,346 @@
+// tcgen05 GEMM on CTA pairs (cta_group::2): one 256 x BN output tile per 2-SM cluster.
+//
+// Each CTA of the pair loads its own half of the operands -- A rows [m0 + 128*rank, +128) and
+// B columns [n0 + BN/2*rank, +BN/2) -- so per-SM operand traffic for a 128 x BN output slice is
+// half of what the single-CTA kernel moves for B.  The leader CTA (rank 0) issues
+// tcgen05.mma.cta_group::2 with M = 256, N = BN; the accumulator rows of each CTA land in that
+// CTA's own TMEM, so both CTAs run the same epilogue as the single-CTA kernel on 128 rows each.
+//
+// Synchronisation (all waits bounded):
+//   full[s]   (leader)  armed by the leader's producer with both CTAs' bytes; both CTAs' TMA loads
+//                       complete on it (cta_group::2 load form, leader barrier address)
+//   empty[s]  (both)    released by the leader's MMA commit, multicast to both CTAs
+//   tfull[a]  (both)    accumulator a ready: leader's commit multicast to both CTAs
+//   tempty[a] (leader)  accumulator a drained: epilogue warps of both CTAs arrive (the peer remotely)
+// No TMA load uses .multicast::cluster: each CTA fetches the tiles it stores.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "gemm_epilogue.cuh"
+
+namespace pcb {
+namespace pair {
+
+constexpr int kBM = 128;  // rows per CTA (256 per pair)
+constexpr int kBK = 64;
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+
+template <int BN>
+struct Cfg {
+  static constexpr int A_BYTES = kBM * kBK * 2;
+  static constexpr int B_BYTES = (BN / 2) * kBK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (BN == 256) ? 6 : 8;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+};
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const GemmArgs args) {
+  using C = Cfg<BN>;
+  constexpr int STAGES = C::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair_id = blockIdx.x >> 1;
+  const int num_pairs = gridDim.x >> 1;
+  const int num_m = (args.M + 2 * kBM - 1) / (2 * kBM);
+  const int num_n = (args.N + BN - 1) / BN;
+  const int total_kb = (args.K + kBK - 1) / kBK;
+  const int tiles = num_m * num_n * args.splits;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&tfull[s], 1);
+      mbar_init(&tempty[s], 2 * kEpiWarps);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated in both
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer (both CTAs) ----------------
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = pair_id; tile < tiles && ok; tile += num_pairs) {
+        const int split = tile % args.splits;
+        const int rest = tile / args.splits;
+        const int mb = rest % num_m, nb = rest / num_m;
+        const int m0 = mb * 2 * kBM + rank * kBM;
+        const int n0 = nb * BN + rank * (BN / 2);
+        const int kb0 = split * args.kb_per_split;
+        const int kb1 = min(total_kb, kb0 + args.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, args.err, kErrTimeoutEmpty, abort_flag)) { ok = false; break; }
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
+          uint8_t* sa = smem + stage * C::STAGE_BYTES;
+          uint8_t* sb = sa + C::A_BYTES;
+          const int k0 = kb * kBK;
+          if (args.a_mn == 0) {
+            tma_load_2d_pair(sa, &tmA, &full[stage], k0, m0);
+          } else {
+#pragma unroll
+            for (int p = 0; p < kBM / 64; ++p) tma_load_2d_pair(sa + p * 8192, &tmA, &full[stage], m0 + 64 * p, k0);
+          }
+          if (args.b_mn == 0) {
+            tma_load_2d_pair(sb, &tmB, &full[stage], k0, n0);
+          } else {
+#pragma unroll
+            for (int p = 0; p < BN / 128; ++p) tma_load_2d_pair(sb + p * 8192, &tmB, &full[stage], n0 + 64 * p, k0);
+          }
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ---------------- MMA issuer (leader only) ----------------
+      const uint32_t idesc = make_idesc_bf16(2 * kBM, BN, args.a_mn, args.b_mn);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = pair_id; tile < tiles && ok; tile += num_pairs) {
+        const int split = tile % args.splits;
+        const int kb0 = split * args.kb_per_split;
+        const int kb1 = min(total_kb, kb0 + args.kb_per_split);
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, args.err, kErrTimeoutTmemEmpty, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full[stage], phase, args.err, kErrTimeoutFull, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES);
+          const uint32_t sb = sa + C::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t ad = args.a_mn ? make_smem_desc(sa + k * 2048, 8192, 1024, 2)
+                                          : make_smem_desc(sa + k * 32, 16, 1024, 2);
+            const uint64_t bd = args.b_mn ? make_smem_desc(sb + k * 2048, 8192, 1024, 2)
+                                          : make_smem_desc(sb + k * 32, 16, 1024, 2);
+            umma_bf16_pair(d_tmem, ad, bd, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit_pair(&empty[stage], 0x3);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        umma_commit_pair(&tfull[acc], 0x3);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+    }
+  } else {
+    // ---------------- epilogue warps (both CTAs, 128 rows each) ----------------
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int row = q * 32 + lane;
+    const uint32_t tempty_leader0 = mapa_shared(smem_u32(&tempty[0]), 0);
+    const uint32_t tempty_leader1 = mapa_shared(smem_u32(&tempty[1]), 0);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = pair_id; tile < tiles; tile += num_pairs) {
+      const int rest = tile / args.splits;
+      const int mb = rest % num_m, nb = rest / num_m;
+      const int m = mb * 2 * kBM + rank * kBM + row;
+      const int n0 = nb * BN;
+      const bool row_ok = m < args.M;
+      if (!mbar_wait(&tfull[acc], acc_phase, args.err, kErrTimeoutTmemFull, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      if (EPI == EPI_SWIGLU) {
+#pragma unroll 1
+        for (int g = 0; g < BN / 128; ++g) {
+          const int h = half;
+          float gv[32], uv[32];
+          tmem_load_f32x32(tbase + g * 128 + h * 32, gv);
+          tmem_load_f32x32(tbase + g * 128 + 64 + h * 32, uv);
+          const int ncol = n0 + g * 128 + h * 32;
+          const int nvalid = min(32, args.N - ncol);
+          if (row_ok && nvalid > 0) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              gv[j] *= args.alpha;
+              uv[j] *= args.alpha;
+            }
+            __nv_bfloat16* pre = reinterpret_cast<__nv_bfloat16*>(args.C) + (long long)m * args.ldc;
+            store_bf16x32(pre + ncol, gv, nvalid);
+            store_bf16x32(pre + ncol + 64, uv, nvalid);
+            float o[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float gg = __bfloat162float(__float2bfloat16_rn(gv[j]));
+              const float uu = __bfloat162float(__float2bfloat16_rn(uv[j]));
+              o[j] = __fdividef(gg, 1.f + __expf(-gg)) * uu;
+            }
+            const int fcol = (n0 >> 1) + g * 64 + h * 32;
+            store_bf16x32(reinterpret_cast<__nv_bfloat16*>(args.D) + (long long)m * args.ldd + fcol, o, nvalid);
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = half; c < BN / 32; c += 2) {
+          float v[32];
+          tmem_load_f32x32(tbase + c * 32, v);
+          epilogue_chunk<EPI>(args, m, n0 + c * 32, v, row_ok);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (leader) mbar_arrive(&tempty[acc]);
+        else mbar_arrive_remote(acc ? tempty_leader1 : tempty_leader0);
+      }
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs done with TMEM and with each other's barriers
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+}
+
+}  // namespace pair
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn2() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+static bool make_map2(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld,
+                      uint32_t box_inner, uint32_t box_outer) {
+  auto fn = encode_fn2();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t es[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN, int EPI>
+static int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int grid, cudaStream_t s) {
+  using C = pair::Cfg<BN>;
+  static bool attr_done = false;
+  if (!attr_done) {
+    cudaFuncSetAttribute(pair::gemm_pair_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    attr_done = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(pair::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, pair::gemm_pair_kernel<BN, EPI>, ta, tb, a);
+  return e == cudaSuccess ? 0 : -3;
+}
+
+template <int BN>
+static int dispatch_pair(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int grid,
+                         cudaStream_t s) {
+  switch (epi) {
+    case EPI_BF16: return launch_pair<BN, EPI_BF16>(ta, tb, a, grid, s);
+    case EPI_F32: return launch_pair<BN, EPI_F32>(ta, tb, a, grid, s);
+    case EPI_ACC_F32: return launch_pair<BN, EPI_ACC_F32>(ta, tb, a, grid, s);
+    case EPI_RED_F32: return launch_pair<BN, EPI_RED_F32>(ta, tb, a, grid, s);
+    case EPI_GELU: return launch_pair<BN, EPI_GELU>(ta, tb, a, grid, s);
+    case EPI_SWIGLU: return launch_pair<BN, EPI_SWIGLU>(ta, tb, a, grid, s);
+    case EPI_SWIGLU_BWD: return launch_pair<BN, EPI_SWIGLU_BWD>(ta, tb, a, grid, s);
+    case EPI_GELU_BWD: return launch_pair<BN, EPI_GELU_BWD>(ta, tb, a, grid, s);
+    case EPI_PC_PRED: return launch_pair<BN, EPI_PC_PRED>(ta, tb, a, grid, s);
+    case EPI_PC_STATE: return launch_pair<BN, EPI_PC_STATE>(ta, tb, a, grid, s);
+    case EPI_PC_WUPD: return launch_pair<BN, EPI_PC_WUPD>(ta, tb, a, grid, s);
+    case EPI_BF16_ACC: return launch_pair<BN, EPI_BF16_ACC>(ta, tb, a, grid, s);
+    case EPI_RESID_F32: return launch_pair<BN, EPI_RESID_F32>(ta, tb, a, grid, s);
+    default: return -2;
+  }
+}
+
+}  // namespace pcb
+
+using namespace pcb;
+
+// CTA-pair GEMM launcher: same contract as pcb_gemm_launch.  bn in {128, 256}; splits >= 1 (split-K only
+// with EPI_RED_F32).  Returns 0 on success.
+int pcb_gemm_pair_launch(const void* A, int a_mn, long long lda, const void* B, int b_mn, long long ldb, int epi,
+                         GemmArgs args, int bn, int splits, int num_sms, cudaStream_t stream) {
+  const int M = args.M, N = args.N, K = args.K;
+  if (M <= 0 || N <= 0 || K <= 0) return -1;
+  if ((lda % 8) != 0 || (ldb % 8) != 0) return -1;
+  if ((reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15)) return -1;
+  if (bn != 128 && bn != 256) return -1;
+  if (num_sms <= 0) num_sms = 148;
+  args.a_mn = a_mn;
+  args.b_mn = b_mn;
+  const int num_m = (M + 255) / 256;
+  const int num_n = (N + bn - 1) / bn;
+  const int total_kb = (K + 63) / 64;
+  if (splits < 1) splits = 1;
+  if (splits > 1 && epi != EPI_RED_F32) return -4;
+  int kbps = (total_kb + splits - 1) / splits;
+  splits = (total_kb + kbps - 1) / kbps;
+  args.splits = splits;
+  args.kb_per_split = kbps;
+  CUtensorMap ta, tb;
+  bool ok = a_mn == 0 ? make_map2(&ta, A, K, M, lda, 64, 128) : make_map2(&ta, A, M, K, lda, 64, 64);
+  if (!ok) return -5;
+  ok = b_mn == 0 ? make_map2(&tb, B, K, N, ldb, 64, bn / 2) : make_map2(&tb, B, N, K, ldb, 64, 64);
+  if (!ok) return -5;
+  const int tiles = num_m * num_n * splits;
+  const int max_pairs = num_sms / 2;
+  const int pairs = tiles < max_pairs ? tiles : max_pairs;
+  return bn == 256 ? dispatch_pair<256>(epi, ta, tb, args, 2 * pairs, stream)
+                   : dispatch_pair<128>(epi, ta, tb, args, 2 * pairs, stream);
+}

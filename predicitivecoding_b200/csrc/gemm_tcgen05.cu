@@ -2,9 +2,11 @@
 #include <cudaTypedefs.h>
 
 #include <cstdio>
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
-#include "gemm_tcgen05.cuh"
+#include "gemm_epilogue.cuh"
 
 namespace pcb {
 
@@ -22,254 +24,6 @@ struct GemmCfg {
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
-
-PCB_DEVICE float act_apply(int act, float x) {
-  switch (act) {
-    case 1: return tanhf(x);
-    case 2: return fmaxf(x, 0.f);
-    case 3: return 1.f / (1.f + __expf(-x));
-    default: return x;
-  }
-}
-// derivative from pre-activation x and activation y (tanh/sigmoid use y as the reference does)
-PCB_DEVICE float act_deriv(int act, float x, float y) {
-  switch (act) {
-    case 1: return 1.f - y * y;
-    case 2: return x > 0.f ? 1.f : 0.f;
-    case 3: return y * (1.f - y);
-    default: return 1.f;
-  }
-}
-
-PCB_DEVICE void store_bf16x32(__nv_bfloat16* dst, const float (&v)[32], int nvalid) {
-  if (nvalid >= 32 && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
-    uint4* d4 = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      uint4 u;
-      u.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
-      u.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
-      u.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
-      u.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
-      d4[j] = u;
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (j < nvalid) dst[j] = __float2bfloat16_rn(v[j]);
-  }
-}
-
-PCB_DEVICE void load_bf16x32(const __nv_bfloat16* src, float (&v)[32], int nvalid) {
-  if (nvalid >= 32 && ((reinterpret_cast<uintptr_t>(src) & 15) == 0)) {
-    const uint4* s4 = reinterpret_cast<const uint4*>(src);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      uint4 u = s4[j];
-      v[8 * j + 0] = bf16_lo(u.x); v[8 * j + 1] = bf16_hi(u.x);
-      v[8 * j + 2] = bf16_lo(u.y); v[8 * j + 3] = bf16_hi(u.y);
-      v[8 * j + 4] = bf16_lo(u.z); v[8 * j + 5] = bf16_hi(u.z);
-      v[8 * j + 6] = bf16_lo(u.w); v[8 * j + 7] = bf16_hi(u.w);
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = (j < nvalid) ? __bfloat162float(src[j]) : 0.f;
-  }
-}
-
-PCB_DEVICE void load_f32x32(const float* src, float (&v)[32], int nvalid) {
-  if (nvalid >= 32 && ((reinterpret_cast<uintptr_t>(src) & 15) == 0)) {
-    const float4* s4 = reinterpret_cast<const float4*>(src);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      float4 f = s4[j];
-      v[4 * j + 0] = f.x; v[4 * j + 1] = f.y; v[4 * j + 2] = f.z; v[4 * j + 3] = f.w;
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = (j < nvalid) ? src[j] : 0.f;
-  }
-}
-
-PCB_DEVICE void store_f32x32(float* dst, const float (&v)[32], int nvalid) {
-  if (nvalid >= 32 && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
-    float4* d4 = reinterpret_cast<float4*>(dst);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-  } else {
-#pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (j < nvalid) dst[j] = v[j];
-  }
-}
-
-PCB_DEVICE void red_f32x32(float* dst, const float (&v)[32], int nvalid) {
-  if (nvalid >= 32 && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
-    float4* d4 = reinterpret_cast<float4*>(dst);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) atomicAdd(d4 + j, make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
-  } else {
-#pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (j < nvalid) atomicAdd(dst + j, v[j]);
-  }
-}
-
-PCB_DEVICE void tmem_load_f32x32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
-  tmem_ld_32x32b_x32(taddr, r);
-  tmem_ld_wait();
-#pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-}
-
-// One 32-column chunk of a "plain" epilogue (everything except the SwiGLU pairs).
-template <int EPI>
-PCB_DEVICE void epilogue_chunk(const GemmArgs& a, int m, int n, float (&v)[32], bool row_ok) {
-  const int nvalid = min(32, a.N - n);
-  if (!row_ok || nvalid <= 0) return;
-  if (EPI == EPI_BF16 || EPI == EPI_F32 || EPI == EPI_ACC_F32 || EPI == EPI_GELU || EPI == EPI_RESID_F32) {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] *= a.alpha;
-    if (a.bias != nullptr) {
-      float b[32];
-      if (a.bias_bf16) load_bf16x32(reinterpret_cast<const __nv_bfloat16*>(a.bias) + n, b, nvalid);
-      else load_f32x32(reinterpret_cast<const float*>(a.bias) + n, b, nvalid);
-#pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] += b[j];
-    }
-  }
-  if (EPI == EPI_BF16) {
-    if (a.rope_cs != nullptr && n < a.rope_cols) {
-      const float2* cs = reinterpret_cast<const float2*>(a.rope_cs) + (long long)(m % a.rope_S) * (a.rope_hd >> 1);
-#pragma unroll
-      for (int j = 0; j < 32; j += 2) {
-        const float2 c = cs[((n + j) % a.rope_hd) >> 1];
-        const float x0 = v[j], x1 = v[j + 1];
-        v[j] = x0 * c.x - x1 * c.y;
-        v[j + 1] = x0 * c.y + x1 * c.x;
-      }
-    }
-    store_bf16x32(reinterpret_cast<__nv_bfloat16*>(a.C) + (long long)m * a.ldc + n, v, nvalid);
-  } else if (EPI == EPI_F32) {
-    store_f32x32(reinterpret_cast<float*>(a.C) + (long long)m * a.ldc + n, v, nvalid);
-  } else if (EPI == EPI_ACC_F32) {
-    float* c = reinterpret_cast<float*>(a.C) + (long long)m * a.ldc + n;
-    float o[32];
-    load_f32x32(c, o, nvalid);
-#pragma unroll
-    for (int j = 0; j < 32; ++j) o[j] += v[j];
-    store_f32x32(c, o, nvalid);
-  } else if (EPI == EPI_RESID_F32) {
-    float r[32];
-    load_f32x32(reinterpret_cast<const float*>(a.aux) + (long long)m * a.ldaux + n, r, nvalid);
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] += r[j];
-    store_f32x32(reinterpret_cast<float*>(a.C) + (long long)m * a.ldc + n, v, nvalid);
-  } else if (EPI == EPI_RED_F32) {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] *= a.alpha;
-    red_f32x32(reinterpret_cast<float*>(a.C) + (long long)m * a.ldc + n, v, nvalid);
-  } else if (EPI == EPI_GELU) {
-    store_bf16x32(reinterpret_cast<__nv_bfloat16*>(a.C) + (long long)m * a.ldc + n, v, nvalid);
-    float g[32];
-#pragma unroll
-    for (int j = 0; j < 32; ++j) g[j] = gelu_tanh_fast(__bfloat162float(__float2bfloat16_rn(v[j])));
-    store_bf16x32(reinterpret_cast<__nv_bfloat16*>(a.D) + (long long)m * a.ldd + n, g, nvalid);
-  } else if (EPI == EPI_GELU_BWD) {
-    float p[32];
-    load_bf16x32(reinterpret_cast<const __nv_bfloat16*>(a.aux) + (long long)m * a.ldaux + n, p, nvalid);
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = a.alpha * v[j] * gelu_tanh_grad_fast(p[j]);
-    store_bf16x32(reinterpret_cast<__nv_bfloat16*>(a.C) + (long long)m * a.ldc + n, v, nvalid);
-  } else if (EPI == EPI_SWIGLU_BWD) {
-    // n indexes the activation columns f; 32 | 64 so a chunk stays inside one group
-    const int grp = n >> 6, off = n & 63;
-    const long long gcol = (long long)grp * 128 + off;
-    const __nv_bfloat16* pre = reinterpret_cast<const __nv_bfloat16*>(a.aux) + (long long)m * a.ldaux;
-    float g[32], u[32];
-    load_bf16x32(pre + gcol, g, nvalid);
-    load_bf16x32(pre + gcol + 64, u, nvalid);
-    float dg[32], du[32];
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const float dh = a.alpha * v[j];
-      const float s = __fdividef(1.f, 1.f + __expf(-g[j]));
-      const float silu = g[j] * s;
-      du[j] = dh * silu;
-      dg[j] = dh * u[j] * s * (1.f + g[j] * (1.f - s));
-    }
-    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.C) + (long long)m * a.ldc;
-    store_bf16x32(out + gcol, dg, nvalid);
-    store_bf16x32(out + gcol + 64, du, nvalid);
-  } else if (EPI == EPI_BF16_ACC) {
-    float r[32];
-    load_bf16x32(reinterpret_cast<const __nv_bfloat16*>(a.aux) + (long long)m * a.ldaux + n, r, nvalid);
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = a.alpha * v[j] + r[j];
-    store_bf16x32(reinterpret_cast<__nv_bfloat16*>(a.C) + (long long)m * a.ldc + n, v, nvalid);
-  } else if (EPI == EPI_PC_PRED) {
-    float b[32];
-    if (a.bias != nullptr) load_f32x32(reinterpret_cast<const float*>(a.bias) + n, b, nvalid);
-    else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) b[j] = 0.f;
-    }
-    float pre[32], pred[32];
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      pre[j] = v[j] + b[j];
-      pred[j] = act_apply(a.act, pre[j]);
-    }
-    if (a.pc_pred_out != nullptr)
-      store_f32x32(reinterpret_cast<float*>(a.pc_pred_out) + (long long)m * a.ld_pred + n, pred, nvalid);
-    if (a.pc_pred_bf16 != nullptr)
-      store_bf16x32(reinterpret_cast<__nv_bfloat16*>(a.pc_pred_bf16) + (long long)m * a.ld_pred + n, pred, nvalid);
-    if (a.C != nullptr) {
-      float mb[32];
-      load_f32x32(reinterpret_cast<const float*>(a.aux) + (long long)m * a.ldaux + n, mb, nvalid);
-      float e[32], dl[32];
-      float sq = 0.f;
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        e[j] = a.pc_pi * (mb[j] - pred[j]);
-        dl[j] = act_deriv(a.act, pre[j], pred[j]) * e[j];
-        if (j < nvalid) sq += e[j] * e[j];
-      }
-      store_f32x32(reinterpret_cast<float*>(a.C) + (long long)m * a.ldc + n, e, nvalid);
-      if (a.D != nullptr)
-        store_bf16x32(reinterpret_cast<__nv_bfloat16*>(a.D) + (long long)m * a.ldd + n, dl, nvalid);
-      if (a.pc_energy != nullptr) atomicAdd(a.pc_energy, sq);
-    }
-  } else if (EPI == EPI_PC_STATE) {
-    float* mu = reinterpret_cast<float*>(a.C) + (long long)m * a.ldc + n;
-    float s[32], e[32];
-    load_f32x32(mu, s, nvalid);
-    if (a.aux != nullptr) load_f32x32(reinterpret_cast<const float*>(a.aux) + (long long)m * a.ldaux + n, e, nvalid);
-    else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) e[j] = 0.f;
-    }
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      float grad = e[j] - v[j];
-      if (a.pc_actreg > 0.f) grad += a.pc_actreg * (s[j] > 0.f ? 1.f : (s[j] < 0.f ? -1.f : 0.f));
-      s[j] -= a.pc_eta * grad;
-    }
-    store_f32x32(mu, s, nvalid);
-    if (a.D != nullptr)
-      store_bf16x32(reinterpret_cast<__nv_bfloat16*>(a.D) + (long long)m * a.ldd + n, s, nvalid);
-  } else if (EPI == EPI_PC_WUPD) {
-    float* w = reinterpret_cast<float*>(a.C) + (long long)m * a.ldc + n;
-    float x[32];
-    load_f32x32(w, x, nvalid);
-#pragma unroll
-    for (int j = 0; j < 32; ++j) x[j] = (x[j] + a.alpha * v[j]) * a.pc_decay;
-    store_f32x32(w, x, nvalid);
-    if (a.D != nullptr)
-      store_bf16x32(reinterpret_cast<__nv_bfloat16*>(a.D) + (long long)m * a.ldd + n, x, nvalid);
-  }
-}
 
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -466,6 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+  __syncwarp();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -540,6 +295,25 @@ static int dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, c
 
 using namespace pcb;
 
+int pcb_gemm_pair_launch(const void* A, int a_mn, long long lda, const void* B, int b_mn, long long ldb, int epi,
+                         GemmArgs args, int bn, int splits, int num_sms, cudaStream_t stream);
+
+// 0 = choose per problem, 1 = single-CTA kernel only, 2 = CTA-pair kernel whenever legal.
+// Read once from PCB_GEMM_MODE ("auto" | "single" | "pair").
+static int g_gemm_mode_override = -1;
+extern "C" void pcb_set_gemm_mode(int mode) { g_gemm_mode_override = mode; }
+static int gemm_mode() {
+  if (g_gemm_mode_override >= 0) return g_gemm_mode_override;
+  static int mode = -1;
+  if (mode < 0) {
+    const char* e = getenv("PCB_GEMM_MODE");
+    mode = 0;
+    if (e && strcmp(e, "single") == 0) mode = 1;
+    if (e && strcmp(e, "pair") == 0) mode = 2;
+  }
+  return mode;
+}
+
 int pcb_gemm_launch(const void* A, int a_mn, long long lda, const void* B, int b_mn, long long ldb, int epi,
                     GemmArgs args, int force_bn, int force_splits, int num_sms, cudaStream_t stream) {
   const int M = args.M, N = args.N, K = args.K;
@@ -554,6 +328,20 @@ int pcb_gemm_launch(const void* A, int a_mn, long long lda, const void* B, int b
 
   const int num_m = (M + kBM - 1) / kBM;
   const int total_kb = (K + kBK - 1) / kBK;
+  {
+    // CTA pairs (256-row tiles, half the B traffic per SM) when the problem has enough pair tiles
+    const int mode = gemm_mode();
+    const int pbn = (force_bn == 128 || force_bn == 256) ? force_bn : (N >= 256 ? 256 : 128);
+    const int ptiles = ((M + 255) / 256) * ((N + pbn - 1) / pbn);
+    int psplits = force_splits > 0 ? force_splits : 1;
+    if (force_splits <= 0 && epi == EPI_RED_F32) {
+      while (ptiles * psplits * 2 <= num_sms / 2 && total_kb / (psplits * 2) >= 4) psplits *= 2;
+    }
+    const bool legal = M >= 256 && (epi != EPI_SWIGLU || pbn % 128 == 0);
+    const bool worth = ptiles * psplits >= num_sms / 4 && total_kb >= 4;
+    if (mode != 1 && legal && (mode == 2 || worth))
+      return pcb_gemm_pair_launch(A, a_mn, lda, B, b_mn, ldb, epi, args, pbn, psplits, num_sms, stream);
+  }
   int bn = force_bn;
   if (bn != 128 && bn != 256) {
     const int tiles256 = num_m * ((N + 255) / 256);

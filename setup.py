@@ -29,6 +29,7 @@ setup(
             sources=[
                 os.path.join(CSRC, "bindings.cpp"),
                 os.path.join(CSRC, "gemm_tcgen05.cu"),
+                os.path.join(CSRC, "gemm2_tcgen05.cu"),
                 os.path.join(CSRC, "ops_llm.cu"),
                 os.path.join(CSRC, "attention.cu"),
                 os.path.join(CSRC, "peer.cu"),

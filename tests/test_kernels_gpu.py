@@ -30,16 +30,39 @@ def _operands(M, N, K, a_mn, b_mn, seed=0):
     return a_st, b_st, ref
 
 
+@pytest.fixture(params=["single", "pair"])
+def gemm_mode(request):
+    ops.ext().set_gemm_mode(1 if request.param == "single" else 2)
+    yield request.param
+    ops.ext().set_gemm_mode(-1)
+
+
 @pytest.mark.parametrize("a_mn", [False, True])
 @pytest.mark.parametrize("b_mn", [False, True])
-@pytest.mark.parametrize("shape", [(256, 256, 128), (384, 512, 320), (200, 136, 72), (1024, 768, 2048)])
-def test_gemm_layouts(a_mn, b_mn, shape):
+@pytest.mark.parametrize("shape", [(256, 256, 128), (384, 512, 320), (200, 136, 72), (1024, 768, 2048),
+                                   (640, 384, 192)])
+def test_gemm_layouts(a_mn, b_mn, shape, gemm_mode):
     M, N, K = shape
     a, b, ref = _operands(M, N, K, a_mn, b_mn)
     out = torch.empty(M, N, device=DEV, dtype=torch.float32)
     ops.gemm(a, b, a_mn=a_mn, b_mn=b_mn, epi=ops.EPI_F32, c=out)
     torch.cuda.synchronize()
     assert rel_err(out, ref) < 1e-3, rel_err(out, ref)
+
+
+@pytest.mark.parametrize("bn", [128, 256])
+def test_gemm_pair_epilogues(bn, gemm_mode):
+    M, N, K = 768, 512, 320
+    a, b, ref = _operands(M, N, K, False, False, seed=9)
+    x = torch.randn(M, N, device=DEV)
+    out = torch.empty_like(x)
+    ops.gemm(a, b, epi=ops.EPI_RESID_F32, c=out, aux=x, bn=bn)
+    red = torch.zeros(M, N, device=DEV)
+    a2, b2, ref2 = _operands(M, N, 4096, True, True, seed=10)
+    ops.gemm(a2, b2, a_mn=True, b_mn=True, epi=ops.EPI_RED_F32, c=red, splits=4, bn=bn)
+    torch.cuda.synchronize()
+    assert rel_err(out, ref + x) < 1e-3
+    assert rel_err(red, ref2) < 1e-3
 
 
 @pytest.mark.parametrize("bn", [128, 256])
