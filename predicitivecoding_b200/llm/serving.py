@@ -1,0 +1,194 @@
+"""KV-cache inference model, exporter and server.
+
+Reference: PredictiveCoding.LLM/Serving/GptExporter.cs:30-193 (positional parameter walk of a
+trained DecoderLM into the inference stack), Serving/LlmServer.cs:16-95 (O(n) decoding with a
+KV cache), Model/Attention.cs:40-184 (per-layer KV cache with optional half-precision storage
+and sliding-window eviction keeping attention sinks), Model/GptModel.cs:67-89 (single-token step).
+
+``InferenceModel`` decodes a whole batch at once: prefill runs the prompt through the
+blocks and fills a preallocated cache [layers, batch, heads, max_seq, head_dim]; each
+``step`` appends one token per sequence.  It supports the dense attention family (RMSNorm
+or LayerNorm, RoPE or sinusoidal positions, GELU or SwiGLU FFN, MoE FFN).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import List, Optional, Sequence, Tuple
+
+import torch
+import torch.nn.functional as F
+
+from ..models.decoder_lm import (AttentionBlock, DecoderLM, apply_rope, gelu_tanh, layer_norm, rms_norm,
+                                 rope_tables, sinusoidal_positions)
+
+
+@dataclass
+class KvCache:
+    k: torch.Tensor          # [L, B, H, S_max, hd]
+    v: torch.Tensor
+    length: int = 0
+    sinks: int = 0           # tokens kept forever at the front when the window slides
+    window: Optional[int] = None
+    position: int = 0        # absolute position of the next token (RoPE angle), unaffected by eviction
+
+    def evict(self) -> None:
+        """Sliding window with attention sinks (Attention.cs:98-109): keep the first ``sinks``
+        positions and the most recent ``window - sinks``."""
+        if self.window is None or self.length <= self.window:
+            return
+        keep_recent = self.window - self.sinks
+        src = slice(self.length - keep_recent, self.length)
+        dst = slice(self.sinks, self.sinks + keep_recent)
+        self.k[:, :, :, dst] = self.k[:, :, :, src].clone()
+        self.v[:, :, :, dst] = self.v[:, :, :, src].clone()
+        self.length = self.window
+
+
+class InferenceModel:
+    """Exported decoder for batched KV-cache decoding."""
+
+    def __init__(self, model: DecoderLM, device=None, dtype: Optional[torch.dtype] = None,
+                 kv_dtype: Optional[torch.dtype] = None):
+        cfg = model.cfg
+        if cfg.block_pattern is not None or cfg.num_loops != 1 or cfg.use_plan:
+            raise NotImplementedError("InferenceModel exports dense attention stacks (no T blocks, loops or plan).")
+        self.cfg = cfg
+        self.device = torch.device(device) if device is not None else model.wemb.device
+        self.dtype = dtype or (torch.bfloat16 if self.device.type == "cuda" else torch.float32)
+        self.kv_dtype = kv_dtype or self.dtype
+        self.model = model
+        self.forward_tokens = 0
+        cast = lambda t: None if t is None else t.detach().to(self.device, self.dtype)
+        self.wemb = cast(model.wemb)
+        self.wout = cast(model.wout)
+        self.lnf = (cast(model.lnf_g), cast(model.lnf_b))
+        self.blocks = []
+        for b in model.blocks:
+            blk = {}
+            for name, p in b.named_parameters():
+                blk[name] = cast(p)
+            blk["_ref"] = b
+            self.blocks.append(blk)
+
+    # ------------------------------------------------------------ pieces
+    def _norm(self, x, g, b):
+        c = self.cfg
+        return rms_norm(x, g, c.eps) if c.use_rms_norm else layer_norm(x, g, b, c.eps)
+
+    def _ffn(self, blk, h):
+        c = self.cfg
+        if c.num_experts > 0:
+            return blk["_ref"].moe_ffn(h.float(), None).to(h.dtype)
+        if c.ffn == "gelu":
+            return gelu_tanh(h @ blk["w1"] + blk["b1"]) @ blk["w2"] + blk["b2"]
+        return (F.silu(h @ blk["w1"]) * (h @ blk["w3"])) @ blk["w2"]
+
+    def new_cache(self, batch: int, max_len: Optional[int] = None, window: Optional[int] = None,
+                  sinks: int = 0) -> KvCache:
+        c = self.cfg
+        S = max_len or c.max_seq
+        shape = (c.num_blocks, batch, c.num_heads, S, c.head_dim)
+        return KvCache(torch.zeros(shape, device=self.device, dtype=self.kv_dtype),
+                       torch.zeros(shape, device=self.device, dtype=self.kv_dtype), 0, sinks, window)
+
+    @torch.no_grad()
+    def _run(self, tokens: torch.Tensor, cache: KvCache) -> torch.Tensor:
+        """tokens [B, T] appended at cache.length; returns logits of every new position [B, T, V]."""
+        c = self.cfg
+        B, T = tokens.shape
+        pos0 = cache.length
+        if pos0 + T > cache.k.shape[3]:
+            raise ValueError("KV cache full: evict or enlarge max_len")
+        self.forward_tokens += B * T
+        x = self.wemb[tokens]
+        rope = None
+        if c.use_rope:
+            cos, sin = rope_tables(T, c.head_dim, cache.position, device=self.device)
+            rope = (cos.to(self.dtype), sin.to(self.dtype))
+        else:
+            p0 = cache.position
+            x = x + sinusoidal_positions(p0 + T, c.dim, device=self.device)[p0:].to(self.dtype)
+        H, hd = c.num_heads, c.head_dim
+        scale = 1.0 / math.sqrt(hd)
+        for l, blk in enumerate(self.blocks):
+            h = self._norm(x, blk["ln1_g"], blk.get("ln1_b"))
+            q = (h @ blk["wq"]).view(B, T, H, hd).transpose(1, 2)
+            k = (h @ blk["wk"]).view(B, T, H, hd).transpose(1, 2)
+            v = (h @ blk["wv"]).view(B, T, H, hd).transpose(1, 2)
+            if rope is not None:
+                q = apply_rope(q, *rope)
+                k = apply_rope(k, *rope)
+            cache.k[l, :, :, pos0:pos0 + T] = k.to(self.kv_dtype)
+            cache.v[l, :, :, pos0:pos0 + T] = v.to(self.kv_dtype)
+            K = cache.k[l, :, :, :pos0 + T].to(self.dtype)
+            V = cache.v[l, :, :, :pos0 + T].to(self.dtype)
+            # causal over the new positions, full over the cached prefix
+            mask = torch.ones(T, pos0 + T, dtype=torch.bool, device=self.device).tril(pos0)
+            o = F.scaled_dot_product_attention(q, K, V, attn_mask=mask, scale=scale)
+            x = x + o.transpose(1, 2).reshape(B, T, c.dim) @ blk["wo"]
+            x = x + self._ffn(blk, self._norm(x, blk["ln2_g"], blk.get("ln2_b")))
+        cache.length = pos0 + T
+        cache.position += T
+        x = self._norm(x, *self.lnf)
+        return (x @ self.wout).float()
+
+    def prefill(self, tokens: torch.Tensor, cache: KvCache) -> torch.Tensor:
+        if tokens.dim() == 1:
+            tokens = tokens[None]
+        return self._run(tokens.to(self.device), cache)
+
+    def step(self, tokens: torch.Tensor, cache: KvCache) -> torch.Tensor:
+        """One token per sequence [B] -> logits [B, V]."""
+        if cache.window is not None and cache.length >= cache.window:
+            cache.evict()
+        return self._run(tokens.to(self.device).view(-1, 1), cache)[:, -1]
+
+    @torch.no_grad()
+    def generate(self, prompts: Sequence[Sequence[int]], max_new_tokens: int, eos: int = -1) -> List[List[int]]:
+        """Greedy batched generation (prompts padded on the left to a common length)."""
+        B = len(prompts)
+        T = max(len(p) for p in prompts)
+        pad = [[p[0]] * (T - len(p)) + list(p) for p in prompts]
+        cache = self.new_cache(B, min(self.cfg.max_seq, T + max_new_tokens))
+        logits = self.prefill(torch.tensor(pad), cache)[:, -1]
+        out = [[] for _ in range(B)]
+        done = [False] * B
+        for _ in range(max_new_tokens):
+            nxt = torch.argmax(logits, -1)
+            for i, t in enumerate(nxt.tolist()):
+                if not done[i]:
+                    out[i].append(t)
+                    done[i] = t == eos
+            if all(done) or cache.length >= cache.k.shape[3]:
+                break
+            logits = self.step(nxt, cache)
+        return out
+
+
+def export(model: DecoderLM, device=None, dtype=None) -> InferenceModel:
+    """GptExporter.Export: a trained DecoderLM becomes a KV-cache inference model."""
+    return InferenceModel(model, device, dtype)
+
+
+class LlmServer:
+    """O(n) decoding over a KV cache (Serving/LlmServer.cs:16-95)."""
+
+    def __init__(self, model: InferenceModel, tokenizer):
+        self.model, self.tok = model, tokenizer
+        self.prompted = 0
+        self.generated = 0
+
+    def generate(self, prompt: str, max_new_tokens: int = 64, stop_at_eos: bool = True) -> str:
+        ids = self.tok.encode(prompt, add_bos=True)
+        out = self.model.generate([ids], max_new_tokens, self.tok.eos if stop_at_eos else -1)[0]
+        if stop_at_eos and out and out[-1] == self.tok.eos:
+            out = out[:-1]
+        self.prompted += len(ids)
+        self.generated += len(out)
+        return self.tok.decode(out)
+
+    def generate_batch(self, prompts: Sequence[str], max_new_tokens: int = 64) -> List[str]:
+        ids = [self.tok.encode(p, add_bos=True) for p in prompts]
+        outs = self.model.generate(ids, max_new_tokens, self.tok.eos)
+        return [self.tok.decode([t for t in o if t != self.tok.eos]) for o in outs]

@@ -302,6 +302,19 @@ class DecoderLM(nn.Module):
             ps.append(self.plan.view(1, -1))
         return ps
 
+    @torch.no_grad()
+    def load_reference_parameters(self, tensors) -> None:
+        """Overwrite every parameter from tensors given in the reference Parameters() order
+        (per-head matrices unpacked), e.g. a legacy LLM1 checkpoint or a FASTER store's tensors."""
+        dst = self.reference_parameters()
+        if len(tensors) != len(dst):
+            raise ValueError(f"expected {len(dst)} tensors in reference order, got {len(tensors)}")
+        for i, (d, src) in enumerate(zip(dst, tensors)):
+            src = torch.as_tensor(src, dtype=torch.float32)
+            if src.numel() != d.numel():
+                raise ValueError(f"tensor {i}: shape {tuple(src.shape)} vs model {tuple(d.shape)}")
+            d.copy_(src.reshape(d.shape).to(d.device))
+
     @property
     def parameter_count(self) -> int:
         return sum(p.numel() for p in self.parameters())
