@@ -163,17 +163,39 @@ class Network:
             if l > 1 and not layers[l - 1].is_clamped:
                 layers[l - 1].mu = layers[l].pred.clone()
 
+    # ---- override points for architecture variants (attention gates, skips, ...)
+    def _lower_error(self, layers: List[Layer], l: int) -> torch.Tensor:
+        """Error of layer l-1 as seen by layer l's state and weight updates."""
+        return layers[l - 1].eps
+
+    def _after_predictions(self, layers: List[Layer]) -> None:
+        """Hook between the top-down predictions and the error computation."""
+
+    def _after_state_updates(self, layers: List[Layer]) -> None:
+        """Hook after the state updates of a relaxation step."""
+
+    def _after_learn(self, layers: List[Layer], lr_scale: float) -> None:
+        """Hook after the Hebbian weight updates of a learning step."""
+
+    def _update_weights(self, layers: List[Layer], lr: float) -> None:
+        for l in range(1, len(layers)):
+            layers[l].update_weights(self._lower_error(layers, l), lr)
+            layers[l].W_half = None
+            self._store.write(l, layers[l])
+
     def _relax_step(self, layers: List[Layer]) -> None:
         L = len(layers)
         for l in range(L - 1, 0, -1):
             layers[l].compute_prediction()
+        self._after_predictions(layers)
         for l in range(1, L):
             layers[l - 1].set_prediction_error(layers[l].pred)
         layers[-1].set_prediction_error(None)
         for l in range(1, L):
             if not layers[l].is_clamped:
-                layers[l].update_state(layers[l - 1].eps, self.config.state_lr,
+                layers[l].update_state(self._lower_error(layers, l), self.config.state_lr,
                                        self.config.activity_regularization)
+        self._after_state_updates(layers)
 
     def _infer_core(self, layers, x, steps, clamp_top, label) -> None:
         self._clamp(layers, 0, self._flatten(x))
@@ -280,10 +302,8 @@ class Network:
             self._infer_core(layers, x, steps, True, label)
             energy = self._energy(layers)
             if gate > 0:
-                for l in range(1, len(layers)):
-                    layers[l].update_weights(layers[l - 1].eps, self.config.weight_lr * gate)
-                    layers[l].W_half = None
-                    self._store.write(l, layers[l])
+                self._update_weights(layers, self.config.weight_lr * gate)
+                self._after_learn(layers, gate)
             return energy
 
     def learn_gated(self, x, label, steps: int, gate: float) -> float:
@@ -440,6 +460,56 @@ class Network:
             self._infer_core(layers, flat, steps, True, lab)
             self._write_back(layers, range(len(layers)))
             return best_c
+
+    def infer_energy_temporal(self, x, label, steps, priors=None, precision: float = 1.0) -> float:
+        with self._lock:
+            layers = self._read_all()
+            if priors is not None:
+                self._inject_temporal(layers, priors, precision)
+            self._infer_core(layers, x, steps, True, label)
+            return self._energy(layers)
+
+    def learn_temporal_gated(self, x, label, steps, priors=None, precision: float = 1.0, gate: float = 1.0):
+        """Temporal learning with the weight lr scaled by ``gate``; returns (hidden states, energy)."""
+        with self._lock:
+            layers = self._read_all()
+            if priors is not None:
+                self._inject_temporal(layers, priors, precision)
+            self._infer_core(layers, x, steps, True, label)
+            energy = self._energy(layers)
+            if gate > 0:
+                for l in range(1, len(layers)):
+                    layers[l].update_weights(layers[l - 1].eps, self.config.weight_lr * gate)
+                    self._store.write(l, layers[l])
+            return self._hidden_states(layers), energy
+
+    def predict_with_energy_temporal(self, x, steps, priors=None, precision: float = 1.0):
+        with self._lock:
+            layers = self._read_all()
+            n = layers[-1].size
+            flat = self._flatten(x)
+            best_e, best_c = float("inf"), 0
+            for c in range(n):
+                for L in layers[1:-1]:
+                    L.mu = torch.zeros_like(L.mu)
+                if priors is not None:
+                    self._inject_temporal(layers, priors, precision)
+                lab = torch.zeros(n)
+                lab[c] = 1.0
+                self._infer_core(layers, flat, steps, True, lab)
+                e = self._energy(layers)
+                if e < best_e:
+                    best_e, best_c = e, c
+            for L in layers[1:-1]:
+                L.mu = torch.zeros_like(L.mu)
+            if priors is not None:
+                self._inject_temporal(layers, priors, precision)
+            lab = torch.zeros(n)
+            lab[best_c] = 1.0
+            self._infer_core(layers, flat, steps, True, lab)
+            winner = self._energy(layers)
+            self._write_back(layers, range(len(layers)))
+            return best_c, winner
 
     def learn_unsupervised_temporal(self, x, steps, priors=None, precision: float = 1.0):
         with self._lock:
