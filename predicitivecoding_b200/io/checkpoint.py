@@ -138,6 +138,30 @@ class CheckpointStore:
         self.close()
 
 
+def save_parameters(directory: str, tensors: Sequence[torch.Tensor], precision: str = "float32") -> None:
+    """Parameters only, keys 0..N-1 (the plain ``Checkpoint.Save(dir, params)`` layout)."""
+    blobs = [tensor_blob(t, precision) for t in tensors]
+    bits = page_size_bits_for(max((len(b) for b in blobs), default=0))
+    clear_store(directory)
+    os.makedirs(directory, exist_ok=True)
+    write_page_size_hint(directory, bits)
+    with CheckpointStore(directory, bits, recover=False) as st:
+        for i, b in enumerate(blobs):
+            st.put_blob(i, b)
+        st.commit()
+
+
+def load_parameters(directory: str) -> List[torch.Tensor]:
+    bits = read_page_size_hint(directory)
+    out = []
+    with CheckpointStore(directory, bits, recover=True) as st:
+        i = 0
+        while (b := st.get_blob(i)) is not None:
+            out.append(torch.from_numpy(read_tensor_blob(b)[0].copy()))
+            i += 1
+    return out
+
+
 def clear_store(directory: str) -> None:
     import glob
     import shutil
