@@ -34,6 +34,17 @@ int pcb_attn_bwd_rope(const void* qkv, long long ld, const void* out, const void
                       const float* lse, float* dvec, float* dq_acc, void* dqkv, long long ld_d, int B, int S, int H,
                       int HD, float scale, const float* rope_cs, cudaStream_t s);
 
+int pcb_decode_attn(const void* q, const void* kc, const void* vc, const int* lens, float* pacc, float* pml,
+                    void* out, int B, int H, int Hkv, int HD, int cap, int nsplit, float scale, float softcap,
+                    cudaStream_t s);
+int pcb_wq_gemv(const float* x, const void* w, const float* scale, float* y, int NB, int rows, int cols, int bits,
+                cudaStream_t s);
+int pcb_softmax_rows(const float* x, float* y, int rows, int n, float scale, cudaStream_t s);
+int pcb_softmax_rows_bwd(const float* y, const float* dy, float* dx, int rows, int n, float scale, cudaStream_t s);
+int pcb_linear_scan(const float* a, const float* b, float* st, int B, int T, int D, cudaStream_t s);
+int pcb_linear_scan_bwd(const float* a, const float* st, const float* ds, float* da, float* db, int B, int T, int D,
+                        cudaStream_t s);
+
 int pcb_peer_alloc(size_t bytes, void** ptr);
 int pcb_peer_free(void* ptr);
 int pcb_ipc_handle(void* ptr, void* out64);
@@ -65,6 +76,12 @@ void check(int rc, const char* what, int kernels = 1) {
 void req(const at::Tensor& t, at::ScalarType dt, const char* name) {
   TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
   TORCH_CHECK(t.scalar_type() == dt, name, " has dtype ", t.scalar_type(), ", expected ", dt);
+}
+
+// req + contiguous (for kernels that index flat)
+void reqc(const at::Tensor& t, at::ScalarType dt, const char* name) {
+  req(t, dt, name);
+  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
 }
 
 // row stride (elements) of a 2-D view whose inner dimension is contiguous
@@ -350,6 +367,72 @@ void peer_reduce(const at::Tensor& in_ptrs, const at::Tensor& out_ptrs, int64_t 
         "peer_reduce");
 }
 
+
+// ---------------------------------------------------------------- serving / small ops
+void decode_attn(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& vc, const at::Tensor& lens,
+                 at::Tensor& pacc, at::Tensor& pml, at::Tensor& out, int64_t nsplit, double scale, double softcap) {
+  reqc(q, at::kBFloat16, "q");
+  reqc(kc, at::kBFloat16, "k_cache");
+  reqc(vc, at::kBFloat16, "v_cache");
+  reqc(lens, at::kInt, "lens");
+  reqc(pacc, at::kFloat, "pacc");
+  reqc(pml, at::kFloat, "pml");
+  reqc(out, at::kBFloat16, "out");
+  TORCH_CHECK(q.dim() == 3 && kc.dim() == 4 && vc.sizes() == kc.sizes(), "decode_attn: q [B,H,hd], caches [B,Hkv,cap,hd]");
+  const int64_t B = q.size(0), H = q.size(1), HD = q.size(2), Hkv = kc.size(1), cap = kc.size(2);
+  TORCH_CHECK(kc.size(0) == B && kc.size(3) == HD && lens.numel() == B, "decode_attn: shape mismatch");
+  TORCH_CHECK(pacc.numel() >= B * H * nsplit * HD && pml.numel() >= B * H * nsplit * 2, "decode_attn: scratch too small");
+  check(pcb_decode_attn(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), lens.data_ptr<int>(), pacc.data_ptr<float>(),
+                        pml.data_ptr<float>(), out.data_ptr(), B, H, Hkv, HD, cap, nsplit, (float)scale,
+                        (float)softcap, cur_stream()),
+        "decode_attn", 2);
+}
+void wq_gemv(const at::Tensor& x, const at::Tensor& w, const at::Tensor& scale, at::Tensor& y, int64_t bits) {
+  reqc(x, at::kFloat, "x");
+  reqc(scale, at::kFloat, "scale");
+  reqc(y, at::kFloat, "y");
+  TORCH_CHECK(w.is_cuda() && w.is_contiguous() && w.element_size() == 1, "wq_gemv: w must be a contiguous byte tensor");
+  const int64_t NB = x.size(0), cols = x.size(1), rows = w.size(0);
+  TORCH_CHECK(w.size(1) == (bits == 8 ? cols : cols / 2) && y.size(0) == NB && y.size(1) == rows, "wq_gemv: shapes");
+  check(pcb_wq_gemv(x.data_ptr<float>(), w.data_ptr(), scale.data_ptr<float>(), y.data_ptr<float>(), NB, rows, cols,
+                    bits, cur_stream()),
+        "wq_gemv");
+}
+void softmax_rows(const at::Tensor& x, at::Tensor& y, double scale) {
+  reqc(x, at::kFloat, "x");
+  reqc(y, at::kFloat, "y");
+  const int64_t n = x.size(-1), rows = x.numel() / n;
+  check(pcb_softmax_rows(x.data_ptr<float>(), y.data_ptr<float>(), rows, n, (float)scale, cur_stream()), "softmax_rows");
+}
+void softmax_rows_bwd(const at::Tensor& y, const at::Tensor& dy, at::Tensor& dx, double scale) {
+  reqc(y, at::kFloat, "y");
+  reqc(dy, at::kFloat, "dy");
+  reqc(dx, at::kFloat, "dx");
+  const int64_t n = y.size(-1), rows = y.numel() / n;
+  check(pcb_softmax_rows_bwd(y.data_ptr<float>(), dy.data_ptr<float>(), dx.data_ptr<float>(), rows, n, (float)scale,
+                             cur_stream()),
+        "softmax_rows_bwd");
+}
+void linear_scan(const at::Tensor& a, const at::Tensor& b, at::Tensor& s) {
+  reqc(a, at::kFloat, "a");
+  reqc(b, at::kFloat, "b");
+  reqc(s, at::kFloat, "s");
+  TORCH_CHECK(a.dim() == 3 && a.sizes() == b.sizes() && s.sizes() == a.sizes(), "linear_scan: [B,T,D]");
+  check(pcb_linear_scan(a.data_ptr<float>(), b.data_ptr<float>(), s.data_ptr<float>(), a.size(0), a.size(1),
+                        a.size(2), cur_stream()),
+        "linear_scan");
+}
+void linear_scan_bwd(const at::Tensor& a, const at::Tensor& s, const at::Tensor& ds, at::Tensor& da, at::Tensor& db) {
+  reqc(a, at::kFloat, "a");
+  reqc(s, at::kFloat, "s");
+  reqc(ds, at::kFloat, "ds");
+  reqc(da, at::kFloat, "da");
+  reqc(db, at::kFloat, "db");
+  check(pcb_linear_scan_bwd(a.data_ptr<float>(), s.data_ptr<float>(), ds.data_ptr<float>(), da.data_ptr<float>(),
+                            db.data_ptr<float>(), a.size(0), a.size(1), a.size(2), cur_stream()),
+        "linear_scan_bwd");
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -371,6 +454,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("launch_count", &launch_count);
   m.def("set_gemm_mode", [](int64_t m) { pcb_set_gemm_mode((int)m); },
         "GEMM kernel choice: -1 env/auto, 0 auto, 1 single-CTA only, 2 CTA pairs when legal");
+  m.def("decode_attn", &decode_attn);
+  m.def("wq_gemv", &wq_gemv);
+  m.def("softmax_rows", &softmax_rows);
+  m.def("softmax_rows_bwd", &softmax_rows_bwd);
+  m.def("linear_scan", &linear_scan);
+  m.def("linear_scan_bwd", &linear_scan_bwd);
   m.def("peer_alloc", &peer_alloc);
   m.def("ipc_handle", &ipc_handle);
   m.def("ipc_open", &ipc_open);

@@ -19,6 +19,8 @@ from typing import List, Optional, Sequence, Tuple
 import torch
 import torch.nn.functional as F
 
+from .. import ops
+
 from ..models.decoder_lm import (AttentionBlock, DecoderLM, apply_rope, gelu_tanh, layer_norm, rms_norm,
                                  rope_tables, sinusoidal_positions)
 
@@ -59,6 +61,9 @@ class InferenceModel:
         self.kv_dtype = kv_dtype or self.dtype
         self.model = model
         self.forward_tokens = 0
+        # the decode kernel reads bf16 caches with head_dim 64 or 128 on the GPU
+        self._fast_decode = (self.device.type == "cuda" and self.kv_dtype == torch.bfloat16
+                             and cfg.head_dim in (64, 128))
         cast = lambda t: None if t is None else t.detach().to(self.device, self.dtype)
         self.wemb = cast(model.wemb)
         self.wout = cast(model.wout)
@@ -111,6 +116,7 @@ class InferenceModel:
             x = x + sinusoidal_positions(p0 + T, c.dim, device=self.device)[p0:].to(self.dtype)
         H, hd = c.num_heads, c.head_dim
         scale = 1.0 / math.sqrt(hd)
+        lens = None
         for l, blk in enumerate(self.blocks):
             h = self._norm(x, blk["ln1_g"], blk.get("ln1_b"))
             q = (h @ blk["wq"]).view(B, T, H, hd).transpose(1, 2)
@@ -121,11 +127,17 @@ class InferenceModel:
                 k = apply_rope(k, *rope)
             cache.k[l, :, :, pos0:pos0 + T] = k.to(self.kv_dtype)
             cache.v[l, :, :, pos0:pos0 + T] = v.to(self.kv_dtype)
-            K = cache.k[l, :, :, :pos0 + T].to(self.dtype)
-            V = cache.v[l, :, :, :pos0 + T].to(self.dtype)
-            # causal over the new positions, full over the cached prefix
-            mask = torch.ones(T, pos0 + T, dtype=torch.bool, device=self.device).tril(pos0)
-            o = F.scaled_dot_product_attention(q, K, V, attn_mask=mask, scale=scale)
+            if T == 1 and self._fast_decode:
+                # one new token per sequence: split-KV decode kernel straight on the cache
+                if lens is None:
+                    lens = torch.full((B,), pos0 + 1, dtype=torch.int32, device=self.device)
+                o = ops.decode_attn(q[:, :, 0].contiguous(), cache.k[l], cache.v[l], lens, scale)[:, :, None]
+            else:
+                K = cache.k[l, :, :, :pos0 + T].to(self.dtype)
+                V = cache.v[l, :, :, :pos0 + T].to(self.dtype)
+                # causal over the new positions, full over the cached prefix
+                mask = torch.ones(T, pos0 + T, dtype=torch.bool, device=self.device).tril(pos0)
+                o = F.scaled_dot_product_attention(q, K, V, attn_mask=mask, scale=scale)
             x = x + o.transpose(1, 2).reshape(B, T, c.dim) @ blk["wo"]
             x = x + self._ffn(blk, self._norm(x, blk["ln2_g"], blk.get("ln2_b")))
         cache.length = pos0 + T

@@ -211,7 +211,13 @@ class AttentionBlock(nn.Module):
 
 
 def recurrent_scan(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
-    """s_t = a_t * s_{t-1} + b_t along the sequence axis (Autograd.cs:741-767).  [B, S, D]."""
+    """s_t = a_t * s_{t-1} + b_t along the sequence axis (Autograd.cs:741-767).  [B, S, D].
+
+    On a CUDA device the scan runs as one kernel per direction (forward scan, reverse-scan backward).
+    """
+    if a.is_cuda:
+        from .. import ops
+        return ops.LinearScan.apply(a, b)
     out = []
     s = torch.zeros_like(b[:, 0])
     for t in range(b.shape[1]):

@@ -141,3 +141,81 @@ def attn_fwd(qkv, out, lse, B, S, H, HD, scale):
 def attn_bwd(qkv, out, dout, lse, dvec, dq_acc, dqkv, B, S, H, HD, scale, rope_cs=None):
     """Attention backward; with ``rope_cs`` the dq/dk written are w.r.t. the pre-RoPE q/k."""
     ext().attn_bwd(qkv, out, dout, lse, dvec, dq_acc, dqkv, int(B), int(S), int(H), int(HD), float(scale), rope_cs)
+
+
+# --------------------------------------------------------------------------- serving / small ops
+def decode_attn(q, k_cache, v_cache, lens, scale, softcap=0.0, nsplit=None, out=None, scratch=None):
+    """Single-token attention against a contiguous KV cache (flash-decoding, GQA).
+
+    q [B, H, hd] bf16; k_cache / v_cache [B, Hkv, cap, hd] bf16; lens [B] int32 valid lengths.
+    Returns out [B, H, hd] bf16.  ``scratch`` = (pacc, pml) may be passed to avoid allocation.
+    """
+    B, H, HD = q.shape
+    cap = k_cache.shape[2]
+    if nsplit is None:
+        # enough CTAs to cover the SMs, at least 128 keys per split
+        want = max(1, (2 * 148) // max(1, B * k_cache.shape[1]))
+        nsplit = max(1, min(want, (cap + 127) // 128))
+    if scratch is None:
+        pacc = torch.empty(B * H * nsplit * HD, device=q.device)
+        pml = torch.empty(B * H * nsplit * 2, device=q.device)
+    else:
+        pacc, pml = scratch
+    if out is None:
+        out = torch.empty_like(q)
+    ext().decode_attn(q, k_cache, v_cache, lens, pacc, pml, out, int(nsplit), float(scale), float(softcap))
+    return out
+
+
+def wq_matmul(x, w, scale, bits):
+    """y = (x @ dequant(w)^T) for weight-only int8 ([rows, cols] int8) or int4 ([rows, cols/2] packed)."""
+    x2 = x.float().reshape(-1, x.shape[-1]).contiguous()
+    rows = w.shape[0]
+    outs = []
+    for i in range(0, x2.shape[0], 8):
+        xb = x2[i:i + 8]
+        y = torch.empty(xb.shape[0], rows, device=x.device)
+        ext().wq_gemv(xb, w, scale, y, int(bits))
+        outs.append(y)
+    return torch.cat(outs).reshape(*x.shape[:-1], rows)
+
+
+def softmax_rows(x, scale=1.0, out=None):
+    out = torch.empty_like(x) if out is None else out
+    ext().softmax_rows(x, out, float(scale))
+    return out
+
+
+def softmax_rows_bwd(y, dy, scale=1.0, out=None):
+    out = torch.empty_like(y) if out is None else out
+    ext().softmax_rows_bwd(y, dy, out, float(scale))
+    return out
+
+
+def linear_scan(a, b, out=None):
+    """s_t = a_t * s_{t-1} + b_t along dim 1 of [B, T, D] fp32 tensors."""
+    out = torch.empty_like(a) if out is None else out
+    ext().linear_scan(a, b, out)
+    return out
+
+
+def linear_scan_bwd(a, s, ds):
+    da, db = torch.empty_like(a), torch.empty_like(a)
+    ext().linear_scan_bwd(a, s, ds, da, db)
+    return da, db
+
+
+class LinearScan(torch.autograd.Function):
+    """Autograd wrapper of the recurrence kernel (used by the temporal blocks on the GPU)."""
+
+    @staticmethod
+    def forward(ctx, a, b):
+        a, b = a.contiguous().float(), b.contiguous().float()
+        s = linear_scan(a, b)
+        ctx.save_for_backward(a, s)
+        return s
+
+    @staticmethod
+    def backward(ctx, ds):
+        a, s = ctx.saved_tensors
+        return linear_scan_bwd(a, s, ds.contiguous().float())

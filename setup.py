@@ -33,6 +33,7 @@ setup(
                 os.path.join(CSRC, "ops_llm.cu"),
                 os.path.join(CSRC, "attention.cu"),
                 os.path.join(CSRC, "peer.cu"),
+                os.path.join(CSRC, "decode.cu"),
             ],
             include_dirs=[os.path.join(HERE, CSRC)],
             extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
