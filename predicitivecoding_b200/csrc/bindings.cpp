@@ -45,6 +45,19 @@ int pcb_linear_scan(const float* a, const float* b, float* st, int B, int T, int
 int pcb_linear_scan_bwd(const float* a, const float* st, const float* ds, float* da, float* db, int B, int T, int D,
                         cudaStream_t s);
 
+int pcb_coll_reduce(const void* const* in_peers, void* out, long long lo, long long hi, int world, int op,
+                    float scale, int dtype, int num_sms, cudaStream_t s);
+int pcb_coll_gather(const void* const* src_peers, void* out, long long chunk, long long src_stride, int world,
+                    int dtype, int num_sms, cudaStream_t s);
+int pcb_alloc(int device, size_t bytes, void* stream, void** out);
+int pcb_free(void* ptr);
+int pcb_record_stream(void* ptr, void* stream);
+void pcb_release_cached(int device);
+void pcb_alloc_stats(int device, long long* out6);
+void pcb_alloc_reset_peak(int device);
+int pcb_stream(int device, int index, int high_priority, int n, void** out);
+int pcb_stream_count(int device, int high_priority);
+
 int pcb_peer_alloc(size_t bytes, void** ptr);
 int pcb_peer_free(void* ptr);
 int pcb_ipc_handle(void* ptr, void* out64);
@@ -433,6 +446,52 @@ void linear_scan_bwd(const at::Tensor& a, const at::Tensor& s, const at::Tensor&
         "linear_scan_bwd");
 }
 
+
+// ---------------------------------------------------------------- collectives over symmetric buffers
+int coll_dtype(const at::Tensor& t) {
+  if (t.scalar_type() == at::kFloat) return 0;
+  TORCH_CHECK(t.scalar_type() == at::kBFloat16, "collectives support fp32 and bf16");
+  return 1;
+}
+void coll_reduce(const at::Tensor& in_ptrs, at::Tensor& out, int64_t lo, int64_t hi, int64_t world, int64_t op,
+                 double scale) {
+  req(in_ptrs, at::kLong, "in_ptrs");
+  TORCH_CHECK(out.is_cuda() && out.is_contiguous() && out.numel() >= hi - lo, "coll_reduce: out too small");
+  check(pcb_coll_reduce(reinterpret_cast<const void* const*>(in_ptrs.data_ptr<int64_t>()), out.data_ptr(), lo, hi,
+                        world, op, (float)scale, coll_dtype(out), num_sms(), cur_stream()),
+        "coll_reduce");
+}
+void coll_gather(const at::Tensor& src_ptrs, at::Tensor& out, int64_t chunk, int64_t src_stride, int64_t world) {
+  req(src_ptrs, at::kLong, "src_ptrs");
+  TORCH_CHECK(out.is_cuda() && out.is_contiguous() && out.numel() >= chunk * world, "coll_gather: out too small");
+  check(pcb_coll_gather(reinterpret_cast<const void* const*>(src_ptrs.data_ptr<int64_t>()), out.data_ptr(), chunk,
+                        src_stride, world, coll_dtype(out), num_sms(), cur_stream()),
+        "coll_gather");
+}
+
+// ---------------------------------------------------------------- native runtime
+at::Tensor dev_alloc(int64_t bytes, int64_t device, int64_t stream) {
+  void* p = nullptr;
+  TORCH_CHECK(pcb_alloc((int)device, (size_t)bytes, reinterpret_cast<void*>(stream), &p) == 0,
+              "dev_alloc: out of device memory");
+  auto opts = at::TensorOptions().dtype(at::kByte).device(at::kCUDA, device);
+  return torch::from_blob(p, {bytes}, [](void* q) { pcb_free(q); }, opts);
+}
+void dev_record_stream(const at::Tensor& t, int64_t stream) {
+  TORCH_CHECK(pcb_record_stream(t.storage().data_ptr().get(), reinterpret_cast<void*>(stream)) == 0,
+              "record_stream: tensor was not allocated by the runtime allocator");
+}
+std::vector<int64_t> dev_alloc_stats(int64_t device) {
+  long long s[6];
+  pcb_alloc_stats((int)device, s);
+  return std::vector<int64_t>(s, s + 6);
+}
+int64_t dev_stream(int64_t device, int64_t index, bool high_priority, int64_t n) {
+  void* s = nullptr;
+  TORCH_CHECK(pcb_stream((int)device, (int)index, high_priority ? 1 : 0, (int)n, &s) == 0, "stream creation failed");
+  return reinterpret_cast<int64_t>(s);
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -460,6 +519,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("softmax_rows_bwd", &softmax_rows_bwd);
   m.def("linear_scan", &linear_scan);
   m.def("linear_scan_bwd", &linear_scan_bwd);
+  m.def("coll_reduce", &coll_reduce);
+  m.def("coll_gather", &coll_gather);
+  m.def("dev_alloc", &dev_alloc);
+  m.def("dev_record_stream", &dev_record_stream);
+  m.def("dev_release_cached", [](int64_t d) { pcb_release_cached((int)d); });
+  m.def("dev_alloc_stats", &dev_alloc_stats);
+  m.def("dev_alloc_reset_peak", [](int64_t d) { pcb_alloc_reset_peak((int)d); });
+  m.def("dev_stream", &dev_stream);
+  m.def("dev_stream_count", [](int64_t d, bool hp) { return pcb_stream_count((int)d, hp ? 1 : 0); });
   m.def("peer_alloc", &peer_alloc);
   m.def("ipc_handle", &ipc_handle);
   m.def("ipc_open", &ipc_open);

@@ -34,6 +34,8 @@ setup(
                 os.path.join(CSRC, "attention.cu"),
                 os.path.join(CSRC, "peer.cu"),
                 os.path.join(CSRC, "decode.cu"),
+                os.path.join(CSRC, "collectives.cu"),
+                os.path.join(CSRC, "runtime.cpp"),
             ],
             include_dirs=[os.path.join(HERE, CSRC)],
             extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
