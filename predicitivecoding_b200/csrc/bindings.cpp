@@ -7,6 +7,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
+#include <pybind11/stl.h>
 
 #include <atomic>
 
@@ -49,6 +50,9 @@ int pcb_coll_reduce(const void* const* in_peers, void* out, long long lo, long l
                     float scale, int dtype, int num_sms, cudaStream_t s);
 int pcb_coll_gather(const void* const* src_peers, void* out, long long chunk, long long src_stride, int world,
                     int dtype, int num_sms, cudaStream_t s);
+int pcb_tp_reduce_norm(const void* slots, int world, int rows, int D, const float* resid, float* x_out,
+                       int accumulate, const void* gamma, void* y, long long ldy, float* inv, float eps,
+                       cudaStream_t s);
 int pcb_alloc(int device, size_t bytes, void* stream, void** out);
 int pcb_free(void* ptr);
 int pcb_record_stream(void* ptr, void* stream);
@@ -122,7 +126,8 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, int64_
           const c10::optional<at::Tensor>& c, const c10::optional<at::Tensor>& d,
           const c10::optional<at::Tensor>& aux, const c10::optional<at::Tensor>& bias, double alpha,
           int64_t force_bn, int64_t force_splits, const c10::optional<at::Tensor>& err,
-          const c10::optional<at::Tensor>& rope_cs, int64_t rope_S, int64_t rope_hd, int64_t rope_cols) {
+          const c10::optional<at::Tensor>& rope_cs, int64_t rope_S, int64_t rope_hd, int64_t rope_cols,
+          const c10::optional<std::vector<int64_t>>& tp) {
   req(a, at::kBFloat16, "a");
   req(b, at::kBFloat16, "b");
   const long long lda = row_stride(a, "a"), ldb = row_stride(b, "b");
@@ -152,6 +157,25 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, int64_
   }
   if (epi == pcb::EPI_SWIGLU) TORCH_CHECK(args.N % 128 == 0, "swiglu gemm needs N % 128 == 0");
   if (epi == pcb::EPI_SWIGLU_BWD) TORCH_CHECK(args.N % 64 == 0, "swiglu bwd gemm needs N % 64 == 0");
+  if (tp) {
+    // tensor-parallel fusion: [ag_peers table, ag_ready counters, ag_rows, ag_rank, ag_world,
+    //                          rs_peers table, rs_rows, rs_rank] (device addresses as integers)
+    const auto& v = *tp;
+    TORCH_CHECK(v.size() == 8, "gemm: tp must have 8 entries");
+    args.ag_peers = reinterpret_cast<const void* const*>(v[0]);
+    args.ag_ready = reinterpret_cast<unsigned int*>(v[1]);
+    args.ag_rows = (int)v[2];
+    args.ag_rank = (int)v[3];
+    args.ag_world = v[0] != 0 ? (int)v[4] : 0;
+    args.ag_local = a.data_ptr();
+    args.rs_peers = reinterpret_cast<void* const*>(v[5]);
+    args.rs_rows = (int)v[6];
+    args.rs_rank = (int)v[7];
+  }
+  if (epi == pcb::EPI_RS_BF16) {
+    TORCH_CHECK(args.rs_peers != nullptr, "EPI_RS_BF16 needs the tp slot table");
+    if (!c) args.ldc = args.N;   // slot buffers are [world * rs_rows, N] row-major
+  }
   const at::cuda::CUDAGuard guard(a.device());
   check(pcb_gemm_launch(a.data_ptr(), a_mn, lda, b.data_ptr(), b_mn, ldb, (int)epi, args, (int)force_bn,
                         (int)force_splits, num_sms(), cur_stream()),
@@ -492,6 +516,29 @@ int64_t dev_stream(int64_t device, int64_t index, bool high_priority, int64_t n)
   return reinterpret_cast<int64_t>(s);
 }
 
+
+// x_out = (resid or x_out if accumulate or 0) + sum of world bf16 slots; optional RMSNorm into y
+void tp_reduce_norm(const at::Tensor& slots, int64_t world, const c10::optional<at::Tensor>& resid, at::Tensor& x_out,
+                    bool accumulate, const c10::optional<at::Tensor>& gamma, const c10::optional<at::Tensor>& y,
+                    const c10::optional<at::Tensor>& inv, double eps) {
+  reqc(slots, at::kBFloat16, "slots");
+  reqc(x_out, at::kFloat, "x_out");
+  const int64_t rows = x_out.size(0), D = x_out.size(1);
+  TORCH_CHECK(slots.numel() >= world * rows * D, "tp_reduce_norm: slots too small");
+  if (resid) reqc(*resid, at::kFloat, "resid");
+  long long ldy = 0;
+  if (gamma) {
+    TORCH_CHECK(y.has_value() && inv.has_value(), "tp_reduce_norm: gamma needs y and inv");
+    req(*y, at::kBFloat16, "y");
+    ldy = row_stride(*y, "y");
+  }
+  check(pcb_tp_reduce_norm(slots.data_ptr(), (int)world, (int)rows, (int)D,
+                           resid ? resid->data_ptr<float>() : nullptr, x_out.data_ptr<float>(), accumulate ? 1 : 0,
+                           gamma ? gamma->data_ptr() : nullptr, y ? y->data_ptr() : nullptr, ldy,
+                           inv ? inv->data_ptr<float>() : nullptr, (float)eps, cur_stream()),
+        "tp_reduce_norm");
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -519,6 +566,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("softmax_rows_bwd", &softmax_rows_bwd);
   m.def("linear_scan", &linear_scan);
   m.def("linear_scan_bwd", &linear_scan_bwd);
+  m.def("tp_reduce_norm", &tp_reduce_norm);
   m.def("coll_reduce", &coll_reduce);
   m.def("coll_gather", &coll_gather);
   m.def("dev_alloc", &dev_alloc);

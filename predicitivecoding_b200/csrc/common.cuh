@@ -26,6 +26,7 @@ enum ErrorCode : int {
   kErrTimeoutTmemEmpty = 4, // MMA waited too long for the epilogue
   kErrTimeoutPeer = 5,      // a peer rank's flag never arrived
   kErrBadArg = 6,
+  kErrTimeoutChunk = 7,     // a gathered chunk of A was never marked copied
 };
 
 // ~2 s at 1.9 GHz.  A legitimate wait in these kernels is microseconds.

@@ -37,6 +37,73 @@ struct Cfg {
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
 };
 
+// Tile -> (split, row-pair block, column block).  Without a gather the row block varies fastest.
+// With a fused all-gather the order is chunk-major, starting at this rank's own chunk and going
+// round the ring, so the first wave computes on local rows while the other chunks are copied.
+PCB_DEVICE void tile_coords(int tile, const GemmArgs& a, int num_m, int num_n, int& split, int& mb, int& nb) {
+  split = tile % a.splits;
+  const int rest = tile / a.splits;
+  if (a.ag_world > 1) {
+    const int mpc = a.ag_rows / (2 * kBM);
+    const int tpc = mpc * num_n;
+    const int c = (a.ag_rank + rest / tpc) % a.ag_world;
+    const int r = rest % tpc;
+    mb = c * mpc + r % mpc;
+    nb = r / mpc;
+  } else {
+    mb = rest % num_m;
+    nb = rest / num_m;
+  }
+}
+
+PCB_DEVICE unsigned int ld_acquire_gpu(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+PCB_DEVICE void red_release_gpu_add(unsigned int* p, unsigned int v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+PCB_DEVICE void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
+// bounded wait until *ctr >= target; false (and an error code) after the clock budget
+PCB_DEVICE bool wait_counter(const unsigned int* ctr, unsigned int target, int* err, volatile int* abort_flag) {
+  const long long t0 = clock64();
+  while (ld_acquire_gpu(ctr) < target) {
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kSpinBudgetCycles) {
+      record_error(err, kErrTimeoutChunk);
+      *abort_flag = 1;
+      return false;
+    }
+    __nanosleep(64);
+  }
+  return true;
+}
+
+// Epilogue warps of every CTA copy an equal share of each remote chunk of A into this rank's
+// gathered buffer (16-byte loads from the peer over NVLink, local stores), then mark it done.
+PCB_DEVICE void gather_chunks(const GemmArgs& a, int tid, int nthreads) {
+  const long long chunk_vec = (long long)a.ag_rows * a.K / 8;   // uint4 per chunk
+  const long long per = (chunk_vec + gridDim.x - 1) / gridDim.x;
+  const long long v0 = blockIdx.x * per;
+  const long long v1 = min(chunk_vec, v0 + per);
+  for (int j = 1; j < a.ag_world; ++j) {
+    const int c = (a.ag_rank + j) % a.ag_world;
+    const uint4* src = reinterpret_cast<const uint4*>(a.ag_peers[c]) + c * chunk_vec;
+    uint4* dst = reinterpret_cast<uint4*>(a.ag_local) + c * chunk_vec;
+    for (long long v = v0 + tid; v < v1; v += nthreads) dst[v] = __ldcg(src + v);
+    fence_proxy_async_global();
+    asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+    if (tid == 0) {
+      __threadfence();
+      red_release_gpu_add(a.ag_ready + c, 1u);
+    }
+  }
+}
+
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -94,14 +161,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      uint32_t ready_mask = args.ag_world > 1 ? (1u << args.ag_rank) : 0xffffffffu;
       for (int tile = pair_id; tile < tiles && ok; tile += num_pairs) {
-        const int split = tile % args.splits;
-        const int rest = tile / args.splits;
-        const int mb = rest % num_m, nb = rest / num_m;
+        int split, mb, nb;
+        tile_coords(tile, args, num_m, num_n, split, mb, nb);
         const int m0 = mb * 2 * kBM + rank * kBM;
         const int n0 = nb * BN + rank * (BN / 2);
         const int kb0 = split * args.kb_per_split;
         const int kb1 = min(total_kb, kb0 + args.kb_per_split);
+        if (args.ag_world > 1) {
+          const int c = m0 / args.ag_rows;
+          if (!((ready_mask >> c) & 1u)) {
+            if (!wait_counter(args.ag_ready + c, gridDim.x, args.err, abort_flag)) { ok = false; break; }
+            fence_proxy_async_global();
+            ready_mask |= 1u << c;
+          }
+        }
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, args.err, kErrTimeoutEmpty, abort_flag)) { ok = false; break; }
           if (leader) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
@@ -134,7 +209,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t acc_phase = 0;
       bool ok = true;
       for (int tile = pair_id; tile < tiles && ok; tile += num_pairs) {
-        const int split = tile % args.splits;
+        const int split = tile % args.splits;   // same in both tile orders
         const int kb0 = split * args.kb_per_split;
         const int kb1 = min(total_kb, kb0 + args.kb_per_split);
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, args.err, kErrTimeoutTmemEmpty, abort_flag)) { ok = false; break; }
@@ -169,11 +244,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = q * 32 + lane;
     const uint32_t tempty_leader0 = mapa_shared(smem_u32(&tempty[0]), 0);
     const uint32_t tempty_leader1 = mapa_shared(smem_u32(&tempty[1]), 0);
+    if (args.ag_world > 1) gather_chunks(args, threadIdx.x - 64, 32 * kEpiWarps);
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = pair_id; tile < tiles; tile += num_pairs) {
-      const int rest = tile / args.splits;
-      const int mb = rest % num_m, nb = rest / num_m;
+      int split_unused, mb, nb;
+      tile_coords(tile, args, num_m, num_n, split_unused, mb, nb);
       const int m = mb * 2 * kBM + rank * kBM + row;
       const int n0 = nb * BN;
       const bool row_ok = m < args.M;
@@ -276,14 +352,24 @@ static int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmA
   cfg.blockDim = dim3(pair::kThreads, 1, 1);
   cfg.dynamicSmemBytes = C::SMEM_BYTES;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  // with a fused gather, CTAs wait on each other's copies: all of them must be resident at once
+  attr[1].id = cudaLaunchAttributeCooperative;
+  attr[1].val.cooperative = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, pair::gemm_pair_kernel<BN, EPI>, ta, tb, a);
+  cfg.numAttrs = a.ag_world > 1 ? 2 : 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, pair::gemm_pair_kernel<BN, EPI>, ta, tb, a);
+  if (e != cudaSuccess && cfg.numAttrs == 2) {
+    // cooperative + cluster refused: one CTA per SM with grid <= SM count is resident anyway on a
+    // stream of its own; the chunk waits stay bounded either way
+    cudaGetLastError();
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, pair::gemm_pair_kernel<BN, EPI>, ta, tb, a);
+  }
   return e == cudaSuccess ? 0 : -3;
 }
 
@@ -304,6 +390,7 @@ static int dispatch_pair(int epi, const CUtensorMap& ta, const CUtensorMap& tb, 
     case EPI_PC_WUPD: return launch_pair<BN, EPI_PC_WUPD>(ta, tb, a, grid, s);
     case EPI_BF16_ACC: return launch_pair<BN, EPI_BF16_ACC>(ta, tb, a, grid, s);
     case EPI_RESID_F32: return launch_pair<BN, EPI_RESID_F32>(ta, tb, a, grid, s);
+    case EPI_RS_BF16: return launch_pair<BN, EPI_RS_BF16>(ta, tb, a, grid, s);
     default: return -2;
   }
 }
@@ -329,6 +416,14 @@ int pcb_gemm_pair_launch(const void* A, int a_mn, long long lda, const void* B, 
   const int total_kb = (K + 63) / 64;
   if (splits < 1) splits = 1;
   if (splits > 1 && epi != EPI_RED_F32) return -4;
+  if (args.ag_world > 1) {
+    // fused gather: K-major A spanning all chunks, whole 256-row tiles per chunk, no split-K
+    if (a_mn != 0 || lda != K || (K % 8) != 0 || args.ag_rows % 256 != 0 || args.ag_world > 32 ||
+        (long long)args.ag_rows * args.ag_world != M || splits != 1 || args.ag_peers == nullptr ||
+        args.ag_ready == nullptr || args.ag_local != A)
+      return -6;
+  }
+  if (epi == EPI_RS_BF16 && (args.rs_peers == nullptr || args.rs_rows <= 0 || (M % args.rs_rows) != 0)) return -6;
   int kbps = (total_kb + splits - 1) / splits;
   splits = (total_kb + kbps - 1) / kbps;
   args.splits = splits;

@@ -18,7 +18,9 @@ enum GemmEpi : int {
   EPI_PC_WUPD = 10,    // PC Hebbian weight update (single rank)
   EPI_BF16_ACC = 11,   // C(bf16) = alpha*acc + aux(bf16)      (bf16 residual add)
   EPI_RESID_F32 = 12,  // C(f32)  = aux(f32) + alpha*acc + bias (residual stream: x_out = x_in + f(x))
-  EPI_COUNT = 13,
+  EPI_RS_BF16 = 13,    // reduce-scatter partials: row m goes to owner c = m / rs_rows, slot rs_rank of
+                       // owner c's buffer rs_peers[c] ([world * rs_rows, N] bf16, row stride ldc)
+  EPI_COUNT = 14,
 };
 
 struct GemmArgs {
@@ -52,6 +54,19 @@ struct GemmArgs {
   int rope_S;
   int rope_hd;
   int rope_cols;
+  // fused all-gather of A (tensor parallel, CTA-pair kernel only): A is this rank's gathered buffer
+  // [ag_world * ag_rows, K]; chunk c of it is copied in-kernel from ag_peers[c] (same layout on
+  // every rank) before the tiles of chunk c are loaded; ag_ready[c] counts CTAs done copying c.
+  const void* const* ag_peers;  // device table [ag_world] (nullptr: no gather)
+  void* ag_local;               // this rank's gathered buffer (same memory as the A operand)
+  unsigned int* ag_ready;       // device counters [ag_world], zero at launch
+  int ag_rows;
+  int ag_rank;
+  int ag_world;
+  // reduce-scatter epilogue (EPI_RS_BF16)
+  void* const* rs_peers;        // device table [world] of owners' slot buffers
+  int rs_rows;
+  int rs_rank;
 };
 
 }  // namespace pcb

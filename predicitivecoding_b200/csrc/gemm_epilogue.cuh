@@ -122,6 +122,15 @@ PCB_DEVICE void epilogue_chunk(const GemmArgs& a, int m, int n, float (&v)[32], 
       for (int j = 0; j < 32; ++j) v[j] += b[j];
     }
   }
+  if (EPI == EPI_RS_BF16) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] *= a.alpha;
+    const int c = m / a.rs_rows;
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.rs_peers[c]) +
+                         (long long)(a.rs_rank * a.rs_rows + (m - c * a.rs_rows)) * a.ldc + n;
+    store_bf16x32(dst, v, nvalid);   // plain stores into the owner's slot over NVLink
+    return;
+  }
   if (EPI == EPI_BF16) {
     if (a.rope_cs != nullptr && n < a.rope_cols) {
       const float2* cs = reinterpret_cast<const float2*>(a.rope_cs) + (long long)(m % a.rope_S) * (a.rope_hd >> 1);

@@ -287,6 +287,7 @@ static int dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, c
     case EPI_PC_WUPD: return launch_one<BN, EPI_PC_WUPD>(ta, tb, a, grid, s);
     case EPI_BF16_ACC: return launch_one<BN, EPI_BF16_ACC>(ta, tb, a, grid, s);
     case EPI_RESID_F32: return launch_one<BN, EPI_RESID_F32>(ta, tb, a, grid, s);
+    case EPI_RS_BF16: return launch_one<BN, EPI_RS_BF16>(ta, tb, a, grid, s);
     default: return -2;
   }
 }
@@ -328,6 +329,10 @@ int pcb_gemm_launch(const void* A, int a_mn, long long lda, const void* B, int b
 
   const int num_m = (M + kBM - 1) / kBM;
   const int total_kb = (K + kBK - 1) / kBK;
+  if (args.ag_world > 1) {  // fused all-gather exists only in the CTA-pair kernel
+    const int pbn = (force_bn == 128 || force_bn == 256) ? force_bn : (N >= 256 ? 256 : 128);
+    return pcb_gemm_pair_launch(A, a_mn, lda, B, b_mn, ldb, epi, args, pbn, 1, num_sms, stream);
+  }
   {
     // CTA pairs (256-row tiles, half the B traffic per SM) when the problem has enough pair tiles
     const int mode = gemm_mode();

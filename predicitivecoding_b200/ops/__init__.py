@@ -8,7 +8,7 @@ cannot be imported, so no GPU code path silently falls back to PyTorch.
 from __future__ import annotations
 
 import importlib
-from typing import Optional
+from typing import Optional, Sequence
 
 import torch
 
@@ -29,6 +29,7 @@ EPI_PC_STATE = 9
 EPI_PC_WUPD = 10
 EPI_BF16_ACC = 11
 EPI_RESID_F32 = 12
+EPI_RS_BF16 = 13
 
 ACT_CODES = {"linear": 0, "tanh": 1, "relu": 2, "sigmoid": 3}
 
@@ -65,7 +66,8 @@ def launch_count() -> int:
 def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = False, epi: int = EPI_BF16,
          c: Optional[torch.Tensor] = None, d: Optional[torch.Tensor] = None, aux: Optional[torch.Tensor] = None,
          bias: Optional[torch.Tensor] = None, alpha: float = 1.0, bn: int = 0, splits: int = 0,
-         err: Optional[torch.Tensor] = None, rope: Optional[tuple] = None) -> Optional[torch.Tensor]:
+         err: Optional[torch.Tensor] = None, rope: Optional[tuple] = None,
+         tp: Optional[Sequence[int]] = None) -> Optional[torch.Tensor]:
     """C = epilogue(op(a) @ op(b)) on the tcgen05 tensor cores.
 
     ``a`` is [M, K] (``a_mn=False``) or [K, M] (``a_mn=True``); ``b`` is [N, K]
@@ -73,6 +75,10 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = F
     With ``epi=EPI_BF16`` and ``c=None`` a new bf16 output is allocated.
     ``rope=(cs, S, hd, cols)`` rotates interleaved column pairs < cols by the RoPE angle of
     position ``row % S`` (``cs`` is the [S, hd/2, 2] cos/sin table); only with EPI_BF16.
+    ``tp`` = (ag_peers, ag_ready, ag_rows, ag_rank, ag_world, rs_peers, rs_rows, rs_rank) turns on
+    the tensor-parallel fusions: ``a`` is this rank's gathered buffer whose remote chunks the kernel
+    copies from ``ag_peers`` before using them (0 = no gather), and EPI_RS_BF16 stores row m into
+    slot ``rs_rank`` of owner ``m // rs_rows``'s buffer from the ``rs_peers`` table.
     """
     if c is None and epi in (EPI_BF16, EPI_F32):
         M = a.shape[1] if a_mn else a.shape[0]
@@ -80,7 +86,7 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = F
         c = torch.empty(M, N, device=a.device, dtype=torch.bfloat16 if epi == EPI_BF16 else torch.float32)
     rc, rS, rhd, rcols = rope if rope is not None else (None, 0, 0, 0)
     ext().gemm(a, a_mn, b, b_mn, epi, c, d, aux, bias, float(alpha), int(bn), int(splits), err, rc, int(rS), int(rhd),
-               int(rcols))
+               int(rcols), None if tp is None else [int(x) for x in tp])
     return c
 
 

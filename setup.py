@@ -35,6 +35,7 @@ setup(
                 os.path.join(CSRC, "peer.cu"),
                 os.path.join(CSRC, "decode.cu"),
                 os.path.join(CSRC, "collectives.cu"),
+                os.path.join(CSRC, "tp.cu"),
                 os.path.join(CSRC, "runtime.cpp"),
             ],
             include_dirs=[os.path.join(HERE, CSRC)],
