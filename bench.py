@@ -13,7 +13,10 @@ sequences per GPU, data parallel over all ranks.  Tokens are seeded Zipf(1.1) ov
 ``--impl ours`` (default) runs the fused sm_100a trainer; ``--impl torch`` runs a
 plain PyTorch autograd + NCCL (+cuBLAS) baseline of the same model;
 ``--impl reference`` reports that the C#/.NET reference cannot run here.
-``--workload pc`` runs the wide predictive-coding MLP (samples/s) instead.
+``--workload pc`` runs the wide predictive-coding MLP (samples/s) instead; ``--workload tp`` runs
+the 1.3B decoder (24 layers, d 2048, 16 heads, ctx 2048, SwiGLU 5504) tensor-parallel over all
+ranks with the all-gather and reduce-scatter fused into the GEMMs (micro-batch 8 sequences per
+tensor-parallel group).
 """
 from __future__ import annotations
 
@@ -36,7 +39,7 @@ def parse():
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="ours", choices=["ours", "torch", "reference"])
-    p.add_argument("--workload", default="decoder", choices=["decoder", "bytelm", "pc"])
+    p.add_argument("--workload", default="decoder", choices=["decoder", "bytelm", "pc", "tp"])
     p.add_argument("--batch", type=int, default=0, help="micro-batch per GPU (default from the workload)")
     p.add_argument("--no-graph", action="store_true")
     p.add_argument("--e2e-steps", type=int, default=0, help="steps of the end-to-end timing (default = --steps)")
@@ -111,21 +114,42 @@ def run_decoder_bench(args, dev, rank, world, pg):
     from predicitivecoding_b200.utils.clocks import ClockSampler
     from predicitivecoding_b200.utils.data import zipf_windows
 
+    tp_mode = args.workload == "tp"
     if args.workload == "bytelm":
         cfg = DecoderLmConfig.byte_lm_4l()
         B = args.batch or 64
         name = "byte-lm-4L-256d"
+    elif tp_mode:
+        cfg = DecoderLmConfig.decoder_1p3b()
+        B = args.batch or 8
+        name = "decoder-1.3B-swiglu"
     else:
         cfg = DecoderLmConfig.gpt2_small_swiglu()
         B = args.batch or 16
         name = "decoder-124M-swiglu"
     S = cfg.max_seq
     M = B * S
-    pool = [zipf_windows(B, S, cfg.vocab, 1.1, seed=1000 * rank + i) for i in range(4)]
+    # data-parallel ranks see different batches; tensor-parallel ranks share theirs
+    pool = [zipf_windows(B, S, cfg.vocab, 1.1, seed=(0 if tp_mode else 1000 * rank) + i) for i in range(4)]
     pool = [(a.to(torch.int32).pin_memory(), b.to(torch.int32).pin_memory()) for a, b in pool]
 
     if args.impl == "torch":
         step_fn, launches_fn, info = _torch_baseline(cfg, B, dev, world, pg)
+    elif tp_mode:
+        from predicitivecoding_b200.engine.tp_trainer import TensorParallelTrainer
+        tr = TensorParallelTrainer(cfg, B, S, device=dev, lr=3e-4, weight_decay=0.1, process_group=pg,
+                                   use_graph=not args.no_graph)
+        info = {"params": cfg.dense_parameter_formula() if hasattr(cfg, "dense_parameter_formula") else None,
+                "grad_sync": f"tp{world}: fused AG->GEMM / GEMM->RS over peer memory"}
+
+        def step_fn(tok, tgt, sync=True):
+            if sync:
+                return tr.step(tok, tgt)
+            tr.launch()
+            return None
+
+        def launches_fn():
+            return ops.launch_count()
     else:
         from predicitivecoding_b200.engine.fused_trainer import FusedDecoderTrainer
         tr = FusedDecoderTrainer(cfg, B, S, device=dev, lr=3e-4, weight_decay=0.1, process_group=pg,
@@ -166,7 +190,8 @@ def run_decoder_bench(args, dev, rank, world, pg):
         launched = tr.launches_per_step * args.steps
     dev_ms = _max_over_ranks(dev_ms, world, dev)
     ms_per_step = dev_ms / args.steps
-    tok_s = world * M * args.steps / (dev_ms / 1e3)
+    groups = 1 if tp_mode else world        # tensor-parallel ranks process one batch together
+    tok_s = groups * M * args.steps / (dev_ms / 1e3)
 
     # ---- end-to-end through the public API: host batch -> step() -> loss on the host
     ek = args.e2e_steps or args.steps
@@ -177,7 +202,7 @@ def run_decoder_bench(args, dev, rank, world, pg):
         last = step_fn(*pool[i % len(pool)])
     t1 = time.perf_counter()
     e2e_s = _max_over_ranks(t1 - t0, world, dev)
-    e2e_tok_s = world * M * ek / e2e_s
+    e2e_tok_s = groups * M * ek / e2e_s
 
     flops = 6.0 * 0  # filled below for our impl
     res = {
@@ -189,7 +214,7 @@ def run_decoder_bench(args, dev, rank, world, pg):
         "warmup": max(3, args.warmup),
         "ms_per_step": round(ms_per_step, 3),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if tp_mode else "weak",
         "vs_baseline": round(tok_s / REF_DECODER_TOKS, 2),
         "vs_baseline_basis": "closest published reference figure: Base preset (135M, ctx 1024) bf16 mixed, "
                              "2680 tok/s on one RTX 4070 SUPER (ROADMAP-Scale.md:69); BASELINE.md lists no "
@@ -197,7 +222,8 @@ def run_decoder_bench(args, dev, rank, world, pg):
         "dtype": "bf16",
         "data": "synthetic (seeded Zipf(1.1) token ids, random-init weights)",
         "impl": args.impl,
-        "config": {"model": name, "global_batch": B * world, "seq_len": S, "parallelism": f"dp{world}",
+        "config": {"model": name, "global_batch": B * groups, "seq_len": S,
+                   "parallelism": f"tp{world}" if tp_mode else f"dp{world}",
                    "micro_batch_per_gpu": B, "optimizer": "AdamW lr 3e-4 wd 0.1 (ZeRO-1 sharded states)",
                    "l2": "no flush needed: per-step working set (~3 GB of activations, 1 GB logits) >> 126 MB L2",
                    **info},
@@ -209,7 +235,7 @@ def run_decoder_bench(args, dev, rank, world, pg):
         "last_loss": last,
     }
     if args.impl != "torch":
-        f = tr.flops_per_step()
+        f = tr.flops_per_step() / (world if tp_mode else 1)
         res["model_tflops_per_gpu"] = round(f / (ms_per_step / 1e3) / 1e12, 1)
     return res
 
