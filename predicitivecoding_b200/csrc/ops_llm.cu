@@ -199,7 +199,7 @@ __global__ void ce_fwd_bwd_kernel(__nv_bfloat16* __restrict__ logits, long long 
   const int t = tgt[r];
   __shared__ float s_m[32], s_s[32];
   float mx = -INFINITY, sm = 0.f;
-  const int nvec = V / 8;  // V % 8 == 0 checked on host
+  const int nvec = V / 8;  // 16-byte vectors; the V % 8 tail is handled element-wise
   const uint4* rv = reinterpret_cast<const uint4*>(row);
   for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
     const uint4 u = rv[i];
@@ -214,6 +214,14 @@ __global__ void ce_fwd_bwd_kernel(__nv_bfloat16* __restrict__ logits, long long 
     }
 #pragma unroll
     for (int j = 0; j < 8; ++j) sm += __expf(f[j] - mx);
+  }
+  for (int j = 8 * nvec + threadIdx.x; j < V; j += blockDim.x) {
+    const float f = __bfloat162float(row[j]);
+    if (f > mx) {
+      sm = (mx == -INFINITY ? 0.f : sm * __expf(mx - f));
+      mx = f;
+    }
+    sm += __expf(f - mx);
   }
   // combine (max, sum) pairs across the block
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
@@ -267,6 +275,11 @@ __global__ void ce_fwd_bwd_kernel(__nv_bfloat16* __restrict__ logits, long long 
     o.z = pack_bf16x2(f[4], f[5]);
     o.w = pack_bf16x2(f[6], f[7]);
     wv[i] = o;
+  }
+  for (int j = 8 * nvec + threadIdx.x; j < V; j += blockDim.x) {
+    float p = counted ? __expf(__bfloat162float(row[j]) - lse) : 0.f;
+    if (counted && j == t) p -= 1.f;
+    row[j] = __float2bfloat16(p * scale);
   }
 }
 
@@ -419,7 +432,7 @@ int pcb_rope(void* buf, long long ld, const float* cs, int M, int S, int D, int 
 
 int pcb_ce(void* logits, long long ld, const int* tgt, float* loss, int M, int V, float scale, int write_grad,
            cudaStream_t s) {
-  if (V % 8 || ld % 8) return -1;
+  if (ld % 8) return -1;
   ce_fwd_bwd_kernel<<<M, 512, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(logits), ld, tgt, loss, M, V, scale,
                                        write_grad);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;

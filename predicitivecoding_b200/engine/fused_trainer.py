@@ -40,8 +40,7 @@ def supports(cfg: DecoderLmConfig, seq: Optional[int] = None) -> bool:
     s = seq or cfg.max_seq
     return (cfg.use_rms_norm and cfg.use_rope and cfg.block_pattern is None and cfg.num_experts == 0
             and cfg.num_loops == 1 and cfg.mtp_weight == 0 and not cfg.use_plan and cfg.dropout == 0
-            and cfg.head_dim in (64, 128) and s % 128 == 0 and cfg.dim % 64 == 0 and cfg.ff_dim % 64 == 0
-            and cfg.vocab % 8 == 0)
+            and cfg.head_dim in (64, 128) and s % 128 == 0 and cfg.dim % 64 == 0 and cfg.ff_dim % 64 == 0)
 
 
 def _interleave_gate_up(gate_t: torch.Tensor, up_t: torch.Tensor) -> torch.Tensor:
@@ -95,7 +94,11 @@ class FusedDecoderTrainer:
         self.peer = None
 
         # ---------------- parameters
-        D, F_, V, L = cfg.dim, cfg.ff_dim, cfg.vocab, cfg.num_blocks
+        D, F_, L = cfg.dim, cfg.ff_dim, cfg.num_blocks
+        # vocabulary rows padded to a multiple of 8 (16-byte TMA strides); the padded rows stay zero
+        # and the cross-entropy only sees the real columns
+        self.Vr = cfg.vocab
+        V = self.Vp = (cfg.vocab + 7) // 8 * 8
         specs = [ParamSpec("wemb", (V, D))]
         for l in range(L):
             specs.append(ParamSpec(f"b{l}.wqkv", (3 * D, D)))
@@ -185,28 +188,32 @@ class FusedDecoderTrainer:
         self.launches_per_step = None
 
     # ------------------------------------------------------------------ weights in/out
-    @torch.no_grad()
-    def import_model(self, model: DecoderLM) -> None:
-        """Copy a DecoderLM's weights (reference [in,out] layout) into the arena."""
+    def _model_to_flat(self, model: DecoderLM) -> torch.Tensor:
+        """DecoderLM tensors (reference [in,out] layout) -> flat fp32 arena (cpu)."""
         cfg = self.cfg
         full = torch.zeros(self.arena.total, dtype=torch.float32)
         V = self.arena.views(full)
-        V["wemb"].copy_(model.wemb.detach().float().cpu())
+        V["wemb"][:self.Vr].copy_(model.wemb.detach().float().cpu())
         for l, blk in enumerate(model.blocks):
-            V[f"b{l}.wqkv"].copy_(torch.cat([blk.wq.T, blk.wk.T, blk.wv.T], 0).cpu())
-            V[f"b{l}.wo"].copy_(blk.wo.T.cpu())
-            V[f"b{l}.ln1"].copy_(blk.ln1_g.cpu())
-            V[f"b{l}.ln2"].copy_(blk.ln2_g.cpu())
+            V[f"b{l}.wqkv"].copy_(torch.cat([blk.wq.T, blk.wk.T, blk.wv.T], 0).detach().cpu())
+            V[f"b{l}.wo"].copy_(blk.wo.detach().T.cpu())
+            V[f"b{l}.ln1"].copy_(blk.ln1_g.detach().cpu())
+            V[f"b{l}.ln2"].copy_(blk.ln2_g.detach().cpu())
             if cfg.ffn == "swiglu":
-                V[f"b{l}.w13"].copy_(_interleave_gate_up(blk.w1.T.cpu(), blk.w3.T.cpu()))
+                V[f"b{l}.w13"].copy_(_interleave_gate_up(blk.w1.detach().T.cpu(), blk.w3.detach().T.cpu()))
             else:
-                V[f"b{l}.w1"].copy_(blk.w1.T.cpu())
-                V[f"b{l}.b1"].copy_(blk.b1.cpu())
-                V[f"b{l}.b2"].copy_(blk.b2.cpu())
-            V[f"b{l}.w2"].copy_(blk.w2.T.cpu())
-        V["lnf"].copy_(model.lnf_g.cpu())
-        V["wout"].copy_(model.wout.T.cpu())
-        full_d = full.to(self.device)
+                V[f"b{l}.w1"].copy_(blk.w1.detach().T.cpu())
+                V[f"b{l}.b1"].copy_(blk.b1.detach().cpu())
+                V[f"b{l}.b2"].copy_(blk.b2.detach().cpu())
+            V[f"b{l}.w2"].copy_(blk.w2.detach().T.cpu())
+        V["lnf"].copy_(model.lnf_g.detach().cpu())
+        V["wout"][:self.Vr].copy_(model.wout.detach().T.cpu())
+        return full
+
+    @torch.no_grad()
+    def import_model(self, model: DecoderLM) -> None:
+        """Copy a DecoderLM's weights (reference [in,out] layout) into the arena."""
+        full_d = self._model_to_flat(model).to(self.device)
         self.w32.copy_(full_d[self.shard_lo:self.shard_hi])
         self.w16.copy_(full_d.to(torch.bfloat16))
         self.m.zero_()
@@ -224,13 +231,10 @@ class FusedDecoderTrainer:
         return out
 
     @torch.no_grad()
-    def export_model(self, model: Optional[DecoderLM] = None) -> DecoderLM:
-        """Write the fp32 master weights back into a DecoderLM (reference layout)."""
+    def _flat_to_model(self, flat: torch.Tensor, model: DecoderLM) -> DecoderLM:
         cfg = self.cfg
-        if model is None:
-            model = DecoderLM(cfg)
-        V = self.arena.views(self.master_weights().cpu())
-        model.wemb.copy_(V["wemb"])
+        V = self.arena.views(flat.cpu())
+        model.wemb.copy_(V["wemb"][:self.Vr])
         D = cfg.dim
         for l, blk in enumerate(model.blocks):
             wqkv = V[f"b{l}.wqkv"]
@@ -250,8 +254,46 @@ class FusedDecoderTrainer:
                 blk.b2.copy_(V[f"b{l}.b2"])
             blk.w2.copy_(V[f"b{l}.w2"].T)
         model.lnf_g.copy_(V["lnf"])
-        model.wout.copy_(V["wout"].T)
+        model.wout.copy_(V["wout"][:self.Vr].T)
         return model
+
+    @torch.no_grad()
+    def export_model(self, model: Optional[DecoderLM] = None) -> DecoderLM:
+        """Write the fp32 master weights back into a DecoderLM (reference layout)."""
+        return self._flat_to_model(self.master_weights(), model if model is not None else DecoderLM(self.cfg))
+
+    def _gather_full(self, shard: torch.Tensor) -> torch.Tensor:
+        if self.world == 1:
+            return shard.clone()
+        import torch.distributed as dist
+        out = torch.empty(self.arena.total, device=self.device, dtype=torch.float32)
+        dist.all_gather_into_tensor(out, shard, group=self.pg)
+        return out
+
+    @torch.no_grad()
+    def save_state(self, path: str) -> None:
+        """Adam moments and step count in the device-trainer state file (DAM1), tensors in the
+        reference Parameters() order and layout (DeviceDecoderTrainer.SaveState)."""
+        from ..io.checkpoint import save_dam1
+        moms = []
+        for buf in (self._gather_full(self.m), self._gather_full(self.v)):
+            moms.append([t.detach().reshape(-1).numpy().copy() for t in
+                         self._flat_to_model(buf, DecoderLM(self.cfg)).reference_parameters()])
+        if self.rank == 0:
+            save_dam1(path, self.t, list(zip(moms[0], moms[1])))
+
+    @torch.no_grad()
+    def load_state(self, path: str) -> None:
+        from ..io.checkpoint import load_dam1
+        ref = DecoderLM(self.cfg)
+        counts = [p.numel() for p in ref.reference_parameters()]
+        t, moms = load_dam1(path, counts)
+        for k, buf in ((0, self.m), (1, self.v)):
+            tensors = [torch.from_numpy(mv[k].copy()).view_as(p) for mv, p in zip(moms, ref.reference_parameters())]
+            ref.load_reference_parameters([x.numpy() for x in tensors])
+            full = self._model_to_flat(ref).to(self.device)
+            buf.copy_(full[self.shard_lo:self.shard_hi])
+        self.t = int(t)
 
     # ------------------------------------------------------------------ the step
     def _forward(self, write_grad: bool = True) -> None:
@@ -277,7 +319,7 @@ class FusedDecoderTrainer:
         L = cfg.num_blocks
         ops.rmsnorm_fwd(self.x[L], W["lnf"], self.nf, self.invf, cfg.eps)
         ops.gemm(self.nf, W["wout"], epi=ops.EPI_BF16, c=self.logits)
-        ops.cross_entropy(self.logits, self.tgt, self.loss_rows, 1.0 / M, write_grad)
+        ops.cross_entropy(self.logits[:, :self.Vr], self.tgt, self.loss_rows, 1.0 / M, write_grad)
         self.loss_sum.zero_()
         ops.sumsq(self.loss_rows, self.loss_sum, square=False)
 

@@ -115,3 +115,34 @@ def test_import_export_roundtrip_and_eval_is_pure():
     l2 = tr.evaluate_loss(tok, tgt)
     assert l1 == l2
     assert torch.equal(before, tr.w32)
+
+
+def test_device_state_roundtrip_and_gpu_pretrainer(tmp_path):
+    from predicitivecoding_b200.engine.fused_trainer import FusedDecoderTrainer
+    from predicitivecoding_b200.engine.pretrainer import DevicePretrainOptions, pretrain
+    from predicitivecoding_b200.llm.data import CorpusSource
+    from predicitivecoding_b200.llm.facade import PredictiveLlm
+    from predicitivecoding_b200.llm.tokenizer import ByteTokenizer
+    from predicitivecoding_b200.models.config import DecoderLmConfig
+    cfg = DecoderLmConfig(260, 128, 2, 2, 256, 128, use_rms_norm=True, use_rope=True, ffn="swiglu")
+    tr = FusedDecoderTrainer(cfg, 2, 128, device="cuda", use_graph=False)
+    g = torch.Generator().manual_seed(0)
+    for _ in range(2):
+        t = torch.randint(0, 260, (2, 129), generator=g)
+        tr.step(t[:, :-1], t[:, 1:])
+    p = str(tmp_path / "adam-device.bin")
+    tr.save_state(p)
+    tr2 = FusedDecoderTrainer(cfg, 2, 128, device="cuda", use_graph=False)
+    tr2.load_state(p)
+    assert tr2.t == tr.t == 2
+    assert torch.allclose(tr2.m, tr.m) and torch.allclose(tr2.v, tr.v)
+    llm = PredictiveLlm(cfg, ByteTokenizer())
+    llm.to("cuda")
+    text = "\n".join(f"sample line number {i}: the quick brown fox jumps over the lazy dog again and again." * 2
+                     for i in range(80))
+    rep = pretrain(llm, CorpusSource.from_text(text),
+                   DevicePretrainOptions(seq_len=128, stride=128, micro_batch_windows=2, max_steps=6, warmup_steps=1,
+                                         peak_lr=1e-3, eval_every_steps=3, eval_windows=4,
+                                         checkpoint_dir=str(tmp_path / "ck"), checkpoint_every_steps=3))
+    assert rep.steps == 6 and rep.final_eval_loss < 6.0
+    assert (tmp_path / "ck" / "adam-device.bin").exists()

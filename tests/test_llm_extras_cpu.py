@@ -1,6 +1,7 @@
 """GPT family, tiny LM, quantisation, GEMM routing, memory budget, continual learning,
 translation and summarisation on the CPU."""
 import math
+import os
 import tempfile
 
 import pytest
@@ -185,3 +186,23 @@ def test_summarizer_methods(method):
     assert text.index(sents[0]) < text.index(sents[1])           # reading order
     assert "stock market" not in out
     assert ExtractiveSummarizer().summarize("One sentence only") == "One sentence only"
+
+
+def test_device_pretrainer_cpu_path(tmp_path):
+    from predicitivecoding_b200.engine.pretrainer import DevicePretrainOptions, lr_at, pretrain
+    from predicitivecoding_b200.llm.data import CorpusSource
+    llm = PredictiveLlm.create_pc(dim=32, blocks=1, heads=2, ff_dim=64, max_seq=64)
+    text = "\n".join(f"line {i} the cat sat on the mat and looked at the dog {i % 7}." for i in range(60))
+    seen = []
+    o = DevicePretrainOptions(seq_len=16, stride=16, micro_batch_windows=2, peak_lr=3e-3, min_lr=3e-4,
+                              warmup_steps=2, max_steps=12, eval_every_steps=4, eval_windows=4, held_out_every=5,
+                              quality_every_steps=6, sample_tokens=4, checkpoint_dir=str(tmp_path / "ck"),
+                              checkpoint_every_steps=6, log_path=str(tmp_path / "log.jsonl"),
+                              on_progress=seen.append)
+    rep = pretrain(llm, CorpusSource.from_text(text), o)
+    assert rep.steps == 12 and rep.tokens == 12 * 2 * 16 and len(seen) == 12
+    assert math.isfinite(rep.final_eval_loss) and rep.best_eval_loss <= rep.final_eval_loss + 1.0
+    assert seen[5].sample is not None and seen[5].bits_per_byte is not None
+    assert len(open(tmp_path / "log.jsonl").read().splitlines()) == 12
+    assert os.path.isdir(tmp_path / "ck" / "best")
+    assert lr_at(1, 100, o) == pytest.approx(1.5e-3) and lr_at(100, 100, o) == pytest.approx(3e-4)
