@@ -53,6 +53,8 @@ int pcb_coll_gather(const void* const* src_peers, void* out, long long chunk, lo
 int pcb_tp_reduce_norm(const void* slots, int world, int rows, int D, const float* resid, float* x_out,
                        int accumulate, const void* gamma, void* y, long long ldy, float* inv, float eps,
                        cudaStream_t s);
+int pcb_attn_fwd_tc(const void* qkv, long long ld, void* out, long long ld_o, float* lse, int B, int S, int H,
+                    int HD, float scale, int* err, cudaStream_t s);
 int pcb_alloc(int device, size_t bytes, void* stream, void** out);
 int pcb_free(void* ptr);
 int pcb_record_stream(void* ptr, void* stream);
@@ -539,6 +541,19 @@ void tp_reduce_norm(const at::Tensor& slots, int64_t world, const c10::optional<
         "tp_reduce_norm");
 }
 
+
+// tcgen05 flash-attention forward (same contract as attn_fwd)
+void attn_fwd_tc(const at::Tensor& qkv, at::Tensor& out, at::Tensor& lse, int64_t B, int64_t S, int64_t H, int64_t HD,
+                 double scale, const c10::optional<at::Tensor>& err) {
+  req(qkv, at::kBFloat16, "qkv");
+  req(out, at::kBFloat16, "out");
+  reqc(lse, at::kFloat, "lse");
+  check(pcb_attn_fwd_tc(qkv.data_ptr(), row_stride(qkv, "qkv"), out.data_ptr(), row_stride(out, "out"),
+                        lse.data_ptr<float>(), B, S, H, HD, (float)scale, err ? err->data_ptr<int>() : nullptr,
+                        cur_stream()),
+        "attn_fwd_tc");
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -556,6 +571,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw", &adamw);
   m.def("f32_to_bf16", &f32_to_bf16);
   m.def("attn_fwd", &attn_fwd);
+  m.def("attn_fwd_tc", &attn_fwd_tc);
   m.def("attn_bwd", &attn_bwd);
   m.def("launch_count", &launch_count);
   m.def("set_gemm_mode", [](int64_t m) { pcb_set_gemm_mode((int)m); },

@@ -8,6 +8,7 @@ cannot be imported, so no GPU code path silently falls back to PyTorch.
 from __future__ import annotations
 
 import importlib
+import os
 from typing import Optional, Sequence
 
 import torch
@@ -140,8 +141,15 @@ def f32_to_bf16(x, y):
     ext().f32_to_bf16(x, y)
 
 
-def attn_fwd(qkv, out, lse, B, S, H, HD, scale):
-    ext().attn_fwd(qkv, out, lse, int(B), int(S), int(H), int(HD), float(scale))
+_ATTN_IMPL = os.environ.get("PCB_ATTN", "mma")    # "mma" (mma.sync kernel, faster today) or "tc" (tcgen05)
+
+
+def attn_fwd(qkv, out, lse, B, S, H, HD, scale, impl: Optional[str] = None):
+    """Causal attention forward; lse [B*H, S] = logsumexp of the scaled scores (for the backward)."""
+    if (impl or _ATTN_IMPL) == "tc":
+        ext().attn_fwd_tc(qkv, out, lse, int(B), int(S), int(H), int(HD), float(scale), None)
+    else:
+        ext().attn_fwd(qkv, out, lse, int(B), int(S), int(H), int(HD), float(scale))
 
 
 def attn_bwd(qkv, out, dout, lse, dvec, dq_acc, dqkv, B, S, H, HD, scale, rope_cs=None):

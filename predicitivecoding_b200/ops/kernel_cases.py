@@ -15,7 +15,7 @@ import torch
 
 from . import ext, gemm, gemm_pc, attn_fwd, attn_bwd, EPI_SWIGLU, EPI_RED_F32, EPI_PC_PRED, EPI_PC_STATE
 
-CASES = ("gemm_swiglu", "gemm_dw", "pc_pred", "pc_state", "attn_fwd", "attn_bwd")
+CASES = ("gemm_swiglu", "gemm_dw", "pc_pred", "pc_state", "attn_fwd", "attn_fwd_mma", "attn_bwd")
 
 
 def build(which: str, dev: str = "cuda"):
@@ -51,7 +51,7 @@ def build(which: str, dev: str = "cuda"):
             mu16 = torch.empty(B, S, device=dev, dtype=bf)
             fn = lambda: gemm_pc(d, w, b_mn=True, epi=EPI_PC_STATE, c=mu, d=mu16, aux=e, eta=0.1)
         return fn, 2 * B * S * S
-    if which in ("attn_fwd", "attn_bwd"):  # causal attention, 8 x 1024 tokens, 12 heads of 64
+    if which in ("attn_fwd", "attn_fwd_mma", "attn_bwd"):  # causal attention, 8 x 1024 tokens, 12 heads of 64
         B, S, H, hd = 8, 1024, 12, 64
         D = H * hd
         qkv = rn(B * S, 3 * D).to(bf)
@@ -59,8 +59,9 @@ def build(which: str, dev: str = "cuda"):
         lse = torch.empty(B * H, S, device=dev)
         causal_mm = B * H * S * S * hd          # one causal S x S x hd matmul = 2 * (S^2 / 2) * hd per head
         attn_fwd(qkv, o, lse, B, S, H, hd, 0.125)
-        if which == "attn_fwd":
-            return (lambda: attn_fwd(qkv, o, lse, B, S, H, hd, 0.125)), 2 * causal_mm
+        if which in ("attn_fwd", "attn_fwd_mma"):
+            impl = "mma" if which == "attn_fwd_mma" else "tc"
+            return (lambda: attn_fwd(qkv, o, lse, B, S, H, hd, 0.125, impl=impl)), 2 * causal_mm
         do = rn(B * S, D).to(bf)
         dq = torch.empty(B * S, D, device=dev)
         dv = torch.empty(B * H, S, device=dev)

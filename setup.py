@@ -32,6 +32,7 @@ setup(
                 os.path.join(CSRC, "gemm2_tcgen05.cu"),
                 os.path.join(CSRC, "ops_llm.cu"),
                 os.path.join(CSRC, "attention.cu"),
+                os.path.join(CSRC, "attention_tc.cu"),
                 os.path.join(CSRC, "peer.cu"),
                 os.path.join(CSRC, "decode.cu"),
                 os.path.join(CSRC, "collectives.cu"),

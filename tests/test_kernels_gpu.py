@@ -233,15 +233,16 @@ def test_adamw_matches_reference_order():
     assert rel_err(w16, wr) < 0.01
 
 
+@pytest.mark.parametrize("impl", ["tc", "mma"])
 @pytest.mark.parametrize("hd", [64, 128])
-def test_attention_fwd_bwd(hd):
+def test_attention_fwd_bwd(hd, impl):
     B, S, H = 2, 256, 2
     D = H * hd
     qkv = (torch.randn(B * S, 3 * D, device=DEV)).to(torch.bfloat16)
     out = torch.empty(B * S, D, device=DEV, dtype=torch.bfloat16)
     lse = torch.empty(B * H, S, device=DEV)
     scale = 1 / math.sqrt(hd)
-    ops.attn_fwd(qkv, out, lse, B, S, H, hd, scale)
+    ops.attn_fwd(qkv, out, lse, B, S, H, hd, scale, impl=impl)
     q, k, v = (qkv.float()[:, i * D:(i + 1) * D].view(B, S, H, hd).transpose(1, 2).clone().requires_grad_()
                for i in range(3))
     s = (q @ k.transpose(-1, -2)) * scale
@@ -263,6 +264,28 @@ def test_attention_fwd_bwd(hd):
     for i, t in enumerate((q, k, v)):
         ref_g = t.grad.transpose(1, 2).reshape(B * S, D)
         assert rel_err(dqkv[:, i * D:(i + 1) * D], ref_g) < 0.03, ("qkv"[i], rel_err(dqkv[:, i * D:(i + 1) * D], ref_g))
+
+
+@pytest.mark.parametrize("hd", [64, 128])
+def test_attention_tc_long_sequence(hd):
+    """Many key tiles per query tile: exercises the 2-stage K/V ring, S/O double buffers, masking."""
+    B, S, H = 2, 1024, 3
+    D = H * hd
+    g = torch.Generator(device=DEV).manual_seed(hd)
+    qkv = (torch.randn(B * S, 3 * D, device=DEV, generator=g) * 1.5).to(torch.bfloat16)
+    out = torch.empty(B * S, D, device=DEV, dtype=torch.bfloat16)
+    lse = torch.empty(B * H, S, device=DEV)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    scale = 1 / math.sqrt(hd)
+    ops.ext().attn_fwd_tc(qkv, out, lse, B, S, H, hd, scale, err)
+    q, k, v = (qkv.float()[:, i * D:(i + 1) * D].view(B, S, H, hd).transpose(1, 2) for i in range(3))
+    s = (q @ k.transpose(-1, -2)) * scale
+    s = s.masked_fill(torch.ones(S, S, dtype=torch.bool, device=DEV).triu(1), float("-inf"))
+    ref = (torch.softmax(s, -1) @ v).transpose(1, 2).reshape(B * S, D)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert rel_err(out, ref) < 0.02
+    assert rel_err(lse.view(B, H, S), torch.logsumexp(s, -1)) < 1e-3
 
 
 def test_embed_fwd_bwd():
