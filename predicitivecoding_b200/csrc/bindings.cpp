@@ -10,6 +10,16 @@
 #include <pybind11/stl.h>
 
 #include <atomic>
+#include <stdexcept>
+
+// Argument and launch checks raise std::invalid_argument (pybind11 turns it into ValueError).
+// c10::Error is not thrown from this library: a c10::Error raised from this extension after CUDA
+// initialisation crashed the interpreter on the GPU hosts, while plain std exceptions go through
+// pybind11's own translator.
+#define PCB_CHECK(cond, ...)                                                    \
+  do {                                                                          \
+    if (!(cond)) throw std::invalid_argument(c10::str(__VA_ARGS__));            \
+  } while (0)
 
 #include "gemm_api.h"
 
@@ -88,25 +98,25 @@ cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
 
 void check(int rc, const char* what, int kernels = 1) {
   g_launches.fetch_add(kernels, std::memory_order_relaxed);
-  TORCH_CHECK(rc == 0, "pcb kernel '", what, "' failed with code ", rc, " (",
+  PCB_CHECK(rc == 0, "pcb kernel '", what, "' failed with code ", rc, " (",
               cudaGetErrorString(cudaGetLastError()), ")");
 }
 
 void req(const at::Tensor& t, at::ScalarType dt, const char* name) {
-  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
-  TORCH_CHECK(t.scalar_type() == dt, name, " has dtype ", t.scalar_type(), ", expected ", dt);
+  PCB_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  PCB_CHECK(t.scalar_type() == dt, name, " has dtype ", t.scalar_type(), ", expected ", dt);
 }
 
 // req + contiguous (for kernels that index flat)
 void reqc(const at::Tensor& t, at::ScalarType dt, const char* name) {
   req(t, dt, name);
-  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+  PCB_CHECK(t.is_contiguous(), name, " must be contiguous");
 }
 
 // row stride (elements) of a 2-D view whose inner dimension is contiguous
 long long row_stride(const at::Tensor& t, const char* name) {
-  TORCH_CHECK(t.dim() == 2, name, " must be 2-D");
-  TORCH_CHECK(t.stride(1) == 1, name, " must have a contiguous inner dimension");
+  PCB_CHECK(t.dim() == 2, name, " must be 2-D");
+  PCB_CHECK(t.stride(1) == 1, name, " must have a contiguous inner dimension");
   return t.stride(0);
 }
 
@@ -138,32 +148,32 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, int64_
   args.K = a_mn ? a.size(0) : a.size(1);
   args.N = b_mn ? b.size(1) : b.size(0);
   const int kb = b_mn ? b.size(0) : b.size(1);
-  TORCH_CHECK(kb == args.K, "gemm: K mismatch (", args.K, " vs ", kb, ")");
+  PCB_CHECK(kb == args.K, "gemm: K mismatch (", args.K, " vs ", kb, ")");
   args.alpha = static_cast<float>(alpha);
   if (c) { args.C = c->data_ptr(); args.ldc = row_stride(*c, "c"); }
   if (d) { args.D = d->data_ptr(); args.ldd = row_stride(*d, "d"); }
   if (aux) { args.aux = aux->data_ptr(); args.ldaux = row_stride(*aux, "aux"); }
   if (bias) {
-    TORCH_CHECK(bias->scalar_type() == at::kFloat || bias->scalar_type() == at::kBFloat16, "bias: fp32 or bf16");
+    PCB_CHECK(bias->scalar_type() == at::kFloat || bias->scalar_type() == at::kBFloat16, "bias: fp32 or bf16");
     args.bias = bias->data_ptr();
     args.bias_bf16 = bias->scalar_type() == at::kBFloat16 ? 1 : 0;
   }
   if (err) args.err = err->data_ptr<int>();
   if (rope_cs) {
     req(*rope_cs, at::kFloat, "rope_cs");
-    TORCH_CHECK(epi == pcb::EPI_BF16 && rope_hd % 2 == 0 && rope_S > 0, "gemm: rope needs EPI_BF16, even hd");
+    PCB_CHECK(epi == pcb::EPI_BF16 && rope_hd % 2 == 0 && rope_S > 0, "gemm: rope needs EPI_BF16, even hd");
     args.rope_cs = rope_cs->data_ptr<float>();
     args.rope_S = (int)rope_S;
     args.rope_hd = (int)rope_hd;
     args.rope_cols = (int)rope_cols;
   }
-  if (epi == pcb::EPI_SWIGLU) TORCH_CHECK(args.N % 128 == 0, "swiglu gemm needs N % 128 == 0");
-  if (epi == pcb::EPI_SWIGLU_BWD) TORCH_CHECK(args.N % 64 == 0, "swiglu bwd gemm needs N % 64 == 0");
+  if (epi == pcb::EPI_SWIGLU) PCB_CHECK(args.N % 128 == 0, "swiglu gemm needs N % 128 == 0");
+  if (epi == pcb::EPI_SWIGLU_BWD) PCB_CHECK(args.N % 64 == 0, "swiglu bwd gemm needs N % 64 == 0");
   if (tp) {
     // tensor-parallel fusion: [ag_peers table, ag_ready counters, ag_rows, ag_rank, ag_world,
     //                          rs_peers table, rs_rows, rs_rank] (device addresses as integers)
     const auto& v = *tp;
-    TORCH_CHECK(v.size() == 8, "gemm: tp must have 8 entries");
+    PCB_CHECK(v.size() == 8, "gemm: tp must have 8 entries");
     args.ag_peers = reinterpret_cast<const void* const*>(v[0]);
     args.ag_ready = reinterpret_cast<unsigned int*>(v[1]);
     args.ag_rows = (int)v[2];
@@ -175,7 +185,7 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, int64_
     args.rs_rank = (int)v[7];
   }
   if (epi == pcb::EPI_RS_BF16) {
-    TORCH_CHECK(args.rs_peers != nullptr, "EPI_RS_BF16 needs the tp slot table");
+    PCB_CHECK(args.rs_peers != nullptr, "EPI_RS_BF16 needs the tp slot table");
     if (!c) args.ldc = args.N;   // slot buffers are [world * rs_rows, N] row-major
   }
   const at::cuda::CUDAGuard guard(a.device());
@@ -199,7 +209,7 @@ void gemm_pc(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, int
   args.K = a_mn ? a.size(0) : a.size(1);
   args.N = b_mn ? b.size(1) : b.size(0);
   const int kb = b_mn ? b.size(0) : b.size(1);
-  TORCH_CHECK(kb == args.K, "gemm_pc: K mismatch");
+  PCB_CHECK(kb == args.K, "gemm_pc: K mismatch");
   args.alpha = static_cast<float>(alpha);
   if (c) { args.C = c->data_ptr(); args.ldc = row_stride(*c, "c"); }
   if (d) { args.D = d->data_ptr(); args.ldd = row_stride(*d, "d"); }
@@ -245,7 +255,7 @@ void rmsnorm_fwd(const at::Tensor& x, const at::Tensor& g, at::Tensor& y, const 
   req(x, at::kFloat, "x");
   req(g, at::kBFloat16, "g");
   req(y, at::kBFloat16, "y");
-  TORCH_CHECK(x.is_contiguous() && y.is_contiguous(), "rmsnorm_fwd: contiguous tensors required");
+  PCB_CHECK(x.is_contiguous() && y.is_contiguous(), "rmsnorm_fwd: contiguous tensors required");
   const int D = x.size(-1);
   const int M = x.numel() / D;
   check(pcb_rmsnorm_fwd(x.data_ptr<float>(), g.data_ptr(), y.data_ptr(),
@@ -289,11 +299,11 @@ void sumsq(const at::Tensor& x, at::Tensor& out, bool square) {
   check(pcb_sumsq(x.data_ptr<float>(), x.numel(), out.data_ptr<float>(), square ? 1 : 0, cur_stream()), "sumsq");
 }
 void colsum(const at::Tensor& x, at::Tensor& out, double scale) {
-  TORCH_CHECK(x.is_cuda(), "x must be CUDA");
+  PCB_CHECK(x.is_cuda(), "x must be CUDA");
   req(out, at::kFloat, "out");
   const long long ld = row_stride(x, "x");
   const bool bf = x.scalar_type() == at::kBFloat16;
-  TORCH_CHECK(bf || x.scalar_type() == at::kFloat, "colsum: bf16 or fp32 input");
+  PCB_CHECK(bf || x.scalar_type() == at::kFloat, "colsum: bf16 or fp32 input");
   check(pcb_colsum(x.data_ptr(), bf ? 1 : 0, ld, out.data_ptr<float>(), x.size(0), x.size(1), (float)scale,
                    cur_stream()),
         "colsum");
@@ -308,7 +318,7 @@ void adamw(at::Tensor& w, const at::Tensor& g, at::Tensor& m, at::Tensor& v, con
   req(v, at::kFloat, "v");
   if (w16) req(*w16, at::kBFloat16, "w16");
   req(hyper, at::kFloat, "hyper");
-  TORCH_CHECK(hyper.numel() >= 5, "adamw: hyper needs 5 values");
+  PCB_CHECK(hyper.numel() >= 5, "adamw: hyper needs 5 values");
   check(pcb_adamw(w.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
                   ptr_or_null(w16), w.numel(), n_decay, hyper.data_ptr<float>(), (float)b1, (float)b2, (float)eps,
                   clip_sumsq ? clip_sumsq->data_ptr<float>() : nullptr, (float)max_norm, cur_stream()),
@@ -317,7 +327,7 @@ void adamw(at::Tensor& w, const at::Tensor& g, at::Tensor& m, at::Tensor& v, con
 void f32_to_bf16(const at::Tensor& x, at::Tensor& y) {
   req(x, at::kFloat, "x");
   req(y, at::kBFloat16, "y");
-  TORCH_CHECK(x.numel() == y.numel(), "f32_to_bf16: size mismatch");
+  PCB_CHECK(x.numel() == y.numel(), "f32_to_bf16: size mismatch");
   check(pcb_f32_to_bf16(x.data_ptr<float>(), y.data_ptr(), x.numel(), cur_stream()), "f32_to_bf16");
 }
 void attn_fwd(const at::Tensor& qkv, at::Tensor& out, at::Tensor& lse, int64_t B, int64_t S, int64_t H, int64_t HD,
@@ -336,7 +346,7 @@ void attn_bwd(const at::Tensor& qkv, const at::Tensor& out, const at::Tensor& do
   req(dout, at::kBFloat16, "dout");
   req(dqkv, at::kBFloat16, "dqkv");
   req(dq_acc, at::kFloat, "dq_acc");
-  TORCH_CHECK(row_stride(out, "out") == row_stride(dout, "dout"), "attn_bwd: out/dout strides differ");
+  PCB_CHECK(row_stride(out, "out") == row_stride(dout, "dout"), "attn_bwd: out/dout strides differ");
   if (rope_cs) req(*rope_cs, at::kFloat, "rope_cs");
   check(pcb_attn_bwd_rope(qkv.data_ptr(), row_stride(qkv, "qkv"), out.data_ptr(), dout.data_ptr(),
                           row_stride(dout, "dout"), lse.data_ptr<float>(), dvec.data_ptr<float>(),
@@ -352,26 +362,26 @@ int64_t launch_count() { return g_launches.load(); }
 at::Tensor peer_alloc(int64_t bytes, int64_t device) {
   const c10::cuda::CUDAGuard guard((c10::DeviceIndex)device);
   void* p = nullptr;
-  TORCH_CHECK(pcb_peer_alloc((size_t)bytes, &p) == 0, "peer_alloc: cudaMalloc failed");
+  PCB_CHECK(pcb_peer_alloc((size_t)bytes, &p) == 0, "peer_alloc: cudaMalloc failed");
   auto opts = at::TensorOptions().dtype(at::kByte).device(at::kCUDA, device);
   return torch::from_blob(p, {bytes}, [](void* q) { pcb_peer_free(q); }, opts);
 }
 py::bytes ipc_handle(const at::Tensor& t) {
   char buf[64];
-  TORCH_CHECK(pcb_ipc_handle(t.data_ptr(), buf) == 0, "ipc_handle: cudaIpcGetMemHandle failed");
+  PCB_CHECK(pcb_ipc_handle(t.data_ptr(), buf) == 0, "ipc_handle: cudaIpcGetMemHandle failed");
   return py::bytes(buf, 64);
 }
 int64_t ipc_open(py::bytes h) {
   std::string s = h;
-  TORCH_CHECK(s.size() == 64, "ipc_open: handle must be 64 bytes");
+  PCB_CHECK(s.size() == 64, "ipc_open: handle must be 64 bytes");
   void* p = nullptr;
-  TORCH_CHECK(pcb_ipc_open(s.data(), &p) == 0, "ipc_open: cudaIpcOpenMemHandle failed");
+  PCB_CHECK(pcb_ipc_open(s.data(), &p) == 0, "ipc_open: cudaIpcOpenMemHandle failed");
   return reinterpret_cast<int64_t>(p);
 }
 void ipc_close(int64_t p) { pcb_ipc_close(reinterpret_cast<void*>(p)); }
 
 void* const* ptr_table(const at::Tensor& t, int world, const char* name) {
-  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kLong && t.numel() >= world, name,
+  PCB_CHECK(t.is_cuda() && t.scalar_type() == at::kLong && t.numel() >= world, name,
               ": device int64 pointer table of size >= world required");
   return reinterpret_cast<void* const*>(t.data_ptr<int64_t>());
 }
@@ -386,7 +396,7 @@ void rs_adamw_ag(const at::Tensor& grad_ptrs, const at::Tensor& w16_ptrs, at::Te
                  int64_t lo, int64_t hi, int64_t n_decay, const at::Tensor& hyper, double b1, double b2, double eps,
                  int64_t world) {
   req(w32, at::kFloat, "w32");
-  TORCH_CHECK(w32.numel() >= hi - lo && m.numel() >= hi - lo && v.numel() >= hi - lo, "rs_adamw_ag: state too small");
+  PCB_CHECK(w32.numel() >= hi - lo && m.numel() >= hi - lo && v.numel() >= hi - lo, "rs_adamw_ag: state too small");
   check(pcb_rs_adamw_ag(ptr_table(grad_ptrs, world, "grad_ptrs"), ptr_table(w16_ptrs, world, "w16_ptrs"),
                         w32.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), lo, hi, n_decay,
                         hyper.data_ptr<float>(), (float)b1, (float)b2, (float)eps, (int)world, num_sms(), cur_stream()),
@@ -417,10 +427,10 @@ void decode_attn(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& vc
   reqc(pacc, at::kFloat, "pacc");
   reqc(pml, at::kFloat, "pml");
   reqc(out, at::kBFloat16, "out");
-  TORCH_CHECK(q.dim() == 3 && kc.dim() == 4 && vc.sizes() == kc.sizes(), "decode_attn: q [B,H,hd], caches [B,Hkv,cap,hd]");
+  PCB_CHECK(q.dim() == 3 && kc.dim() == 4 && vc.sizes() == kc.sizes(), "decode_attn: q [B,H,hd], caches [B,Hkv,cap,hd]");
   const int64_t B = q.size(0), H = q.size(1), HD = q.size(2), Hkv = kc.size(1), cap = kc.size(2);
-  TORCH_CHECK(kc.size(0) == B && kc.size(3) == HD && lens.numel() == B, "decode_attn: shape mismatch");
-  TORCH_CHECK(pacc.numel() >= B * H * nsplit * HD && pml.numel() >= B * H * nsplit * 2, "decode_attn: scratch too small");
+  PCB_CHECK(kc.size(0) == B && kc.size(3) == HD && lens.numel() == B, "decode_attn: shape mismatch");
+  PCB_CHECK(pacc.numel() >= B * H * nsplit * HD && pml.numel() >= B * H * nsplit * 2, "decode_attn: scratch too small");
   check(pcb_decode_attn(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), lens.data_ptr<int>(), pacc.data_ptr<float>(),
                         pml.data_ptr<float>(), out.data_ptr(), B, H, Hkv, HD, cap, nsplit, (float)scale,
                         (float)softcap, cur_stream()),
@@ -430,9 +440,9 @@ void wq_gemv(const at::Tensor& x, const at::Tensor& w, const at::Tensor& scale, 
   reqc(x, at::kFloat, "x");
   reqc(scale, at::kFloat, "scale");
   reqc(y, at::kFloat, "y");
-  TORCH_CHECK(w.is_cuda() && w.is_contiguous() && w.element_size() == 1, "wq_gemv: w must be a contiguous byte tensor");
+  PCB_CHECK(w.is_cuda() && w.is_contiguous() && w.element_size() == 1, "wq_gemv: w must be a contiguous byte tensor");
   const int64_t NB = x.size(0), cols = x.size(1), rows = w.size(0);
-  TORCH_CHECK(w.size(1) == (bits == 8 ? cols : cols / 2) && y.size(0) == NB && y.size(1) == rows, "wq_gemv: shapes");
+  PCB_CHECK(w.size(1) == (bits == 8 ? cols : cols / 2) && y.size(0) == NB && y.size(1) == rows, "wq_gemv: shapes");
   check(pcb_wq_gemv(x.data_ptr<float>(), w.data_ptr(), scale.data_ptr<float>(), y.data_ptr<float>(), NB, rows, cols,
                     bits, cur_stream()),
         "wq_gemv");
@@ -456,7 +466,7 @@ void linear_scan(const at::Tensor& a, const at::Tensor& b, at::Tensor& s) {
   reqc(a, at::kFloat, "a");
   reqc(b, at::kFloat, "b");
   reqc(s, at::kFloat, "s");
-  TORCH_CHECK(a.dim() == 3 && a.sizes() == b.sizes() && s.sizes() == a.sizes(), "linear_scan: [B,T,D]");
+  PCB_CHECK(a.dim() == 3 && a.sizes() == b.sizes() && s.sizes() == a.sizes(), "linear_scan: [B,T,D]");
   check(pcb_linear_scan(a.data_ptr<float>(), b.data_ptr<float>(), s.data_ptr<float>(), a.size(0), a.size(1),
                         a.size(2), cur_stream()),
         "linear_scan");
@@ -476,20 +486,20 @@ void linear_scan_bwd(const at::Tensor& a, const at::Tensor& s, const at::Tensor&
 // ---------------------------------------------------------------- collectives over symmetric buffers
 int coll_dtype(const at::Tensor& t) {
   if (t.scalar_type() == at::kFloat) return 0;
-  TORCH_CHECK(t.scalar_type() == at::kBFloat16, "collectives support fp32 and bf16");
+  PCB_CHECK(t.scalar_type() == at::kBFloat16, "collectives support fp32 and bf16");
   return 1;
 }
 void coll_reduce(const at::Tensor& in_ptrs, at::Tensor& out, int64_t lo, int64_t hi, int64_t world, int64_t op,
                  double scale) {
   req(in_ptrs, at::kLong, "in_ptrs");
-  TORCH_CHECK(out.is_cuda() && out.is_contiguous() && out.numel() >= hi - lo, "coll_reduce: out too small");
+  PCB_CHECK(out.is_cuda() && out.is_contiguous() && out.numel() >= hi - lo, "coll_reduce: out too small");
   check(pcb_coll_reduce(reinterpret_cast<const void* const*>(in_ptrs.data_ptr<int64_t>()), out.data_ptr(), lo, hi,
                         world, op, (float)scale, coll_dtype(out), num_sms(), cur_stream()),
         "coll_reduce");
 }
 void coll_gather(const at::Tensor& src_ptrs, at::Tensor& out, int64_t chunk, int64_t src_stride, int64_t world) {
   req(src_ptrs, at::kLong, "src_ptrs");
-  TORCH_CHECK(out.is_cuda() && out.is_contiguous() && out.numel() >= chunk * world, "coll_gather: out too small");
+  PCB_CHECK(out.is_cuda() && out.is_contiguous() && out.numel() >= chunk * world, "coll_gather: out too small");
   check(pcb_coll_gather(reinterpret_cast<const void* const*>(src_ptrs.data_ptr<int64_t>()), out.data_ptr(), chunk,
                         src_stride, world, coll_dtype(out), num_sms(), cur_stream()),
         "coll_gather");
@@ -498,13 +508,13 @@ void coll_gather(const at::Tensor& src_ptrs, at::Tensor& out, int64_t chunk, int
 // ---------------------------------------------------------------- native runtime
 at::Tensor dev_alloc(int64_t bytes, int64_t device, int64_t stream) {
   void* p = nullptr;
-  TORCH_CHECK(pcb_alloc((int)device, (size_t)bytes, reinterpret_cast<void*>(stream), &p) == 0,
+  PCB_CHECK(pcb_alloc((int)device, (size_t)bytes, reinterpret_cast<void*>(stream), &p) == 0,
               "dev_alloc: out of device memory");
   auto opts = at::TensorOptions().dtype(at::kByte).device(at::kCUDA, device);
   return torch::from_blob(p, {bytes}, [](void* q) { pcb_free(q); }, opts);
 }
 void dev_record_stream(const at::Tensor& t, int64_t stream) {
-  TORCH_CHECK(pcb_record_stream(t.storage().data_ptr().get(), reinterpret_cast<void*>(stream)) == 0,
+  PCB_CHECK(pcb_record_stream(t.storage().data_ptr().get(), reinterpret_cast<void*>(stream)) == 0,
               "record_stream: tensor was not allocated by the runtime allocator");
 }
 std::vector<int64_t> dev_alloc_stats(int64_t device) {
@@ -514,7 +524,7 @@ std::vector<int64_t> dev_alloc_stats(int64_t device) {
 }
 int64_t dev_stream(int64_t device, int64_t index, bool high_priority, int64_t n) {
   void* s = nullptr;
-  TORCH_CHECK(pcb_stream((int)device, (int)index, high_priority ? 1 : 0, (int)n, &s) == 0, "stream creation failed");
+  PCB_CHECK(pcb_stream((int)device, (int)index, high_priority ? 1 : 0, (int)n, &s) == 0, "stream creation failed");
   return reinterpret_cast<int64_t>(s);
 }
 
@@ -526,11 +536,11 @@ void tp_reduce_norm(const at::Tensor& slots, int64_t world, const c10::optional<
   reqc(slots, at::kBFloat16, "slots");
   reqc(x_out, at::kFloat, "x_out");
   const int64_t rows = x_out.size(0), D = x_out.size(1);
-  TORCH_CHECK(slots.numel() >= world * rows * D, "tp_reduce_norm: slots too small");
+  PCB_CHECK(slots.numel() >= world * rows * D, "tp_reduce_norm: slots too small");
   if (resid) reqc(*resid, at::kFloat, "resid");
   long long ldy = 0;
   if (gamma) {
-    TORCH_CHECK(y.has_value() && inv.has_value(), "tp_reduce_norm: gamma needs y and inv");
+    PCB_CHECK(y.has_value() && inv.has_value(), "tp_reduce_norm: gamma needs y and inv");
     req(*y, at::kBFloat16, "y");
     ldy = row_stride(*y, "y");
   }
