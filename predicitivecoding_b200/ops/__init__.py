@@ -64,6 +64,19 @@ def launch_count() -> int:
 
 
 # --------------------------------------------------------------------------- GEMM
+def _check_gemm(a: torch.Tensor, b: torch.Tensor, a_mn: bool, b_mn: bool) -> None:
+    """Validate operands in Python, before the extension is entered (its own checks are a backstop)."""
+    for name, t in (("a", a), ("b", b)):
+        if not t.is_cuda or t.dtype != torch.bfloat16 or t.dim() != 2 or t.stride(1) != 1:
+            raise ValueError(f"gemm: {name} must be a 2-D bf16 CUDA tensor with a contiguous inner dimension")
+        if t.stride(0) % 8 or t.data_ptr() % 16:
+            raise ValueError(f"gemm: {name} rows must start on 16-byte boundaries (row stride % 8 == 0)")
+    K = a.shape[0] if a_mn else a.shape[1]
+    kb = b.shape[0] if b_mn else b.shape[1]
+    if K != kb:
+        raise ValueError(f"gemm: K mismatch ({K} vs {kb})")
+
+
 def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = False, epi: int = EPI_BF16,
          c: Optional[torch.Tensor] = None, d: Optional[torch.Tensor] = None, aux: Optional[torch.Tensor] = None,
          bias: Optional[torch.Tensor] = None, alpha: float = 1.0, bn: int = 0, splits: int = 0,
@@ -81,6 +94,7 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = F
     copies from ``ag_peers`` before using them (0 = no gather), and EPI_RS_BF16 stores row m into
     slot ``rs_rank`` of owner ``m // rs_rows``'s buffer from the ``rs_peers`` table.
     """
+    _check_gemm(a, b, a_mn, b_mn)
     if c is None and epi in (EPI_BF16, EPI_F32):
         M = a.shape[1] if a_mn else a.shape[0]
         N = b.shape[1] if b_mn else b.shape[0]
@@ -94,6 +108,7 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = F
 def gemm_pc(a, b, *, a_mn=False, b_mn=False, epi, c=None, d=None, aux=None, bias=None, alpha=1.0, act="tanh",
             pi=1.0, eta=0.1, actreg=0.0, decay=1.0, energy=None, pred_out=None, pred_bf16=None, err=None):
     """GEMM with a predictive-coding epilogue (prediction/error, state update or weight update)."""
+    _check_gemm(a, b, a_mn, b_mn)
     ext().gemm_pc(a, a_mn, b, b_mn, epi, c, d, aux, bias, float(alpha), ACT_CODES[act] if isinstance(act, str) else int(act),
                   float(pi), float(eta), float(actreg), float(decay), energy, pred_out, pred_bf16, err)
 
