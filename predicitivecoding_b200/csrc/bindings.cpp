@@ -65,6 +65,8 @@ int pcb_tp_reduce_norm(const void* slots, int world, int rows, int D, const floa
                        cudaStream_t s);
 int pcb_attn_fwd_tc(const void* qkv, long long ld, void* out, long long ld_o, float* lse, int B, int S, int H,
                     int HD, float scale, int* err, cudaStream_t s);
+int pcb_annotate(uint8_t* img, int W, int H, const int* boxes, int n, int thickness, const int* segs, int m,
+                 const uint8_t* colors, int* owner, cudaStream_t s);
 int pcb_alloc(int device, size_t bytes, void* stream, void** out);
 int pcb_free(void* ptr);
 int pcb_record_stream(void* ptr, void* stream);
@@ -564,6 +566,24 @@ void attn_fwd_tc(const at::Tensor& qkv, at::Tensor& out, at::Tensor& lse, int64_
         "attn_fwd_tc");
 }
 
+
+// box outlines + segments rasterised onto a device RGB image (annotation)
+void annotate(at::Tensor& img, const at::Tensor& boxes, int64_t thickness, const at::Tensor& segs,
+              const at::Tensor& colors, at::Tensor& owner) {
+  reqc(img, at::kByte, "img");
+  reqc(boxes, at::kInt, "boxes");
+  reqc(segs, at::kInt, "segs");
+  reqc(colors, at::kByte, "colors");
+  reqc(owner, at::kInt, "owner");
+  PCB_CHECK(img.dim() == 3 && img.size(2) == 3, "annotate: img must be [H, W, 3]");
+  const int64_t H = img.size(0), W = img.size(1);
+  const int64_t n = boxes.numel() / 4, m = segs.numel() / 4;
+  PCB_CHECK(owner.numel() >= H * W && colors.numel() >= 3 * (n + m), "annotate: scratch or colours too small");
+  check(pcb_annotate(img.data_ptr<uint8_t>(), (int)W, (int)H, boxes.data_ptr<int>(), (int)n, (int)thickness,
+                     segs.data_ptr<int>(), (int)m, colors.data_ptr<uint8_t>(), owner.data_ptr<int>(), cur_stream()),
+        "annotate", 3);
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -593,6 +613,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("linear_scan", &linear_scan);
   m.def("linear_scan_bwd", &linear_scan_bwd);
   m.def("tp_reduce_norm", &tp_reduce_norm);
+  m.def("annotate", &annotate);
   m.def("coll_reduce", &coll_reduce);
   m.def("coll_gather", &coll_gather);
   m.def("dev_alloc", &dev_alloc);

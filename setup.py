@@ -37,6 +37,7 @@ setup(
                 os.path.join(CSRC, "decode.cu"),
                 os.path.join(CSRC, "collectives.cu"),
                 os.path.join(CSRC, "tp.cu"),
+                os.path.join(CSRC, "vision.cu"),
                 os.path.join(CSRC, "runtime.cpp"),
             ],
             include_dirs=[os.path.join(HERE, CSRC)],

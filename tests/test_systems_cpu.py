@@ -1,0 +1,113 @@
+"""Imaging codecs and the people-counting stack on the CPU."""
+import numpy as np
+import pytest
+
+from predicitivecoding_b200.systems import imaging as im
+from predicitivecoding_b200.systems import vision as vi
+
+
+def _img():
+    rng = np.random.default_rng(0)
+    return im.RgbImage.from_pixel_data(rng.integers(0, 256, (7, 9, 3), dtype=np.uint8), 9, 7)
+
+
+def test_netpbm_ascii_binary_and_16bit():
+    p3 = b"P3\n# comment\n2 1\n255\n255 0 0  0 255 0\n"
+    a = im.RgbImage.load(p3)
+    assert a[0, 0] == (255, 0, 0) and a[1, 0] == (0, 255, 0)
+    p5 = b"P5 2 2 65535\n" + bytes([0xFF, 0xFF, 0, 0, 0x80, 0, 0x40, 0])
+    g = im.RgbImage.load(p5)
+    assert g[0, 0] == (255, 255, 255) and g[1, 0] == (0, 0, 0) and g[0, 1][0] == 0x8000 * 255 // 65535
+    with pytest.raises(ValueError):
+        im.decode_netpbm(b"P6 2 2 255\n" + b"\x00" * 5)
+
+
+def test_png_bmp_roundtrip_and_ops(tmp_path):
+    a = _img()
+    for ext in ("png", "bmp"):
+        p = str(tmp_path / f"x.{ext}")
+        getattr(a, f"save_as_{ext}")(p)
+        b = im.RgbImage.load(p)
+        assert np.array_equal(a.pixels, b.pixels)
+    c = a.crop(2, 1, 4, 3)
+    assert (c.width, c.height) == (4, 3) and c[0, 0] == a[2, 1]
+    r = a.resize(18, 14)
+    assert (r.width, r.height) == (18, 14)
+    gray = a.to_gray()
+    assert gray.shape == (7, 9) and gray.dtype == np.uint8
+
+
+def test_gif_exact_palette_and_quantised(tmp_path):
+    f1 = im.RgbImage(4, 3, im.Rgb24(10, 20, 30))
+    f2 = f1.clone()
+    f2[1, 1] = im.Rgb24(200, 100, 50)
+    data = im.encode_gif([f1, f2], 5)
+    assert data[:6] == b"GIF89a" and b"NETSCAPE2.0" in data and data[-1] == 0x3B
+    frames = im.decode_gif_indices(data)
+    assert len(frames) == 2 and len(frames[0]) == 12 and frames[1][1 * 4 + 1] != frames[1][0]
+    big = im.RgbImage.from_pixel_data(np.arange(300 * 3, dtype=np.uint32).astype(np.uint8).reshape(30, 10, 3) * 0
+                                      + np.random.default_rng(1).integers(0, 256, (30, 10, 3), dtype=np.uint8), 10, 30)
+    q = im.decode_gif_indices(im.encode_gif([big]))[0]
+    p = big.pixels.reshape(-1, 3).astype(int)
+    assert np.array_equal(q, (p[:, 0] & 0xE0) | ((p[:, 1] >> 3) & 0x1C) | (p[:, 2] >> 6))
+    with pytest.raises(ValueError):
+        im.encode_gif([f1, im.RgbImage(3, 3)])
+
+
+def test_nms_and_iou():
+    a = vi.Detection(0, 0, 10, 10, 0.9)
+    b = vi.Detection(1, 1, 11, 11, 0.8)
+    c = vi.Detection(20, 20, 30, 30, 0.7)
+    assert vi.iou(a, b) == pytest.approx(81 / 119)
+    assert vi.nms([c, b, a], 0.5) == [a, c]
+
+
+def test_sort_tracker_confirms_counts_and_expires():
+    tr = vi.SortTracker(iou_threshold=0.3, max_age=2, min_hits=3)
+    for f in range(5):
+        out = tr.update([vi.Detection(10 + 2 * f, 10, 30 + 2 * f, 50)])
+        assert len(out) == (1 if f >= 2 else 0)
+    assert tr.unique_count == 1 and tr.current_count == 1
+    for _ in range(4):
+        tr.update([])
+    assert tr.tracks == [] and tr.unique_count == 1
+
+
+def test_line_and_zone_counters_and_smoother():
+    lc = vi.LineCounter(0, 5, 10, 5)
+    lc.update([(1, 5, 2), (2, 5, 8)])
+    lc.update([(1, 5, 8), (2, 5, 2)])
+    assert (lc.inbound, lc.outbound, lc.net) == (1, 1, 0)
+    z = vi.ZoneCounter([(0, 0), (10, 0), (10, 10), (0, 10)])
+    z.update([(1, 5, 5), (2, 20, 5)])
+    z.update([(1, 6, 5)])
+    assert z.occupancy == 1 and z.entered == 1 and z.dwell_frames(1) == 2
+    sm = vi.CountSmoother(3)
+    assert [sm.add(v) for v in (5, 1, 9, 2)] == [5, 5, 5, 2]
+
+
+def test_reid_gallery_and_hog():
+    frame = im.RgbImage(20, 20, im.Rgb24(200, 10, 10))
+    emb = vi.ColorHistogramEmbedder(8, 0.6)
+    e1 = emb.embed(frame, vi.Detection(2, 2, 12, 12))
+    assert e1.shape == (24,) and abs(np.linalg.norm(e1) - 1) < 1e-6
+    g = vi.PersonGallery(0.9)
+    assert g.identify_or_register(e1) == 1 and g.identify_or_register(e1) == 1
+    other = im.RgbImage(20, 20, im.Rgb24(10, 10, 200))
+    assert g.identify_or_register(emb.embed(other, vi.Detection(2, 2, 12, 12))) == 2
+    hog = vi.HogDescriptor(16, 16, 8, 9)
+    x = np.tile(np.arange(16, dtype=np.float32), (16, 1))
+    f = hog.compute_gray(x)
+    assert f.shape == (hog.dimension,) == (36,) and f.max() > 0
+
+
+def test_counting_pipeline_and_cpu_annotation():
+    boxes = [vi.Detection(5, 5, 15, 25)]
+    pipe = vi.PeopleCountingPipeline(lambda fr: boxes, vi.SortTracker(min_hits=2), detect_every_n=2)
+    res = [pipe.process(im.RgbImage(32, 32)) for _ in range(4)]
+    assert [r.detected for r in res] == [True, False, True, False] and res[-1].current_count == 1
+    ann = vi.Annotator(2).draw_boxes(boxes).draw_line(0, 31, 31, 0).draw_zone([(2, 2), (29, 2), (29, 29)])
+    img = ann.render_cpu(im.RgbImage(32, 32))
+    assert img[5, 5] == vi.DET_COLOR or img[5, 5] in (vi.LINE_COLOR, vi.ZONE_COLOR)
+    assert img[10, 15] == (0, 0, 0)
+    assert (img.pixels != 0).any(axis=2).sum() > 100
