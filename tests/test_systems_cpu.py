@@ -111,3 +111,59 @@ def test_counting_pipeline_and_cpu_annotation():
     assert img[5, 5] == vi.DET_COLOR or img[5, 5] in (vi.LINE_COLOR, vi.ZONE_COLOR)
     assert img[10, 15] == (0, 0, 0)
     assert (img.pixels != 0).any(axis=2).sum() > 100
+
+
+# ---------------------------------------------------------------- Thousand Brains
+from predicitivecoding_b200.systems import brain as br
+
+
+def test_sdr_ops_and_encoders():
+    a, b = br.Sdr(10, [1, 3, 3, 5]), br.Sdr(10, [3, 5, 7])
+    assert a.bits == (1, 3, 5) and a.overlap(b) == 2 and a.union(b).bits == (1, 3, 5, 7)
+    assert a.intersect(b).bits == (3, 5) and abs(a.overlap_score(b) - 2 / 3) < 1e-6
+    with pytest.raises(ValueError):
+        br.Sdr(4, [4])
+    rng = np.random.default_rng(0)
+    r = br.Sdr.random(100, 10, rng)
+    n = r.add_noise(0.3, rng)
+    assert n.cardinality == 10 and r.overlap(n) == 7
+    se = br.ScalarEncoder(0, 1, 20, 5)
+    assert se.encode(0).bits == (0, 1, 2, 3, 4) and se.encode(1).bits[-1] == 19
+    assert se.encode(0.5).overlap(se.encode(0.55)) >= 4
+    pe = br.PoseEncoder(0, 10, 0, 10, 50, 5, 8, 3)
+    assert pe.encode(1, 2, 90).cardinality == 13 and pe.size == 124
+    pi = br.PathIntegrator()
+    pi.move(1.0)
+    pi.move(1.0, 90)
+    dx, dy = pi.displacement(0, 2)
+    assert abs(dx - 1) < 1e-9 and abs(dy - 1) < 1e-9
+
+
+def test_spatial_pooler_and_temporal_memory_learn_a_sequence():
+    sp = br.SpatialPooler(br.SpatialPoolerConfig(200, 256, 10, seed=1))
+    rng = np.random.default_rng(2)
+    x = br.Sdr.random(200, 20, rng)
+    out1 = sp.compute(x, True)
+    for _ in range(5):
+        sp.compute(x, True)
+    assert out1.cardinality == 10 and sp.compute(x, False).overlap(out1) >= 8
+    tm = br.TemporalMemory(br.TemporalMemoryConfig(64, 4, activation_threshold=3, min_threshold=2,
+                                                   max_new_synapse_count=8))
+    seq = [br.Sdr(64, range(i * 8, i * 8 + 5)) for i in range(4)]
+    anomalies = []
+    for rep in range(8):
+        tm.reset()
+        anomalies.append([tm.compute(s, True).anomaly for s in seq])
+    assert anomalies[0][1:] == [1.0, 1.0, 1.0] and max(anomalies[-1][1:]) == 0.0
+
+
+def test_multi_column_recognition():
+    data = br.SyntheticObjectDataset(n_objects=6, points=8, seed=3)
+    tbs = br.ThousandBrainsSystem(data.size, data.size, n_columns=3, columns=256)
+    rep = br.recognition_benchmark(tbs, data)
+    assert rep.n == 6 and rep.accuracy >= 0.8
+    cons = br.Consensus(0.5).compute([[1, 2], [2], [2, 3]])
+    assert cons.candidates == [2] and cons.reached
+    lv = br.LateralVoting(4, "ring")
+    assert lv.neighbors(0) == [1, 3]
+    assert br.k_winners([0.1, 0.9, 0.5, 0.9], 2) == [1, 3]
