@@ -167,3 +167,91 @@ def test_multi_column_recognition():
     lv = br.LateralVoting(4, "ring")
     assert lv.neighbors(0) == [1, 3]
     assert br.k_winners([0.1, 0.9, 0.5, 0.9], 2) == [1, 3]
+
+
+# ---------------------------------------------------------------- cortex
+import torch
+
+from predicitivecoding_b200.pc.network import NetworkConfig
+from predicitivecoding_b200.pc.networks import HierarchicalNetworkConfig, HopfieldNetworkConfig
+from predicitivecoding_b200.systems import cortex as cx
+
+
+def test_retinotopic_map_roundtrip_and_visual_cortex():
+    m = cx.RetinotopicMap(1, 8, 8, 4, 2)
+    img = torch.arange(64, dtype=torch.float32)
+    patches = m.extract(img)
+    assert len(patches) == 9 and torch.allclose(m.assemble(patches), img)
+    cfg = cx.VisualCortexConfig(1, 8, 8, 4, 4, NetworkConfig(layer_sizes=(16, 8, 4)),
+                                HierarchicalNetworkConfig([NetworkConfig(layer_sizes=(16, 8, 3))]),
+                                NetworkConfig(layer_sizes=(3, 6, 2)))
+    vc = cx.VisualCortex(cfg)
+    x = torch.rand(64)
+    vc.learn_supervised(x, torch.tensor([1.0, 0.0]), 5)
+    assert vc.encode(x, 5).shape == (3,) and vc.predict(x, 5) in (0, 1)
+    assert vc.reconstruct(x, 5).shape == (64,) and len(vc.encode_areas(x, 5)) == 2
+
+
+def test_scalar_areas():
+    bg = cx.BasalGanglia(1.0, no_go_threshold=5.0)
+    a, g = bg.select([3.0, 1.0, 2.0])
+    assert a == 1 and abs(sum(g) - 1) < 1e-6 and bg.select([6.0, 7.0])[0] == -1
+    th = cx.Thalamus(1.0, 1.0).allocate([1.0, 1.0])
+    assert th == pytest.approx([1.0, 1.0])
+    cc = cx.CingulateCortex()
+    assert cc.conflict([1.0, 1.0, 1.0]) == pytest.approx(1.0) and cc.conflict([0.0, 50.0]) < 0.01
+    da = cx.DopaminergicSystem(0.9)
+    assert da.reward_prediction_error(1.0, 0.5, 1.0) == pytest.approx(1.4) and da.step(1.0) == 1.0
+    lc = cx.LocusCoeruleus()
+    assert lc.process(1.0) == (False, 1.0) and lc.process(10.0) == (True, 4.0)
+    assert cx.Habenula().suppress_dopamine(1.0, 0.0, 0.5) == 0.5
+    assert cx.RapheNuclei(1.0).time_horizon() == pytest.approx(100.0)
+    nb = cx.NucleusBasalis(2)
+    assert list(nb.update([1.0, 2.0])) == [1.0, 2.0]
+    hy = cx.Hypothalamus([1.0, 1.0])
+    assert hy.need_level([1.0, 0.0]) == 1.0
+    assert cx.PeriaqueductalGray().respond(0.7) == "flight"
+    sc = cx.SuperiorColliculus(4, enhancement=1.0)
+    assert sc.scan([0.1, 0.9, 0.2, 0.0], [0.0, 0.0, 0.9, 0.0], 2) == [2, 1]
+    assert cx.Claustrum.coherence([[1, 0], [1, 0]]) == pytest.approx(1.0)
+    ret = cx.RetinaLgn(1, 9, 9)
+    flat = ret.process(torch.ones(81))
+    spot = torch.zeros(81)
+    spot[40] = 1
+    assert flat.abs().max() < 1e-5 and ret.process(spot)[40] > 0
+    gc = cx.GridCellEncoder(2, 9, 1.0, 1.4)
+    assert gc.encode(0.3, 0.7).shape == (18,)
+    assert cx.OlfactoryBulb(2).process([0.1, 3.0, 0.2, 2.0]).count_nonzero() == 2
+    assert cx.InferiorColliculus(4).process(torch.sin(torch.arange(64.0))).shape == (4,)
+
+
+def test_network_backed_areas():
+    am = cx.Amygdala(NetworkConfig(layer_sizes=(4, 6, 2)))
+    am.learn(torch.ones(4), torch.tensor([1.0, 0.0]), 5)
+    assert am.salience_gain(torch.ones(4), 5) >= 1.0
+    cb = cx.CerebellarCortex(cx.CerebellarCortexConfig(2, 1, NetworkConfig(layer_sizes=(3, 8, 2))))
+    cb.learn([0.0, 0.0], [1.0], [0.5, 0.5], 5)
+    assert cb.prediction_error([0.0, 0.0], [1.0], [0.5, 0.5], 5) >= 0
+    mc = cx.MotorCortex(cb, [[1.0], [-1.0]])
+    assert mc.select_command([0.0, 0.0], [0.5, 0.5], 5) in (0, 1)
+    hf = cx.HippocampalFormation(cx.HippocampalFormationConfig(
+        HopfieldNetworkConfig(NetworkConfig(layer_sizes=(4, 6, 3))), NetworkConfig(layer_sizes=(4, 6, 3))))
+    for k in range(3):
+        hf.experience(torch.eye(4)[k], 5)
+    hf.replay(1, 3)
+    assert hf.episode_count == 3 and hf.recall(torch.eye(4)[0], 5).shape == (4,)
+    pr = cx.PerirhinalCortex(NetworkConfig(layer_sizes=(4, 6, 3)))
+    pr.remember(torch.eye(4)[0], 5)
+    assert not pr.is_novel(torch.eye(4)[0], 5)
+    pc = cx.PiriformCortex()
+    pc.memorize([1, 0, 0], "rose")
+    assert pc.recognize([0.9, 0.1, 0]) == "rose"
+    we = cx.WernickeArea(NetworkConfig(layer_sizes=(5, 6, 2)))
+    we.learn_utterance(torch.ones(5), torch.tensor([0.0, 1.0]), 5)
+    assert we.surprise(torch.ones(5), 5) >= 0
+    assert cx.BrocaArea(NetworkConfig(layer_sizes=(5, 6, 2))).produce(torch.tensor([0.0, 1.0]), 5) in range(5)
+    dm = cx.DefaultModeNetwork(NetworkConfig(layer_sizes=(4, 6, 3)))
+    dm.learn_from_experience(torch.ones(4), 3)
+    dm.learn_from_experience(torch.zeros(4), 3)
+    assert len(dm.imagine_sequence(2, 3)) == 2
+    assert len(cx.AREAS) >= 49
