@@ -255,3 +255,60 @@ def test_network_backed_areas():
     dm.learn_from_experience(torch.zeros(4), 3)
     assert len(dm.imagine_sequence(2, 3)) == 2
     assert len(cx.AREAS) >= 49
+
+
+# ---------------------------------------------------------------- ONNX subset
+from predicitivecoding_b200.systems import onnx as ox
+
+
+def _graph():
+    g = torch.Generator().manual_seed(0)
+    w = torch.randn(4, 3, 3, 3, generator=g)
+    b = torch.randn(4, generator=g)
+    sc, bi = torch.rand(4, generator=g) + 0.5, torch.randn(4, generator=g)
+    mu, var = torch.randn(4, generator=g), torch.rand(4, generator=g) + 0.5
+    fc = torch.randn(4 * 4 * 4, 5, generator=g)
+    T = ox.TensorData.from_torch
+    A = lambda name, typ, **kw: ox.Attribute(name, typ, **kw)
+    nodes = [
+        ox.Node("c", "Conv", ["x", "w", "b"], ["c"], {"pads": A("pads", ox.A_INTS, ints=[1, 1, 1, 1])}),
+        ox.Node("bn", "BatchNormalization", ["c", "sc", "bi", "mu", "var"], ["n"]),
+        ox.Node("r", "Relu", ["n"], ["r"]),
+        ox.Node("p", "MaxPool", ["r"], ["p"], {"kernel_shape": A("kernel_shape", ox.A_INTS, ints=[2, 2]),
+                                                "strides": A("strides", ox.A_INTS, ints=[2, 2])}),
+        ox.Node("k", "Constant", [], ["shape"], {"value": A("value", ox.A_TENSOR, t=T("", torch.tensor([1, -1])))}),
+        ox.Node("f", "Reshape", ["p", "shape"], ["f"]),
+        ox.Node("id", "Identity", ["f"], ["fi"]),
+        ox.Node("g", "Gemm", ["fi", "fc"], ["g"]),
+        ox.Node("s", "Softmax", ["g"], ["y"], {"axis": A("axis", ox.A_INT, i=1)}),
+        ox.Node("dead", "Relu", ["g"], ["unused"]),
+    ]
+    inits = {k: T(k, v) for k, v in dict(w=w, b=b, sc=sc, bi=bi, mu=mu, var=var, fc=fc).items()}
+    gr = ox.Graph("tiny", 13, nodes, inits, [ox.ValueInfo("x", [1, 3, 8, 8])], [ox.ValueInfo("y", [1, 5])])
+
+    def ref(x):
+        c = torch.nn.functional.conv2d(x, w, b, padding=1)
+        n = (c - mu.view(1, -1, 1, 1)) / torch.sqrt(var.view(1, -1, 1, 1) + 1e-5) * sc.view(1, -1, 1, 1) + bi.view(1, -1, 1, 1)
+        p = torch.nn.functional.max_pool2d(torch.relu(n), 2, 2)
+        return torch.softmax(p.reshape(1, -1) @ fc, 1)
+    return gr, ref
+
+
+def test_onnx_protobuf_roundtrip_execution_optimizer_and_pcnx(tmp_path):
+    gr, ref = _graph()
+    blob = ox.encode_model(gr)
+    m = ox.OnnxModel.load(blob)
+    assert m.input_names == ["x"] and m.output_names == ["y"] and m.graph.opset == 13
+    x = torch.randn(1, 3, 8, 8)
+    y = m.run({"x": x})["y"]
+    assert torch.allclose(y, ref(x), atol=1e-5)
+    opt = ox.optimize_graph(m.graph)
+    ops = [n.op_type for n in opt.nodes]
+    assert "Constant" not in ops and "Identity" not in ops and "Reshape" in ops and len(ops) == 7
+    p = str(tmp_path / "tiny.pcnx")
+    m.save(p)
+    back = ox.OnnxModel.load(p)
+    assert torch.equal(back.run({"x": x})["y"], ox.OnnxModel(opt).run({"x": x})["y"])
+    assert torch.allclose(back.run({"x": x})["y"], y, atol=1e-6)
+    with pytest.raises(ValueError):
+        ox.read_pcnx(b"NOPE" + b"\x00" * 16)
