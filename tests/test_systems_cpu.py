@@ -312,3 +312,101 @@ def test_onnx_protobuf_roundtrip_execution_optimizer_and_pcnx(tmp_path):
     assert torch.allclose(back.run({"x": x})["y"], y, atol=1e-6)
     with pytest.raises(ValueError):
         ox.read_pcnx(b"NOPE" + b"\x00" * 16)
+
+
+# ---------------------------------------------------------------- data sources
+import gzip
+import json
+import struct as st
+
+from predicitivecoding_b200.systems import data as dt
+
+
+def test_idx_mnist_and_cifar(tmp_path):
+    imgs = np.arange(2 * 3 * 3, dtype=np.uint8).reshape(2, 3, 3)
+    (tmp_path / "i.gz").write_bytes(gzip.compress(b"\x00\x00\x08\x03" + st.pack(">3I", 2, 3, 3) + imgs.tobytes()))
+    (tmp_path / "l").write_bytes(b"\x00\x00\x08\x01" + st.pack(">I", 2) + bytes([3, 7]))
+    ds = dt.load_mnist(str(tmp_path / "i.gz"), str(tmp_path / "l"))
+    assert ds.images.shape == (2, 1, 3, 3) and ds.labels.tolist() == [3, 7] and ds.one_hot(1)[7] == 1
+    rec = bytes([5]) + bytes(range(256)) * 12
+    (tmp_path / "c.bin").write_bytes(rec * 2)
+    cf = dt.load_cifar10([str(tmp_path / "c.bin")])
+    assert len(cf) == 2 and cf.images.shape == (2, 3, 32, 32) and int(cf.labels[0]) == 5
+
+
+def test_csv_sqlite_and_shards(tmp_path):
+    t = dt.load_csv("a,b\n1,2\n3,4\n")
+    assert t.numeric().tolist() == [[1, 2], [3, 4]] and t.column("b") == ["2", "4"]
+    import sqlite3
+    db = str(tmp_path / "x.db")
+    con = sqlite3.connect(db)
+    con.execute("create table t(x int, y text)")
+    con.execute("insert into t values (1, 'a'), (2, 'b')")
+    con.commit()
+    con.close()
+    assert dt.sqlite_table(db, "select * from t where x > ?", (1,)).rows == [["2", "b"]]
+    w = dt.ShardedCorpusWriter(str(tmp_path / "sh"), 1024)
+    for i in range(60):
+        w.append([f"document {i} line one", "  second   line "])
+    w.close()
+    assert len(w.shards()) > 1 and w.documents == 60
+    w2 = dt.ShardedCorpusWriter(str(tmp_path / "sh"), 1024)
+    lines = list(w2.lines())
+    assert lines[0] == "document 0 line one" and lines[1] == "second line" and len(lines) == 120
+
+
+def test_html_rss_and_language_id(tmp_path):
+    page = "<html><script>x=1</script><h1>Title &amp; more</h1><p>Para <b>one</b>.</p><p>Two</p></html>"
+    assert dt.html_to_text(page) == ["Title & more", "Para one .", "Two"]
+    rss = "<rss><channel><item><title>A</title><link>u</link></item><item><title>B</title></item></channel></rss>"
+    assert [i["title"] for i in dt.read_rss(rss)] == ["A", "B"]
+    tr = dt.NGramLanguageClassifierTrainer()
+    tr.add("en", "the quick brown fox jumps over the lazy dog and the cat sat on the mat with the hat")
+    tr.add("it", "il gatto nero dorme sul divano e la casa della nonna era piena di gente allegra")
+    clf = tr.train()
+    assert clf.predict("the dog and the hat") == "en" and clf.predict("la gatta della casa") == "it"
+    p = str(tmp_path / "lid.bin")
+    clf.save(p)
+    assert dt.NGramLanguageClassifier.load(p).predict("the cat") == "en"
+
+
+def test_signal_formats():
+    s = dt.spectrogram(torch.sin(torch.arange(2048.0) * 0.3))
+    assert s.shape[0] == 129
+    # EDF: one signal, 2 records of 4 samples
+    ns = 1
+    hdr = (b"0".ljust(8) + b"pat".ljust(80) + b"rec".ljust(80) + b"01.01.01" + b"00.00.00" + b"512".ljust(8)
+           + b"".ljust(44) + b"2".ljust(8) + b"1".ljust(8) + b"1".ljust(4))
+    sh = (b"EEG".ljust(16) + b"".ljust(80) + b"uV".ljust(8) + b"-100".ljust(8) + b"100".ljust(8) + b"-32768".ljust(8)
+          + b"32767".ljust(8) + b"".ljust(80) + b"4".ljust(8) + b"".ljust(32))
+    body = np.array([0, 32767, -32768, 0, 1, 2, 3, 4], "<i2").tobytes()
+    rec = dt.read_edf(hdr + sh + body)
+    assert rec.labels == ["EEG"] and rec.sample_rates == [4.0] and abs(rec.signals[0][1] - 100) < 0.01
+    # NIfTI-1: 2x3x1 float volume
+    h = bytearray(352)
+    st.pack_into("<i", h, 0, 348)
+    st.pack_into("<8h", h, 40, 3, 2, 3, 1, 1, 1, 1, 1)
+    st.pack_into("<h", h, 70, 16)
+    st.pack_into("<8f", h, 76, 1, 1, 2, 3, 1, 1, 1, 1)
+    st.pack_into("<f", h, 108, 352.0)
+    st.pack_into("<2f", h, 112, 1.0, 0.0)
+    vol, pix = dt.read_nifti(bytes(h) + np.arange(6, dtype="<f4").tobytes())
+    assert vol.shape == (2, 3, 1) and vol[1, 0, 0] == 1 and pix == (1.0, 2.0, 3.0)
+    # MIDI: one track, note 60 on at 0, off at 96
+    trk = b"\x00\x90\x3c\x40" + b"\x60\x80\x3c\x00" + b"\x00\xff\x2f\x00"
+    mid = b"MThd" + st.pack(">IHHH", 6, 0, 1, 96) + b"MTrk" + st.pack(">I", len(trk)) + trk
+    div, notes = dt.read_midi(mid)
+    assert div == 96 and notes == [dt.MidiNote(0, 0, 60, 64, 0, 96)]
+
+
+def test_web_sources_with_injected_fetch():
+    pages = {"https://en.wikipedia.org/w/api.php?action=query&prop=extracts&explaintext=1&format=json&titles=Cat":
+             json.dumps({"query": {"pages": {"1": {"extract": "Cats purr.\n\nThey nap."}}}}),
+             "https://hacker-news.firebaseio.com/v0/topstories.json": "[1, 2]",
+             "https://hacker-news.firebaseio.com/v0/item/1.json": '{"title": "A"}',
+             "https://hacker-news.firebaseio.com/v0/item/2.json": '{"title": "B"}'}
+    assert dt.WikipediaSource(pages.__getitem__).article("Cat") == ["Cats purr.", "They nap."]
+    assert [s["title"] for s in dt.HackerNewsSource(pages.__getitem__).top_stories(2)] == ["A", "B"]
+    atom = ("<feed xmlns='http://www.w3.org/2005/Atom'><entry><title> Paper\n one </title><summary>S</summary>"
+            "<id>x</id></entry></feed>")
+    assert dt.ArxivSource(lambda u: atom).search("pc")[0]["title"] == "Paper one"
