@@ -410,3 +410,52 @@ def test_web_sources_with_injected_fetch():
     atom = ("<feed xmlns='http://www.w3.org/2005/Atom'><entry><title> Paper\n one </title><summary>S</summary>"
             "<id>x</id></entry></feed>")
     assert dt.ArxivSource(lambda u: atom).search("pc")[0]["title"] == "Paper one"
+
+
+# ---------------------------------------------------------------- faces
+from predicitivecoding_b200.systems import faces as fc
+
+
+def _face(seed, person):
+    rng = np.random.default_rng(1000 * person + seed)
+    base = np.random.default_rng(person).integers(0, 256, (16, 16, 3)).astype(np.float64)
+    noisy = np.clip(base + rng.normal(0, 12, base.shape), 0, 255).astype(np.uint8)
+    big = np.kron(noisy, np.ones((8, 8, 1), np.uint8))
+    return im.RgbImage.from_pixel_data(big, 128, 128)
+
+
+def test_lbp_descriptor_and_tan_triggs():
+    assert (fc.UNIFORM < 58).sum() == 58 and fc.UNIFORM[0b01010101] == 58
+    g = fc.face_pixels(_face(0, 1))
+    d = fc.lbp_descriptor(g)
+    assert d.shape == (fc.DIMENSION,) and abs(np.linalg.norm(d) - 1) < 1e-5
+    t = fc.tan_triggs(g)
+    assert t.dtype == np.uint8 and t.min() == 0 and t.max() == 255
+
+
+def test_pca_whitening_and_embedders_and_benchmarks():
+    rng = np.random.default_rng(0)
+    X = rng.normal(size=(200, 20)) @ np.diag(np.linspace(5, 0.1, 20))
+    p = fc.PcaProjector().fit(X, 5)
+    z = p.project(X).numpy()
+    assert z.shape == (200, 5) and np.allclose(z.var(0, ddof=1), 1, atol=0.05)
+    people = [0, 1, 2]
+    imgs = [_face(s, pp) for pp in people for s in range(3)]
+    lbp = fc.LbpEmbedder()
+    db = fc.FaceDatabase(lbp, threshold=0.0)
+    for pp in people:
+        db.enroll(f"p{pp}", _face(0, pp))
+    assert db.identify(_face(5, 1))[0] == "p1"
+    pairs = [(_face(1, a), _face(2, b), a == b) for a in people for b in people]
+    res = fc.verification_benchmark(lbp, pairs, folds=3)
+    assert res.auc_roc > 0.9 and res.mean_same > res.mean_diff
+    assert fc.identification_benchmark(lbp, {f"p{pp}": _face(0, pp) for pp in people},
+                                       [(f"p{pp}", _face(4, pp)) for pp in people]) == 1.0
+    enh = fc.EnhancedLbpEmbedder(target_dim=4)
+    enh.fit(imgs)
+    assert enh.embed(imgs[0]).shape == (4,)
+    pce = fc.PcFaceEmbedder(latent_dim=8, inference_steps=2, epochs=1, hidden=16)
+    pce.fit(imgs[:3])
+    fused = fc.FusedEmbedder([lbp, pce])
+    assert fused.embed(imgs[0]).shape == (fc.DIMENSION + 8,)
+    assert fc.auc_roc([0.9, 0.8, 0.1], [True, True, False]) == 1.0
