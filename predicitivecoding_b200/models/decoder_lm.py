@@ -428,7 +428,8 @@ def cross_entropy_masked(logits: torch.Tensor, targets: torch.Tensor, ignore_ind
     measurable for non-degenerate rows, so the pure log-softmax form is used.
     """
     V = logits.shape[-1]
-    lg = logits.reshape(-1, V).float()
+    lg = logits.reshape(-1, V)
+    lg = lg if lg.dtype == torch.float64 else lg.float()
     t = targets.reshape(-1)
     keep = t != ignore_index
     if not bool(keep.any()):
