@@ -297,6 +297,170 @@ class NGramLanguageClassifierTrainer:
         return NGramLanguageClassifier(self.min_n, self.max_n, langs, prior, prob, fb)
 
 
+# Seed corpus for the default n-gram classifier: short everyday sentences written for this
+# package (a few per language); train on a real corpus for serious use.
+SEED_SAMPLES: Dict[str, List[str]] = {
+    "English": ["We read the newspaper every morning before the children go to school.",
+                "This text is written in English to check which language it uses.",
+                "The weather is nice today and we are going for a walk in the park.",
+                "Could you tell me where the nearest train station is, please?",
+                "She has been working on this project for three years with her friends."],
+    "Italian": ["Ogni mattina leggiamo il giornale prima che i bambini vadano a scuola.",
+                "Questo testo è scritto in italiano per controllare quale lingua usa.",
+                "Oggi il tempo è bello e andiamo a fare una passeggiata nel parco.",
+                "Mi potrebbe dire dove si trova la stazione dei treni più vicina?",
+                "Lei lavora a questo progetto da tre anni insieme ai suoi amici."],
+    "French": ["Nous lisons le journal chaque matin avant que les enfants aillent à l'école.",
+               "Ce texte est écrit en français pour vérifier quelle langue il utilise.",
+               "Je voudrais un café et un croissant, merci beaucoup.",
+               "Il fait beau aujourd'hui et nous allons nous promener dans le parc.",
+               "Pourriez-vous me dire où se trouve la gare la plus proche, s'il vous plaît ?",
+               "Elle travaille sur ce projet depuis trois ans avec ses amis."],
+    "German": ["Wir lesen jeden Morgen die Zeitung, bevor die Kinder zur Schule gehen.",
+               "Dieser Text ist auf Deutsch geschrieben, um die Sprache zu prüfen.",
+               "Heute ist das Wetter schön und wir gehen im Park spazieren.",
+               "Können Sie mir bitte sagen, wo der nächste Bahnhof ist?",
+               "Sie arbeitet seit drei Jahren mit ihren Freunden an diesem Projekt."],
+    "Spanish": ["Leemos el periódico cada mañana antes de que los niños vayan a la escuela.",
+                "Este texto está escrito en español para comprobar qué idioma usa.",
+                "Hoy hace buen tiempo y vamos a dar un paseo por el parque.",
+                "¿Podría decirme dónde está la estación de tren más cercana, por favor?",
+                "Ella ha trabajado en este proyecto durante tres años con sus amigos."],
+    "Portuguese": ["Lemos o jornal todas as manhãs antes de as crianças irem para a escola.",
+                   "Este texto está escrito em português para verificar qual língua ele usa.",
+                   "Hoje o tempo está bom e vamos dar um passeio no parque.",
+                   "Você poderia me dizer onde fica a estação de trem mais próxima, por favor?",
+                   "Ela trabalha neste projeto há três anos com os seus amigos."],
+    "Dutch": ["We lezen elke ochtend de krant voordat de kinderen naar school gaan.",
+              "Deze tekst is in het Nederlands geschreven om de taal te controleren.",
+              "Vandaag is het mooi weer en we gaan wandelen in het park.",
+              "Kunt u mij vertellen waar het dichtstbijzijnde treinstation is?",
+              "Zij werkt al drie jaar met haar vrienden aan dit project."],
+}
+
+
+def default_language_classifier() -> "NGramLanguageClassifier":
+    """Classifier trained on :data:`SEED_SAMPLES` (NGramLanguageClassifier.cs:93-99 trains on a bundled corpus)."""
+    t = NGramLanguageClassifierTrainer()
+    for lang, texts in SEED_SAMPLES.items():
+        for x in texts:
+            t.add(lang, x)
+    return t.train()
+
+
+@dataclass
+class LanguageProfile:
+    """n-gram frequency profile in the JSON layout of the langdetect project:
+    ``{"name": code, "freq": {gram: count}, "n_words": [#1-grams, #2-grams, #3-grams]}``."""
+    name: str
+    freq: Dict[str, int]
+    n_words: List[int]
+
+    @staticmethod
+    def load(path: str) -> "LanguageProfile":
+        d = json.load(open(path, encoding="utf-8"))
+        return LanguageProfile(d["name"], {k: int(v) for k, v in d["freq"].items()}, list(d["n_words"]))
+
+    def save(self, path: str) -> None:
+        json.dump({"name": self.name, "freq": self.freq, "n_words": self.n_words}, open(path, "w", encoding="utf-8"),
+                  ensure_ascii=False)
+
+    @staticmethod
+    def from_texts(name: str, texts: Iterable[str]) -> "LanguageProfile":
+        freq: Counter = Counter()
+        for t in texts:
+            freq.update(LanguageDetector.ngrams(t))
+        n_words = [sum(v for k, v in freq.items() if len(k) == n) for n in (1, 2, 3)]
+        return LanguageProfile(name, dict(freq), n_words)
+
+
+class LanguageDetector:
+    """Naive-Bayes language identification by random n-gram sampling (Nakatani Shuyo, "Language
+    Detection Library for Java", 2010): each of ``n_trial`` trials draws n-grams of the text at random,
+    multiplies per-language likelihoods p(gram | lang) smoothed by ``alpha`` (jittered per trial by a
+    Gaussian), renormalises every 5 draws and stops once one language exceeds ``conv_threshold``; the
+    trial posteriors are averaged.  Reference: PredictiveCoding.Data/Text/LanguageDetection/
+    LanguageDetector.cs (Detect / DetectAll, names from ISO 639-1 codes).  Profiles are read from a
+    directory of langdetect-format JSON files or built from text with :meth:`LanguageProfile.from_texts`."""
+
+    BASE_FREQ = 10000
+    ITERATION_LIMIT = 10000
+    PROB_THRESHOLD = 0.1
+    CONV_THRESHOLD = 0.99999
+    ALPHA_DEFAULT, ALPHA_WIDTH = 0.5, 0.05
+    N_TRIAL = 7
+    NAMES = {"en": "English", "it": "Italian", "fr": "French", "de": "German", "es": "Spanish",
+             "pt": "Portuguese", "nl": "Dutch", "ro": "Romanian", "zh-cn": "Chinese", "zh-tw": "Chinese"}
+
+    def __init__(self, profiles: Sequence[LanguageProfile], seed: Optional[int] = None):
+        if not profiles:
+            raise ValueError("no language profiles")
+        self.langs = [p.name for p in profiles]
+        self.word_prob: Dict[str, np.ndarray] = {}
+        for i, p in enumerate(profiles):
+            for g, c in p.freq.items():
+                n = len(g)
+                if 1 <= n <= 3 and p.n_words[n - 1] > 0:
+                    self.word_prob.setdefault(g, np.zeros(len(profiles)))[i] = c / p.n_words[n - 1]
+        self.seed = seed
+
+    @staticmethod
+    def from_directory(path: str, seed: Optional[int] = None) -> "LanguageDetector":
+        return LanguageDetector([LanguageProfile.load(os.path.join(path, f)) for f in sorted(os.listdir(path))], seed)
+
+    @staticmethod
+    def ngrams(text: str) -> Counter:
+        c: Counter = Counter()
+        for word in re.findall(r"[^\W\d_]+", text.lower()):
+            w = " " + word + " "
+            for n in (1, 2, 3):
+                for i in range(len(w) - n + 1):
+                    g = w[i:i + n]
+                    if g != " " and not (n > 1 and g.count(" ") == n):
+                        c[g] += 1
+        return c
+
+    def _grams(self, text: str) -> List[str]:
+        text = re.sub(r"https?://\S+|\S+@\S+", " ", text)[:10000]
+        out = []
+        for g, k in self.ngrams(text).items():
+            if g in self.word_prob:
+                out.extend([g] * k)
+        return out
+
+    def detect_all(self, text: str) -> List[DetectedLanguage]:
+        grams = self._grams(text)
+        if not grams:
+            return []
+        rng = np.random.default_rng(self.seed)
+        L = len(self.langs)
+        total = np.zeros(L)
+        for _ in range(self.N_TRIAL):
+            prob = np.full(L, 1.0 / L)
+            alpha = self.ALPHA_DEFAULT + rng.normal() * self.ALPHA_WIDTH
+            weight = alpha / self.BASE_FREQ
+            for i in range(self.ITERATION_LIMIT):
+                prob *= weight + self.word_prob[grams[rng.integers(len(grams))]]
+                if i % 5 == 0:
+                    prob /= prob.sum()
+                    if prob.max() > self.CONV_THRESHOLD:
+                        break
+            total += prob / prob.sum()
+        total /= self.N_TRIAL
+        ranked = sorted(((self.langs[i], float(total[i])) for i in range(L)), key=lambda t: -t[1])
+        return [DetectedLanguage(self.NAMES.get(c, c), p) for c, p in ranked if p > self.PROB_THRESHOLD]
+
+    def detect(self, text: str) -> str:
+        r = self.detect_all(text)
+        return r[0].language if r else "Unknown"
+
+    @staticmethod
+    def create_default(seed: Optional[int] = None) -> "LanguageDetector":
+        """Detector over profiles built from :data:`SEED_SAMPLES` (no bundled Wikipedia profiles)."""
+        codes = {v: k for k, v in LanguageDetector.NAMES.items() if "-" not in k}
+        return LanguageDetector([LanguageProfile.from_texts(codes[n], t) for n, t in SEED_SAMPLES.items()], seed)
+
+
 # ---------------------------------------------------------------- signals and formats
 def spectrogram(samples, n_fft: int = 256, hop: int = 128, log: bool = True) -> torch.Tensor:
     x = torch.as_tensor(samples, dtype=torch.float32).reshape(-1)

@@ -334,27 +334,60 @@ class HogDescriptor:
             raise ValueError("Window too small for a 2x2 block grid.")
 
     def compute_gray(self, gray: np.ndarray) -> np.ndarray:
-        g = np.asarray(gray, np.float32).reshape(self.wh, self.ww)
-        xs = np.clip(np.arange(self.ww) + 1, 0, self.ww - 1), np.clip(np.arange(self.ww) - 1, 0, self.ww - 1)
-        ys = np.clip(np.arange(self.wh) + 1, 0, self.wh - 1), np.clip(np.arange(self.wh) - 1, 0, self.wh - 1)
-        gx = g[:, xs[0]] - g[:, xs[1]]
-        gy = g[ys[0], :] - g[ys[1], :]
+        return self.compute_gray_batch(np.asarray(gray, np.float32).reshape(1, self.wh, self.ww))[0]
+
+    def compute_gray_batch(self, grays: np.ndarray) -> np.ndarray:
+        """HOG of N windows at once: [N, wh, ww] luma -> [N, dimension] (clamped central differences,
+        unsigned 9-bin orientation, 2x2-cell blocks, L2 normalisation)."""
+        g = np.asarray(grays, np.float32).reshape(-1, self.wh, self.ww)
+        n = g.shape[0]
+        xp, xm = np.clip(np.arange(self.ww) + 1, 0, self.ww - 1), np.clip(np.arange(self.ww) - 1, 0, self.ww - 1)
+        yp, ym = np.clip(np.arange(self.wh) + 1, 0, self.wh - 1), np.clip(np.arange(self.wh) - 1, 0, self.wh - 1)
+        gx = g[:, :, xp] - g[:, :, xm]
+        gy = g[:, yp, :] - g[:, ym, :]
         mag = np.sqrt(gx * gx + gy * gy)
         ang = np.degrees(np.arctan2(gy, gx))
         ang = np.where(ang < 0, ang + 180, ang)
         ang = np.where(ang >= 180, ang - 180, ang)
         b = np.minimum(self.bins - 1, (ang / (180.0 / self.bins)).astype(np.int64))
         cell_idx = (np.arange(self.wh)[:, None] // self.cell) * self.cx + np.arange(self.ww)[None, :] // self.cell
-        hist = np.zeros((self.cy * self.cx, self.bins), np.float64)
-        m = mag > 0
-        np.add.at(hist, (cell_idx[m], b[m]), mag[m])
-        hist = hist.reshape(self.cy, self.cx, self.bins)
-        feats = []
-        for by in range(self.cy - 1):
-            for bx in range(self.cx - 1):
-                blk = hist[by:by + 2, bx:bx + 2].reshape(-1)
-                feats.append(blk / np.sqrt((blk * blk).sum() + 1e-6 ** 2))
-        return np.concatenate(feats).astype(np.float32)
+        flat = (np.arange(n)[:, None, None] * (self.cy * self.cx) + cell_idx[None]) * self.bins + b
+        hist = np.bincount(flat.reshape(-1), weights=mag.reshape(-1).astype(np.float64),
+                           minlength=n * self.cy * self.cx * self.bins).reshape(n, self.cy, self.cx, self.bins)
+        blk = np.concatenate([hist[:, :-1, :-1], hist[:, :-1, 1:], hist[:, 1:, :-1], hist[:, 1:, 1:]], axis=-1)
+        # block layout: cells (y, x), (y, x+1), (y+1, x), (y+1, x+1), bins innermost
+        norm = np.sqrt((blk * blk).sum(-1, keepdims=True) + 1e-6 ** 2)
+        return (blk / norm).reshape(n, -1).astype(np.float32)
+
+    @staticmethod
+    def _luma(pixels: np.ndarray) -> np.ndarray:
+        p = pixels.astype(np.float32)
+        return 0.299 * p[..., 0] + 0.587 * p[..., 1] + 0.114 * p[..., 2]
+
+    def from_window(self, image: RgbImage, x0: int, y0: int) -> np.ndarray:
+        """HOG of the window whose top-left corner is (x0, y0) (HogDescriptor.cs:109-120)."""
+        return self.compute_gray(self._luma(image.pixels[y0:y0 + self.wh, x0:x0 + self.ww]))
+
+    def from_crop(self, image: RgbImage, box: Tuple[int, int, int, int]) -> np.ndarray:
+        """HOG of an (x, y, w, h) box cropped and resized to the window (HogDescriptor.cs:124-140)."""
+        x, y, w, h = box
+        x0, y0 = max(0, x), max(0, y)
+        x1, y1 = min(image.width, x + w), min(image.height, y + h)
+        if x1 <= x0 or y1 <= y0:
+            return np.zeros(self.dimension, np.float32)
+        crop = image.crop(x0, y0, x1 - x0, y1 - y0).resize(self.ww, self.wh)
+        return self.compute_gray(self._luma(crop.pixels))
+
+    def windows(self, image: RgbImage, stride: int) -> Tuple[np.ndarray, np.ndarray]:
+        """Every window at the given stride: ([N, dimension] features, [N, 2] top-left corners)."""
+        lum = self._luma(image.pixels)
+        ys = np.arange(0, image.height - self.wh + 1, stride)
+        xs = np.arange(0, image.width - self.ww + 1, stride)
+        if len(ys) == 0 or len(xs) == 0:
+            return np.zeros((0, self.dimension), np.float32), np.zeros((0, 2), np.int64)
+        view = np.lib.stride_tricks.sliding_window_view(lum, (self.wh, self.ww))[ys][:, xs]
+        corners = np.stack(np.meshgrid(xs, ys), -1).reshape(-1, 2)
+        return self.compute_gray_batch(view.reshape(-1, self.wh, self.ww)), corners
 
 
 @dataclass(frozen=True)
