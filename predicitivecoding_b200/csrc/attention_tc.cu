@@ -1,19 +1,26 @@
 // Causal flash-attention forward on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
 //
 // Reference counterpart: PredictiveCoding.Device/Kernels/DeviceTrainKernels.cs (attn_fwd: one
-// block per (query, head), fp32 SIMT).  One CTA computes a 128-query tile of one (batch, head):
+// block per (query, head), fp32 SIMT).  One CTA owns two consecutive 128-query tiles (A and B) of
+// one (batch, head) and streams the 128-key tiles they need once:
 //
-//   warp 4     TMA producer: Q once, then K_j / V_j 128-key tiles into a 2-stage ring
-//   warp 5     MMA issuer:   S_j = Q K_j^T (M=128, N=128, K=hd) into one of two TMEM S buffers,
-//                            then O_j = P_j V_j (M=128, N=hd, K=128) into one of two TMEM O buffers;
-//                            S_{j+1} is issued before waiting for P_j, so QK^T overlaps the softmax
-//   warps 0-3  softmax:      thread r owns query row r (TMEM lane r): row max over the S tile,
-//                            p = exp((s - m) * scale) written as bf16 straight into the swizzled
-//                            shared-memory layout the P operand descriptor expects, running sum l,
-//                            and O accumulated in registers: O = O * exp((m_old - m) * scale) + O_j
-//   epilogue   O / l in bf16, lse = m * scale + log(l) (the backward's convention)
+//   warp 8      TMA producer: Q_A and Q_B once, then K_j / V_j into a 3-stage ring
+//   warp 9      MMA issuer (one thread), per key tile j, in this order:
+//                 PV_A(j-1), S_A(j), PV_B(j-1), S_B(j)
+//               S_w = Q_w K_j^T lands in TMEM (128 columns per tile); O_w += P_w V_j accumulates
+//               in TMEM.  Because one commit covers every earlier MMA of the issuing thread, the
+//               commit that announces S_w(j) also proves PV_w(j-1) finished: softmax warpgroup w
+//               may then rewrite P_w and rescale O_w without another barrier.
+//   warps 0-3   softmax of tile A, warps 4-7 softmax of tile B (thread = query row = TMEM lane):
+//               the whole 128-key row is read from TMEM at once, p = 2^(s*c - m*c) with
+//               c = scale*log2(e) on the SFU, bf16 P goes to shared memory in the swizzled K-major
+//               layout of the PV MMA's A operand.  The running max is only moved (and O rescaled
+//               in TMEM) when a warp sees a row max grow by more than 2^8, so most tiles skip the
+//               O round trip.  The two warpgroups alternate: one computes exponentials while the
+//               tensor cores run the other's MMAs.
+//   epilogue    O / l in bf16, lse = m*scale + ln(l) (the backward's convention)
 //
-// Heavy (late) query tiles are scheduled first.  Every wait is bounded and unwinds on timeout.
+// Heavy (late) tile pairs are scheduled first.  Every wait is bounded and unwinds on timeout.
 #include <cudaTypedefs.h>
 
 #include <mutex>
@@ -25,20 +32,23 @@ namespace fa {
 
 constexpr int kBQ = 128;
 constexpr int kBKV = 128;
-constexpr int kThreads = 192;
+constexpr int kStages = 3;
+constexpr int kThreads = 320;
 constexpr int kAtom = 128 * 128;  // bytes of one [128 rows x 64 bf16] swizzled atom
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleLog2 = 8.f;  // move the running max only when it grows by more than 2^8
 
 template <int HD>
 struct Cfg {
   static constexpr int ATOMS = HD / 64;
-  static constexpr int Q_OFF = 0;
-  static constexpr int K_OFF = Q_OFF + ATOMS * kAtom;              // 2 stages
-  static constexpr int V_OFF = K_OFF + 2 * ATOMS * kAtom;          // 2 stages
-  static constexpr int P_OFF = V_OFF + 2 * ATOMS * kAtom;          // 2 atoms (128 keys)
-  static constexpr int BAR_OFF = P_OFF + 2 * kAtom;
-  static constexpr int USED = BAR_OFF + 256;
-  // keep one CTA per SM: a second CTA could not allocate its 512 TMEM columns anyway
-  static constexpr int SMEM = (USED + 1024 > 120 * 1024 ? USED + 1024 : 120 * 1024);
+  static constexpr int Q_OFF = 0;                                   // tiles A, B
+  static constexpr int K_OFF = Q_OFF + 2 * ATOMS * kAtom;           // kStages stages
+  static constexpr int V_OFF = K_OFF + kStages * ATOMS * kAtom;     // kStages stages
+  static constexpr int P_OFF = V_OFF + kStages * ATOMS * kAtom;     // tiles A, B: 2 atoms each
+  static constexpr int BAR_OFF = P_OFF + 2 * 2 * kAtom;
+  static constexpr int SMEM = BAR_OFF + 256 + 1024;
+  static constexpr int TM_S = 0;                                    // + w * 128
+  static constexpr int TM_O = 2 * kBKV;                             // + w * HD
 };
 
 PCB_DEVICE void fence_view_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
@@ -56,35 +66,38 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sP = smem + C::P_OFF;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;   // [2]
-  uint64_t* kv_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;    // [2]
-  uint64_t* p_full = bars + 7;
-  uint64_t* o_full = bars + 8;    // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+  uint64_t* kv_full = bars + 1;              // [kStages]
+  uint64_t* kv_empty = bars + 1 + kStages;   // [kStages]
+  uint64_t* s_full = bars + 1 + 2 * kStages; // [2]
+  uint64_t* p_full = s_full + 2;             // [2]
+  uint64_t* o_final = p_full + 2;            // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_final + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = gridDim.x - 1 - blockIdx.x;   // heavy tiles first
-  const int bh = blockIdx.y;
+  const int t = gridDim.y - 1 - blockIdx.y;  // tile pair index, heavy pairs first
+  const int bh = blockIdx.x;
   const int b = bh / H, h = bh % H;
-  const int n_kv = qt + 1;                      // causal: key tiles 0..qt
-  const int row0 = b * S + qt * kBQ;
+  const int last_a = 2 * t, last_b = 2 * t + 1;  // causal: tile A needs key tiles 0..2t, B 0..2t+1
+  const int n_kv = last_b + 1;
+  const int row0 = b * S + t * 2 * kBQ;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kStages; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
-      mbar_init(&s_full[i], 1);
-      mbar_init(&o_full[i], 1);
     }
-    mbar_init(p_full, 4);
+    for (int w = 0; w < 2; ++w) {
+      mbar_init(&s_full[w], 1);
+      mbar_init(&p_full[w], 4);
+      mbar_init(&o_final[w], 1);
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 4 && lane == 0) prefetch_tmap(&tm);
-  if (warp == 5) {
+  if (warp == 8 && lane == 0) prefetch_tmap(&tm);
+  if (warp == 9) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -93,15 +106,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == 8) {
     if (lane == 0) {
       // ---------------- TMA producer ----------------
-      mbar_arrive_expect_tx(q_full, C::ATOMS * kAtom);
+      mbar_arrive_expect_tx(q_full, 2 * C::ATOMS * kAtom);
 #pragma unroll
-      for (int a = 0; a < C::ATOMS; ++a) tma_load_2d(sQ + a * kAtom, &tm, q_full, h * HD + a * 64, row0);
+      for (int w = 0; w < 2; ++w)
+#pragma unroll
+        for (int a = 0; a < C::ATOMS; ++a)
+          tma_load_2d(sQ + (w * C::ATOMS + a) * kAtom, &tm, q_full, h * HD + a * 64, row0 + w * kBQ);
       for (int j = 0; j < n_kv; ++j) {
-        const int st = j & 1;
-        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1u, err, kErrTimeoutEmpty, abort_flag)) break;
+        const int st = j % kStages;
+        if (!mbar_wait(&kv_empty[st], ((j / kStages) & 1) ^ 1u, err, kErrTimeoutEmpty, abort_flag)) break;
         mbar_arrive_expect_tx(&kv_full[st], 2 * C::ATOMS * kAtom);
         const int krow = b * S + j * kBKV;
 #pragma unroll
@@ -111,130 +127,155 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
       constexpr uint32_t idesc_s = make_idesc_bf16(kBQ, kBKV, 0, 0);
       constexpr uint32_t idesc_o = make_idesc_bf16(kBQ, HD, 0, 1);
       const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV), p_addr = smem_u32(sP);
-      bool ok = mbar_wait(q_full, 0, err, kErrTimeoutFull, abort_flag);
-      auto issue_s = [&](int j) -> bool {
-        const int st = j & 1;
-        if (!mbar_wait(&kv_full[st], (j >> 1) & 1, err, kErrTimeoutFull, abort_flag)) return false;
+      auto kv_ready = [&](int j) -> bool {
+        return mbar_wait(&kv_full[j % kStages], (j / kStages) & 1, err, kErrTimeoutFull, abort_flag);
+      };
+      auto issue_s = [&](int w, int j) {
+        const uint32_t kb = k_addr + (j % kStages) * C::ATOMS * kAtom;
+        const uint32_t qb = q_addr + w * C::ATOMS * kAtom;
         tc_fence_after();
-        const uint32_t d = tmem + st * kBKV;
 #pragma unroll
         for (int k = 0; k < HD / 16; ++k) {
           const uint32_t off = (k >> 2) * kAtom + (k & 3) * 32;
-          const uint64_t ad = make_smem_desc(q_addr + off, 16, 1024, 2);
-          const uint64_t bd = make_smem_desc(k_addr + st * C::ATOMS * kAtom + off, 16, 1024, 2);
-          umma_bf16(d, ad, bd, idesc_s, k > 0 ? 1u : 0u);
+          umma_bf16(tmem + C::TM_S + w * kBKV, make_smem_desc(qb + off, 16, 1024, 2),
+                    make_smem_desc(kb + off, 16, 1024, 2), idesc_s, k > 0 ? 1u : 0u);
         }
-        umma_commit(&s_full[st]);
-        return true;
+        umma_commit(&s_full[w]);
       };
-      if (ok) ok = issue_s(0);
-      for (int j = 0; j < n_kv && ok; ++j) {
-        if (j + 1 < n_kv && !issue_s(j + 1)) break;
-        if (!mbar_wait(p_full, j & 1, err, kErrTimeoutTmemEmpty, abort_flag)) break;
+      auto issue_pv = [&](int w, int j) {
+        const uint32_t vb = v_addr + (j % kStages) * C::ATOMS * kAtom;
+        const uint32_t pb = p_addr + w * 2 * kAtom;
         tc_fence_after();
-        const int st = j & 1;
-        const uint32_t d = tmem + 2 * kBKV + st * HD;
 #pragma unroll
-        for (int k = 0; k < kBKV / 16; ++k) {
-          const uint64_t ad = make_smem_desc(p_addr + (k >> 2) * kAtom + (k & 3) * 32, 16, 1024, 2);
-          const uint64_t bd = make_smem_desc(v_addr + st * C::ATOMS * kAtom + k * 2048, kAtom, 1024, 2);
-          umma_bf16(d, ad, bd, idesc_o, k > 0 ? 1u : 0u);
+        for (int k = 0; k < kBKV / 16; ++k)
+          umma_bf16(tmem + C::TM_O + w * HD, make_smem_desc(pb + (k >> 2) * kAtom + (k & 3) * 32, 16, 1024, 2),
+                    make_smem_desc(vb + k * 2048, kAtom, 1024, 2), idesc_o, (j > 0 || k > 0) ? 1u : 0u);
+      };
+      bool ok = mbar_wait(q_full, 0, err, kErrTimeoutFull, abort_flag) && kv_ready(0);
+      if (ok) {
+        issue_s(0, 0);
+        issue_s(1, 0);
+      }
+      for (int j = 0; j < n_kv && ok; ++j) {
+        if (j <= last_a) {
+          if (!(ok = mbar_wait(&p_full[0], j & 1, err, kErrTimeoutTmemEmpty, abort_flag))) break;
+          issue_pv(0, j);
+          if (j + 1 <= last_a) {
+            if (!(ok = kv_ready(j + 1))) break;
+            issue_s(0, j + 1);
+          } else {
+            umma_commit(&o_final[0]);
+          }
         }
-        umma_commit(&o_full[st]);
-        umma_commit(&kv_empty[st]);
+        if (!(ok = mbar_wait(&p_full[1], j & 1, err, kErrTimeoutTmemEmpty, abort_flag))) break;
+        issue_pv(1, j);
+        umma_commit(&kv_empty[j % kStages]);
+        if (j + 1 < n_kv) {
+          if (!(ok = kv_ready(j + 1))) break;
+          issue_s(1, j + 1);
+        } else {
+          umma_commit(&o_final[1]);
+        }
       }
     }
   } else {
-    // ---------------- softmax warps: one query row per thread ----------------
-    const int r = threadIdx.x;                 // 0..127 == TMEM lane
-    const int q = qt * kBQ + r;
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    // ---------------- softmax warpgroups: one query row per thread ----------------
+    const int w = warp >> 2;                    // 0 = tile A, 1 = tile B
+    const int r = threadIdx.x & 127;            // row within the tile == TMEM lane
+    const int last = w == 0 ? last_a : last_b;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    const uint32_t s_col = lane_base + C::TM_S + w * kBKV;
+    const uint32_t o_col = lane_base + C::TM_O + w * HD;
+    uint8_t* prow = sP + w * 2 * kAtom + r * 128;
+    const float c = scale * kLog2e;
     float m = -INFINITY, l = 0.f;
-    float o[HD];
-#pragma unroll
-    for (int d = 0; d < HD; ++d) o[d] = 0.f;
     bool ok = true;
-    for (int j = 0; j < n_kv && ok; ++j) {
-      const int st = j & 1;
-      if (!mbar_wait(&s_full[st], (j >> 1) & 1, err, kErrTimeoutTmemFull, abort_flag)) { ok = false; break; }
+    for (int j = 0; j <= last; ++j) {
+      ok = mbar_wait(&s_full[w], j & 1, err, kErrTimeoutTmemFull, abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
-      const uint32_t sbase = lane_base + st * kBKV;
-      const bool diag = (j == qt);
-      // pass 1: row max of this tile
-      float tmax = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < kBKV / 32; ++c) {
-        uint32_t u[32];
-        tmem_ld_32x32b_x32(sbase + c * 32, u);
-        tmem_ld_wait();
+      uint32_t sv_u[128];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const float s = __uint_as_float(u[e]);
-          const bool valid = !diag || (c * 32 + e <= r);
-          tmax = valid ? fmaxf(tmax, s) : tmax;
-        }
+      for (int cc = 0; cc < 4; ++cc)
+        tmem_ld_32x32b_x32(s_col + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(sv_u + cc * 32));
+      tmem_ld_wait();
+#define SV(e) __uint_as_float(sv_u[e])
+      if (j == last) {  // diagonal tile: key column e is visible to row r iff e <= r
+#pragma unroll
+        for (int e = 0; e < 128; ++e) sv_u[e] = e <= r ? sv_u[e] : __float_as_uint(-INFINITY);
       }
-      const float m_new = fmaxf(m, tmax);
-      const float corr = (m == -INFINITY) ? 0.f : __expf((m - m_new) * scale);
-      const float msc = m_new * scale;
-      // pass 2: probabilities -> bf16 P (swizzled K-major atoms), row sum
-      float rs = 0.f;
-#pragma unroll 1
-      for (int c = 0; c < kBKV / 32; ++c) {
-        uint32_t u[32];
-        tmem_ld_32x32b_x32(sbase + c * 32, u);
-        tmem_ld_wait();
-        uint32_t pk[16];
+      float tmax = SV(0);
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const bool v0 = !diag || (c * 32 + e <= r);
-          const bool v1 = !diag || (c * 32 + e + 1 <= r);
-          const float p0 = v0 ? __expf(__uint_as_float(u[e]) * scale - msc) : 0.f;
-          const float p1 = v1 ? __expf(__uint_as_float(u[e + 1]) * scale - msc) : 0.f;
+      for (int e = 1; e < 128; ++e) tmax = fmaxf(tmax, SV(e));
+      const float m_new = fmaxf(m, tmax);
+      const bool grow = (m_new - m) * c > kRescaleLog2;  // always true on the first tile (m = -inf)
+      const bool rescale = __any_sync(0xffffffffu, grow);
+      float corr = 1.f;
+      if (rescale) {
+        corr = ex2_approx((m - m_new) * c);  // 0 when m = -inf
+        m = m_new;
+        l *= corr;
+      }
+      const float msc = m * c;
+      float rs = 0.f;
+#pragma unroll
+      for (int ch = 0; ch < 16; ++ch) {  // 16-byte chunk ch = keys 8ch..8ch+7
+        uint32_t pk[4];
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) {
+          const float p0 = ex2_approx(fmaf(SV(ch * 8 + e), c, -msc));
+          const float p1 = ex2_approx(fmaf(SV(ch * 8 + e + 1), c, -msc));
           rs += p0 + p1;
           pk[e >> 1] = pack_bf16x2(p0, p1);
         }
-        uint8_t* atom = sP + (c >> 1) * kAtom + r * 128;
-#pragma unroll
-        for (int e4 = 0; e4 < 4; ++e4) {
-          const int chunk = (c & 1) * 4 + e4;
-          uint4 v = make_uint4(pk[4 * e4], pk[4 * e4 + 1], pk[4 * e4 + 2], pk[4 * e4 + 3]);
-          *reinterpret_cast<uint4*>(atom + ((chunk ^ (r & 7)) << 4)) = v;
-        }
+        *reinterpret_cast<uint4*>(prow + (ch >> 3) * kAtom + (((ch & 7) ^ (r & 7)) << 4)) =
+            make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
-      l = l * corr + rs;
-      m = m_new;
+#undef SV
+      l += rs;
+      if (rescale && j > 0) {  // O holds PV(0..j-1): scale it in place (PV_w(j-1) is complete, see above)
+#pragma unroll 1
+        for (int cc = 0; cc < HD / 32; ++cc) {
+          uint32_t ov[32];
+          tmem_ld_32x32b_x32(o_col + cc * 32, ov);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * corr);
+          tmem_st_32x32b_x32(o_col + cc * 32, ov);
+        }
+        tmem_st_wait();
+      }
       fence_view_async_shared();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
-      // O_j = P_j V_j: fold into the register accumulator
-      if (!mbar_wait(&o_full[st], (j >> 1) & 1, err, kErrTimeoutTmemFull, abort_flag)) { ok = false; break; }
-      tc_fence_after();
-      const uint32_t obase = lane_base + 2 * kBKV + st * HD;
-#pragma unroll
-      for (int c = 0; c < HD / 32; ++c) {
-        uint32_t u[32];
-        tmem_ld_32x32b_x32(obase + c * 32, u);
-        tmem_ld_wait();
-#pragma unroll
-        for (int e = 0; e < 32; ++e) o[c * 32 + e] = o[c * 32 + e] * corr + __uint_as_float(u[e]);
-      }
+      if (lane == 0) mbar_arrive(&p_full[w]);
     }
-    if (ok) {
+    if (ok) ok = mbar_wait(&o_final[w], 0, err, kErrTimeoutTmemFull, abort_flag);
+    if (__all_sync(0xffffffffu, ok)) {
+      tc_fence_after();
+      const int q = t * 2 * kBQ + w * kBQ + r;
       const float inv = l > 0.f ? 1.f / l : 0.f;
       __nv_bfloat16* orow = out + (long long)(b * S + q) * ld_o + h * HD;
 #pragma unroll
-      for (int d = 0; d < HD; d += 8) {
-        uint4 v = make_uint4(pack_bf16x2(o[d] * inv, o[d + 1] * inv), pack_bf16x2(o[d + 2] * inv, o[d + 3] * inv),
-                             pack_bf16x2(o[d + 4] * inv, o[d + 5] * inv), pack_bf16x2(o[d + 6] * inv, o[d + 7] * inv));
-        *reinterpret_cast<uint4*>(orow + d) = v;
+      for (int cc = 0; cc < HD / 32; ++cc) {
+        uint32_t ov[32];
+        tmem_ld_32x32b_x32(o_col + cc * 32, ov);
+        tmem_ld_wait();
+#pragma unroll
+        for (int d = 0; d < 32; d += 8) {
+          uint4 v = make_uint4(
+              pack_bf16x2(__uint_as_float(ov[d]) * inv, __uint_as_float(ov[d + 1]) * inv),
+              pack_bf16x2(__uint_as_float(ov[d + 2]) * inv, __uint_as_float(ov[d + 3]) * inv),
+              pack_bf16x2(__uint_as_float(ov[d + 4]) * inv, __uint_as_float(ov[d + 5]) * inv),
+              pack_bf16x2(__uint_as_float(ov[d + 6]) * inv, __uint_as_float(ov[d + 7]) * inv));
+          *reinterpret_cast<uint4*>(orow + cc * 32 + d) = v;
+        }
       }
       lse[(long long)bh * S + q] = m * scale + logf(l);
     }
@@ -245,7 +286,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 5) tmem_dealloc(tmem, 512);
+  if (warp == 9) tmem_dealloc(tmem, 512);
 }
 
 }  // namespace fa
@@ -283,21 +324,21 @@ static int fa_launch(const void* qkv, long long ld, void* out, long long ld_o, f
     cudaFuncSetAttribute(fa::attn_fwd_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     attr = true;
   }
-  dim3 grid(S / fa::kBQ, B * H);
+  dim3 grid(B * H, S / (2 * fa::kBQ));
   fa::attn_fwd_tc_kernel<HD><<<grid, fa::kThreads, C::SMEM, s>>>(tm, reinterpret_cast<__nv_bfloat16*>(out), ld_o,
                                                                    lse, S, H, scale, err);
-  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : -(1000 + static_cast<int>(e));
 }
 
 }  // namespace pcb
 
 // Same contract as pcb_attn_fwd (qkv [B*S, 3*H*HD] bf16 with q|k|v column blocks, out [B*S, H*HD]
-// bf16, lse [B*H, S] fp32), on tcgen05.  S % 128 == 0, HD in {64, 128}, row strides % 8 == 0.
+// bf16, lse [B*H, S] fp32), on tcgen05.  S % 256 == 0, HD == 64, row strides % 8 == 0.
 int pcb_attn_fwd_tc(const void* qkv, long long ld, void* out, long long ld_o, float* lse, int B, int S, int H,
                     int HD, float scale, int* err, cudaStream_t s) {
-  if (S % 128 != 0 || ld % 8 || ld_o % 8) return -1;
+  if (S % 256 != 0 || ld % 8 || ld_o % 8) return -1;
   if (reinterpret_cast<uintptr_t>(qkv) & 15) return -1;
   if (HD == 64) return pcb::fa_launch<64>(qkv, ld, out, ld_o, lse, B, S, H, scale, err, s);
-  if (HD == 128) return pcb::fa_launch<128>(qkv, ld, out, ld_o, lse, B, S, H, scale, err, s);
   return -1;
 }

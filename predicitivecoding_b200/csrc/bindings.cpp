@@ -554,16 +554,17 @@ void tp_reduce_norm(const at::Tensor& slots, int64_t world, const c10::optional<
 }
 
 
-// tcgen05 flash-attention forward (same contract as attn_fwd)
-void attn_fwd_tc(const at::Tensor& qkv, at::Tensor& out, at::Tensor& lse, int64_t B, int64_t S, int64_t H, int64_t HD,
-                 double scale, const c10::optional<at::Tensor>& err) {
+// tcgen05 flash-attention forward (same contract as attn_fwd).  Returns the launcher's status
+// (0 ok, -1 unsupported shape, -5 tensor-map encode failure, -(1000 + cudaError) launch failure)
+// instead of raising, so the Python caller reports it.
+int64_t attn_fwd_tc(const at::Tensor& qkv, at::Tensor& out, at::Tensor& lse, int64_t B, int64_t S, int64_t H,
+                    int64_t HD, double scale, const c10::optional<at::Tensor>& err) {
   req(qkv, at::kBFloat16, "qkv");
   req(out, at::kBFloat16, "out");
   reqc(lse, at::kFloat, "lse");
-  check(pcb_attn_fwd_tc(qkv.data_ptr(), row_stride(qkv, "qkv"), out.data_ptr(), row_stride(out, "out"),
-                        lse.data_ptr<float>(), B, S, H, HD, (float)scale, err ? err->data_ptr<int>() : nullptr,
-                        cur_stream()),
-        "attn_fwd_tc");
+  return pcb_attn_fwd_tc(qkv.data_ptr(), row_stride(qkv, "qkv"), out.data_ptr(), row_stride(out, "out"),
+                         lse.data_ptr<float>(), B, S, H, HD, (float)scale, err ? err->data_ptr<int>() : nullptr,
+                         cur_stream());
 }
 
 

@@ -159,10 +159,17 @@ def f32_to_bf16(x, y):
 _ATTN_IMPL = os.environ.get("PCB_ATTN", "mma")    # "mma" (mma.sync kernel, faster today) or "tc" (tcgen05)
 
 
+def tc_attention_supported(S: int, HD: int) -> bool:
+    """Shapes the tcgen05 attention kernels take (two 128-query tiles per CTA, head dim 64)."""
+    return S % 256 == 0 and HD == 64
+
+
 def attn_fwd(qkv, out, lse, B, S, H, HD, scale, impl: Optional[str] = None):
     """Causal attention forward; lse [B*H, S] = logsumexp of the scaled scores (for the backward)."""
-    if (impl or _ATTN_IMPL) == "tc":
-        ext().attn_fwd_tc(qkv, out, lse, int(B), int(S), int(H), int(HD), float(scale), None)
+    if (impl or _ATTN_IMPL) == "tc" and tc_attention_supported(S, HD):
+        rc = ext().attn_fwd_tc(qkv, out, lse, int(B), int(S), int(H), int(HD), float(scale), None)
+        if rc != 0:
+            raise RuntimeError(f"attn_fwd_tc failed with status {rc}")
     else:
         ext().attn_fwd(qkv, out, lse, int(B), int(S), int(H), int(HD), float(scale))
 
