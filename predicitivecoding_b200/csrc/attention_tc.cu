@@ -33,7 +33,12 @@ namespace fa {
 constexpr int kBQ = 128;
 constexpr int kBKV = 128;
 constexpr int kStages = 3;
-constexpr int kThreads = 320;
+constexpr int kThreads = 384;  // warpgroups 0, 1: softmax; warpgroup 2: TMA warp, MMA warp, two idle warps
+// Register split (setmaxnreg): launched at 168 per thread (384 x 168 = 64512); warpgroup 2 drops to
+// 56 (frees 4 x 32 x 112 = 14336), the softmax warpgroups rise to 216 (take 2 x 4 x 32 x 48 = 12288).
+constexpr int kRegsCtl = 56;
+constexpr int kRegsSoftmax = 216;
+static_assert(4 * 32 * (2 * kRegsSoftmax + kRegsCtl) <= kThreads * 168, "register split exceeds the launch");
 constexpr int kAtom = 128 * 128;  // bytes of one [128 rows x 64 bf16] swizzled atom
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleLog2 = 8.f;  // move the running max only when it grows by more than 2^8
@@ -105,8 +110,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-
-  if (warp == 8) {
+  if (warp >= 8) {
+    // control warpgroup: registers down, then the TMA warp and the MMA warp
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsCtl));
+    if (warp == 8) {
     if (lane == 0) {
       // ---------------- TMA producer ----------------
       mbar_arrive_expect_tx(q_full, 2 * C::ATOMS * kAtom);
@@ -184,7 +191,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+    }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
     // ---------------- softmax warpgroups: one query row per thread ----------------
     const int w = warp >> 2;                    // 0 = tile A, 1 = tile B
     const int r = threadIdx.x & 127;            // row within the tile == TMEM lane
@@ -210,9 +219,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int e = 0; e < 128; ++e) sv_u[e] = e <= r ? sv_u[e] : __float_as_uint(-INFINITY);
       }
-      float tmax = SV(0);
+      float mx[8];
 #pragma unroll
-      for (int e = 1; e < 128; ++e) tmax = fmaxf(tmax, SV(e));
+      for (int e = 0; e < 8; ++e) mx[e] = SV(e);
+#pragma unroll
+      for (int e = 8; e < 128; ++e) mx[e & 7] = fmaxf(mx[e & 7], SV(e));
+      const float tmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                               fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
       const float m_new = fmaxf(m, tmax);
       const bool grow = (m_new - m) * c > kRescaleLog2;  // always true on the first tile (m = -inf)
       const bool rescale = __any_sync(0xffffffffu, grow);
@@ -223,7 +236,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         l *= corr;
       }
       const float msc = m * c;
-      float rs = 0.f;
+      float rsv[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int ch = 0; ch < 16; ++ch) {  // 16-byte chunk ch = keys 8ch..8ch+7
         uint32_t pk[4];
@@ -231,14 +244,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int e = 0; e < 8; e += 2) {
           const float p0 = ex2_approx(fmaf(SV(ch * 8 + e), c, -msc));
           const float p1 = ex2_approx(fmaf(SV(ch * 8 + e + 1), c, -msc));
-          rs += p0 + p1;
+          rsv[e >> 1] += p0 + p1;
           pk[e >> 1] = pack_bf16x2(p0, p1);
         }
         *reinterpret_cast<uint4*>(prow + (ch >> 3) * kAtom + (((ch & 7) ^ (r & 7)) << 4)) =
             make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
 #undef SV
-      l += rs;
+      l += (rsv[0] + rsv[1]) + (rsv[2] + rsv[3]);
       if (rescale && j > 0) {  // O holds PV(0..j-1): scale it in place (PV_w(j-1) is complete, see above)
 #pragma unroll 1
         for (int cc = 0; cc < HD / 32; ++cc) {
