@@ -163,22 +163,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto issue_s = [&](int w, int qb, int n) {
         const uint32_t kb = k_addr + (n % kStages) * C::ATOMS * kAtom;
         const uint32_t qa = q_addr + (qb * 2 + w) * C::ATOMS * kAtom;
+        const uint64_t ad = make_smem_desc(qa, 16, 1024, 2), bd = make_smem_desc(kb, 16, 1024, 2);
         tc_fence_after();
 #pragma unroll
-        for (int k = 0; k < HD / 16; ++k) {
-          const uint32_t off = (k >> 2) * kAtom + (k & 3) * 32;
-          umma_bf16(tmem + C::TM_S + w * kBKV, make_smem_desc(qa + off, 16, 1024, 2),
-                    make_smem_desc(kb + off, 16, 1024, 2), idesc_s, k > 0 ? 1u : 0u);
+        for (int k = 0; k < HD / 16; ++k) {  // advancing the start address = adding (bytes >> 4) to the descriptor
+          const uint64_t off = ((k >> 2) * kAtom + (k & 3) * 32) >> 4;
+          umma_bf16(tmem + C::TM_S + w * kBKV, ad + off, bd + off, idesc_s, k > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[w]);
       };
       auto issue_pv = [&](int w, int n, bool first) {  // A = P from TMEM (16 keys = 8 columns per step)
         const uint32_t vb = v_addr + (n % kStages) * C::ATOMS * kAtom;
+        const uint64_t bd = make_smem_desc(vb, kAtom, 1024, 2);
         tc_fence_after();
 #pragma unroll
         for (int k = 0; k < kBKV / 16; ++k)
-          umma_bf16_ts(tmem + C::TM_O + w * HD, tmem + C::TM_P + w * 64 + k * 8,
-                       make_smem_desc(vb + k * 2048, kAtom, 1024, 2), idesc_o, (!first || k > 0) ? 1u : 0u);
+          umma_bf16_ts(tmem + C::TM_O + w * HD, tmem + C::TM_P + w * 64 + k * 8, bd + (k * 2048 >> 4), idesc_o,
+                       (!first || k > 0) ? 1u : 0u);
       };
       int qc = 0, kc = 0, ta = 0, tb = 0;
       bool ok = true;

@@ -156,7 +156,7 @@ def f32_to_bf16(x, y):
     ext().f32_to_bf16(x, y)
 
 
-_ATTN_IMPL = os.environ.get("PCB_ATTN", "mma")    # "mma" (mma.sync kernel, faster today) or "tc" (tcgen05)
+_ATTN_IMPL = os.environ.get("PCB_ATTN", "tc")     # "tc" (tcgen05, where the shape allows) or "mma" (mma.sync)
 
 
 def tc_attention_supported(S: int, HD: int) -> bool:
@@ -174,9 +174,16 @@ def attn_fwd(qkv, out, lse, B, S, H, HD, scale, impl: Optional[str] = None):
         ext().attn_fwd(qkv, out, lse, int(B), int(S), int(H), int(HD), float(scale))
 
 
-def attn_bwd(qkv, out, dout, lse, dvec, dq_acc, dqkv, B, S, H, HD, scale, rope_cs=None):
+def attn_bwd(qkv, out, dout, lse, dvec, dq_acc, dqkv, B, S, H, HD, scale, rope_cs=None, impl: Optional[str] = None):
     """Attention backward; with ``rope_cs`` the dq/dk written are w.r.t. the pre-RoPE q/k."""
-    ext().attn_bwd(qkv, out, dout, lse, dvec, dq_acc, dqkv, int(B), int(S), int(H), int(HD), float(scale), rope_cs)
+    if (impl or _ATTN_IMPL) == "tc" and HD == 64 and S % 128 == 0:
+        rc = ext().attn_bwd_tc(qkv, out, dout, lse, dvec, dq_acc, dqkv, int(B), int(S), int(H), int(HD),
+                               float(scale), rope_cs, None)
+        if rc != 0:
+            raise RuntimeError(f"attn_bwd_tc failed with status {rc}")
+    else:
+        ext().attn_bwd(qkv, out, dout, lse, dvec, dq_acc, dqkv, int(B), int(S), int(H), int(HD), float(scale),
+                       rope_cs)
 
 
 # --------------------------------------------------------------------------- serving / small ops
