@@ -575,6 +575,29 @@ int pcb_attn_bwd_rope(const void* qkv, long long ld, const void* out, const void
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
+// The two helper passes of the backward, shared with the tcgen05 main kernel (attention_bwd_tc.cu).
+int pcb_attn_bwd_pre(const void* out, const void* dout, long long ld_o, float* dvec, float* dq_acc, int B, int S,
+                     int H, int HD, cudaStream_t s) {
+  const long long rows = (long long)B * S * H;
+  attn_bwd_pre_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(out),
+                                                                  reinterpret_cast<const __nv_bfloat16*>(dout), ld_o,
+                                                                  dvec, dq_acc, B, S, H, HD);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : -(1000 + static_cast<int>(e));
+}
+
+int pcb_attn_dq_convert(const float* dq_acc, void* dqkv, long long ld_d, int B, int S, int H, int HD,
+                        const float* rope_cs, cudaStream_t s) {
+  const long long total = (long long)B * S * (H * HD / 2);
+  long long blocks = (total + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  attn_dq_convert_kernel<<<(unsigned)blocks, 256, 0, s>>>(dq_acc, reinterpret_cast<__nv_bfloat16*>(dqkv), ld_d,
+                                                          (long long)B * S, H * HD, S, HD,
+                                                          reinterpret_cast<const float2*>(rope_cs));
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : -(1000 + static_cast<int>(e));
+}
+
 int pcb_attn_bwd(const void* qkv, long long ld, const void* out, const void* dout, long long ld_o, const float* lse,
                  float* dvec, float* dq_acc, void* dqkv, long long ld_d, int B, int S, int H, int HD, float scale,
                  cudaStream_t s) {

@@ -1,0 +1,457 @@
+// Causal flash-attention backward on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+//
+// Reference counterpart: PredictiveCoding.Device/Kernels/DeviceTrainKernels.cs (attn_bwd_dq,
+// attn_bwd_dkv: one block per query / per key, fp32 SIMT, P replayed from the logsumexp).
+//
+// Work item = one 128-key tile (kb) of one (batch, head); persistent CTAs walk the items heaviest
+// first (kb = 0 sees every query tile).  For each query tile i >= kb the CTA computes, with the
+// keys on the TMEM lanes:
+//   (1) S^T  = K Q_i^T          M=128 keys, N=128 queries, K=hd     -> TMEM S
+//   (2) dP^T = V dO_i^T         M=128 keys, N=128 queries, K=hd     -> TMEM dP
+//   gradient warpgroup: P^T = 2^(S^T c - lse_i log2 e) (c = scale log2 e), causal mask on the
+//       diagonal tile, dS^T = P^T (dP^T - D_i); P^T goes back to TMEM as bf16 (the A operand of
+//       (3)), dS^T to shared memory in the 128B-swizzled layout that is K-major for (4) and
+//       M-major for (5)
+//   (3) dV  += P^T dO_i         A = P^T from TMEM, B = dO_i (MN-major)
+//   (4) dK  += dS^T Q_i         A = dS^T (K-major), B = Q_i (MN-major)
+//   (5) dQ_i = dS K             A = dS^T read M-major, B = K (MN-major) -> TMEM dQ
+//   dQ warpgroup: dQ_i * scale is added to the fp32 accumulator with vector reductions.
+// After the last query tile the gradient warpgroup writes dK * scale (rotated back by -theta when
+// a RoPE table is given) and dV in bf16.  TMEM: S 128 + dP 128 + P 64 + dV 64 + dK 64 + dQ 64 = 512
+// columns, no aliasing.  The MMA thread issues S/dP of tile i+1 as soon as the gradient warpgroup
+// has read S/dP of tile i, so those MMAs overlap the elementwise work; every other hazard is
+// covered by a commit that follows the MMAs it protects.  Every wait is bounded.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace pcb {
+namespace fab {
+
+constexpr int kT = 128;            // keys per item, queries per tile
+constexpr int kHD = 64;
+constexpr int kThreads = 384;      // WG0 gradient, WG1 dQ, warp 8 TMA, warp 9 MMA, warps 10-11 idle
+constexpr int kAtom = 128 * 128;   // one [128 rows x 64 bf16] swizzled atom
+constexpr float kLog2e = 1.4426950408889634f;
+
+// shared memory
+constexpr int K_OFF = 0;                        // K tile (1 atom)
+constexpr int V_OFF = K_OFF + kAtom;            // V tile
+constexpr int Q_OFF = V_OFF + kAtom;            // 2 stages
+constexpr int DO_OFF = Q_OFF + 2 * kAtom;       // 2 stages
+constexpr int DS_OFF = DO_OFF + 2 * kAtom;      // dS^T: 2 atoms (queries 0-63, 64-127)
+constexpr int VEC_OFF = DS_OFF + 2 * kAtom;     // per stage: lse[128], delta[128] fp32
+constexpr int BAR_OFF = VEC_OFF + 2 * 2 * kT * 4;
+constexpr int SMEM = BAR_OFF + 256 + 1024;
+static_assert(SMEM <= 232448, "shared memory budget");
+
+// TMEM columns
+constexpr int TM_S = 0, TM_DP = 128, TM_P = 256, TM_DV = 320, TM_DK = 384, TM_DQ = 448;
+
+struct Item {
+  int kb, b, h, bh;
+};
+PCB_DEVICE Item item_of(int i, int BH, int H) {
+  Item it;
+  it.kb = i / BH;
+  it.bh = i % BH;
+  it.b = it.bh / H;
+  it.h = it.bh % H;
+  return it;
+}
+
+PCB_DEVICE void bulk_load(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(smem_dst)),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+PCB_DEVICE void red_add_v4(float* addr, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
+                       const float* __restrict__ lse, const float* __restrict__ dvec, float* __restrict__ dq_acc,
+                       __nv_bfloat16* __restrict__ dqkv, long long ld_d, int S, int H, float scale,
+                       const float2* __restrict__ rope_cs, int BH, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem + K_OFF;
+  uint8_t* sV = smem + V_OFF;
+  uint8_t* sQ = smem + Q_OFF;
+  uint8_t* sDO = smem + DO_OFF;
+  uint8_t* sDS = smem + DS_OFF;
+  float* sVec = reinterpret_cast<float*>(smem + VEC_OFF);  // [stage][lse 128 | delta 128]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BAR_OFF);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* kv_empty = bars + 1;
+  uint64_t* ld_full = bars + 2;    // [2]
+  uint64_t* ld_empty = bars + 4;   // [2]
+  uint64_t* s_full = bars + 6;
+  uint64_t* s_free = bars + 7;
+  uint64_t* ds_full = bars + 8;
+  uint64_t* grad_done = bars + 9;
+  uint64_t* dq_full = bars + 10;
+  uint64_t* dq_empty = bars + 11;
+  uint64_t* acc_full = bars + 12;  // dK / dV of the item complete
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int T = S / kT;
+  const int n_items = T * BH;
+  const int D = H * kHD;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    mbar_init(kv_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&ld_full[i], 1);
+      mbar_init(&ld_empty[i], 1 + 4);  // MMA commit + the 4 gradient warps (lse / delta read)
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 4);
+    mbar_init(ds_full, 4);
+    mbar_init(grad_done, 1);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_empty, 4);
+    mbar_init(acc_full, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 8 && lane == 0) {
+    prefetch_tmap(&tm_qkv);
+    prefetch_tmap(&tm_do);
+  }
+  if (warp == 9) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 8) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      int ic = 0, lc = 0;
+      bool ok = true;
+      for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++ic) {
+        const Item it = item_of(i, BH, H);
+        if (!(ok = mbar_wait(kv_empty, (ic & 1) ^ 1u, err, kErrTimeoutEmpty, abort_flag))) break;
+        mbar_arrive_expect_tx(kv_full, 2 * kAtom);
+        const int krow = it.b * S + it.kb * kT;
+        tma_load_2d(sK, &tm_qkv, kv_full, (H + it.h) * kHD, krow);
+        tma_load_2d(sV, &tm_qkv, kv_full, (2 * H + it.h) * kHD, krow);
+        for (int qi = it.kb; qi < T; ++qi, ++lc) {
+          const int st = lc & 1;
+          if (!(ok = mbar_wait(&ld_empty[st], ((lc >> 1) & 1) ^ 1u, err, kErrTimeoutEmpty, abort_flag))) break;
+          mbar_arrive_expect_tx(&ld_full[st], 2 * kAtom + 2 * kT * 4);
+          const int qrow = it.b * S + qi * kT;
+          tma_load_2d(sQ + st * kAtom, &tm_qkv, &ld_full[st], it.h * kHD, qrow);
+          tma_load_2d(sDO + st * kAtom, &tm_do, &ld_full[st], it.h * kHD, qrow);
+          bulk_load(sVec + st * 2 * kT, lse + (long long)it.bh * S + qi * kT, kT * 4, &ld_full[st]);
+          bulk_load(sVec + st * 2 * kT + kT, dvec + (long long)it.bh * S + qi * kT, kT * 4, &ld_full[st]);
+        }
+      }
+    }
+  } else if (warp == 9) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      constexpr uint32_t idesc_kk = make_idesc_bf16(128, 128, 0, 0);  // S^T, dP^T: both operands K-major
+      constexpr uint32_t idesc_ts = make_idesc_bf16(128, kHD, 0, 1);  // dV: A TMEM, B MN-major
+      constexpr uint32_t idesc_dk = make_idesc_bf16(128, kHD, 0, 1);  // dK: A K-major, B MN-major
+      constexpr uint32_t idesc_dq = make_idesc_bf16(128, kHD, 1, 1);  // dQ: A M-major, B MN-major
+      const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV), q_addr = smem_u32(sQ), do_addr = smem_u32(sDO),
+                     ds_addr = smem_u32(sDS);
+      int ic = 0, lc = 0, tcount = 0;  // items, loaded tiles, tiles processed (phase counters)
+      bool ok = true;
+      auto grad = [&](int v, int st, bool first) -> bool {  // MMAs (3)(4)(5) of the tile with counter v
+        if (!mbar_wait(ds_full, v & 1, err, kErrTimeoutTmemEmpty, abort_flag)) return false;
+        tc_fence_after();
+        const uint64_t bdo = make_smem_desc(do_addr + st * kAtom, kAtom, 1024, 2);
+        const uint64_t bq = make_smem_desc(q_addr + st * kAtom, kAtom, 1024, 2);
+        const uint64_t ads = make_smem_desc(ds_addr, 16, 1024, 2);
+#pragma unroll
+        for (int k = 0; k < kT / 16; ++k) {  // (3) dV += P^T dO_i
+          umma_bf16_ts(tmem + TM_DV, tmem + TM_P + k * 8, bdo + (k * 2048 >> 4), idesc_ts,
+                       (!first || k > 0) ? 1u : 0u);
+        }
+#pragma unroll
+        for (int k = 0; k < kT / 16; ++k) {  // (4) dK += dS^T Q_i
+          const uint32_t off = (k >> 2) * kAtom + (k & 3) * 32;
+          umma_bf16(tmem + TM_DK, ads + (off >> 4), bq + (k * 2048 >> 4), idesc_dk, (!first || k > 0) ? 1u : 0u);
+        }
+        if (v > 0 && !mbar_wait(dq_empty, (v - 1) & 1, err, kErrTimeoutTmemEmpty, abort_flag)) return false;
+        tc_fence_after();
+        const uint64_t adq = make_smem_desc(ds_addr, kAtom, 1024, 2);
+        const uint64_t bk = make_smem_desc(k_addr, kAtom, 1024, 2);
+#pragma unroll
+        for (int k = 0; k < kT / 16; ++k)  // (5) dQ_i = dS K
+          umma_bf16(tmem + TM_DQ, adq + (k * 2048 >> 4), bk + (k * 2048 >> 4), idesc_dq, k > 0 ? 1u : 0u);
+        umma_commit(dq_full);
+        umma_commit(grad_done);  // (3)(4)(5) have read P and dS of this tile
+        umma_commit(&ld_empty[st]);
+        return true;
+      };
+      for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++ic) {
+        const Item it = item_of(i, BH, H);
+        if (!(ok = mbar_wait(kv_full, ic & 1, err, kErrTimeoutFull, abort_flag))) break;
+        const uint64_t ak = make_smem_desc(k_addr, 16, 1024, 2), av = make_smem_desc(v_addr, 16, 1024, 2);
+        int prev_st = 0;
+        for (int qi = it.kb; qi < T && ok; ++qi, ++lc, ++tcount) {
+          const int st = lc & 1;
+          if (!(ok = mbar_wait(&ld_full[st], (lc >> 1) & 1, err, kErrTimeoutFull, abort_flag))) break;
+          // S/dP may be overwritten once the gradient warpgroup has read the previous tile's
+          if (tcount > 0 && !(ok = mbar_wait(s_free, (tcount - 1) & 1, err, kErrTimeoutTmemEmpty, abort_flag))) break;
+          tc_fence_after();
+          const uint64_t bq = make_smem_desc(q_addr + st * kAtom, 16, 1024, 2);
+          const uint64_t bdo = make_smem_desc(do_addr + st * kAtom, 16, 1024, 2);
+#pragma unroll
+          for (int k = 0; k < kHD / 16; ++k) {  // (1) S^T = K Q_i^T, (2) dP^T = V dO_i^T
+            const uint64_t off = ((k & 3) * 32) >> 4;
+            umma_bf16(tmem + TM_S, ak + off, bq + off, idesc_kk, k > 0 ? 1u : 0u);
+            umma_bf16(tmem + TM_DP, av + off, bdo + off, idesc_kk, k > 0 ? 1u : 0u);
+          }
+          umma_commit(s_full);
+          if (qi > it.kb && !(ok = grad(tcount - 1, prev_st, qi - 1 == it.kb))) break;
+          prev_st = st;
+        }
+        if (!ok) break;
+        if (!(ok = grad(tcount - 1, prev_st, T - 1 == it.kb))) break;
+        umma_commit(acc_full);
+        umma_commit(kv_empty);
+      }
+    }
+  } else if (warp < 4) {
+    // ---------------- gradient warpgroup: thread = key row = TMEM lane ----------------
+    const int r = threadIdx.x;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    const float c = scale * kLog2e;
+    int ic = 0, lc = 0, tcount = 0;
+    bool ok = true;
+    for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++ic) {
+      const Item it = item_of(i, BH, H);
+      for (int qi = it.kb; qi < T; ++qi, ++lc, ++tcount) {
+        const int st = lc & 1;
+        ok = mbar_wait(&ld_full[st], (lc >> 1) & 1, err, kErrTimeoutFull, abort_flag) &&
+             mbar_wait(s_full, tcount & 1, err, kErrTimeoutTmemFull, abort_flag);
+        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+        tc_fence_after();
+        const float* sl = sVec + st * 2 * kT;
+        const float* sd = sl + kT;
+        const bool diag = qi == it.kb;
+#pragma unroll 1
+        for (int qt = 0; qt < 4; ++qt) {  // 32 query columns at a time
+          uint32_t su[32], du[32];
+          tmem_ld_32x32b_x32(lane_base + TM_S + qt * 32, su);
+          tmem_ld_32x32b_x32(lane_base + TM_DP + qt * 32, du);
+          tmem_ld_wait();
+          if (qt == 3) {  // S/dP of this tile are all in registers: the next tile's MMAs may start
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(s_free);
+          }
+          if (qt == 0 && tcount > 0) {
+            // P / dS of the previous tile must have been consumed by its MMAs (3)(4)(5)
+            ok = mbar_wait(grad_done, (tcount - 1) & 1, err, kErrTimeoutTmemFull, abort_flag);
+            if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+            tc_fence_after();
+          }
+          uint32_t pk[16], dk[16];
+#pragma unroll
+          for (int e = 0; e < 32; e += 4) {
+            const int q = qt * 32 + e;  // query column
+            const float4 l4 = *reinterpret_cast<const float4*>(sl + q);
+            const float4 d4 = *reinterpret_cast<const float4*>(sd + q);
+            const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv[4] = {d4.x, d4.y, d4.z, d4.w};
+            float p[4], ds[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const bool vis = !diag || r <= q + u;
+              p[u] = vis ? ex2_approx(fmaf(__uint_as_float(su[e + u]), c, -lv[u] * kLog2e)) : 0.f;
+              ds[u] = p[u] * (__uint_as_float(du[e + u]) - dv[u]);
+            }
+            pk[e >> 1] = pack_bf16x2(p[0], p[1]);
+            pk[(e >> 1) + 1] = pack_bf16x2(p[2], p[3]);
+            dk[e >> 1] = pack_bf16x2(ds[0], ds[1]);
+            dk[(e >> 1) + 1] = pack_bf16x2(ds[2], ds[3]);
+          }
+          tmem_st_32x32b_x16(lane_base + TM_P + qt * 16, pk);
+          // dS^T row r: queries 64*(qt/2).. live in atom qt/2; 16-byte chunk = 8 queries, swizzled by (r & 7)
+          uint8_t* drow = sDS + (qt >> 1) * kAtom + r * 128;
+#pragma unroll
+          for (int ch = 0; ch < 4; ++ch) {
+            const int chunk = (qt & 1) * 4 + ch;
+            *reinterpret_cast<uint4*>(drow + ((chunk ^ (r & 7)) << 4)) =
+                make_uint4(dk[4 * ch], dk[4 * ch + 1], dk[4 * ch + 2], dk[4 * ch + 3]);
+          }
+        }
+        if (!ok) break;
+        tmem_st_wait();
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(ds_full);
+          mbar_arrive(&ld_empty[st]);  // lse / delta of this stage are no longer read
+        }
+      }
+      if (!ok) break;
+      // ---- dK, dV of this key tile ----
+      ok = mbar_wait(acc_full, ic & 1, err, kErrTimeoutTmemFull, abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+      tc_fence_after();
+      const long long row = (long long)it.b * S + it.kb * kT + r;
+      __nv_bfloat16* dkp = dqkv + row * ld_d + D + it.h * kHD;
+      __nv_bfloat16* dvp = dqkv + row * ld_d + 2 * D + it.h * kHD;
+      const int pos = it.kb * kT + r;
+#pragma unroll 1
+      for (int cc = 0; cc < kHD / 32; ++cc) {
+        uint32_t ku[32], vu[32];
+        tmem_ld_32x32b_x32(lane_base + TM_DK + cc * 32, ku);
+        tmem_ld_32x32b_x32(lane_base + TM_DV + cc * 32, vu);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; e += 8) {
+          float kv[8];
+#pragma unroll
+          for (int u = 0; u < 8; u += 2) {
+            float a0 = __uint_as_float(ku[e + u]) * scale, a1 = __uint_as_float(ku[e + u + 1]) * scale;
+            if (rope_cs != nullptr) {  // k was rotated by +theta in the forward: rotate its gradient by -theta
+              const float2 cs = rope_cs[pos * (kHD / 2) + ((cc * 32 + e + u) >> 1)];
+              const float b0 = a0 * cs.x + a1 * cs.y, b1 = -a0 * cs.y + a1 * cs.x;
+              a0 = b0;
+              a1 = b1;
+            }
+            kv[u] = a0;
+            kv[u + 1] = a1;
+          }
+          *reinterpret_cast<uint4*>(dkp + cc * 32 + e) =
+              make_uint4(pack_bf16x2(kv[0], kv[1]), pack_bf16x2(kv[2], kv[3]), pack_bf16x2(kv[4], kv[5]),
+                         pack_bf16x2(kv[6], kv[7]));
+          *reinterpret_cast<uint4*>(dvp + cc * 32 + e) = make_uint4(
+              pack_bf16x2(__uint_as_float(vu[e]), __uint_as_float(vu[e + 1])),
+              pack_bf16x2(__uint_as_float(vu[e + 2]), __uint_as_float(vu[e + 3])),
+              pack_bf16x2(__uint_as_float(vu[e + 4]), __uint_as_float(vu[e + 5])),
+              pack_bf16x2(__uint_as_float(vu[e + 6]), __uint_as_float(vu[e + 7])));
+        }
+      }
+      tc_fence_before();
+    }
+  } else if (warp < 8) {
+    // ---------------- dQ warpgroup: thread = query row = TMEM lane ----------------
+    const int r = threadIdx.x - 128;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    int tcount = 0;
+    bool ok = true;
+    for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
+      const Item it = item_of(i, BH, H);
+      for (int qi = it.kb; qi < T; ++qi, ++tcount) {
+        ok = mbar_wait(dq_full, tcount & 1, err, kErrTimeoutTmemFull, abort_flag);
+        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+        tc_fence_after();
+        uint32_t qu[64];
+        tmem_ld_32x32b_x32(lane_base + TM_DQ, *reinterpret_cast<uint32_t(*)[32]>(qu));
+        tmem_ld_32x32b_x32(lane_base + TM_DQ + 32, *reinterpret_cast<uint32_t(*)[32]>(qu + 32));
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(dq_empty);
+        float* dq = dq_acc + ((long long)it.b * S + qi * kT + r) * D + it.h * kHD;
+#pragma unroll
+        for (int e = 0; e < 64; e += 4)
+          red_add_v4(dq + e, __uint_as_float(qu[e]) * scale, __uint_as_float(qu[e + 1]) * scale,
+                     __uint_as_float(qu[e + 2]) * scale, __uint_as_float(qu[e + 3]) * scale);
+      }
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 9) tmem_dealloc(tmem, 512);
+}
+
+}  // namespace fab
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn_fab() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+static bool encode_rows(PFN_cuTensorMapEncodeTiled_v12000 fn, CUtensorMap* tm, const void* base, long long cols,
+                        long long rows, long long ld) {
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+  cuuint32_t box[2] = {64, 128};
+  cuuint32_t es[2] = {1, 1};
+  return fn(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace pcb
+
+// Preprocess (delta = rowsum(dO * O), zeroed dQ accumulator) and the dQ conversion live with the
+// mma.sync backward; this file only replaces its main kernel.
+int pcb_attn_bwd_pre(const void* out, const void* dout, long long ld_o, float* dvec, float* dq_acc, int B, int S,
+                     int H, int HD, cudaStream_t s);
+int pcb_attn_dq_convert(const float* dq_acc, void* dqkv, long long ld_d, int B, int S, int H, int HD,
+                        const float* rope_cs, cudaStream_t s);
+
+// Same contract as pcb_attn_bwd_rope, on tcgen05: S % 128 == 0, HD == 64, row strides % 8 == 0.
+// Returns 0, -1 (unsupported shape), -5 (tensor-map encode) or -(1000 + cudaError) (launch).
+int pcb_attn_bwd_tc(const void* qkv, long long ld, const void* out, const void* dout, long long ld_o,
+                    const float* lse, float* dvec, float* dq_acc, void* dqkv, long long ld_d, int B, int S, int H,
+                    int HD, float scale, const float* rope_cs, int* err, cudaStream_t s) {
+  using namespace pcb;
+  if (HD != 64 || S % 128 != 0 || ld % 8 || ld_o % 8 || ld_d % 8) return -1;
+  if ((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(dout) | reinterpret_cast<uintptr_t>(lse) |
+       reinterpret_cast<uintptr_t>(dvec) | reinterpret_cast<uintptr_t>(dq_acc)) & 15)
+    return -1;
+  int r = pcb_attn_bwd_pre(out, dout, ld_o, dvec, dq_acc, B, S, H, HD, s);
+  if (r) return r;
+  auto fn = encode_fn_fab();
+  if (!fn) return -5;
+  CUtensorMap tq, td;
+  if (!encode_rows(fn, &tq, qkv, 3LL * H * HD, (long long)B * S, ld) ||
+      !encode_rows(fn, &td, dout, (long long)H * HD, (long long)B * S, ld_o))
+    return -5;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(fab::attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fab::SMEM);
+    attr = true;
+  }
+  static int num_sms = 0;
+  if (num_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (num_sms <= 0) num_sms = 148;
+  }
+  const int n_items = B * H * (S / fab::kT);
+  const int grid = n_items < num_sms ? n_items : num_sms;  // persistent: one CTA per SM
+  fab::attn_bwd_tc_kernel<<<grid, fab::kThreads, fab::SMEM, s>>>(tq, td, lse, dvec, dq_acc,
+                                                                  reinterpret_cast<__nv_bfloat16*>(dqkv), ld_d, S, H,
+                                                                  scale, reinterpret_cast<const float2*>(rope_cs),
+                                                                  B * H, err);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return -(1000 + static_cast<int>(e));
+  return pcb_attn_dq_convert(dq_acc, dqkv, ld_d, B, S, H, HD, rope_cs, s);
+}

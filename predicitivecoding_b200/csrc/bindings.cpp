@@ -65,6 +65,9 @@ int pcb_tp_reduce_norm(const void* slots, int world, int rows, int D, const floa
                        cudaStream_t s);
 int pcb_attn_fwd_tc(const void* qkv, long long ld, void* out, long long ld_o, float* lse, int B, int S, int H,
                     int HD, float scale, int* err, cudaStream_t s);
+int pcb_attn_bwd_tc(const void* qkv, long long ld, const void* out, const void* dout, long long ld_o,
+                    const float* lse, float* dvec, float* dq_acc, void* dqkv, long long ld_d, int B, int S, int H,
+                    int HD, float scale, const float* rope_cs, int* err, cudaStream_t s);
 int pcb_annotate(uint8_t* img, int W, int H, const int* boxes, int n, int thickness, const int* segs, int m,
                  const uint8_t* colors, int* owner, cudaStream_t s);
 int pcb_alloc(int device, size_t bytes, void* stream, void** out);
@@ -568,6 +571,26 @@ int64_t attn_fwd_tc(const at::Tensor& qkv, at::Tensor& out, at::Tensor& lse, int
 }
 
 
+// tcgen05 attention backward (same contract as attn_bwd); returns the launcher status like attn_fwd_tc.
+int64_t attn_bwd_tc(const at::Tensor& qkv, const at::Tensor& out, const at::Tensor& dout, const at::Tensor& lse,
+                    at::Tensor& dvec, at::Tensor& dq_acc, at::Tensor& dqkv, int64_t B, int64_t S, int64_t H,
+                    int64_t HD, double scale, const c10::optional<at::Tensor>& rope_cs,
+                    const c10::optional<at::Tensor>& err) {
+  req(qkv, at::kBFloat16, "qkv");
+  req(out, at::kBFloat16, "out");
+  req(dout, at::kBFloat16, "dout");
+  req(dqkv, at::kBFloat16, "dqkv");
+  reqc(lse, at::kFloat, "lse");
+  reqc(dvec, at::kFloat, "dvec");
+  reqc(dq_acc, at::kFloat, "dq_acc");
+  return pcb_attn_bwd_tc(qkv.data_ptr(), row_stride(qkv, "qkv"), out.data_ptr(), dout.data_ptr(),
+                         row_stride(dout, "dout"), lse.data_ptr<float>(), dvec.data_ptr<float>(),
+                         dq_acc.data_ptr<float>(), dqkv.data_ptr(), row_stride(dqkv, "dqkv"), B, S, H, HD,
+                         (float)scale, rope_cs ? rope_cs->data_ptr<float>() : nullptr,
+                         err ? err->data_ptr<int>() : nullptr, cur_stream());
+}
+
+
 // box outlines + segments rasterised onto a device RGB image (annotation)
 void annotate(at::Tensor& img, const at::Tensor& boxes, int64_t thickness, const at::Tensor& segs,
               const at::Tensor& colors, at::Tensor& owner) {
@@ -603,6 +626,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("f32_to_bf16", &f32_to_bf16);
   m.def("attn_fwd", &attn_fwd);
   m.def("attn_fwd_tc", &attn_fwd_tc);
+  m.def("attn_bwd_tc", &attn_bwd_tc);
   m.def("attn_bwd", &attn_bwd);
   m.def("launch_count", &launch_count);
   m.def("set_gemm_mode", [](int64_t m) { pcb_set_gemm_mode((int)m); },

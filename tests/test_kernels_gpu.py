@@ -259,7 +259,7 @@ def test_attention_fwd_bwd(hd, impl):
     dqkv = torch.zeros(B * S, 3 * D, device=DEV, dtype=torch.bfloat16)
     dvec = torch.empty(B * H, S, device=DEV)
     dq_acc = torch.empty(B * S, D, device=DEV)
-    ops.attn_bwd(qkv, out, do, lse, dvec, dq_acc, dqkv, B, S, H, hd, scale)
+    ops.attn_bwd(qkv, out, do, lse, dvec, dq_acc, dqkv, B, S, H, hd, scale, impl=impl)
     torch.cuda.synchronize()
     for i, t in enumerate((q, k, v)):
         ref_g = t.grad.transpose(1, 2).reshape(B * S, D)
@@ -288,6 +288,50 @@ def test_attention_tc_long_sequence(S, mag):
     assert int(err.item()) == 0
     assert rel_err(out, ref) < 0.02
     assert rel_err(lse.view(B, H, S), torch.logsumexp(s, -1)) < 1e-3
+
+
+@pytest.mark.parametrize("S,B,H", [(1024, 2, 3), (384, 3, 2)])
+def test_attention_bwd_tc_matches_autograd(S, B, H):
+    """tcgen05 backward over many key/query tiles (persistent CTAs, 2-stage Q/dO ring, dQ reductions),
+    with and without the RoPE rotation of dq/dk."""
+    hd = 64
+    D = H * hd
+    g = torch.Generator(device=DEV).manual_seed(S + B)
+    qkv = torch.randn(B * S, 3 * D, device=DEV, generator=g).to(torch.bfloat16)
+    scale = 1 / math.sqrt(hd)
+    out = torch.empty(B * S, D, device=DEV, dtype=torch.bfloat16)
+    lse = torch.empty(B * H, S, device=DEV)
+    ops.attn_fwd(qkv, out, lse, B, S, H, hd, scale, impl="mma")
+    do = torch.randn(B * S, D, device=DEV, generator=g).to(torch.bfloat16)
+    q, k, v = (qkv.float()[:, i * D:(i + 1) * D].view(B, S, H, hd).transpose(1, 2).clone().requires_grad_()
+               for i in range(3))
+    s = ((q @ k.transpose(-1, -2)) * scale).masked_fill(
+        torch.ones(S, S, dtype=torch.bool, device=DEV).triu(1), float("-inf"))
+    (torch.softmax(s, -1) @ v).backward(do.float().view(B, S, H, hd).transpose(1, 2))
+    ref = [t.grad.transpose(1, 2).reshape(B * S, D) for t in (q, k, v)]
+    pos = torch.arange(S, device=DEV, dtype=torch.float32)
+    inv = 10000.0 ** (-torch.arange(0, hd, 2, device=DEV, dtype=torch.float32) / hd)
+    ang = pos[:, None] * inv[None, :]
+    cs = torch.stack([ang.cos(), ang.sin()], -1).contiguous()          # [S, hd/2, 2]
+    for rope in (None, cs):
+        dqkv = torch.zeros(B * S, 3 * D, device=DEV, dtype=torch.bfloat16)
+        dvec = torch.empty(B * H, S, device=DEV)
+        dq_acc = torch.empty(B * S, D, device=DEV)
+        err = torch.zeros(1, dtype=torch.int32, device=DEV)
+        rc = ops.ext().attn_bwd_tc(qkv, out, do, lse, dvec, dq_acc, dqkv, B, S, H, hd, scale, rope, err)
+        torch.cuda.synchronize()
+        assert rc == 0 and int(err.item()) == 0
+        got = [dqkv[:, i * D:(i + 1) * D].float() for i in range(3)]
+        if rope is not None:  # rotate the reference dq, dk by -theta
+            c, s_ = cs[..., 0].repeat(B, 1), cs[..., 1].repeat(B, 1)
+            for i in (0, 1):
+                x = ref[i].view(B * S, H, hd // 2, 2)
+                a, b = x[..., 0], x[..., 1]
+                ref_i = torch.stack([a * c[:, None] + b * s_[:, None], -a * s_[:, None] + b * c[:, None]], -1)
+                assert rel_err(got[i], ref_i.reshape(B * S, D)) < 0.03
+        else:
+            for i in range(3):
+                assert rel_err(got[i], ref[i]) < 0.03, ("qkv"[i], rel_err(got[i], ref[i]))
 
 
 def test_embed_fwd_bwd():
