@@ -16,8 +16,10 @@
 //   (4) dK  += dS^T Q_i         A = dS^T (K-major), B = Q_i (MN-major)
 //   (5) dQ_i = dS K             A = dS^T read M-major, B = K (MN-major) -> TMEM dQ
 //   dQ warpgroup: dQ_i * scale is added to the fp32 accumulator with vector reductions.
-// After the last query tile the gradient warpgroup writes dK * scale (rotated back by -theta when
-// a RoPE table is given) and dV in bf16.  TMEM: S 128 + dP 128 + P 64 + dV 64 + dK 64 + dQ 64 = 512
+// Two gradient warpgroups share the elementwise work (query columns 0-63 and 64-127).  After the
+// last query tile they write dK * scale (rotated back by -theta when a RoPE table is given) and dV
+// in bf16.  dS^T is double-buffered in shared memory, so a tile's gradient math waits only for the
+// previous tile's dV MMA (which read P) before storing.  TMEM: S 128 + dP 128 + P 64 + dV 64 + dK 64 + dQ 64 = 512
 // columns, no aliasing.  The MMA thread issues S/dP of tile i+1 as soon as the gradient warpgroup
 // has read S/dP of tile i, so those MMAs overlap the elementwise work; every other hazard is
 // covered by a commit that follows the MMAs it protects.  Every wait is bounded.
@@ -32,7 +34,8 @@ namespace fab {
 
 constexpr int kT = 128;            // keys per item, queries per tile
 constexpr int kHD = 64;
-constexpr int kThreads = 384;      // WG0 gradient, WG1 dQ, warp 8 TMA, warp 9 MMA, warps 10-11 idle
+constexpr int kThreads = 512;  // WG0/WG1 gradient (query columns 0-63 / 64-127), WG2 dQ, warp 12 TMA, warp 13 MMA
+constexpr int kTmaWarp = 12, kMmaWarp = 13;
 constexpr int kAtom = 128 * 128;   // one [128 rows x 64 bf16] swizzled atom
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -41,8 +44,8 @@ constexpr int K_OFF = 0;                        // K tile (1 atom)
 constexpr int V_OFF = K_OFF + kAtom;            // V tile
 constexpr int Q_OFF = V_OFF + kAtom;            // 2 stages
 constexpr int DO_OFF = Q_OFF + 2 * kAtom;       // 2 stages
-constexpr int DS_OFF = DO_OFF + 2 * kAtom;      // dS^T: 2 atoms (queries 0-63, 64-127)
-constexpr int VEC_OFF = DS_OFF + 2 * kAtom;     // per stage: lse[128], delta[128] fp32
+constexpr int DS_OFF = DO_OFF + 2 * kAtom;      // dS^T, 2 buffers x 2 atoms (queries 0-63, 64-127)
+constexpr int VEC_OFF = DS_OFF + 4 * kAtom;     // per stage: lse[128], delta[128] fp32
 constexpr int BAR_OFF = VEC_OFF + 2 * 2 * kT * 4;
 constexpr int SMEM = BAR_OFF + 256 + 1024;
 static_assert(SMEM <= 232448, "shared memory budget");
@@ -95,11 +98,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* s_full = bars + 6;
   uint64_t* s_free = bars + 7;
   uint64_t* ds_full = bars + 8;
-  uint64_t* grad_done = bars + 9;
+  uint64_t* grad_done = bars + 13;  // [2]: per dS buffer, after (4)(5) of a tile read it
+  uint64_t* p_done = bars + 9;      // after (3) read P
   uint64_t* dq_full = bars + 10;
   uint64_t* dq_empty = bars + 11;
   uint64_t* acc_full = bars + 12;  // dK / dV of the item complete
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -112,23 +116,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(kv_empty, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&ld_full[i], 1);
-      mbar_init(&ld_empty[i], 1 + 4);  // MMA commit + the 4 gradient warps (lse / delta read)
+      mbar_init(&ld_empty[i], 1 + 8);  // MMA commit + the 8 gradient warps (lse / delta read)
+      mbar_init(&grad_done[i], 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(s_free, 4);
-    mbar_init(ds_full, 4);
-    mbar_init(grad_done, 1);
+    mbar_init(s_free, 8);
+    mbar_init(ds_full, 8);
+    mbar_init(p_done, 1);
     mbar_init(dq_full, 1);
     mbar_init(dq_empty, 4);
     mbar_init(acc_full, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 8 && lane == 0) {
+  if (warp == kTmaWarp && lane == 0) {
     prefetch_tmap(&tm_qkv);
     prefetch_tmap(&tm_do);
   }
-  if (warp == 9) {
+  if (warp == kMmaWarp) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -137,7 +142,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 8) {
+  if (warp == kTmaWarp) {
     if (lane == 0) {
       // ---------------- TMA producer ----------------
       int ic = 0, lc = 0;
@@ -161,7 +166,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == kMmaWarp) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
       constexpr uint32_t idesc_kk = make_idesc_bf16(128, 128, 0, 0);  // S^T, dP^T: both operands K-major
@@ -177,12 +182,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint64_t bdo = make_smem_desc(do_addr + st * kAtom, kAtom, 1024, 2);
         const uint64_t bq = make_smem_desc(q_addr + st * kAtom, kAtom, 1024, 2);
-        const uint64_t ads = make_smem_desc(ds_addr, 16, 1024, 2);
+        const uint32_t dsb = ds_addr + (v & 1) * 2 * kAtom;
+        const uint64_t ads = make_smem_desc(dsb, 16, 1024, 2);
 #pragma unroll
         for (int k = 0; k < kT / 16; ++k) {  // (3) dV += P^T dO_i
           umma_bf16_ts(tmem + TM_DV, tmem + TM_P + k * 8, bdo + (k * 2048 >> 4), idesc_ts,
                        (!first || k > 0) ? 1u : 0u);
         }
+        umma_commit(p_done);  // (3) has read P: the next tile's P may be written
 #pragma unroll
         for (int k = 0; k < kT / 16; ++k) {  // (4) dK += dS^T Q_i
           const uint32_t off = (k >> 2) * kAtom + (k & 3) * 32;
@@ -190,13 +197,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (v > 0 && !mbar_wait(dq_empty, (v - 1) & 1, err, kErrTimeoutTmemEmpty, abort_flag)) return false;
         tc_fence_after();
-        const uint64_t adq = make_smem_desc(ds_addr, kAtom, 1024, 2);
+        const uint64_t adq = make_smem_desc(dsb, kAtom, 1024, 2);
         const uint64_t bk = make_smem_desc(k_addr, kAtom, 1024, 2);
 #pragma unroll
         for (int k = 0; k < kT / 16; ++k)  // (5) dQ_i = dS K
           umma_bf16(tmem + TM_DQ, adq + (k * 2048 >> 4), bk + (k * 2048 >> 4), idesc_dq, k > 0 ? 1u : 0u);
         umma_commit(dq_full);
-        umma_commit(grad_done);  // (3)(4)(5) have read P and dS of this tile
+        umma_commit(&grad_done[v & 1]);  // (4)(5) have read this tile's dS buffer
         umma_commit(&ld_empty[st]);
         return true;
       };
@@ -229,10 +236,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma_commit(kv_empty);
       }
     }
-  } else if (warp < 4) {
-    // ---------------- gradient warpgroup: thread = key row = TMEM lane ----------------
-    const int r = threadIdx.x;
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+  } else if (warp < 8) {
+    // ---------------- gradient warpgroups: thread = key row = TMEM lane; gw owns queries 64gw.. ----------------
+    const int gw = warp >> 2;
+    const int r = threadIdx.x & 127;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     const float c = scale * kLog2e;
     int ic = 0, lc = 0, tcount = 0;
     bool ok = true;
@@ -247,20 +255,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float* sl = sVec + st * 2 * kT;
         const float* sd = sl + kT;
         const bool diag = qi == it.kb;
+        uint8_t* ds_buf = sDS + (tcount & 1) * 2 * kAtom;
 #pragma unroll 1
-        for (int qt = 0; qt < 4; ++qt) {  // 32 query columns at a time
+        for (int qt = 2 * gw; qt < 2 * gw + 2; ++qt) {  // 32 query columns at a time
           uint32_t su[32], du[32];
           tmem_ld_32x32b_x32(lane_base + TM_S + qt * 32, su);
           tmem_ld_32x32b_x32(lane_base + TM_DP + qt * 32, du);
           tmem_ld_wait();
-          if (qt == 3) {  // S/dP of this tile are all in registers: the next tile's MMAs may start
+          if (qt == 2 * gw + 1) {  // this warpgroup's S/dP are in registers: the next tile's MMAs may start
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(s_free);
           }
-          if (qt == 0 && tcount > 0) {
-            // P / dS of the previous tile must have been consumed by its MMAs (3)(4)(5)
-            ok = mbar_wait(grad_done, (tcount - 1) & 1, err, kErrTimeoutTmemFull, abort_flag);
+          if (qt == 2 * gw) {
+            // P of the previous tile must have been read by its (3); this tile's dS buffer by (4)(5)
+            // of the tile two back (each barrier is waited once per phase, in order)
+            if (tcount > 0) ok = mbar_wait(p_done, (tcount - 1) & 1, err, kErrTimeoutTmemFull, abort_flag);
+            if (ok && tcount > 1)
+              ok = mbar_wait(&grad_done[tcount & 1], ((tcount - 2) >> 1) & 1, err, kErrTimeoutTmemFull, abort_flag);
             if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
             tc_fence_after();
           }
@@ -285,7 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tmem_st_32x32b_x16(lane_base + TM_P + qt * 16, pk);
           // dS^T row r: queries 64*(qt/2).. live in atom qt/2; 16-byte chunk = 8 queries, swizzled by (r & 7)
-          uint8_t* drow = sDS + (qt >> 1) * kAtom + r * 128;
+          uint8_t* drow = ds_buf + (qt >> 1) * kAtom + r * 128;
 #pragma unroll
           for (int ch = 0; ch < 4; ++ch) {
             const int chunk = (qt & 1) * 4 + ch;
@@ -308,23 +320,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = mbar_wait(acc_full, ic & 1, err, kErrTimeoutTmemFull, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
+      // warpgroup 0 writes dK * scale (rotated back by -theta with a RoPE table), warpgroup 1 writes dV
       const long long row = (long long)it.b * S + it.kb * kT + r;
-      __nv_bfloat16* dkp = dqkv + row * ld_d + D + it.h * kHD;
-      __nv_bfloat16* dvp = dqkv + row * ld_d + 2 * D + it.h * kHD;
+      __nv_bfloat16* dst = dqkv + row * ld_d + (gw == 0 ? D : 2 * D) + it.h * kHD;
+      const float mul = gw == 0 ? scale : 1.f;
+      const bool rot = gw == 0 && rope_cs != nullptr;
       const int pos = it.kb * kT + r;
 #pragma unroll 1
       for (int cc = 0; cc < kHD / 32; ++cc) {
-        uint32_t ku[32], vu[32];
-        tmem_ld_32x32b_x32(lane_base + TM_DK + cc * 32, ku);
-        tmem_ld_32x32b_x32(lane_base + TM_DV + cc * 32, vu);
+        uint32_t u32[32];
+        tmem_ld_32x32b_x32(lane_base + (gw == 0 ? TM_DK : TM_DV) + cc * 32, u32);
         tmem_ld_wait();
 #pragma unroll
         for (int e = 0; e < 32; e += 8) {
           float kv[8];
 #pragma unroll
           for (int u = 0; u < 8; u += 2) {
-            float a0 = __uint_as_float(ku[e + u]) * scale, a1 = __uint_as_float(ku[e + u + 1]) * scale;
-            if (rope_cs != nullptr) {  // k was rotated by +theta in the forward: rotate its gradient by -theta
+            float a0 = __uint_as_float(u32[e + u]) * mul, a1 = __uint_as_float(u32[e + u + 1]) * mul;
+            if (rot) {  // k was rotated by +theta in the forward: rotate its gradient by -theta
               const float2 cs = rope_cs[pos * (kHD / 2) + ((cc * 32 + e + u) >> 1)];
               const float b0 = a0 * cs.x + a1 * cs.y, b1 = -a0 * cs.y + a1 * cs.x;
               a0 = b0;
@@ -333,21 +346,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             kv[u] = a0;
             kv[u + 1] = a1;
           }
-          *reinterpret_cast<uint4*>(dkp + cc * 32 + e) =
+          *reinterpret_cast<uint4*>(dst + cc * 32 + e) =
               make_uint4(pack_bf16x2(kv[0], kv[1]), pack_bf16x2(kv[2], kv[3]), pack_bf16x2(kv[4], kv[5]),
                          pack_bf16x2(kv[6], kv[7]));
-          *reinterpret_cast<uint4*>(dvp + cc * 32 + e) = make_uint4(
-              pack_bf16x2(__uint_as_float(vu[e]), __uint_as_float(vu[e + 1])),
-              pack_bf16x2(__uint_as_float(vu[e + 2]), __uint_as_float(vu[e + 3])),
-              pack_bf16x2(__uint_as_float(vu[e + 4]), __uint_as_float(vu[e + 5])),
-              pack_bf16x2(__uint_as_float(vu[e + 6]), __uint_as_float(vu[e + 7])));
         }
       }
       tc_fence_before();
     }
-  } else if (warp < 8) {
+  } else if (warp < 12) {
     // ---------------- dQ warpgroup: thread = query row = TMEM lane ----------------
-    const int r = threadIdx.x - 128;
+    const int r = threadIdx.x - 256;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     int tcount = 0;
     bool ok = true;
@@ -377,7 +385,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 9) tmem_dealloc(tmem, 512);
+  if (warp == kMmaWarp) tmem_dealloc(tmem, 512);
 }
 
 }  // namespace fab
