@@ -36,6 +36,11 @@ constexpr int kT = 128;            // keys per item, queries per tile
 constexpr int kHD = 64;
 constexpr int kThreads = 512;  // WG0/WG1 gradient (query columns 0-63 / 64-127), WG2 dQ, warp 12 TMA, warp 13 MMA
 constexpr int kTmaWarp = 12, kMmaWarp = 13;
+// Register split (setmaxnreg): launched at 128 per thread (512 x 128 = 65536); the control warpgroup
+// drops to 80 and the dQ warpgroup to 96 (freeing 4 x 32 x (48 + 32) = 10240), the gradient
+// warpgroups rise to 168 (taking 2 x 4 x 32 x 40 = 10240).
+constexpr int kRegsCtl = 80, kRegsDq = 96, kRegsGrad = 168;
+static_assert(4 * 32 * (2 * kRegsGrad + kRegsDq + kRegsCtl) <= kThreads * 128, "register split exceeds the launch");
 constexpr int kAtom = 128 * 128;   // one [128 rows x 64 bf16] swizzled atom
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -142,7 +147,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == kTmaWarp) {
+  if (warp >= 12) {
+   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsCtl));
+   if (warp == kTmaWarp) {
     if (lane == 0) {
       // ---------------- TMA producer ----------------
       int ic = 0, lc = 0;
@@ -166,7 +173,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp == kMmaWarp) {
+   } else if (warp == kMmaWarp) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
       constexpr uint32_t idesc_kk = make_idesc_bf16(128, 128, 0, 0);  // S^T, dP^T: both operands K-major
@@ -236,8 +243,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma_commit(kv_empty);
       }
     }
+   }
   } else if (warp < 8) {
     // ---------------- gradient warpgroups: thread = key row = TMEM lane; gw owns queries 64gw.. ----------------
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsGrad));
     const int gw = warp >> 2;
     const int r = threadIdx.x & 127;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
@@ -258,6 +267,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t* ds_buf = sDS + (tcount & 1) * 2 * kAtom;
 #pragma unroll 1
         for (int qt = 2 * gw; qt < 2 * gw + 2; ++qt) {  // 32 query columns at a time
+          // this quarter's lse / delta first: once the next tile's MMAs stream operands out of shared
+          // memory, loads issued in the arithmetic below would queue behind them
+          float lv[32], dv[32];
+#pragma unroll
+          for (int e = 0; e < 32; e += 4) {
+            const float4 l4 = *reinterpret_cast<const float4*>(sl + qt * 32 + e);
+            const float4 d4 = *reinterpret_cast<const float4*>(sd + qt * 32 + e);
+            lv[e] = l4.x * kLog2e;
+            lv[e + 1] = l4.y * kLog2e;
+            lv[e + 2] = l4.z * kLog2e;
+            lv[e + 3] = l4.w * kLog2e;
+            dv[e] = d4.x;
+            dv[e + 1] = d4.y;
+            dv[e + 2] = d4.z;
+            dv[e + 3] = d4.w;
+          }
           uint32_t su[32], du[32];
           tmem_ld_32x32b_x32(lane_base + TM_S + qt * 32, su);
           tmem_ld_32x32b_x32(lane_base + TM_DP + qt * 32, du);
@@ -280,15 +305,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int e = 0; e < 32; e += 4) {
             const int q = qt * 32 + e;  // query column
-            const float4 l4 = *reinterpret_cast<const float4*>(sl + q);
-            const float4 d4 = *reinterpret_cast<const float4*>(sd + q);
-            const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv[4] = {d4.x, d4.y, d4.z, d4.w};
             float p[4], ds[4];
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
               const bool vis = !diag || r <= q + u;
-              p[u] = vis ? ex2_approx(fmaf(__uint_as_float(su[e + u]), c, -lv[u] * kLog2e)) : 0.f;
-              ds[u] = p[u] * (__uint_as_float(du[e + u]) - dv[u]);
+              p[u] = vis ? ex2_approx(fmaf(__uint_as_float(su[e + u]), c, -lv[e + u])) : 0.f;
+              ds[u] = p[u] * (__uint_as_float(du[e + u]) - dv[e + u]);
             }
             pk[e >> 1] = pack_bf16x2(p[0], p[1]);
             pk[(e >> 1) + 1] = pack_bf16x2(p[2], p[3]);
@@ -355,6 +377,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp < 12) {
     // ---------------- dQ warpgroup: thread = query row = TMEM lane ----------------
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsDq));
     const int r = threadIdx.x - 256;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     int tcount = 0;
