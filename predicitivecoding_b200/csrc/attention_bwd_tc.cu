@@ -50,7 +50,8 @@ constexpr int V_OFF = K_OFF + kAtom;            // V tile
 constexpr int Q_OFF = V_OFF + kAtom;            // 2 stages
 constexpr int DO_OFF = Q_OFF + 2 * kAtom;       // 2 stages
 constexpr int DS_OFF = DO_OFF + 2 * kAtom;      // dS^T, 2 buffers x 2 atoms (queries 0-63, 64-127)
-constexpr int VEC_OFF = DS_OFF + 4 * kAtom;     // per stage: lse[128], delta[128] fp32
+constexpr int DQ_OFF = DS_OFF + 4 * kAtom;      // dQ staging: 2 boxes of [128 rows x 32 fp32], swizzled
+constexpr int VEC_OFF = DQ_OFF + 2 * kAtom;     // per stage: lse[128], delta[128] fp32
 constexpr int BAR_OFF = VEC_OFF + 2 * 2 * kT * 4;
 constexpr int SMEM = BAR_OFF + 256 + 1024;
 static_assert(SMEM <= 232448, "shared memory budget");
@@ -77,14 +78,34 @@ PCB_DEVICE void bulk_load(void* smem_dst, const void* src, uint32_t bytes, uint6
                : "memory");
 }
 
-PCB_DEVICE void red_add_v4(float* addr, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+// TMA reduce-add of a shared-memory box into global fp32 (x, y non-negative, x * 4 bytes 16-aligned)
+PCB_DEVICE void tma_reduce_add_2d(const CUtensorMap* map, const void* smem_src, int x, int y) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(smem_src)), "r"(x), "r"(y)
                : "memory");
+}
+PCB_DEVICE void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+PCB_DEVICE void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+PCB_DEVICE void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+PCB_DEVICE void dq_wg_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// AND of `v` over the dQ warpgroup (named barrier 1): every thread gets the same answer, so an error
+// seen by one warp makes the whole group leave together instead of stranding the others at a barrier
+PCB_DEVICE bool dq_wg_all(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\tbar.red.and.pred p, 1, 128, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v))
+      : "memory");
+  return r != 0;
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
-                       const float* __restrict__ lse, const float* __restrict__ dvec, float* __restrict__ dq_acc,
+                       const __grid_constant__ CUtensorMap tm_dq,
+                       const float* __restrict__ lse, const float* __restrict__ dvec,
                        __nv_bfloat16* __restrict__ dqkv, long long ld_d, int S, int H, float scale,
                        const float2* __restrict__ rope_cs, int BH, int* err) {
   extern __shared__ uint8_t smem_raw[];
@@ -94,6 +115,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sQ = smem + Q_OFF;
   uint8_t* sDO = smem + DO_OFF;
   uint8_t* sDS = smem + DS_OFF;
+  uint8_t* sDQ = smem + DQ_OFF;
   float* sVec = reinterpret_cast<float*>(smem + VEC_OFF);  // [stage][lse 128 | delta 128]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BAR_OFF);
   uint64_t* kv_full = bars + 0;
@@ -385,8 +407,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
       const Item it = item_of(i, BH, H);
       for (int qi = it.kb; qi < T; ++qi, ++tcount) {
-        ok = mbar_wait(dq_full, tcount & 1, err, kErrTimeoutTmemFull, abort_flag);
-        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+        ok = dq_wg_all(mbar_wait(dq_full, tcount & 1, err, kErrTimeoutTmemFull, abort_flag));
+        if (!ok) break;
         tc_fence_after();
         uint32_t qu[64];
         tmem_ld_32x32b_x32(lane_base + TM_DQ, *reinterpret_cast<uint32_t(*)[32]>(qu));
@@ -395,13 +417,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(dq_empty);
-        float* dq = dq_acc + ((long long)it.b * S + qi * kT + r) * D + it.h * kHD;
+        // stage dQ * scale in shared memory (two 128B-swizzled boxes of 32 columns), then one thread
+        // adds both boxes into the fp32 accumulator with TMA reductions
+        if (r == 0) bulk_wait_read0();  // the previous tile's reductions have read the staging buffer
+        dq_wg_sync();
 #pragma unroll
-        for (int e = 0; e < 64; e += 4)
-          red_add_v4(dq + e, __uint_as_float(qu[e]) * scale, __uint_as_float(qu[e + 1]) * scale,
-                     __uint_as_float(qu[e + 2]) * scale, __uint_as_float(qu[e + 3]) * scale);
+        for (int bx = 0; bx < 2; ++bx) {
+          uint8_t* row = sDQ + bx * kAtom + r * 128;
+#pragma unroll
+          for (int ch = 0; ch < 8; ++ch) {
+            const int e = bx * 32 + ch * 4;
+            *reinterpret_cast<float4*>(row + ((ch ^ (r & 7)) << 4)) =
+                make_float4(__uint_as_float(qu[e]) * scale, __uint_as_float(qu[e + 1]) * scale,
+                            __uint_as_float(qu[e + 2]) * scale, __uint_as_float(qu[e + 3]) * scale);
+          }
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        dq_wg_sync();
+        if (r == 0) {
+          const int y = it.b * S + qi * kT;
+          tma_reduce_add_2d(&tm_dq, sDQ, it.h * kHD, y);
+          tma_reduce_add_2d(&tm_dq, sDQ + kAtom, it.h * kHD + 32, y);
+          bulk_commit();
+        }
       }
     }
+    if (r == 0) bulk_wait0();  // every reduction has landed before the CTA exits
   }
 
   __syncwarp();
@@ -409,6 +450,58 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == kMmaWarp) tmem_dealloc(tmem, 512);
+}
+
+// delta[b*H + h][i] = sum_d dO[row, h, d] * O[row, h, d]: 8 lanes per (row, head), 16-byte loads
+__global__ void bwd_delta_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout,
+                                 long long ld_o, float* __restrict__ dvec, long long rows_h, int S, int H) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x; t < rows_h * 8; t += stride) {
+    const long long hr = t >> 3;
+    const int part = (int)(t & 7);
+    const long long row = hr / H;
+    const int h = (int)(hr % H);
+    const uint4 a = *reinterpret_cast<const uint4*>(o + row * ld_o + h * kHD + part * 8);
+    const uint4 g = *reinterpret_cast<const uint4*>(dout + row * ld_o + h * kHD + part * 8);
+    const uint32_t av[4] = {a.x, a.y, a.z, a.w}, gv[4] = {g.x, g.y, g.z, g.w};
+    float acc = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) acc += bf16_lo(av[k]) * bf16_lo(gv[k]) + bf16_hi(av[k]) * bf16_hi(gv[k]);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+    if (part == 0) {
+      const long long b = row / S;
+      dvec[(b * H + h) * S + row % S] = acc;
+    }
+  }
+}
+
+// dqkv[:, 0:D] = bf16(dq_acc) (rotated by -theta with a RoPE table): 8 values per thread
+__global__ void bwd_dq_convert_kernel(const float* __restrict__ dq_acc, __nv_bfloat16* __restrict__ dqkv,
+                                      long long ld_d, long long rows, int D, int S,
+                                      const float2* __restrict__ rope_cs) {
+  const long long per_row = D / 8;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x; t < rows * per_row; t += stride) {
+    const long long r = t / per_row;
+    const int c = (int)(t % per_row) * 8;
+    const float4 x0 = *reinterpret_cast<const float4*>(dq_acc + r * D + c);
+    const float4 x1 = *reinterpret_cast<const float4*>(dq_acc + r * D + c + 4);
+    float v[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+    if (rope_cs != nullptr) {
+      const float2* cs = rope_cs + (r % S) * (kHD / 2) + ((c % kHD) >> 1);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 q = cs[k];
+        const float a = v[2 * k], b = v[2 * k + 1];
+        v[2 * k] = a * q.x + b * q.y;
+        v[2 * k + 1] = -a * q.y + b * q.x;
+      }
+    }
+    *reinterpret_cast<uint4*>(dqkv + r * ld_d + c) = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]),
+                                                                pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+  }
 }
 
 }  // namespace fab
@@ -439,12 +532,6 @@ static bool encode_rows(PFN_cuTensorMapEncodeTiled_v12000 fn, CUtensorMap* tm, c
 
 }  // namespace pcb
 
-// Preprocess (delta = rowsum(dO * O), zeroed dQ accumulator) and the dQ conversion live with the
-// mma.sync backward; this file only replaces its main kernel.
-int pcb_attn_bwd_pre(const void* out, const void* dout, long long ld_o, float* dvec, float* dq_acc, int B, int S,
-                     int H, int HD, cudaStream_t s);
-int pcb_attn_dq_convert(const float* dq_acc, void* dqkv, long long ld_d, int B, int S, int H, int HD,
-                        const float* rope_cs, cudaStream_t s);
 
 // Same contract as pcb_attn_bwd_rope, on tcgen05: S % 128 == 0, HD == 64, row strides % 8 == 0.
 // Returns 0, -1 (unsupported shape), -5 (tensor-map encode) or -(1000 + cudaError) (launch).
@@ -456,14 +543,27 @@ int pcb_attn_bwd_tc(const void* qkv, long long ld, const void* out, const void* 
   if ((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(dout) | reinterpret_cast<uintptr_t>(lse) |
        reinterpret_cast<uintptr_t>(dvec) | reinterpret_cast<uintptr_t>(dq_acc)) & 15)
     return -1;
-  int r = pcb_attn_bwd_pre(out, dout, ld_o, dvec, dq_acc, B, S, H, HD, s);
-  if (r) return r;
   auto fn = encode_fn_fab();
   if (!fn) return -5;
-  CUtensorMap tq, td;
+  CUtensorMap tq, td, tdq;
   if (!encode_rows(fn, &tq, qkv, 3LL * H * HD, (long long)B * S, ld) ||
       !encode_rows(fn, &td, dout, (long long)H * HD, (long long)B * S, ld_o))
     return -5;
+  {  // fp32 dQ accumulator: boxes of 32 columns x 128 rows, 128-byte swizzle (the staging layout)
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(H) * HD, static_cast<cuuint64_t>(B) * S};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(H) * HD * 4};
+    cuuint32_t box[2] = {32, 128};
+    cuuint32_t es[2] = {1, 1};
+    if (fn(&tdq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, dq_acc, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return -5;
+  }
+  const long long rows = (long long)B * S;
+  if (cudaMemsetAsync(dq_acc, 0, rows * H * HD * sizeof(float), s) != cudaSuccess) return -1003;
+  fab::bwd_delta_kernel<<<148 * 8, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(out),
+                                                reinterpret_cast<const __nv_bfloat16*>(dout), ld_o, dvec, rows * H,
+                                                S, H);
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(fab::attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fab::SMEM);
@@ -478,11 +578,14 @@ int pcb_attn_bwd_tc(const void* qkv, long long ld, const void* out, const void* 
   }
   const int n_items = B * H * (S / fab::kT);
   const int grid = n_items < num_sms ? n_items : num_sms;  // persistent: one CTA per SM
-  fab::attn_bwd_tc_kernel<<<grid, fab::kThreads, fab::SMEM, s>>>(tq, td, lse, dvec, dq_acc,
+  fab::attn_bwd_tc_kernel<<<grid, fab::kThreads, fab::SMEM, s>>>(tq, td, tdq, lse, dvec,
                                                                   reinterpret_cast<__nv_bfloat16*>(dqkv), ld_d, S, H,
                                                                   scale, reinterpret_cast<const float2*>(rope_cs),
                                                                   B * H, err);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return -(1000 + static_cast<int>(e));
-  return pcb_attn_dq_convert(dq_acc, dqkv, ld_d, B, S, H, HD, rope_cs, s);
+  fab::bwd_dq_convert_kernel<<<148 * 8, 256, 0, s>>>(dq_acc, reinterpret_cast<__nv_bfloat16*>(dqkv), ld_d, rows,
+                                                     H * HD, S, reinterpret_cast<const float2*>(rope_cs));
+  const cudaError_t e2 = cudaGetLastError();
+  return e2 == cudaSuccess ? 0 : -(1000 + static_cast<int>(e2));
 }
