@@ -39,8 +39,10 @@ def parse():
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="ours", choices=["ours", "torch", "reference"])
-    p.add_argument("--workload", default="decoder", choices=["decoder", "bytelm", "pc", "tp"])
+    p.add_argument("--workload", default="decoder", choices=["decoder", "bytelm", "pc", "tp", "tp_decode"])
     p.add_argument("--batch", type=int, default=0, help="micro-batch per GPU (default from the workload)")
+    p.add_argument("--tp", type=int, default=0,
+                   help="tensor-parallel size of --workload tp (default: all GPUs); the rest is data parallel")
     p.add_argument("--no-graph", action="store_true")
     p.add_argument("--e2e-steps", type=int, default=0, help="steps of the end-to-end timing (default = --steps)")
     return p.parse_args()
@@ -78,6 +80,8 @@ def main():
     if args.workload == "pc":
         from predicitivecoding_b200.bench_pc import run_pc_bench
         res = run_pc_bench(args, dev, rank, world, pg)
+    elif args.workload == "tp_decode":
+        res = run_tp_decode_bench(args, dev, rank, world, pg)
     else:
         res = run_decoder_bench(args, dev, rank, world, pg)
     if rank == 0:
@@ -114,6 +118,8 @@ def run_decoder_bench(args, dev, rank, world, pg):
     from predicitivecoding_b200.utils.clocks import ClockSampler
     from predicitivecoding_b200.utils.data import zipf_windows
 
+    import torch.distributed as dist
+
     tp_mode = args.workload == "tp"
     if args.workload == "bytelm":
         cfg = DecoderLmConfig.byte_lm_4l()
@@ -129,18 +135,34 @@ def run_decoder_bench(args, dev, rank, world, pg):
         name = "decoder-124M-swiglu"
     S = cfg.max_seq
     M = B * S
-    # data-parallel ranks see different batches; tensor-parallel ranks share theirs
-    pool = [zipf_windows(B, S, cfg.vocab, 1.1, seed=(0 if tp_mode else 1000 * rank) + i) for i in range(4)]
+    T = (args.tp or world) if tp_mode else 1
+    if tp_mode and (T < 1 or world % T):
+        raise SystemExit(f"--tp {T} must divide the GPU count {world}")
+    dp = world // T if tp_mode else world
+    tp_pg, dp_pg = pg, None
+    if tp_mode and 1 < T < world:
+        # every rank creates every group, in the same order: TP groups of consecutive ranks, DP groups
+        # of the ranks that hold the same shard
+        tp_groups = [dist.new_group(list(range(d * T, (d + 1) * T))) for d in range(dp)]
+        dp_groups = [dist.new_group(list(range(t, world, T))) for t in range(T)]
+        tp_pg, dp_pg = tp_groups[rank // T], dp_groups[rank % T]
+    elif tp_mode and T == 1 and world > 1:
+        tp_groups = [dist.new_group([r]) for r in range(world)]
+        tp_pg, dp_pg = tp_groups[rank], pg
+    # data-parallel replicas see different batches; the ranks of one tensor-parallel group share theirs
+    replica = rank // T if tp_mode else rank
+    pool = [zipf_windows(B, S, cfg.vocab, 1.1, seed=1000 * replica + i) for i in range(4)]
     pool = [(a.to(torch.int32).pin_memory(), b.to(torch.int32).pin_memory()) for a, b in pool]
 
     if args.impl == "torch":
         step_fn, launches_fn, info = _torch_baseline(cfg, B, dev, world, pg)
     elif tp_mode:
         from predicitivecoding_b200.engine.tp_trainer import TensorParallelTrainer
-        tr = TensorParallelTrainer(cfg, B, S, device=dev, lr=3e-4, weight_decay=0.1, process_group=pg,
-                                   use_graph=not args.no_graph)
+        tr = TensorParallelTrainer(cfg, B, S, device=dev, lr=3e-4, weight_decay=0.1, process_group=tp_pg,
+                                   use_graph=not args.no_graph, dp_group=dp_pg)
         info = {"params": cfg.dense_parameter_formula() if hasattr(cfg, "dense_parameter_formula") else None,
-                "grad_sync": f"tp{world}: fused AG->GEMM / GEMM->RS over peer memory"}
+                "grad_sync": f"tp{T}: fused AG->GEMM / GEMM->RS over peer memory"
+                             + (f"; dp{dp}: peer-memory gradient all-reduce" if dp > 1 else "")}
 
         def step_fn(tok, tgt, sync=True):
             if sync:
@@ -190,7 +212,7 @@ def run_decoder_bench(args, dev, rank, world, pg):
         launched = tr.launches_per_step * args.steps
     dev_ms = _max_over_ranks(dev_ms, world, dev)
     ms_per_step = dev_ms / args.steps
-    groups = 1 if tp_mode else world        # tensor-parallel ranks process one batch together
+    groups = dp                             # each data-parallel replica processes its own batch
     tok_s = groups * M * args.steps / (dev_ms / 1e3)
 
     # ---- end-to-end through the public API: host batch -> step() -> loss on the host
@@ -214,7 +236,7 @@ def run_decoder_bench(args, dev, rank, world, pg):
         "warmup": max(3, args.warmup),
         "ms_per_step": round(ms_per_step, 3),
         "higher_is_better": True,
-        "scaling": "strong" if tp_mode else "weak",
+        "scaling": "strong" if (tp_mode and dp == 1) else "weak",
         "vs_baseline": round(tok_s / REF_DECODER_TOKS, 2),
         "vs_baseline_basis": "closest published reference figure: Base preset (135M, ctx 1024) bf16 mixed, "
                              "2680 tok/s on one RTX 4070 SUPER (ROADMAP-Scale.md:69); BASELINE.md lists no "
@@ -223,7 +245,7 @@ def run_decoder_bench(args, dev, rank, world, pg):
         "data": "synthetic (seeded Zipf(1.1) token ids, random-init weights)",
         "impl": args.impl,
         "config": {"model": name, "global_batch": B * groups, "seq_len": S,
-                   "parallelism": f"tp{world}" if tp_mode else f"dp{world}",
+                   "parallelism": (f"tp{T}" + (f"xdp{dp}" if dp > 1 else "")) if tp_mode else f"dp{world}",
                    "micro_batch_per_gpu": B, "optimizer": "AdamW lr 3e-4 wd 0.1 (ZeRO-1 sharded states)",
                    "l2": "no flush needed: per-step working set (~3 GB of activations, 1 GB logits) >> 126 MB L2",
                    **info},
@@ -234,10 +256,88 @@ def run_decoder_bench(args, dev, rank, world, pg):
         "gpu_launches": int(launched),
         "last_loss": last,
     }
+    if args.impl != "torch" and hasattr(tr, "release"):
+        tr.release()
     if args.impl != "torch":
-        f = tr.flops_per_step() / (world if tp_mode else 1)
+        f = tr.flops_per_step() / (T if tp_mode else 1)
         res["model_tflops_per_gpu"] = round(f / (ms_per_step / 1e3) / 1e12, 1)
     return res
+
+
+def run_tp_decode_bench(args, dev, rank, world, pg):
+    """1.3B decoder, tensor parallel over all GPUs: batch 32, 512 prompt tokens, 256 generated (greedy)."""
+    import torch
+
+    from predicitivecoding_b200 import ops
+    from predicitivecoding_b200.llm.tp_decode import TensorParallelDecoder
+    from predicitivecoding_b200.models.config import DecoderLmConfig
+    from predicitivecoding_b200.utils.clocks import ClockSampler
+    from predicitivecoding_b200.utils.data import zipf_windows
+
+    cfg = DecoderLmConfig.decoder_1p3b()
+    B, P, G = args.batch or 32, 512, 256
+    dec = TensorParallelDecoder(cfg, B, P + G, process_group=pg, device=dev, seed=42, use_graph=not args.no_graph)
+    prompts = [zipf_windows(B, P, cfg.vocab, 1.1, seed=7 + i)[0].to(torch.int64).pin_memory() for i in range(2)]
+    stream = torch.cuda.current_stream(dev)
+    for i in range(max(3, args.warmup)):
+        dec.prefill(prompts[i % 2])
+        dec.decode(G - 1)
+    _sync_all(world, dev)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    pre_ms = dec_ms = 0.0
+    l0 = ops.launch_count()
+    with ClockSampler(dev.index) as clk:
+        for k in range(args.steps):
+            _sync_all(world, dev)
+            ev[0].record(stream)
+            dec.prefill(prompts[k % 2])
+            ev[1].record(stream)
+            dec.decode(G - 1)
+            ev[2].record(stream)
+            torch.cuda.synchronize(dev)
+            pre_ms += ev[0].elapsed_time(ev[1])
+            dec_ms += ev[1].elapsed_time(ev[2])
+    launched = ops.launch_count() - l0
+    if dec.graph is not None and dec.launches_per_step:
+        launched += dec.launches_per_step * (G - 1) * args.steps
+    pre_ms = _max_over_ranks(pre_ms, world, dev)
+    dec_ms = _max_over_ranks(dec_ms, world, dev)
+    decode_tok_s = B * (G - 1) * args.steps / (dec_ms / 1e3)
+    # end to end through the public API: host prompt in, host tokens out
+    _sync_all(world, dev)
+    t0 = time.perf_counter()
+    out = None
+    for k in range(args.steps):
+        out = dec.generate(prompts[k % 2], G)
+    e2e = _max_over_ranks(time.perf_counter() - t0, world, dev)
+    dec.check()
+    dec.release()
+    return {
+        "metric": "TP KV-cache decode tokens/s (max over ranks)",
+        "value": round(decode_tok_s, 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": max(3, args.warmup),
+        "ms_per_step": round(dec_ms / args.steps / (G - 1), 4),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded Zipf(1.1) prompts, random-init weights)",
+        "impl": args.impl,
+        "config": {"model": "decoder-1.3B-swiglu", "batch": B, "prompt_tokens": P, "generated_tokens": G,
+                   "parallelism": f"tp{world}", "sampling": "greedy",
+                   "prefill_ms": round(pre_ms / args.steps, 3),
+                   "prefill_tokens_per_s": round(B * P * args.steps / (pre_ms / 1e3), 1),
+                   "l2": "per-step weight + KV-cache stream (~0.3-0.9 GB per GPU) >> 126 MB L2"},
+        "clocks": clk.summary(),
+        "e2e": {"value": round(B * G * args.steps / e2e, 1), "unit": "tokens/s (prefill + decode)",
+                "h2d_bytes_per_step": B * P * 8, "d2h_bytes_per_step": B * G * 8,
+                "api": "TensorParallelDecoder.generate(prompt, 256) -> host tokens"},
+        "gpu_launches": int(launched),
+        "sample_tokens": out[0, :8].tolist() if out is not None else None,
+    }
 
 
 def _torch_baseline(cfg, B, dev, world, pg):

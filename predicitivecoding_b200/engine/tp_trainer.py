@@ -17,7 +17,10 @@ layout for the dense RMSNorm/RoPE/SwiGLU decoder on T GPUs (one process each):
   and applies the next RMSNorm in one kernel that writes straight into the next gather buffer;
 * the backward mirrors it (dgrad of a row-parallel GEMM is a gather-GEMM, of a column-parallel
   one a reduce-scatter GEMM); replicated parameters' gradients are summed over ranks with the
-  peer-memory all-reduce, then every rank runs AdamW on its parameters.
+  peer-memory all-reduce, then every rank runs AdamW on its parameters;
+* with a data-parallel group (TP x DP, e.g. 4 x 2 on 8 GPUs) every TP replica trains its own batch;
+  before AdamW the replicated and the sharded gradients are summed across the replicas (ranks with the
+  same TP index) by the peer-memory all-reduce, and AdamW folds the 1/DP mean into its gradient scale.
 
 All cross-rank ordering is by the bounded device barrier; nothing waits on the host.
 """
@@ -54,7 +57,8 @@ def tp_supports(cfg: DecoderLmConfig, batch: int, seq: int, world: int) -> bool:
 class TensorParallelTrainer:
     def __init__(self, cfg: DecoderLmConfig, batch: int, seq: Optional[int] = None, *, process_group=None,
                  device="cuda", lr: float = 3e-4, weight_decay: float = 0.1, betas=(0.9, 0.999), eps: float = 1e-8,
-                 seed: int = 42, model: Optional[DecoderLM] = None, decay_all: bool = True, use_graph: bool = True):
+                 seed: int = 42, model: Optional[DecoderLM] = None, decay_all: bool = True, use_graph: bool = True,
+                 dp_group=None):
         from ..parallel.collectives import Communicator
         from ..parallel.peer import PeerGroup
         seq = seq or cfg.max_seq
@@ -109,6 +113,10 @@ class TensorParallelTrainer:
         self.slots = self.peer.symmetric(M * D, bf16)       # [T, R, D]: slot s holds rank s's partials
         self.ready = torch.zeros(max(T, 1), device=dev, dtype=torch.int32)
         self.comm = Communicator(self.pg, backend="peer", device=dev, capacity_bytes=64 << 20) if T > 1 else None
+        self.dp_group = dp_group
+        self.dp = dist.get_world_size(dp_group) if (dp_group is not None and dist.is_initialized()) else 1
+        self.dp_comm = Communicator(dp_group, backend="peer", device=dev, capacity_bytes=64 << 20) \
+            if self.dp > 1 else None
 
         if model is None:
             model = DecoderLM(cfg, seed=seed)
@@ -285,6 +293,9 @@ class TensorParallelTrainer:
         self.hyper.copy_(self.hyper_host, non_blocking=True)
         if self.comm is not None:
             self.comm.all_reduce(self.grad["rep"])       # replicated parameters: sum of row partials
+        if self.dp_comm is not None:                     # data-parallel replicas: sum, AdamW scales by 1/DP
+            self.dp_comm.all_reduce(self.grad["rep"])
+            self.dp_comm.all_reduce(self.grad["shd"])
         for key, arena in (("rep", self.rep), ("shd", self.shd)):
             ops.adamw(self.w32[key], self.grad[key], self.m[key], self.v[key], self.w16[key], arena.n_decay,
                       self.hyper, self.betas[0], self.betas[1], self.eps)
@@ -307,7 +318,7 @@ class TensorParallelTrainer:
         self.hyper_host[1] = self.wd
         self.hyper_host[2] = 1.0 - b1 ** self.step_count
         self.hyper_host[3] = 1.0 - b2 ** self.step_count
-        self.hyper_host[4] = 1.0
+        self.hyper_host[4] = 1.0 / self.dp
 
     def stage(self, tokens: torch.Tensor, targets: torch.Tensor) -> None:
         self.tok_pin.copy_(tokens.reshape(-1).to(torch.int32))
@@ -349,7 +360,10 @@ class TensorParallelTrainer:
         if self.T > 1:
             v = v.to(self.device)
             dist.all_reduce(v, group=self.pg)
-        return float(v) / self.M
+        if self.dp > 1:
+            v = v.to(self.device)
+            dist.all_reduce(v, group=self.dp_group)
+        return float(v) / (self.M * self.dp)
 
     def step(self, tokens: torch.Tensor, targets: torch.Tensor, lr: Optional[float] = None) -> float:
         self.stage(tokens, targets)
@@ -358,6 +372,8 @@ class TensorParallelTrainer:
 
     def check(self) -> None:
         self.peer.check()
+        if self.dp_comm is not None:
+            self.dp_comm.check()
 
     def release(self) -> None:
         """Drop the CUDA graph (it holds peer-memory kernels) before the process group goes away."""
