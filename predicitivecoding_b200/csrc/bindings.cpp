@@ -60,6 +60,11 @@ int pcb_coll_reduce(const void* const* in_peers, void* out, long long lo, long l
                     float scale, int dtype, int num_sms, cudaStream_t s);
 int pcb_coll_gather(const void* const* src_peers, void* out, long long chunk, long long src_stride, int world,
                     int dtype, int num_sms, cudaStream_t s);
+int pcb_rope_append(const void* qkv, const float* cs_table, const long long* pos, void* qo, void* kc, void* vc, int B,
+                    int H, int HD, int cap, cudaStream_t s);
+int pcb_swiglu_rows(const void* gu, void* a, int rows, int F, cudaStream_t s);
+int pcb_tp_allreduce_norm(const void* peers, int world, int rows, int D, float* x, const void* gamma, void* y,
+                          float eps, cudaStream_t s);
 int pcb_tp_reduce_norm(const void* slots, int world, int rows, int D, const float* resid, float* x_out,
                        int accumulate, const void* gamma, void* y, long long ldy, float* inv, float eps,
                        cudaStream_t s);
@@ -557,6 +562,43 @@ void tp_reduce_norm(const at::Tensor& slots, int64_t world, const c10::optional<
 }
 
 
+// decode helpers: RoPE on one token's q/k + KV-cache append; SwiGLU activation of [rows, 2F] rows
+int64_t rope_append(const at::Tensor& qkv, const at::Tensor& cs_table, const at::Tensor& pos, at::Tensor& qo,
+                    at::Tensor& kc, at::Tensor& vc) {
+  reqc(qkv, at::kBFloat16, "qkv");
+  reqc(cs_table, at::kFloat, "cs_table");
+  reqc(qo, at::kBFloat16, "qo");
+  reqc(kc, at::kBFloat16, "kc");
+  reqc(vc, at::kBFloat16, "vc");
+  PCB_CHECK(pos.dtype() == at::kLong && pos.is_cuda(), "rope_append: pos must be a cuda int64 scalar tensor");
+  PCB_CHECK(kc.dim() == 4, "rope_append: caches are [B, H, cap, HD]");
+  return pcb_rope_append(qkv.data_ptr(), cs_table.data_ptr<float>(),
+                         reinterpret_cast<const long long*>(pos.data_ptr<int64_t>()), qo.data_ptr(),
+                         kc.data_ptr(), vc.data_ptr(), (int)kc.size(0), (int)kc.size(1), (int)kc.size(3),
+                         (int)kc.size(2), cur_stream());
+}
+int64_t swiglu_rows(const at::Tensor& gu, at::Tensor& a) {
+  reqc(gu, at::kBFloat16, "gu");
+  reqc(a, at::kBFloat16, "a");
+  const int F = a.size(-1);
+  PCB_CHECK(gu.size(-1) == 2 * F, "swiglu_rows: gu must be [rows, 2F]");
+  return pcb_swiglu_rows(gu.data_ptr(), a.data_ptr(), (int)(a.numel() / F), F, cur_stream());
+}
+
+
+// fused all-reduce (peer loads) + residual add + RMSNorm of replicated rows; returns the status
+int64_t tp_allreduce_norm(const at::Tensor& peers, int64_t world, at::Tensor& x, const at::Tensor& gamma, at::Tensor& y,
+                          double eps) {
+  reqc(x, at::kFloat, "x");
+  reqc(y, at::kBFloat16, "y");
+  req(gamma, at::kBFloat16, "gamma");
+  PCB_CHECK(peers.dtype() == at::kLong && peers.numel() >= world, "tp_allreduce_norm: pointer table");
+  const int D = x.size(-1);
+  return pcb_tp_allreduce_norm(peers.data_ptr(), (int)world, (int)(x.numel() / D), D, x.data_ptr<float>(),
+                               gamma.data_ptr(), y.data_ptr(), (float)eps, cur_stream());
+}
+
+
 // tcgen05 flash-attention forward (same contract as attn_fwd).  Returns the launcher's status
 // (0 ok, -1 unsupported shape, -5 tensor-map encode failure, -(1000 + cudaError) launch failure)
 // instead of raising, so the Python caller reports it.
@@ -638,6 +680,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("linear_scan", &linear_scan);
   m.def("linear_scan_bwd", &linear_scan_bwd);
   m.def("tp_reduce_norm", &tp_reduce_norm);
+  m.def("tp_allreduce_norm", &tp_allreduce_norm);
+  m.def("rope_append", &rope_append);
+  m.def("swiglu_rows", &swiglu_rows);
   m.def("annotate", &annotate);
   m.def("coll_reduce", &coll_reduce);
   m.def("coll_gather", &coll_gather);

@@ -62,31 +62,44 @@ decode_attn_split_kernel(const __nv_bfloat16* __restrict__ q,      // [B, H, HD]
     for (int j = 0; j < DPL; ++j) acc[hh][j] = 0.f;
   }
 
+  __shared__ float ssc[kDecWarps][G][32];
   for (int tile = t0 + warp * 32; tile < t1; tile += kDecWarps * 32) {
-    const int t = tile + lane;
-    float s[G];
+    // scores: half-warps take one key row each (HD/8 lanes x 16 bytes, coalesced), two rows per step;
+    // the partial dot products are reduced across the half-warp and parked in shared memory
+    constexpr int LPK = HD / 8;                   // lanes per key row (16 for HD 128, 8 for HD 64)
+    constexpr int KPS = 32 / LPK;                 // keys per warp step
+    const int sub = lane / LPK, c = lane % LPK;
+    for (int kk = 0; kk < 32; kk += KPS) {
+      const int t = tile + kk + sub;
+      float part[G];
 #pragma unroll
-    for (int hh = 0; hh < G; ++hh) s[hh] = 0.f;
-    if (t < t1) {
-      const uint4* krow = reinterpret_cast<const uint4*>(kc + kvbase + (long long)t * HD);
-#pragma unroll
-      for (int c = 0; c < HD / 8; ++c) {
-        uint4 raw = __ldg(krow + c);
+      for (int hh = 0; hh < G; ++hh) part[hh] = 0.f;
+      if (t < t1) {
+        const uint4 raw = __ldg(reinterpret_cast<const uint4*>(kc + kvbase + (long long)t * HD) + c);
         const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          float2 kv = __bfloat1622float2(p2[e]);
+          const float2 kv = __bfloat1622float2(p2[e]);
 #pragma unroll
-          for (int hh = 0; hh < G; ++hh) s[hh] += sq[hh][c * 8 + 2 * e] * kv.x + sq[hh][c * 8 + 2 * e + 1] * kv.y;
+          for (int hh = 0; hh < G; ++hh) part[hh] += sq[hh][c * 8 + 2 * e] * kv.x + sq[hh][c * 8 + 2 * e + 1] * kv.y;
         }
       }
 #pragma unroll
-      for (int hh = 0; hh < G; ++hh)
-        if (softcap > 0.f) s[hh] = softcap * tanhf(s[hh] / softcap);
-    } else {
+      for (int hh = 0; hh < G; ++hh) {
 #pragma unroll
-      for (int hh = 0; hh < G; ++hh) s[hh] = -INFINITY;
+        for (int o = LPK / 2; o > 0; o >>= 1) part[hh] += __shfl_xor_sync(0xffffffffu, part[hh], o);
+        if (c == 0) ssc[warp][hh][kk + sub] = part[hh];
+      }
     }
+    __syncwarp();
+    const int t = tile + lane;
+    float s[G];
+#pragma unroll
+    for (int hh = 0; hh < G; ++hh) {
+      s[hh] = t < t1 ? ssc[warp][hh][lane] : -INFINITY;
+      if (t < t1 && softcap > 0.f) s[hh] = softcap * tanhf(s[hh] / softcap);
+    }
+    __syncwarp();
     // online softmax over this 32-key tile, per head
     float p[G];
 #pragma unroll
@@ -319,6 +332,43 @@ int launch_decode(const __nv_bfloat16* q, const __nv_bfloat16* kc, const __nv_bf
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
+// One decode token per row: rotate q and k of qkv [B, 3*H*HD] (RoPE angle table row cs [HD/2]
+// float2 for position *pos), write q to qo [B, H, HD] and append k, v to the caches at *pos.
+__global__ void rope_append_kernel(const __nv_bfloat16* __restrict__ qkv, const float2* __restrict__ cs_table,
+                                   const long long* __restrict__ pos, __nv_bfloat16* __restrict__ qo,
+                                   __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ vc, int H, int HD,
+                                   int cap) {
+  const int b = blockIdx.x;
+  const long long p = *pos;
+  const int D = H * HD;
+  const __nv_bfloat16* row = qkv + (long long)b * 3 * D;
+  const float2* cs = cs_table + p * (HD / 2);
+  for (int i = threadIdx.x; i < D / 2; i += blockDim.x) {  // pair i of q and of k
+    const int h = (2 * i) / HD, d = (2 * i) % HD;
+    const float2 c = cs[d / 2];
+    const float2 qv = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(row)[i]);
+    const float2 kv = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(row + D)[i]);
+    reinterpret_cast<__nv_bfloat162*>(qo + (long long)b * D)[i] =
+        __floats2bfloat162_rn(qv.x * c.x - qv.y * c.y, qv.x * c.y + qv.y * c.x);
+    const long long o = (((long long)b * H + h) * cap + p) * HD + d;
+    *reinterpret_cast<__nv_bfloat162*>(kc + o) = __floats2bfloat162_rn(kv.x * c.x - kv.y * c.y, kv.x * c.y + kv.y * c.x);
+    *reinterpret_cast<__nv_bfloat162*>(vc + o) = reinterpret_cast<const __nv_bfloat162*>(row + 2 * D)[i];
+  }
+}
+
+// a[r, j] = silu(gu[r, j]) * gu[r, F + j] for gu [rows, 2F] bf16 (gate | up), a [rows, F] bf16
+__global__ void swiglu_rows_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* __restrict__ a, int rows,
+                                   int F) {
+  const long long n = (long long)rows * F;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / F;
+    const int j = (int)(i % F);
+    const float g = __bfloat162float(gu[r * 2 * F + j]);
+    const float u = __bfloat162float(gu[r * 2 * F + F + j]);
+    a[i] = __float2bfloat16(g / (1.f + __expf(-g)) * u);
+  }
+}
+
 }  // namespace
 
 // q [B, H, HD] bf16; caches [B, Hkv, cap, HD] bf16; lens [B] int32 (valid entries);
@@ -382,5 +432,24 @@ int pcb_linear_scan_bwd(const float* a, const float* st, const float* ds, float*
                         cudaStream_t s) {
   const long long n = (long long)B * D;
   linear_scan_bwd_kernel<<<(n + 255) / 256, 256, 0, s>>>(a, st, ds, da, db, B, T, D);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+int pcb_rope_append(const void* qkv, const float* cs_table, const long long* pos, void* qo, void* kc, void* vc, int B,
+                    int H, int HD, int cap, cudaStream_t s) {
+  if (HD % 2 || B <= 0) return -2;
+  rope_append_kernel<<<B, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(qkv),
+                                       reinterpret_cast<const float2*>(cs_table), pos,
+                                       reinterpret_cast<__nv_bfloat16*>(qo), reinterpret_cast<__nv_bfloat16*>(kc),
+                                       reinterpret_cast<__nv_bfloat16*>(vc), H, HD, cap);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+int pcb_swiglu_rows(const void* gu, void* a, int rows, int F, cudaStream_t s) {
+  const long long n = (long long)rows * F;
+  long long blocks = (n + 255) / 256;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  swiglu_rows_kernel<<<(unsigned)blocks, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(gu),
+                                                      reinterpret_cast<__nv_bfloat16*>(a), rows, F);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }

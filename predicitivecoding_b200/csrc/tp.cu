@@ -100,3 +100,70 @@ int pcb_tp_reduce_norm(const void* slots, int world, int rows, int D, const floa
                                                       reinterpret_cast<__nv_bfloat16*>(y), ldy, inv, eps);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
+
+namespace {
+// x[r] += sum_s peers[s][r] (bf16 partial products read from every rank's buffer over NVLink, summed
+// in rank order), then y[r] = x[r] * gamma / rms(x[r]) in bf16: the all-reduce of a row-parallel
+// product fused with the residual add and the next RMSNorm.  Rows are replicated on every rank.
+__global__ void __launch_bounds__(kTpThreads)
+tp_allreduce_norm_kernel(const __nv_bfloat16* const* __restrict__ peers, int world, int D, float* __restrict__ x,
+                         const __nv_bfloat16* __restrict__ gamma, __nv_bfloat16* __restrict__ y, float eps) {
+  const int r = blockIdx.x;
+  float ss = 0.f;
+  for (int i = threadIdx.x * 8; i < D; i += kTpThreads * 8) {
+    const long long o = (long long)r * D + i;
+    const float4 a = *reinterpret_cast<const float4*>(x + o);
+    const float4 b = *reinterpret_cast<const float4*>(x + o + 4);
+    float acc[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    for (int s = 0; s < world; ++s) {
+      const uint4 u = *reinterpret_cast<const uint4*>(peers[s] + o);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(h[e]);
+        acc[2 * e] += f.x;
+        acc[2 * e + 1] += f.y;
+      }
+    }
+    *reinterpret_cast<float4*>(x + o) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    *reinterpret_cast<float4*>(x + o + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss += acc[e] * acc[e];
+  }
+  __shared__ float red[kTpThreads / 32];
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int w = 0; w < kTpThreads / 32; ++w) tot += red[w];
+  const float rinv = rsqrtf(tot / D + eps);
+  for (int i = threadIdx.x * 8; i < D; i += kTpThreads * 8) {
+    const long long o = (long long)r * D + i;
+    const float4 a = *reinterpret_cast<const float4*>(x + o);
+    const float4 b = *reinterpret_cast<const float4*>(x + o + 4);
+    const uint4 gu = *reinterpret_cast<const uint4*>(gamma + i);
+    const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gu);
+    const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    uint4 out;
+    uint32_t* ow = reinterpret_cast<uint32_t*>(&out);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 g = __bfloat1622float2(g2[e]);
+      ow[e] = pack_bf16x2(xv[2 * e] * rinv * g.x, xv[2 * e + 1] * rinv * g.y);
+    }
+    *reinterpret_cast<uint4*>(y + o) = out;
+  }
+}
+}  // namespace
+
+// peers: device array of `world` pointers to [rows, D] bf16 partials (this rank's included); the
+// caller orders it after a barrier that follows every rank's write of its partial.
+int pcb_tp_allreduce_norm(const void* peers, int world, int rows, int D, float* x, const void* gamma, void* y,
+                          float eps, cudaStream_t s) {
+  if (D % 8 || rows <= 0 || world <= 0) return -2;
+  tp_allreduce_norm_kernel<<<rows, kTpThreads, 0, s>>>(reinterpret_cast<const __nv_bfloat16* const*>(peers), world,
+                                                         D, x, reinterpret_cast<const __nv_bfloat16*>(gamma),
+                                                         reinterpret_cast<__nv_bfloat16*>(y), eps);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}

@@ -9,10 +9,12 @@ layout runs on T GPUs:
   [t*F/T, (t+1)*F/T) (column-parallel W_1/W_3, row-parallel W_2) and vocabulary slice
   [t*V/T, (t+1)*V/T) of the LM head; the embedding and the norm gains are replicated;
 * each rank keeps the KV cache of its own heads ([B, H/T, capacity, hd] bf16 per layer);
-* the two row-parallel products of a layer are summed over ranks by the peer-memory all-reduce
-  (one-shot kernel over NVLink for decode-sized rows), the residual stream stays replicated in fp32;
-* prefill runs the prompt through the causal attention kernel; each decode step uses the
-  flash-decoding split-KV kernel over the cache; greedy sampling takes the per-rank vocabulary
+* each row-parallel product lands in this rank's half of a double-buffered symmetric buffer; after
+  one device barrier a single kernel reads every rank's partial over NVLink, sums them in rank
+  order, adds the fp32 residual (replicated on every rank) and writes the next RMSNorm's bf16
+  input -- all-reduce, residual add and norm in one launch;
+* prefill runs the prompt through the causal attention kernel; each decode step rotates q/k and
+  appends k/v to the cache in one kernel, then runs the flash-decoding split-KV kernel; greedy sampling takes the per-rank vocabulary
   maxima and gathers them (value, index) over the ranks;
 * one decode step is captured in a CUDA graph and replayed, so a step costs one graph launch.
 """
@@ -59,18 +61,24 @@ class TensorParallelDecoder:
             self._import(model)
         else:
             self._random(seed)
-        self.comm = Communicator(self.pg, backend="peer", device=dev, capacity_bytes=64 << 20) if T > 1 else None
+        from ..parallel.peer import PeerGroup
+        self.comm = Communicator(self.pg, backend="peer", device=dev, capacity_bytes=1 << 20) if T > 1 else None
+        self.peer = PeerGroup(self.pg, dev)
+        self.pbuf = [self.peer.symmetric(batch * D, bf16) for _ in range(2)]   # decode partials
+        self.pbuf_prefill = None
+        self._flip = 0
         self.kc = [torch.zeros(batch, self.Hl, self.cap, hd, device=dev, dtype=bf16) for _ in range(L)]
         self.vc = [torch.zeros(batch, self.Hl, self.cap, hd, device=dev, dtype=bf16) for _ in range(L)]
         cos, sin = rope_tables(self.cap, hd, 0, device=dev)
         self.rope_cs = torch.stack((cos, sin), dim=-1).contiguous()          # [cap, hd/2, 2]
         self.scale = 1.0 / math.sqrt(hd)
         # decode-step state (static buffers so the step can be captured)
-        nsplit = max(1, min(max(1, (2 * 148) // max(1, batch * self.Hl)), self.cap // 128))
+        nsplit = max(1, min(max(1, (4 * 148) // max(1, batch * self.Hl)), self.cap // 64))
         self.nsplit = nsplit
         self.pacc = torch.empty(batch * self.Hl * nsplit * hd, device=dev)
         self.pml = torch.empty(batch * self.Hl * nsplit * 2, device=dev)
         self.tok = torch.zeros(batch, device=dev, dtype=torch.int64)
+        self.qbuf = torch.zeros(batch, self.Hl, hd, device=dev, dtype=bf16)
         self.pos = torch.zeros(1, device=dev, dtype=torch.int64)
         self.lens = torch.zeros(batch, device=dev, dtype=torch.int32)
         self.out_tokens = torch.zeros(batch, self.cap, device=dev, dtype=torch.int64)
@@ -122,21 +130,36 @@ class TensorParallelDecoder:
             self.W[f"b{l}.w2"] = rn(own, self.Fl, D)
 
     # ------------------------------------------------------------------ pieces
-    def _allreduce(self, part: torch.Tensor) -> torch.Tensor:
-        if self.comm is not None:
-            self.comm.all_reduce(part)
-        return part
-
     def _norm(self, x: torch.Tensor, g: torch.Tensor) -> torch.Tensor:
         y = torch.empty(x.shape, device=self.device, dtype=torch.bfloat16)
         ops.rmsnorm_fwd(x, g, y, None, self.cfg.eps)
         return y
 
-    def _ffn(self, x: torch.Tensor, l: int) -> None:
-        h = self._norm(x, self.W[f"b{l}.ln2"])
-        gu = h @ self.W[f"b{l}.w13"]
-        a = torch.nn.functional.silu(gu[:, :self.Fl]) * gu[:, self.Fl:]
-        x += self._allreduce((a @ self.W[f"b{l}.w2"]).float())
+    def _row_parallel(self, a: torch.Tensor, w: torch.Tensor, x: torch.Tensor, gamma: torch.Tensor,
+                      bufs) -> torch.Tensor:
+        """x += sum over ranks of a @ w; returns rmsnorm(x) * gamma in bf16."""
+        buf = bufs[self._flip]
+        self._flip ^= 1
+        rows = a.shape[0]
+        torch.matmul(a, w, out=buf.local[:rows * self.cfg.dim].view(rows, self.cfg.dim))
+        if self.T > 1:
+            self.peer.barrier()
+        y = torch.empty(x.shape, device=self.device, dtype=torch.bfloat16)
+        rc = ops.ext().tp_allreduce_norm(buf.ptrs, self.T, x, gamma, y, self.cfg.eps)
+        if rc != 0:
+            raise RuntimeError(f"tp_allreduce_norm failed with status {rc}")
+        return y
+
+    def _layer(self, x: torch.Tensor, h: torch.Tensor, l: int, attn, bufs) -> torch.Tensor:
+        """One block on normalised input h (residual x updated in place); returns the next norm's output."""
+        W, L = self.W, self.cfg.num_blocks
+        o = attn(h @ W[f"b{l}.wqkv"], l)
+        h2 = self._row_parallel(o, W[f"b{l}.wo"], x, W[f"b{l}.ln2"], bufs)
+        gu = h2 @ W[f"b{l}.w13"]
+        a = torch.empty(gu.shape[0], self.Fl, device=self.device, dtype=torch.bfloat16)
+        ops.ext().swiglu_rows(gu, a)
+        nxt = W[f"b{l + 1}.ln1"] if l + 1 < L else W["lnf"]
+        return self._row_parallel(a, W[f"b{l}.w2"], x, nxt, bufs)
 
     def _argmax_tokens(self, hf: torch.Tensor) -> torch.Tensor:
         """Greedy next tokens from the final normalised rows [B, D] (vocabulary split over ranks)."""
@@ -162,24 +185,29 @@ class TensorParallelDecoder:
             raise ValueError("prompt must be [batch, P] with P % 128 == 0 and P < capacity")
         D, Dl, Hl, hd = cfg.dim, self.Dl, self.Hl, cfg.head_dim
         M = B * P
+        if self.pbuf_prefill is None or self.pbuf_prefill[0].local.numel() < M * D:
+            self.pbuf_prefill = [self.peer.symmetric(M * D, torch.bfloat16) for _ in range(2)]
         tok = prompt.to(self.device, torch.int32).reshape(-1)
         x = torch.empty(M, D, device=self.device)
         ops.embed_fwd(tok, self.W["wemb"], x)
         out = torch.empty(M, Dl, device=self.device, dtype=torch.bfloat16)
         lse = torch.empty(B * Hl, P, device=self.device)
         cs = self.rope_cs[:P].contiguous()
-        for l in range(cfg.num_blocks):
-            h = self._norm(x, self.W[f"b{l}.ln1"])
-            qkv = h @ self.W[f"b{l}.wqkv"]                       # [M, 3*Dl] = q | k | v column blocks
+
+        def attn(qkv, l):                                      # qkv [M, 3*Dl] = q | k | v column blocks
             ops.rope(qkv, cs, P, Dl, hd, 2, 1.0)
             kv = qkv.view(B, P, 3, Hl, hd)
             self.kc[l][:, :, :P].copy_(kv[:, :, 1].transpose(1, 2))
             self.vc[l][:, :, :P].copy_(kv[:, :, 2].transpose(1, 2))
             ops.attn_fwd(qkv, out, lse, B, P, Hl, hd, self.scale)
-            x += self._allreduce((out @ self.W[f"b{l}.wo"]).float())
-            self._ffn(x, l)
-        last = x.view(B, P, D)[:, -1].contiguous()
-        nxt = self._argmax_tokens(self._norm(last, self.W["lnf"]))
+            return out
+
+        self._flip = 0
+        h = self._norm(x, self.W["b0.ln1"])
+        for l in range(cfg.num_blocks):
+            h = self._layer(x, h, l, attn, self.pbuf_prefill)
+        last = h.view(B, P, D)[:, -1].contiguous()             # lnf already applied
+        nxt = self._argmax_tokens(last)
         self.tok.copy_(nxt)
         self.pos.fill_(P)
         self.lens.fill_(P)
@@ -193,21 +221,20 @@ class TensorParallelDecoder:
         cfg, B = self.cfg, self.B
         D, Dl, Hl, hd = cfg.dim, self.Dl, self.Hl, cfg.head_dim
         x = self.W["wemb"].index_select(0, self.tok).float()   # [B, D]
-        cs = self.rope_cs.index_select(0, self.pos).contiguous()   # [1, hd/2, 2]: every row at self.pos
         self.lens.add_(1)
-        for l in range(cfg.num_blocks):
-            h = self._norm(x, self.W[f"b{l}.ln1"])
-            qkv = h @ self.W[f"b{l}.wqkv"]                       # [B, 3*Dl]
-            ops.rope(qkv, cs, 1, Dl, hd, 2, 1.0)
-            kv = qkv.view(B, 3, Hl, 1, hd)
-            self.kc[l].index_copy_(2, self.pos, kv[:, 1])
-            self.vc[l].index_copy_(2, self.pos, kv[:, 2])
-            q = kv[:, 0, :, 0].contiguous()                      # [B, Hl, hd]
-            o = ops.decode_attn(q, self.kc[l], self.vc[l], self.lens, self.scale, nsplit=self.nsplit,
+
+        def attn(qkv, l):                                      # qkv [B, 3*Dl]
+            # RoPE on q and k at self.pos, q -> self.qbuf, k / v appended to the caches (one kernel)
+            ops.ext().rope_append(qkv, self.rope_cs, self.pos, self.qbuf, self.kc[l], self.vc[l])
+            o = ops.decode_attn(self.qbuf, self.kc[l], self.vc[l], self.lens, self.scale, nsplit=self.nsplit,
                                 scratch=(self.pacc, self.pml))
-            x += self._allreduce((o.view(B, Dl) @ self.W[f"b{l}.wo"]).float())
-            self._ffn(x, l)
-        nxt = self._argmax_tokens(self._norm(x, self.W["lnf"]))
+            return o.view(B, Dl)
+
+        self._flip = 0
+        h = self._norm(x, self.W["b0.ln1"])
+        for l in range(cfg.num_blocks):
+            h = self._layer(x, h, l, attn, self.pbuf)
+        nxt = self._argmax_tokens(h)
         self.tok.copy_(nxt)
         self.pos.add_(1)
         self.out_tokens.index_copy_(1, self.pos - self.prompt_len, nxt[:, None])
@@ -220,8 +247,8 @@ class TensorParallelDecoder:
         self.launches_per_step = ops.launch_count() - before
         torch.cuda.synchronize(self.device)
         self.tok.copy_(saved[0]); self.pos.copy_(saved[1]); self.lens.copy_(saved[2])
-        if self.comm is not None:
-            self.comm._peer.barrier()
+        if self.T > 1:
+            self.peer.barrier()
         torch.cuda.synchronize(self.device)
         self.graph = torch.cuda.CUDAGraph()
         s = torch.cuda.Stream(self.device)
@@ -253,6 +280,7 @@ class TensorParallelDecoder:
         return self.out_tokens[:, :new_tokens].cpu()
 
     def check(self) -> None:
+        self.peer.check()
         if self.comm is not None:
             self.comm.check()
 
