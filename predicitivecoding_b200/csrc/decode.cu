@@ -69,13 +69,22 @@ decode_attn_split_kernel(const __nv_bfloat16* __restrict__ q,      // [B, H, HD]
     constexpr int LPK = HD / 8;                   // lanes per key row (16 for HD 128, 8 for HD 64)
     constexpr int KPS = 32 / LPK;                 // keys per warp step
     const int sub = lane / LPK, c = lane % LPK;
-    for (int kk = 0; kk < 32; kk += KPS) {
-      const int t = tile + kk + sub;
+    constexpr int STEPS = 32 / KPS;
+    uint4 raw_all[STEPS];                         // every load of the tile in flight before any math
+#pragma unroll
+    for (int it = 0; it < STEPS; ++it) {
+      const int t = tile + it * KPS + sub;
+      raw_all[it] = t < t1 ? __ldg(reinterpret_cast<const uint4*>(kc + kvbase + (long long)t * HD) + c)
+                           : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int it = 0; it < STEPS; ++it) {
+      const int kk = it * KPS;
       float part[G];
 #pragma unroll
       for (int hh = 0; hh < G; ++hh) part[hh] = 0.f;
-      if (t < t1) {
-        const uint4 raw = __ldg(reinterpret_cast<const uint4*>(kc + kvbase + (long long)t * HD) + c);
+      {
+        const uint4 raw = raw_all[it];
         const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -114,24 +123,27 @@ decode_attn_split_kernel(const __nv_bfloat16* __restrict__ q,      // [B, H, HD]
       for (int j = 0; j < DPL; ++j) acc[hh][j] *= corr;
     }
     const int nk = min(32, t1 - tile);
-    for (int kk = 0; kk < nk; ++kk) {
-      const __nv_bfloat16* vrow = vc + kvbase + (long long)(tile + kk) * HD + lane * DPL;
-      float vv[DPL];
-      if constexpr (DPL == 2) {
-        float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(vrow));
-        vv[0] = f.x; vv[1] = f.y;
-      } else {
+    for (int k0 = 0; k0 < nk; k0 += 8) {         // eight value rows in flight at a time
+      float vv[8][DPL];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int kk = min(k0 + u, nk - 1);       // rows past nk get weight 0 below
+        const __nv_bfloat16* vrow = vc + kvbase + (long long)(tile + kk) * HD + lane * DPL;
 #pragma unroll
         for (int j = 0; j < DPL; j += 2) {
-          float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(vrow + j));
-          vv[j] = f.x; vv[j + 1] = f.y;
+          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(vrow + j));
+          vv[u][j] = f.x;
+          vv[u][j + 1] = f.y;
         }
       }
 #pragma unroll
-      for (int hh = 0; hh < G; ++hh) {
-        float pk = __shfl_sync(0xffffffffu, p[hh], kk);
+      for (int u = 0; u < 8; ++u) {
 #pragma unroll
-        for (int j = 0; j < DPL; ++j) acc[hh][j] += pk * vv[j];
+        for (int hh = 0; hh < G; ++hh) {
+          const float pk = k0 + u < nk ? __shfl_sync(0xffffffffu, p[hh], k0 + u) : 0.f;
+#pragma unroll
+          for (int j = 0; j < DPL; ++j) acc[hh][j] += pk * vv[u][j];
+        }
       }
     }
   }

@@ -73,7 +73,7 @@ class TensorParallelDecoder:
         self.rope_cs = torch.stack((cos, sin), dim=-1).contiguous()          # [cap, hd/2, 2]
         self.scale = 1.0 / math.sqrt(hd)
         # decode-step state (static buffers so the step can be captured)
-        nsplit = max(1, min(max(1, (4 * 148) // max(1, batch * self.Hl)), self.cap // 64))
+        nsplit = max(1, min(max(1, (8 * 148) // max(1, batch * self.Hl)), self.cap // 64))
         self.nsplit = nsplit
         self.pacc = torch.empty(batch * self.Hl * nsplit * hd, device=dev)
         self.pml = torch.empty(batch * self.Hl * nsplit * 2, device=dev)
