@@ -315,6 +315,25 @@ static int gemm_mode() {
   return mode;
 }
 
+// Split-K count for the atomic (EPI_RED_F32) epilogue: the split s minimising
+//   waves(s) * (k-blocks per split + per-tile overhead),  waves(s) = ceil(tiles * s / slots),
+// i.e. the one that fills the persistent grid best without paying more tile prologues/epilogues
+// than the extra parallelism buys.  The overhead is counted as 8 k-blocks per tile.
+static int pick_splits(int tiles, int total_kb, int slots) {
+  int best = 1;
+  long long best_cost = -1;
+  for (int sp = 1; sp <= 16; ++sp) {
+    if (sp > 1 && total_kb / sp < 4) break;
+    const long long waves = ((long long)tiles * sp + slots - 1) / slots;
+    const long long cost = waves * ((total_kb + sp - 1) / sp + 8);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = sp;
+    }
+  }
+  return best;
+}
+
 int pcb_gemm_launch(const void* A, int a_mn, long long lda, const void* B, int b_mn, long long ldb, int epi,
                     GemmArgs args, int force_bn, int force_splits, int num_sms, cudaStream_t stream) {
   const int M = args.M, N = args.N, K = args.K;
@@ -339,9 +358,7 @@ int pcb_gemm_launch(const void* A, int a_mn, long long lda, const void* B, int b
     const int pbn = (force_bn == 128 || force_bn == 256) ? force_bn : (N >= 256 ? 256 : 128);
     const int ptiles = ((M + 255) / 256) * ((N + pbn - 1) / pbn);
     int psplits = force_splits > 0 ? force_splits : 1;
-    if (force_splits <= 0 && epi == EPI_RED_F32) {
-      while (ptiles * psplits * 2 <= num_sms / 2 && total_kb / (psplits * 2) >= 4) psplits *= 2;
-    }
+    if (force_splits <= 0 && epi == EPI_RED_F32) psplits = pick_splits(ptiles, total_kb, num_sms / 2);
     const bool legal = M >= 256 && (epi != EPI_SWIGLU || pbn % 128 == 0);
     const bool worth = ptiles * psplits >= num_sms / 4 && total_kb >= 4;
     if (mode != 1 && legal && (mode == 2 || worth))
@@ -356,10 +373,7 @@ int pcb_gemm_launch(const void* A, int a_mn, long long lda, const void* B, int b
   int splits = force_splits;
   if (splits <= 0) {
     splits = 1;
-    if (epi == EPI_RED_F32) {
-      const int tiles = num_m * num_n;
-      while (tiles * splits * 2 <= num_sms && total_kb / (splits * 2) >= 4) splits *= 2;
-    }
+    if (epi == EPI_RED_F32) splits = pick_splits(num_m * num_n, total_kb, num_sms);
   }
   if (splits > 1 && epi != EPI_RED_F32) return -4;  // only the atomic epilogue may split K
   int kbps = (total_kb + splits - 1) / splits;
