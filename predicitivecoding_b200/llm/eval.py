@@ -203,3 +203,68 @@ def html_report(path: str, title: str, ppl: PerplexityResult, probe: Optional[Ac
     with open(path, "w", encoding="utf-8") as f:
         f.write(doc)
     return path
+
+
+# ---------------------------------------------------------------- fixed yardstick text + multi-metric bundle
+# A small, fixed text written for this package so that perplexities quoted by tests and demos are
+# always measured on the same bytes (Eval/EvalCorpus.cs plays this role in the reference, with its own
+# text; the two corpora differ, so their numbers are not comparable).
+EVAL_CORPUS_LINES = (
+    "Rivers carry the memory of rain down to the sea.",
+    "A map is a guess about a territory that keeps changing.",
+    "Each morning the baker checks whether the dough has risen as expected.",
+    "When the forecast is wrong, the sailor trims the sails and watches the sky.",
+    "Small surprises teach more than large certainties.",
+    "The orchestra listens to itself and corrects the tempo bar by bar.",
+    "Rivers carry the memory of rain down to the sea.",
+    "A good guess saves words, and saved words make a short message.",
+    "The lighthouse keeper counts ships and notes the ones that never arrive.",
+    "Small surprises teach more than large certainties.",
+)
+
+
+def eval_corpus() -> str:
+    return "\n".join(EVAL_CORPUS_LINES)
+
+
+@dataclass(frozen=True)
+class ProbeScores:
+    echo: float
+    induction: float
+
+
+@dataclass(frozen=True)
+class ProEvalReport:
+    bits_per_byte: BitsPerByteResult
+    per_domain_perplexity: Dict[str, float]
+    probes: ProbeScores
+    serve_tokens_per_second: float
+
+
+def next_token_accuracy(llm, text: str) -> float:
+    """Share of positions whose greedy next token equals the text's next token."""
+    ids = llm.tokenizer.encode(text)
+    n = min(len(ids), llm.config.max_seq)
+    if n < 2:
+        return 0.0
+    tokens = torch.tensor(ids[:n], dtype=torch.long, device=next(llm.model.parameters()).device)
+    with torch.no_grad():
+        pred = llm.model(tokens).argmax(-1)
+    return float((pred[:-1] == tokens[1:]).float().mean())
+
+
+def pro_eval(llm, reference_text: str, domains: Dict[str, str], serve_tokens: int = 32) -> ProEvalReport:
+    """Bits per byte on a reference text, perplexity per domain, two in-context probes (echo: a
+    repeated token; induction: a repeated pair) and generation throughput (ProEval.cs:8-100)."""
+    import time
+    if not reference_text:
+        raise ValueError("reference_text must not be empty")
+    bpb = llm.evaluate_bits_per_byte(reference_text)
+    per = {name: llm.evaluate(text).perplexity for name, text in domains.items()}
+    probes = ProbeScores(next_token_accuracy(llm, "A " * 24), next_token_accuracy(llm, "A B " * 16))
+    prompt = reference_text[:24]
+    llm.generate(prompt, max_new_tokens=4)
+    t0 = time.perf_counter()
+    llm.generate(prompt, max_new_tokens=serve_tokens)
+    dt = time.perf_counter() - t0
+    return ProEvalReport(bpb, per, probes, serve_tokens / dt if dt > 0 else 0.0)

@@ -161,3 +161,19 @@ def test_peer_collectives_match_nccl_two_ranks():
     for r in range(world):
         # sums over 2 ranks are order-independent except bf16 rounding of the result
         assert max(res[r]) < 2e-2, res[r]
+
+
+def test_runtime_kernel_saxpy_matches_torch():
+    from predicitivecoding_b200.runtime.kernel import RuntimeKernel
+    src = r'''
+extern "C" __global__ void saxpy(float a, const float* x, float* y, int n) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = a * x[i] + y[i];
+}'''
+    k = RuntimeKernel(src, "saxpy")
+    x = torch.randn(100_003, device="cuda")
+    y = torch.randn(100_003, device="cuda")
+    ref = 1.5 * x + y
+    k.launch_1d(x.numel(), [1.5, x, y, x.numel()], sync=True)
+    assert torch.allclose(y, ref)
+    k.close()
