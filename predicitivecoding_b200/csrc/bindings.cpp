@@ -63,6 +63,7 @@ int pcb_coll_gather(const void* const* src_peers, void* out, long long chunk, lo
 int pcb_rope_append(const void* qkv, const float* cs_table, const long long* pos, void* qo, void* kc, void* vc, int B,
                     int H, int HD, int cap, cudaStream_t s);
 int pcb_swiglu_rows(const void* gu, void* a, int rows, int F, cudaStream_t s);
+long long pcb_checked_violations();
 int pcb_tp_allreduce_norm(const void* peers, int world, int rows, int D, float* x, const void* gamma, void* y,
                           float eps, cudaStream_t s);
 int pcb_tp_reduce_norm(const void* slots, int world, int rows, int D, const float* resid, float* x_out,
@@ -682,6 +683,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tp_reduce_norm", &tp_reduce_norm);
   m.def("tp_allreduce_norm", &tp_allreduce_norm);
   m.def("rope_append", &rope_append);
+  m.def("checked_violations", []() { return (int64_t)pcb_checked_violations(); });
   m.def("swiglu_rows", &swiglu_rows);
   m.def("annotate", &annotate);
   m.def("coll_reduce", &coll_reduce);

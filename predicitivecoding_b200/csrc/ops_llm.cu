@@ -14,11 +14,21 @@ namespace pcb {
 // ------------------------------------------------------------------ embedding
 // x[t,:] = W[tok[t],:]   (fp32 residual stream)
 // W is the bf16 working copy of the table (the fp32 master may be sharded across ranks).
+// Checked builds (-DPCB_CHECKED, setup.py with PCB_CHECKED=1) count the out-of-range token ids that the
+// embedding kernels clamp or skip, so a test can assert that none occurred.
+#ifdef PCB_CHECKED
+__device__ unsigned long long g_checked_violations = 0;
+#define PCB_COUNT_VIOLATION() atomicAdd(&g_checked_violations, 1ull)
+#else
+#define PCB_COUNT_VIOLATION() ((void)0)
+#endif
+
 __global__ void embed_fwd_kernel(const int* __restrict__ tok, const __nv_bfloat16* __restrict__ W,
                                  float* __restrict__ x, int M, int D, int V) {
   const int t = blockIdx.x;
   if (t >= M) return;
   int id = tok[t];
+  if ((id < 0 || id >= V) && threadIdx.x == 0) PCB_COUNT_VIOLATION();
   id = id < 0 ? 0 : (id >= V ? V - 1 : id);
   const uint2* src = reinterpret_cast<const uint2*>(W + (long long)id * D);
   float4* dst = reinterpret_cast<float4*>(x + (long long)t * D);
@@ -34,7 +44,10 @@ __global__ void embed_bwd_kernel(const int* __restrict__ tok, const float* __res
   const int t = blockIdx.x;
   if (t >= M) return;
   int id = tok[t];
-  if (id < 0 || id >= V) return;
+  if (id < 0 || id >= V) {
+    if (threadIdx.x == 0) PCB_COUNT_VIOLATION();
+    return;
+  }
   const float4* src = reinterpret_cast<const float4*>(dx + (long long)t * D);
   float4* dst = reinterpret_cast<float4*>(dW + (long long)id * D);
   for (int i = threadIdx.x; i < D / 4; i += blockDim.x) atomicAdd(dst + i, src[i]);
@@ -383,6 +396,18 @@ int pcb_embed_fwd(const int* tok, const void* W, float* x, int M, int D, int V, 
   if (D % 4) return -1;
   embed_fwd_kernel<<<M, 128, 0, s>>>(tok, reinterpret_cast<const __nv_bfloat16*>(W), x, M, D, V);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+// Number of bounds violations counted since the last call (and reset it); -1 in unchecked builds.
+long long pcb_checked_violations() {
+#ifdef PCB_CHECKED
+  unsigned long long v = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&v, g_checked_violations, sizeof(v)) != cudaSuccess) return -2;
+  cudaMemcpyToSymbol(g_checked_violations, &zero, sizeof(zero));
+  return (long long)v;
+#else
+  return -1;
+#endif
 }
 
 int pcb_embed_bwd(const int* tok, const float* dx, float* dW, int M, int D, int V, cudaStream_t s) {

@@ -30,6 +30,7 @@ from typing import Dict, List, Optional, Sequence
 import torch
 
 from .. import ops
+from ..utils.trace import nvtx_range
 from ..models.config import DecoderLmConfig
 from ..models.decoder_lm import DecoderLM, rope_tables
 from .arena import ParamArena, ParamSpec
@@ -394,9 +395,12 @@ class FusedDecoderTrainer:
         self.tok.copy_(self.tok_pin, non_blocking=True)
         self.tgt.copy_(self.tgt_pin, non_blocking=True)
         self.grad.zero_()
-        self._forward(True)
-        self._backward()
-        self._optimizer()
+        with nvtx_range("forward"):
+            self._forward(True)
+        with nvtx_range("backward"):
+            self._backward()
+        with nvtx_range("optimizer"):
+            self._optimizer()
         self.loss_pin.copy_(self.loss_sum, non_blocking=True)
 
     def _set_hyper(self, lr: float) -> None:

@@ -33,6 +33,7 @@ import torch
 import torch.distributed as dist
 
 from .. import ops
+from ..utils.trace import nvtx_range
 from ..models.config import DecoderLmConfig
 from ..models.decoder_lm import DecoderLM, rope_tables
 from .arena import ParamArena, ParamSpec
@@ -306,9 +307,12 @@ class TensorParallelTrainer:
         self.tgt.copy_(self.tgt_pin, non_blocking=True)
         self.grad["rep"].zero_()
         self.grad["shd"].zero_()
-        self._forward(True)
-        self._backward()
-        self._optimizer()
+        with nvtx_range("tp_forward"):
+            self._forward(True)
+        with nvtx_range("tp_backward"):
+            self._backward()
+        with nvtx_range("tp_optimizer"):
+            self._optimizer()
         self.loss_pin.copy_(self.loss_sum, non_blocking=True)
 
     def _set_hyper(self, lr: float) -> None:

@@ -77,6 +77,21 @@ def _check_gemm(a: torch.Tensor, b: torch.Tensor, a_mn: bool, b_mn: bool) -> Non
         raise ValueError(f"gemm: K mismatch ({K} vs {kb})")
 
 
+_DETERMINISTIC = os.environ.get("PCB_DETERMINISTIC", "0") == "1"
+
+
+def set_deterministic(on: bool) -> None:
+    """Deterministic reductions: weight-gradient GEMMs run without split-K, so every gradient element
+    receives exactly one partial sum and repeated runs are bitwise identical.  Slower when the output has
+    few tiles.  (The attention backward's dQ accumulation stays order-dependent.)"""
+    global _DETERMINISTIC
+    _DETERMINISTIC = bool(on)
+
+
+def deterministic() -> bool:
+    return _DETERMINISTIC
+
+
 def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = False, epi: int = EPI_BF16,
          c: Optional[torch.Tensor] = None, d: Optional[torch.Tensor] = None, aux: Optional[torch.Tensor] = None,
          bias: Optional[torch.Tensor] = None, alpha: float = 1.0, bn: int = 0, splits: int = 0,
@@ -95,6 +110,8 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = F
     slot ``rs_rank`` of owner ``m // rs_rows``'s buffer from the ``rs_peers`` table.
     """
     _check_gemm(a, b, a_mn, b_mn)
+    if epi == EPI_RED_F32 and splits == 0 and deterministic():
+        splits = 1          # one partial per output element: the atomic epilogue adds in a fixed order
     if c is None and epi in (EPI_BF16, EPI_F32):
         M = a.shape[1] if a_mn else a.shape[0]
         N = b.shape[1] if b_mn else b.shape[0]

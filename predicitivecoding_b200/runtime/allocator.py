@@ -54,3 +54,34 @@ class DeviceAllocator:
 
     def empty_cache(self) -> None:
         ops.ext().dev_release_cached(self.device)
+
+
+CANARY_BYTES = 256
+_CANARY_BYTE = 0xA5
+
+
+class CanaryAllocator(DeviceAllocator):
+    """Debug allocator: every block gets CANARY_BYTES of a fixed byte pattern behind it; `verify()`
+    reports blocks whose guard was overwritten (an out-of-bounds write by some kernel)."""
+
+    def __init__(self, device: int = 0):
+        super().__init__(device)
+        self._blocks = []
+
+    def alloc(self, shape, dtype=torch.float32, stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+        shape = tuple(shape) if not isinstance(shape, int) else (shape,)
+        n = 1
+        for s in shape:
+            n *= s
+        nbytes = max(1, n * _ELT[dtype])
+        st = (stream or torch.cuda.current_stream(self.device)).cuda_stream
+        raw = ops.ext().dev_alloc(nbytes + CANARY_BYTES, self.device, st)
+        raw[nbytes:nbytes + CANARY_BYTES].fill_(_CANARY_BYTE)
+        self._blocks.append((raw, nbytes))
+        return raw[:nbytes].view(dtype).view(shape)
+
+    def verify(self) -> list:
+        """Indices of blocks whose guard bytes changed (synchronises the device)."""
+        torch.cuda.synchronize(self.device)
+        return [i for i, (raw, n) in enumerate(self._blocks)
+                if not bool((raw[n:n + CANARY_BYTES] == _CANARY_BYTE).all())]

@@ -18,6 +18,8 @@ NVCC_FLAGS = [
     "--expt-relaxed-constexpr",
     "-Xptxas", "-warn-spills",
 ]
+if os.environ.get("PCB_CHECKED") == "1":   # debug build: bounds-violation counters in the kernels
+    NVCC_FLAGS.append("-DPCB_CHECKED")
 
 setup(
     name="predicitivecoding_b200",
