@@ -32,9 +32,10 @@ struct Cfg {
   static constexpr int A_BYTES = kBM * kBK * 2;
   static constexpr int B_BYTES = (BN / 2) * kBK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (BN == 256) ? 6 : 8;
+  static constexpr int STAGES = (BN == 256) ? 5 : 7;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr int EPI_OFF = STAGES * STAGE_BYTES + 256;       // 8 epilogue warps x [32 x 32] fp32
+  static constexpr int SMEM_BYTES = EPI_OFF + 8 * 32 * 32 * 4 + 1024;
 };
 
 // Tile -> (split, row-pair block, column block).  Without a gather the row block varies fastest.
@@ -284,6 +285,40 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int fcol = (n0 >> 1) + g * 64 + h * 32;
             store_bf16x32(reinterpret_cast<__nv_bfloat16*>(args.D) + (long long)m * args.ldd + fcol, o, nvalid);
           }
+        }
+      } else if (epi_coalesced<EPI>()) {
+        // transpose each 32x32 chunk through this warp's shared scratch (16-byte cells, XOR-swizzled by
+        // row) so that 8 lanes then cover one 128-byte row segment of the output
+        float4* scr = reinterpret_cast<float4*>(smem + C::EPI_OFF) + (warp - 2) * 32 * 8;
+        const int row0 = mb * 2 * kBM + rank * kBM + q * 32;
+        float sq = 0.f;
+#pragma unroll 1
+        for (int c = half; c < BN / 32; c += 2) {
+          float v[32];
+          tmem_load_f32x32(tbase + c * 32, v);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            scr[lane * 8 + (j ^ (lane & 7))] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          __syncwarp();
+          const int c4 = lane & 7, ncol = n0 + c * 32 + c4 * 4;
+          float pf[8][8];
+#pragma unroll
+          for (int it = 0; it < 8; ++it) {   // every row's operand loads in flight first
+            const int rr = it * 4 + (lane >> 3);
+            epi_prefetch<EPI>(args, row0 + rr, ncol, pf[it], row0 + rr < args.M);
+          }
+#pragma unroll
+          for (int it = 0; it < 8; ++it) {
+            const int rr = it * 4 + (lane >> 3);
+            const float4 x = scr[rr * 8 + (c4 ^ (rr & 7))];
+            float e[4] = {x.x, x.y, x.z, x.w};
+            sq += epilogue_vec4<EPI>(args, row0 + rr, ncol, e, pf[it], row0 + rr < args.M);
+          }
+          __syncwarp();
+        }
+        if (EPI == EPI_PC_PRED && args.pc_energy != nullptr) {
+          sq = warp_sum(sq);
+          if (lane == 0) atomicAdd(args.pc_energy, sq);
         }
       } else {
 #pragma unroll 1

@@ -263,4 +263,216 @@ PCB_DEVICE void epilogue_chunk(const GemmArgs& a, int m, int n, float (&v)[32], 
   }
 }
 
+
+// ---------------------------------------------------------------------------------------------
+// Coalesced epilogue: the same transformations, applied to 4 consecutive columns of one row by one
+// lane after the warp has transposed its 32x32 accumulator chunk through shared memory, so that 8
+// lanes cover one 128-byte row segment and every global load / store instruction touches 4 full
+// rows instead of 32 partial ones.  Returns this lane's squared-error contribution (EPI_PC_PRED).
+// EPI_SWIGLU_BWD has a vec4 form too but measured slower than the row path (its gate / up halves
+// are 64 columns apart), so it stays on the row path.
+template <int EPI>
+PCB_DEVICE constexpr bool epi_coalesced() {
+  return EPI == EPI_BF16 || EPI == EPI_F32 || EPI == EPI_ACC_F32 || EPI == EPI_RESID_F32 || EPI == EPI_RED_F32 ||
+         EPI == EPI_GELU || EPI == EPI_GELU_BWD || EPI == EPI_BF16_ACC ||
+         EPI == EPI_PC_PRED || EPI == EPI_PC_STATE || EPI == EPI_PC_WUPD;
+}
+
+PCB_DEVICE bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+PCB_DEVICE bool al8(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7) == 0; }
+
+PCB_DEVICE void ld_f32x4(const float* p, float (&v)[4], int nv) {
+  if (nv == 4 && al16(p)) {
+    const float4 f = *reinterpret_cast<const float4*>(p);
+    v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = j < nv ? p[j] : 0.f;
+  }
+}
+PCB_DEVICE void st_f32x4(float* p, const float (&v)[4], int nv) {
+  if (nv == 4 && al16(p)) {
+    *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (j < nv) p[j] = v[j];
+  }
+}
+PCB_DEVICE void ld_bf16x4(const __nv_bfloat16* p, float (&v)[4], int nv) {
+  if (nv == 4 && al8(p)) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    v[0] = bf16_lo(u.x); v[1] = bf16_hi(u.x); v[2] = bf16_lo(u.y); v[3] = bf16_hi(u.y);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = j < nv ? __bfloat162float(p[j]) : 0.f;
+  }
+}
+PCB_DEVICE void st_bf16x4(__nv_bfloat16* p, const float (&v)[4], int nv) {
+  if (nv == 4 && al8(p)) {
+    *reinterpret_cast<uint2*>(p) = make_uint2(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]));
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (j < nv) p[j] = __float2bfloat16_rn(v[j]);
+  }
+}
+
+// Everything a vec4 epilogue reads besides the accumulator and per-column vectors, issued for all
+// of a chunk's rows before any of them is finished so the loads overlap (p[0..3], p[4..7]).
+template <int EPI>
+PCB_DEVICE void epi_prefetch(const GemmArgs& a, int m, int n, float (&p)[8], bool row_ok) {
+  const int nv = min(4, a.N - n);
+  if (!row_ok || nv <= 0) return;
+  float* q0 = p;
+  float (&lo)[4] = *reinterpret_cast<float(*)[4]>(q0);
+  float (&hi)[4] = *reinterpret_cast<float(*)[4]>(q0 + 4);
+  if (EPI == EPI_ACC_F32 || EPI == EPI_PC_STATE || EPI == EPI_PC_WUPD) {
+    ld_f32x4(reinterpret_cast<const float*>(a.C) + (long long)m * a.ldc + n, lo, nv);
+    if (EPI == EPI_PC_STATE) {
+      if (a.aux != nullptr) ld_f32x4(reinterpret_cast<const float*>(a.aux) + (long long)m * a.ldaux + n, hi, nv);
+      else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) hi[j] = 0.f;
+      }
+    }
+  } else if (EPI == EPI_RESID_F32 || (EPI == EPI_PC_PRED)) {
+    if (EPI == EPI_PC_PRED && a.C == nullptr) return;
+    ld_f32x4(reinterpret_cast<const float*>(a.aux) + (long long)m * a.ldaux + n, lo, nv);
+  } else if (EPI == EPI_GELU_BWD || EPI == EPI_BF16_ACC) {
+    ld_bf16x4(reinterpret_cast<const __nv_bfloat16*>(a.aux) + (long long)m * a.ldaux + n, lo, nv);
+  } else if (EPI == EPI_SWIGLU_BWD) {
+    const long long gcol = (long long)(n >> 6) * 128 + (n & 63);
+    const __nv_bfloat16* pre = reinterpret_cast<const __nv_bfloat16*>(a.aux) + (long long)m * a.ldaux;
+    ld_bf16x4(pre + gcol, lo, nv);
+    ld_bf16x4(pre + gcol + 64, hi, nv);
+  }
+}
+
+template <int EPI>
+PCB_DEVICE float epilogue_vec4(const GemmArgs& a, int m, int n, float (&v)[4], const float (&p)[8], bool row_ok) {
+  const int nv = min(4, a.N - n);
+  if (!row_ok || nv <= 0) return 0.f;
+  if (EPI == EPI_BF16 || EPI == EPI_F32 || EPI == EPI_ACC_F32 || EPI == EPI_GELU || EPI == EPI_RESID_F32) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] *= a.alpha;
+    if (a.bias != nullptr) {
+      float b[4];
+      if (a.bias_bf16) ld_bf16x4(reinterpret_cast<const __nv_bfloat16*>(a.bias) + n, b, nv);
+      else ld_f32x4(reinterpret_cast<const float*>(a.bias) + n, b, nv);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] += b[j];
+    }
+  }
+  if (EPI == EPI_BF16) {
+    if (a.rope_cs != nullptr && n < a.rope_cols) {
+      const float2* cs = reinterpret_cast<const float2*>(a.rope_cs) + (long long)(m % a.rope_S) * (a.rope_hd >> 1);
+#pragma unroll
+      for (int j = 0; j < 4; j += 2) {
+        const float2 c = cs[((n + j) % a.rope_hd) >> 1];
+        const float x0 = v[j], x1 = v[j + 1];
+        v[j] = x0 * c.x - x1 * c.y;
+        v[j + 1] = x0 * c.y + x1 * c.x;
+      }
+    }
+    st_bf16x4(reinterpret_cast<__nv_bfloat16*>(a.C) + (long long)m * a.ldc + n, v, nv);
+  } else if (EPI == EPI_F32) {
+    st_f32x4(reinterpret_cast<float*>(a.C) + (long long)m * a.ldc + n, v, nv);
+  } else if (EPI == EPI_ACC_F32) {
+    float o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o[j] = p[j] + v[j];
+    st_f32x4(reinterpret_cast<float*>(a.C) + (long long)m * a.ldc + n, o, nv);
+  } else if (EPI == EPI_RESID_F32) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] += p[j];
+    st_f32x4(reinterpret_cast<float*>(a.C) + (long long)m * a.ldc + n, v, nv);
+  } else if (EPI == EPI_RED_F32) {
+    float* c = reinterpret_cast<float*>(a.C) + (long long)m * a.ldc + n;
+    if (nv == 4 && al16(c)) {
+      atomicAdd(reinterpret_cast<float4*>(c), make_float4(a.alpha * v[0], a.alpha * v[1], a.alpha * v[2], a.alpha * v[3]));
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (j < nv) atomicAdd(c + j, a.alpha * v[j]);
+    }
+  } else if (EPI == EPI_GELU) {
+    st_bf16x4(reinterpret_cast<__nv_bfloat16*>(a.C) + (long long)m * a.ldc + n, v, nv);
+    float g[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) g[j] = gelu_tanh_fast(__bfloat162float(__float2bfloat16_rn(v[j])));
+    st_bf16x4(reinterpret_cast<__nv_bfloat16*>(a.D) + (long long)m * a.ldd + n, g, nv);
+  } else if (EPI == EPI_GELU_BWD) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = a.alpha * v[j] * gelu_tanh_grad_fast(p[j]);
+    st_bf16x4(reinterpret_cast<__nv_bfloat16*>(a.C) + (long long)m * a.ldc + n, v, nv);
+  } else if (EPI == EPI_SWIGLU_BWD) {
+    const int grp = n >> 6, off = n & 63;
+    const long long gcol = (long long)grp * 128 + off;
+    float dg[4], du[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float g = p[j], u = p[4 + j];
+      const float dh = a.alpha * v[j];
+      const float s = __fdividef(1.f, 1.f + __expf(-g));
+      du[j] = dh * g * s;
+      dg[j] = dh * u * s * (1.f + g * (1.f - s));
+    }
+    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.C) + (long long)m * a.ldc;
+    st_bf16x4(out + gcol, dg, nv);
+    st_bf16x4(out + gcol + 64, du, nv);
+  } else if (EPI == EPI_BF16_ACC) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = a.alpha * v[j] + p[j];
+    st_bf16x4(reinterpret_cast<__nv_bfloat16*>(a.C) + (long long)m * a.ldc + n, v, nv);
+  } else if (EPI == EPI_PC_PRED) {
+    float b[4] = {0.f, 0.f, 0.f, 0.f};
+    if (a.bias != nullptr) ld_f32x4(reinterpret_cast<const float*>(a.bias) + n, b, nv);
+    float pre[4], pred[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      pre[j] = v[j] + b[j];
+      pred[j] = act_apply(a.act, pre[j]);
+    }
+    if (a.pc_pred_out != nullptr)
+      st_f32x4(reinterpret_cast<float*>(a.pc_pred_out) + (long long)m * a.ld_pred + n, pred, nv);
+    if (a.pc_pred_bf16 != nullptr)
+      st_bf16x4(reinterpret_cast<__nv_bfloat16*>(a.pc_pred_bf16) + (long long)m * a.ld_pred + n, pred, nv);
+    float sq = 0.f;
+    if (a.C != nullptr) {
+      float e[4], dl[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        e[j] = a.pc_pi * (p[j] - pred[j]);
+        dl[j] = act_deriv(a.act, pre[j], pred[j]) * e[j];
+        if (j < nv) sq += e[j] * e[j];
+      }
+      st_f32x4(reinterpret_cast<float*>(a.C) + (long long)m * a.ldc + n, e, nv);
+      if (a.D != nullptr) st_bf16x4(reinterpret_cast<__nv_bfloat16*>(a.D) + (long long)m * a.ldd + n, dl, nv);
+    }
+    return sq;
+  } else if (EPI == EPI_PC_STATE) {
+    float* mu = reinterpret_cast<float*>(a.C) + (long long)m * a.ldc + n;
+    float s[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) s[j] = p[j];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float grad = p[4 + j] - v[j];
+      if (a.pc_actreg > 0.f) grad += a.pc_actreg * (s[j] > 0.f ? 1.f : (s[j] < 0.f ? -1.f : 0.f));
+      s[j] -= a.pc_eta * grad;
+    }
+    st_f32x4(mu, s, nv);
+    if (a.D != nullptr) st_bf16x4(reinterpret_cast<__nv_bfloat16*>(a.D) + (long long)m * a.ldd + n, s, nv);
+  } else if (EPI == EPI_PC_WUPD) {
+    float* w = reinterpret_cast<float*>(a.C) + (long long)m * a.ldc + n;
+    float x[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) x[j] = (p[j] + a.alpha * v[j]) * a.pc_decay;
+    st_f32x4(w, x, nv);
+    if (a.D != nullptr) st_bf16x4(reinterpret_cast<__nv_bfloat16*>(a.D) + (long long)m * a.ldd + n, x, nv);
+  }
+  return 0.f;
+}
+
 }  // namespace pcb
