@@ -320,6 +320,61 @@ __global__ void __launch_bounds__(kThreads, 1)
           sq = warp_sum(sq);
           if (lane == 0) atomicAdd(args.pc_energy, sq);
         }
+      } else if (EPI == EPI_SWIGLU_BWD) {
+        // row path with the next chunk's gate / up rows prefetched while this chunk is finished
+        const __nv_bfloat16* pre = reinterpret_cast<const __nv_bfloat16*>(args.aux) + (long long)m * args.ldaux;
+        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.C) + (long long)m * args.ldc;
+        auto gcol_of = [&](int c) -> long long {
+          const int n = n0 + c * 32;
+          return (long long)(n >> 6) * 128 + (n & 63);
+        };
+        const bool vec_ok = (args.ldaux % 8) == 0 && (args.ldc % 8) == 0 &&
+                            ((reinterpret_cast<uintptr_t>(args.aux) | reinterpret_cast<uintptr_t>(args.C)) & 15) == 0;
+        auto fetch = [&](int c, uint4 (&g4)[4], uint4 (&u4)[4]) {
+          const int nvalid = min(32, args.N - (n0 + c * 32));
+          if (vec_ok && row_ok && nvalid >= 32) {
+            const uint4* gp = reinterpret_cast<const uint4*>(pre + gcol_of(c));
+            const uint4* up = reinterpret_cast<const uint4*>(pre + gcol_of(c) + 64);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              g4[j] = gp[j];
+              u4[j] = up[j];
+            }
+          }
+        };
+        uint4 cg[4], cu[4], ng[4], nu[4];
+        fetch(half, cg, cu);
+#pragma unroll 1
+        for (int c = half; c < BN / 32; c += 2) {
+          if (c + 2 < BN / 32) fetch(c + 2, ng, nu);
+          float v[32];
+          tmem_load_f32x32(tbase + c * 32, v);
+          const int n = n0 + c * 32;
+          const int nvalid = min(32, args.N - n);
+          if (vec_ok && row_ok && nvalid >= 32) {
+            float dg[32], du[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const uint32_t gw = reinterpret_cast<const uint32_t*>(cg)[j >> 1];
+              const uint32_t uw = reinterpret_cast<const uint32_t*>(cu)[j >> 1];
+              const float g = (j & 1) ? bf16_hi(gw) : bf16_lo(gw);
+              const float u = (j & 1) ? bf16_hi(uw) : bf16_lo(uw);
+              const float dh = args.alpha * v[j];
+              const float sg = __fdividef(1.f, 1.f + __expf(-g));
+              du[j] = dh * g * sg;
+              dg[j] = dh * u * sg * (1.f + g * (1.f - sg));
+            }
+            store_bf16x32(out + gcol_of(c), dg, 32);
+            store_bf16x32(out + gcol_of(c) + 64, du, 32);
+          } else {
+            epilogue_chunk<EPI>(args, m, n, v, row_ok);
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            cg[j] = ng[j];
+            cu[j] = nu[j];
+          }
+        }
       } else {
 #pragma unroll 1
         for (int c = half; c < BN / 32; c += 2) {
