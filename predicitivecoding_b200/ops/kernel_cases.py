@@ -13,7 +13,8 @@ import json
 
 import torch
 
-from . import ext, gemm, gemm_pc, attn_fwd, attn_bwd, EPI_SWIGLU, EPI_RED_F32, EPI_PC_PRED, EPI_PC_STATE
+from . import (ext, gemm, gemm_pc, attn_fwd, attn_bwd, EPI_BF16, EPI_F32, EPI_RESID_F32, EPI_SWIGLU, EPI_SWIGLU_BWD,
+               EPI_RED_F32, EPI_PC_PRED, EPI_PC_STATE)
 
 CASES = ("gemm_swiglu", "gemm_dw", "pc_pred", "pc_state", "attn_fwd", "attn_fwd_mma", "attn_bwd")
 
@@ -85,12 +86,77 @@ def time_case(which: str, iters: int = 20) -> dict:
     return {"case": which, "us": round(us, 2), "tflops": round(flops / us * 1e-6, 1)}
 
 
+def decoder_gemm_table(iters: int = 20) -> list:
+    """Every GEMM of one layer of the 124M decoder step (micro-batch 16 x 1024 tokens) plus the LM head,
+    with the epilogue the fused trainer uses; CUDA-event time per launch and TFLOP/s."""
+    dev = "cuda"
+    M, D, F, V = 16384, 768, 2048, 32000
+    bf = torch.bfloat16
+
+    def rn(*shape, dt=bf):
+        return torch.randn(*shape, device=dev).to(dt)
+
+    rows = []
+
+    def t(fn, flops, name, it=iters):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(it):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        us = a.elapsed_time(b) * 1e3 / it
+        rows.append({"gemm": name, "us": round(us, 1), "tflops": round(flops / us * 1e-6, 1)})
+
+    n1, x = rn(M, D), rn(M, D, dt=torch.float32)
+    wqkv, wo, w13, w2, wout = rn(3 * D, D), rn(D, D), rn(2 * F, D), rn(D, F), rn(V, D)
+    qkv = torch.empty(M, 3 * D, device=dev, dtype=bf)
+    xo = torch.empty(M, D, device=dev)
+    pre = torch.empty(M, 2 * F, device=dev, dtype=bf)
+    act = torch.empty(M, F, device=dev, dtype=bf)
+    logits = torch.empty(M, V, device=dev, dtype=bf)
+    dn = torch.empty(M, D, device=dev)
+    t(lambda: gemm(n1, wqkv, epi=EPI_BF16, c=qkv), 2 * M * D * 3 * D, "qkv fwd [M,2304,768] bf16")
+    ao = rn(M, D)
+    t(lambda: gemm(ao, wo, epi=EPI_RESID_F32, c=xo, aux=x), 2 * M * D * D, "o fwd [M,768,768] +resid f32")
+    t(lambda: gemm(n1, w13, epi=EPI_SWIGLU, c=pre, d=act), 2 * M * D * 2 * F, "w13 fwd [M,4096,768] swiglu")
+    t(lambda: gemm(act, w2, epi=EPI_RESID_F32, c=xo, aux=x), 2 * M * F * D, "w2 fwd [M,768,2048] +resid f32")
+    t(lambda: gemm(n1, wout, epi=EPI_BF16, c=logits), 2 * M * D * V, "lm head [M,32000,768]", 5)
+    t(lambda: gemm(logits, wout, b_mn=True, epi=EPI_F32, c=dn), 2 * M * D * V, "lm dgrad [M,768,32000]", 5)
+    gW = torch.zeros(V, D, device=dev)
+    t(lambda: gemm(logits, n1, a_mn=True, b_mn=True, epi=EPI_RED_F32, c=gW), 2 * M * D * V, "lm wgrad [32000,768,M]", 5)
+    dx16, dpre = rn(M, D), torch.empty(M, 2 * F, device=dev, dtype=bf)
+    t(lambda: gemm(dx16, w2, b_mn=True, epi=EPI_SWIGLU_BWD, c=dpre, aux=pre), 2 * M * D * F,
+      "w2 dgrad [M,2048,768] swiglu bwd")
+    g2 = torch.zeros(D, F, device=dev)
+    t(lambda: gemm(dx16, act, a_mn=True, b_mn=True, epi=EPI_RED_F32, c=g2), 2 * M * D * F, "w2 wgrad [768,2048,M]")
+    g13 = torch.zeros(2 * F, D, device=dev)
+    t(lambda: gemm(dpre, n1, a_mn=True, b_mn=True, epi=EPI_RED_F32, c=g13), 2 * M * D * 2 * F, "w13 wgrad [4096,768,M]")
+    t(lambda: gemm(dpre, w13, b_mn=True, epi=EPI_F32, c=dn), 2 * M * D * 2 * F, "w13 dgrad [M,768,4096] f32")
+    dao = torch.empty(M, D, device=dev, dtype=bf)
+    t(lambda: gemm(dx16, wo, b_mn=True, epi=EPI_BF16, c=dao), 2 * M * D * D, "o dgrad [M,768,768] bf16")
+    go = torch.zeros(D, D, device=dev)
+    t(lambda: gemm(dx16, ao, a_mn=True, b_mn=True, epi=EPI_RED_F32, c=go), 2 * M * D * D, "o wgrad [768,768,M]")
+    dqkv = rn(M, 3 * D)
+    gq = torch.zeros(3 * D, D, device=dev)
+    t(lambda: gemm(dqkv, n1, a_mn=True, b_mn=True, epi=EPI_RED_F32, c=gq), 2 * M * D * 3 * D, "qkv wgrad [2304,768,M]")
+    t(lambda: gemm(dqkv, wqkv, b_mn=True, epi=EPI_F32, c=dn), 2 * M * D * 3 * D, "qkv dgrad [M,768,2304] f32")
+    return rows
+
+
 def main() -> None:
     p = argparse.ArgumentParser()
-    p.add_argument("case", choices=CASES + ("all",))
+    p.add_argument("case", choices=CASES + ("all", "decoder_gemms"))
     p.add_argument("--time", type=int, default=0, help="time N launches after warm-up")
     a = p.parse_args()
     ext()
+    if a.case == "decoder_gemms":
+        for row in decoder_gemm_table():
+            print(json.dumps(row))
+        return
     for c in (CASES if a.case == "all" else (a.case,)):
         if a.time:
             print(json.dumps(time_case(c, a.time)))
