@@ -17,6 +17,8 @@ a constant row uses s = max(|min|, 1e-12)/127, z = 0.  bf16 rounding is round-to
 """
 from __future__ import annotations
 
+import enum
+
 import struct
 
 import numpy as np
@@ -26,6 +28,15 @@ from ..pc.layer import Layer
 
 _HDR = struct.Struct("<iiffff BB 2x")
 PRECISIONS = ("float32", "half", "bfloat16", "int8")
+
+
+class WeightStoragePrecision(str, enum.Enum):
+    """Stored weight precision (Model/WeightStoragePrecision.cs:12); members compare equal to the strings
+    accepted everywhere a precision is taken."""
+    FLOAT32 = "float32"
+    HALF = "half"
+    BFLOAT16 = "bfloat16"
+    INT8 = "int8"
 _FLAG = {"float32": 0, "half": 4, "bfloat16": 8, "int8": 16}
 
 
