@@ -1,0 +1,133 @@
+"""Device timing of the fused peer-memory collectives against their NVLink roofline.
+
+Run one process per GPU, e.g. on 8 GPUs:
+
+    timeout -k 60 600 python -m torch.distributed.run --nnodes=1 --nproc-per-node 8 --master-addr 127.0.0.1 \\
+        --master-port 29541 -m predicitivecoding_b200.parallel.bench_collectives
+
+Cases (each timed with CUDA events on the launching stream after warm-up, max over ranks):
+
+* ``rs_adamw_ag``: the data-parallel optimizer step of the 124M decoder (134,105,856 parameters):
+  every rank reads its 1/T shard of every rank's fp32 gradients over NVLink, runs AdamW on it and
+  writes the bf16 weights of the shard into every rank's weight buffer.  Bytes that cross NVLink per
+  rank: in (T-1)/T * N * 4, out (T-1)/T * N * 2;
+* ``pc_allreduce_update``: the PC data-parallel weight step (64 Mi fp32 weights): sum of every
+  rank's delta-W shard, weight update, fp32 + bf16 weights written to every rank.  In (T-1)/T * N * 4,
+  out (T-1)/T * N * 6;
+* ``all_reduce``: the Communicator's peer all-reduce (one-shot below 512 KiB, two-shot above).
+
+The roofline time is the slower direction's bytes at the measured 770 GB/s per direction per GPU;
+each line reports achieved / roofline.  Every case includes the device barriers it needs in the
+trainer (before: all inputs written; after: all outputs written).
+"""
+from __future__ import annotations
+
+import json
+import os
+from datetime import timedelta
+
+import torch
+import torch.distributed as dist
+
+LINK_GBS = 770.0   # measured peer copy per direction per GPU on this pool
+
+
+def _time(fn, iters: int, dev) -> float:
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s = torch.cuda.current_stream(dev)
+    a.record(s)
+    for _ in range(iters):
+        fn()
+    b.record(s)
+    torch.cuda.synchronize(dev)
+    t = torch.tensor([a.elapsed_time(b) / iters], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t)
+
+
+def main() -> None:
+    from .. import ops
+    from .collectives import Communicator
+    from .peer import PeerGroup
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    rank, T = dist.get_rank(), dist.get_world_size()
+    peer = PeerGroup(None, dev)
+    out = []
+
+    # ---- data-parallel AdamW step of the 124M decoder
+    N = 134_105_856
+    N -= N % (8 * T)
+    grad = peer.symmetric(N, torch.float32)
+    w16 = peer.symmetric(N, torch.bfloat16)
+    grad.local.normal_()
+    per = N // T
+    lo, hi = rank * per, (rank + 1) * per
+    w32 = torch.randn(per, device=dev)
+    m = torch.zeros(per, device=dev)
+    v = torch.zeros(per, device=dev)
+    hyper = torch.tensor([1e-4, 0.1, 0.1, 0.001, 1.0 / T, 0, 0, 0], device=dev)
+
+    def dp_step():
+        peer.barrier()
+        ops.ext().rs_adamw_ag(grad.ptrs, w16.ptrs, w32, m, v, lo, hi, hi, hyper, 0.9, 0.999, 1e-8, T)
+        peer.barrier()
+
+    ms = _time(dp_step, 10, dev)
+    b_in, b_out = (T - 1) / T * N * 4, (T - 1) / T * N * 2
+    roof = max(b_in, b_out) / (LINK_GBS * 1e9) * 1e3
+    out.append({"case": "rs_adamw_ag (124M params, fp32 grads in, bf16 weights out)", "world": T,
+                "ms": round(ms, 3), "nvlink_in_gb": round(b_in / 1e9, 3), "nvlink_out_gb": round(b_out / 1e9, 3),
+                "roofline_ms": round(roof, 3), "of_roofline": round(roof / ms, 3) if T > 1 else None})
+    del grad, w16, w32, m, v
+
+    # ---- PC data-parallel delta-W all-reduce + update
+    N2 = 64 << 20
+    dlt = peer.symmetric(N2, torch.float32)
+    wts = peer.symmetric(N2, torch.float32)
+    w16b = peer.symmetric(N2, torch.bfloat16)
+    dlt.local.normal_()
+    wts.local.normal_()
+    per2 = N2 // T
+    lo2, hi2 = rank * per2, (rank + 1) * per2
+
+    def pc_step():
+        peer.barrier()
+        ops.ext().pc_allreduce_update(dlt.ptrs, wts.ptrs, w16b.ptrs, lo2, hi2, 1e-6, 1.0, T, rank)
+        peer.barrier()
+
+    ms = _time(pc_step, 10, dev)
+    b_in, b_out = (T - 1) / T * N2 * 4, (T - 1) / T * N2 * 6
+    roof = max(b_in, b_out) / (LINK_GBS * 1e9) * 1e3
+    out.append({"case": "pc_allreduce_update (64 Mi fp32 weights)", "world": T, "ms": round(ms, 3),
+                "nvlink_in_gb": round(b_in / 1e9, 3), "nvlink_out_gb": round(b_out / 1e9, 3),
+                "roofline_ms": round(roof, 3), "of_roofline": round(roof / ms, 3) if T > 1 else None})
+    del dlt, wts, w16b
+
+    # ---- Communicator all-reduce (fp32)
+    comm = Communicator(None, backend="peer", device=dev, capacity_bytes=256 << 20)
+    for nbytes in (256 << 10, 32 << 20, 256 << 20):
+        x = torch.randn(nbytes // 4, device=dev)
+        ms = _time(lambda: comm.all_reduce(x), 10, dev)
+        # ring-equivalent bytes per direction: 2 (T-1)/T * size
+        roof = 2 * (T - 1) / T * nbytes / (LINK_GBS * 1e9) * 1e3
+        out.append({"case": f"all_reduce fp32 {nbytes >> 10} KiB", "world": T, "ms": round(ms, 4),
+                    "bus_gbs": round(2 * (T - 1) / T * nbytes / (ms * 1e-3) / 1e9, 1),
+                    "roofline_ms": round(roof, 4), "of_roofline": round(roof / ms, 3) if T > 1 else None})
+    peer.check()
+    comm.check()
+    if rank == 0:
+        for o in out:
+            print(json.dumps(o), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
