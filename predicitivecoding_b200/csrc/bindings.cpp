@@ -109,8 +109,11 @@ cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
 
 void check(int rc, const char* what, int kernels = 1) {
   g_launches.fetch_add(kernels, std::memory_order_relaxed);
-  PCB_CHECK(rc == 0, "pcb kernel '", what, "' failed with code ", rc, " (",
-              cudaGetErrorString(cudaGetLastError()), ")");
+  if (rc == 0) return;
+  // Only the numeric CUDA status goes into the message: formatting the runtime's error string here
+  // crashed the process on GPU hosts instead of raising.
+  const int e = (int)cudaGetLastError();
+  PCB_CHECK(false, "pcb kernel '", what, "' failed with code ", rc, " (cuda status ", e, ")");
 }
 
 void req(const at::Tensor& t, at::ScalarType dt, const char* name) {

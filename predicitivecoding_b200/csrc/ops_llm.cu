@@ -115,15 +115,27 @@ __global__ void rmsnorm_bwd_kernel(const float* __restrict__ dy, const float* __
   for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < M; row += gridDim.x * warps) {
     const float4* xr = reinterpret_cast<const float4*>(x + (long long)row * D);
     const float4* dyr = reinterpret_cast<const float4*>(dy + (long long)row * D);
+    float4* dxr = reinterpret_cast<float4*>(dx + (long long)row * D);
     const float inv = inv_in[row];
-    float4 xv[VPT], dv[VPT];
-    float dot = 0.f;
+    // Up to D = 1024 every load of the row (x, dy and, when accumulating, dx) is issued before any
+    // arithmetic; wider rows read the previous dx at the store, which keeps the row within registers.
+    constexpr bool kBatchPrev = VPT <= 8;
+    constexpr int PV = kBatchPrev ? VPT : 1;
+    float4 xv[VPT], dv[VPT], pv[PV];
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
       const int c = lane + 32 * i;
       if (c < nvec) {
         xv[i] = xr[c];
         dv[i] = dyr[c];
+        if constexpr (kBatchPrev) pv[i] = accumulate ? dxr[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    float dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int c = lane + 32 * i;
+      if (c < nvec) {
         const float4 gg = load_g4(g, c);
         dot += gg.x * dv[i].x * xv[i].x + gg.y * dv[i].y * xv[i].y + gg.z * dv[i].z * xv[i].z +
                gg.w * dv[i].w * xv[i].w;
@@ -135,21 +147,19 @@ __global__ void rmsnorm_bwd_kernel(const float* __restrict__ dy, const float* __
     }
     dot = warp_sum(dot);
     const float k = inv * inv * dot / (float)D;
-    float4* dxr = reinterpret_cast<float4*>(dx + (long long)row * D);
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
       const int c = lane + 32 * i;
       if (c < nvec) {
         const float4 gg = load_g4(g, c);
+        float4 p;
+        if constexpr (kBatchPrev) p = pv[i];
+        else p = accumulate ? dxr[c] : make_float4(0.f, 0.f, 0.f, 0.f);
         float4 o;
-        o.x = inv * (gg.x * dv[i].x - xv[i].x * k);
-        o.y = inv * (gg.y * dv[i].y - xv[i].y * k);
-        o.z = inv * (gg.z * dv[i].z - xv[i].z * k);
-        o.w = inv * (gg.w * dv[i].w - xv[i].w * k);
-        if (accumulate) {
-          const float4 p = dxr[c];
-          o.x += p.x; o.y += p.y; o.z += p.z; o.w += p.w;
-        }
+        o.x = inv * (gg.x * dv[i].x - xv[i].x * k) + p.x;
+        o.y = inv * (gg.y * dv[i].y - xv[i].y * k) + p.y;
+        o.z = inv * (gg.z * dv[i].z - xv[i].z * k) + p.z;
+        o.w = inv * (gg.w * dv[i].w - xv[i].w * k) + p.w;
         dxr[c] = o;
         if (dx16 != nullptr) {
           uint2 u;
@@ -212,7 +222,8 @@ __global__ void ce_fwd_bwd_kernel(__nv_bfloat16* __restrict__ logits, long long 
   const int t = tgt[r];
   __shared__ float s_m[32], s_s[32];
   float mx = -INFINITY, sm = 0.f;
-  const int nvec = V / 8;  // 16-byte vectors; the V % 8 tail is handled element-wise
+  // 16-byte vectors when the row stride allows them; the rest is handled element-wise
+  const int nvec = (ld % 8 == 0 && ((uintptr_t)logits & 15) == 0) ? V / 8 : 0;
   const uint4* rv = reinterpret_cast<const uint4*>(row);
   for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
     const uint4 u = rv[i];
@@ -293,6 +304,97 @@ __global__ void ce_fwd_bwd_kernel(__nv_bfloat16* __restrict__ logits, long long 
     float p = counted ? __expf(__bfloat162float(row[j]) - lse) : 0.f;
     if (counted && j == t) p -= 1.f;
     row[j] = __float2bfloat16(p * scale);
+  }
+}
+
+// Register-resident variant for V <= 8 * 512 * RV (V % 8 == 0): a persistent block of 512 threads owns
+// one row at a time with the whole row in registers, so each logit is read once, exponentiated once
+// (p = exp(f - max) is kept for the gradient) and written once.  The next row's loads are issued
+// before the block-wide sum reduction of the current row, so HBM traffic continues through the
+// reductions and the gradient stores.
+template <int RV>
+__global__ void __launch_bounds__(512, 1)
+    ce_rows_kernel(__nv_bfloat16* __restrict__ logits, long long ld, const int* __restrict__ tgt,
+                   float* __restrict__ loss, int M, int V, float scale, int write_grad) {
+  __shared__ float red_m[2][16], red_s[2][16];
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int nvec = V >> 3;
+  int r = blockIdx.x;
+  if (r >= M) return;
+  uint4 raw[RV];
+  auto load_row = [&](int row) {
+    const uint4* rv = reinterpret_cast<const uint4*>(logits + (long long)row * ld);
+#pragma unroll
+    for (int i = 0; i < RV; ++i) {
+      const int c = tid + 512 * i;
+      raw[i] = c < nvec ? rv[c] : make_uint4(0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u);  // -inf
+    }
+  };
+  load_row(r);
+  int par = 0;
+  while (true) {
+    const int t = tgt[r];
+    const bool counted = t >= 0 && t < V;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < RV; ++i) {
+      mx = fmaxf(mx, fmaxf(fmaxf(bf16_lo(raw[i].x), bf16_hi(raw[i].x)), fmaxf(bf16_lo(raw[i].y), bf16_hi(raw[i].y))));
+      mx = fmaxf(mx, fmaxf(fmaxf(bf16_lo(raw[i].z), bf16_hi(raw[i].z)), fmaxf(bf16_lo(raw[i].w), bf16_hi(raw[i].w))));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) red_m[par][w] = mx;
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < 16; ++k) mx = fmaxf(mx, red_m[par][k]);
+    float p[RV * 8];
+    float sm = 0.f, ft = 0.f;
+    bool own = false;
+#pragma unroll
+    for (int i = 0; i < RV; ++i) {
+      const float f[8] = {bf16_lo(raw[i].x), bf16_hi(raw[i].x), bf16_lo(raw[i].y), bf16_hi(raw[i].y),
+                          bf16_lo(raw[i].z), bf16_hi(raw[i].z), bf16_lo(raw[i].w), bf16_hi(raw[i].w)};
+      const int base = 8 * (tid + 512 * i);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        p[8 * i + j] = __expf(f[j] - mx);
+        sm += p[8 * i + j];
+        if (base + j == t) { ft = f[j]; own = true; }
+      }
+    }
+    const int next = r + gridDim.x;
+    if (next < M) load_row(next);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
+    if (lane == 0) red_s[par][w] = sm;
+    __syncthreads();
+    sm = 0.f;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) sm += red_s[par][k];
+    if (own) loss[r] = mx + __logf(sm) - ft;
+    else if (!counted && tid == 0) loss[r] = 0.f;
+    if (write_grad) {
+      const float k = counted ? scale / sm : 0.f;
+      uint4* wv = reinterpret_cast<uint4*>(logits + (long long)r * ld);
+#pragma unroll
+      for (int i = 0; i < RV; ++i) {
+        const int c = tid + 512 * i;
+        if (c < nvec) {
+          float g[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) g[j] = p[8 * i + j] * k - (8 * c + j == t ? scale : 0.f);
+          uint4 o;
+          o.x = pack_bf16x2(g[0], g[1]);
+          o.y = pack_bf16x2(g[2], g[3]);
+          o.z = pack_bf16x2(g[4], g[5]);
+          o.w = pack_bf16x2(g[6], g[7]);
+          wv[c] = o;
+        }
+      }
+    }
+    if (next >= M) break;
+    r = next;
+    par ^= 1;
   }
 }
 
@@ -429,21 +531,49 @@ int pcb_rmsnorm_fwd(const float* x, const void* gv, void* y, float* inv, int M, 
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
+// One warp per row with exactly ceil(D / 128) float4 per lane (registers are sized to the row, so
+// occupancy is not spent on unused lanes); a persistent grid of every block that fits at once.
+template <int VPT>
+static int launch_rmsnorm_bwd(const float* dy, const float* x, const __nv_bfloat16* g, const float* inv, float* dx,
+                              __nv_bfloat16* dx16, float* dg, int M, int D, int accumulate, int num_sms,
+                              cudaStream_t s) {
+  static int per_sm = 0;
+  if (per_sm == 0) {
+    int n = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, rmsnorm_bwd_kernel<VPT>, 256, 128 * VPT * sizeof(float));
+    per_sm = n > 0 ? n : 1;
+  }
+  int grid = (M + 7) / 8;
+  const int cap = (num_sms > 0 ? num_sms : 148) * per_sm;
+  if (grid > cap) grid = cap;
+  rmsnorm_bwd_kernel<VPT><<<grid, 256, (size_t)D * sizeof(float), s>>>(dy, x, g, inv, dx, dx16, dg, M, D, accumulate);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
 int pcb_rmsnorm_bwd(const float* dy, const float* x, const void* gv, const float* inv, float* dx, void* dx16v,
                     float* dg, int M, int D, int accumulate, int num_sms, cudaStream_t s) {
   const __nv_bfloat16* g = reinterpret_cast<const __nv_bfloat16*>(gv);
   __nv_bfloat16* dx16 = reinterpret_cast<__nv_bfloat16*>(dx16v);
   if (D % 4 || D > 4096) return -1;
-  const int warps = 8;
-  int grid = (M + warps - 1) / warps;
-  const int cap = (num_sms > 0 ? num_sms : 148) * 4;
-  if (grid > cap) grid = cap;
-  const size_t sm = (size_t)D * sizeof(float);
-  if (D <= 512) rmsnorm_bwd_kernel<4><<<grid, 256, sm, s>>>(dy, x, g, inv, dx, dx16, dg, M, D, accumulate);
-  else if (D <= 1024) rmsnorm_bwd_kernel<8><<<grid, 256, sm, s>>>(dy, x, g, inv, dx, dx16, dg, M, D, accumulate);
-  else if (D <= 2048) rmsnorm_bwd_kernel<16><<<grid, 256, sm, s>>>(dy, x, g, inv, dx, dx16, dg, M, D, accumulate);
-  else rmsnorm_bwd_kernel<32><<<grid, 256, sm, s>>>(dy, x, g, inv, dx, dx16, dg, M, D, accumulate);
-  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+  if (M <= 0) return 0;
+  const int v = (D / 4 + 31) / 32;
+#define PCB_RMS_BWD(N) launch_rmsnorm_bwd<N>(dy, x, g, inv, dx, dx16, dg, M, D, accumulate, num_sms, s)
+  switch (v) {
+    case 1: return PCB_RMS_BWD(1);
+    case 2: return PCB_RMS_BWD(2);
+    case 3: return PCB_RMS_BWD(3);
+    case 4: return PCB_RMS_BWD(4);
+    case 5: return PCB_RMS_BWD(5);
+    case 6: return PCB_RMS_BWD(6);
+    case 7: return PCB_RMS_BWD(7);
+    case 8: return PCB_RMS_BWD(8);
+    default: break;
+  }
+  if (v <= 12) return PCB_RMS_BWD(12);
+  if (v <= 16) return PCB_RMS_BWD(16);
+  if (v <= 24) return PCB_RMS_BWD(24);
+  return PCB_RMS_BWD(32);
+#undef PCB_RMS_BWD
 }
 
 int pcb_rope(void* buf, long long ld, const float* cs, int M, int S, int D, int hd, int nparts, float sign,
@@ -457,7 +587,20 @@ int pcb_rope(void* buf, long long ld, const float* cs, int M, int S, int D, int 
 
 int pcb_ce(void* logits, long long ld, const int* tgt, float* loss, int M, int V, float scale, int write_grad,
            cudaStream_t s) {
-  if (ld % 8) return -1;
+  if (M <= 0) return 0;
+  const int nvec = V / 8;
+  if (((uintptr_t)logits & 15) == 0 && ld % 8 == 0 && V % 8 == 0 && nvec <= 8 * 512 && M > 0) {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int grid = M < sms ? M : sms;
+    auto* lg = reinterpret_cast<__nv_bfloat16*>(logits);
+    if (nvec <= 512) ce_rows_kernel<1><<<grid, 512, 0, s>>>(lg, ld, tgt, loss, M, V, scale, write_grad);
+    else if (nvec <= 1024) ce_rows_kernel<2><<<grid, 512, 0, s>>>(lg, ld, tgt, loss, M, V, scale, write_grad);
+    else if (nvec <= 2048) ce_rows_kernel<4><<<grid, 512, 0, s>>>(lg, ld, tgt, loss, M, V, scale, write_grad);
+    else ce_rows_kernel<8><<<grid, 512, 0, s>>>(lg, ld, tgt, loss, M, V, scale, write_grad);
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+  }
   ce_fwd_bwd_kernel<<<M, 512, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(logits), ld, tgt, loss, M, V, scale,
                                        write_grad);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;

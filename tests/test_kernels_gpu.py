@@ -152,8 +152,9 @@ def test_gemm_swiglu_and_bwd():
     assert rel_err(d[:, :, 1].reshape(M, F), uu.grad) < 0.02
 
 
-def test_rmsnorm_fwd_bwd():
-    M, D = 1000, 768
+@pytest.mark.parametrize("D", [768, 2048, 3072])
+def test_rmsnorm_fwd_bwd(D):
+    M = 1000
     x = torch.randn(M, D, device=DEV)
     g = (1 + 0.1 * torch.randn(D, device=DEV)).to(torch.bfloat16)
     y = torch.empty(M, D, device=DEV, dtype=torch.bfloat16)
@@ -194,8 +195,10 @@ def test_rope_roundtrip_and_values():
     assert rel_err(out, qkv) < 0.02
 
 
-def test_cross_entropy_fused():
-    M, V = 300, 32000
+@pytest.mark.parametrize("V", [32000, 1000, 4104, 50257])
+def test_cross_entropy_fused(V):
+    # 32000 / 1000 / 4104: register-resident rows (8, 1 and 2 vectors per thread); 50257: streaming path
+    M = 300
     logits = (torch.randn(M, V, device=DEV) * 2).to(torch.bfloat16)
     tgt = torch.randint(0, V, (M,), device=DEV, dtype=torch.int32)
     tgt[5] = -1
