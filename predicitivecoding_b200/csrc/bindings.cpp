@@ -675,6 +675,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_bwd_tc", &attn_bwd_tc);
   m.def("attn_bwd", &attn_bwd);
   m.def("launch_count", &launch_count);
+  m.def("_check_status", [](int rc) { check(rc, "status probe", 0); });
   m.def("set_gemm_mode", [](int64_t m) { pcb_set_gemm_mode((int)m); },
         "GEMM kernel choice: -1 env/auto, 0 auto, 1 single-CTA only, 2 CTA pairs when legal");
   m.def("decode_attn", &decode_attn);

@@ -16,7 +16,7 @@ import torch
 from . import (ext, gemm, gemm_pc, attn_fwd, attn_bwd, EPI_BF16, EPI_F32, EPI_RESID_F32, EPI_SWIGLU, EPI_SWIGLU_BWD,
                EPI_RED_F32, EPI_PC_PRED, EPI_PC_STATE)
 
-CASES = ("gemm_swiglu", "gemm_dw", "pc_pred", "pc_state", "attn_fwd", "attn_fwd_mma", "attn_bwd")
+CASES = ("gemm_swiglu", "gemm_lmhead", "gemm_dw", "pc_pred", "pc_state", "attn_fwd", "attn_fwd_mma", "attn_bwd")
 
 
 def build(which: str, dev: str = "cuda"):
@@ -33,6 +33,11 @@ def build(which: str, dev: str = "cuda"):
         pre = torch.empty(M, 2 * F, device=dev, dtype=bf)
         act = torch.empty(M, F, device=dev, dtype=bf)
         return (lambda: gemm(x, w, epi=EPI_SWIGLU, c=pre, d=act)), 2 * M * 2 * F * D
+    if which == "gemm_lmhead":          # decoder LM head (vocabulary 32000, d 768) on 4 sequences of 1024
+        M, D, V = 4096, 768, 32000
+        x, w = rn(M, D).to(bf), rn(V, D, scale=0.03).to(bf)
+        logits = torch.empty(M, V, device=dev, dtype=bf)
+        return (lambda: gemm(x, w, epi=EPI_BF16, c=logits)), 2 * M * V * D
     if which == "gemm_dw":              # weight-gradient GEMM: MN-major operands, split-K fp32 atomics
         M, N, K = 2048, 768, 8192
         a, b = rn(K, M).to(bf), rn(K, N).to(bf)

@@ -18,6 +18,26 @@ NVCC_FLAGS = [
     "--expt-relaxed-constexpr",
     "-Xptxas", "-warn-spills",
 ]
+
+
+def _shared_libstdcxx() -> list:
+    """Link the extension against the C++ runtime this interpreter has loaded (a shared libstdc++).
+
+    When the compiler driver finds only a static libstdc++ it embeds a second copy of the runtime in the
+    extension; that copy's locale is never initialised inside the Python process, and formatting a
+    number into an error message then crashes instead of raising.
+    """
+    try:
+        with open("/proc/self/maps") as f:
+            for line in f:
+                path = line.split()[-1]
+                if "/libstdc++.so" in path and os.path.exists(path):
+                    return [path]
+    except OSError:
+        pass
+    return []
+
+
 if os.environ.get("PCB_CHECKED") == "1":   # debug build: bounds-violation counters in the kernels
     NVCC_FLAGS.append("-DPCB_CHECKED")
 
@@ -45,6 +65,7 @@ setup(
             ],
             include_dirs=[os.path.join(HERE, CSRC)],
             extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
+            extra_link_args=_shared_libstdcxx(),
         )
     ],
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
