@@ -688,6 +688,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tp_allreduce_norm", &tp_allreduce_norm);
   m.def("rope_append", &rope_append);
   m.def("checked_violations", []() { return (int64_t)pcb_checked_violations(); });
+  m.def("gemm_pair_stats", []() {
+    unsigned long long v[12] = {};
+    std::vector<int64_t> out;
+    if (pcb::pcb_gemm_pair_stats(v) == 0)
+      for (int i = 0; i < 12; ++i) out.push_back((int64_t)v[i]);
+    return out;
+  });
   m.def("swiglu_rows", &swiglu_rows);
   m.def("annotate", &annotate);
   m.def("coll_reduce", &coll_reduce);

@@ -55,6 +55,13 @@ PCB_DEVICE void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Bulk-async groups of TMA stores issued by this thread.
+PCB_DEVICE void bulk_group_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// wait until at most N of this thread's groups still read their shared-memory source
+template <int N>
+PCB_DEVICE void bulk_group_wait_read() { asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory"); }
+PCB_DEVICE void bulk_group_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 PCB_DEVICE void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                : "memory");
@@ -98,6 +105,15 @@ PCB_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
 // TMA (bulk tensor copies).  Loads never use .multicast::cluster: this library
 // is meant to run on every GPU count, including kernels that read peer memory.
 // ---------------------------------------------------------------------------
+// TMA tile store: the [box] at smem_src (laid out with the map's swizzle) to global coordinates (c0, c1);
+// the copy joins this thread's current bulk-async group.
+PCB_DEVICE void tma_store_2d(const CUtensorMap* map, const void* smem_src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(smem_src)), "r"(c0), "r"(c1)
+               : "memory");
+}
+
 PCB_DEVICE void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"

@@ -15,12 +15,31 @@
 // No TMA load uses .multicast::cluster: each CTA fetches the tiles it stores.
 #include <cudaTypedefs.h>
 
+#include <cstring>
 #include <mutex>
 
 #include "gemm_epilogue.cuh"
 
 namespace pcb {
 namespace pair {
+
+// Optional cycle counters (build with -DPCB_GEMM_STATS): where the roles of the pair kernel wait.
+//   0 MMA issuer: cycles in its tile loop   1: waiting for a drained accumulator   2: waiting for operands
+//   3 producer: waiting for a free stage    4 epilogue warp 2: waiting for an accumulator
+//   5 epilogue warp 2: cycles draining      6 tiles issued by the MMA threads     7 producer cycles in its loop
+//   8 epilogue warp 2: accumulator loads (coalesced path)   9: staging, operand loads and stores
+#ifdef PCB_GEMM_STATS
+__device__ unsigned long long g_pair_stats[12];
+#define PAIR_STAT_DECL(v) long long v = 0
+#define PAIR_STAT_T0(t) const long long t = clock64()
+#define PAIR_STAT_ADD(v, t) v += clock64() - t
+#define PAIR_STAT_FLUSH(i, v) atomicAdd(&g_pair_stats[i], (unsigned long long)(v))
+#else
+#define PAIR_STAT_DECL(v)
+#define PAIR_STAT_T0(t)
+#define PAIR_STAT_ADD(v, t)
+#define PAIR_STAT_FLUSH(i, v)
+#endif
 
 constexpr int kBM = 128;  // rows per CTA (256 per pair)
 constexpr int kBK = 64;
@@ -32,10 +51,16 @@ struct Cfg {
   static constexpr int A_BYTES = kBM * kBK * 2;
   static constexpr int B_BYTES = (BN / 2) * kBK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (BN == 256) ? 5 : 7;
+  static constexpr int STAGES = (BN == 256) ? 5 : 6;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int EPI_OFF = STAGES * STAGE_BYTES + 256;       // 8 epilogue warps x [32 x 32] fp32
-  static constexpr int SMEM_BYTES = EPI_OFF + 8 * 32 * 32 * 4 + 1024;
+  // barriers in the first 256 bytes after the ring; then, 1024-aligned for the 128-byte swizzle of the
+  // TMA-store boxes, 8 KB per epilogue warp: two [32 x 64] bf16 store boxes, or one [32 x 32] fp32
+  // transpose scratch on the coalesced path
+  static constexpr int EPI_OFF = STAGES * STAGE_BYTES + 1024;
+  static constexpr int EPI_WARP_BYTES = 8192;
+  static constexpr int SMEM_BYTES = EPI_OFF + 8 * EPI_WARP_BYTES + 1024;
+  static_assert(SMEM_BYTES <= 232448, "dynamic shared memory above the 227 KB per-block limit");
+  static_assert(8 * (2 * STAGES + 4) + 8 <= 256, "barriers do not fit their 256-byte slot");
 };
 
 // Tile -> (split, row-pair block, column block).  Without a gather the row block varies fastest.
@@ -108,7 +133,7 @@ PCB_DEVICE void gather_chunks(const GemmArgs& a, int tid, int nthreads) {
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const GemmArgs args) {
+                     const __grid_constant__ CUtensorMap tmC, const GemmArgs args) {
   using C = Cfg<BN>;
   constexpr int STAGES = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -146,6 +171,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
+    if (EPI == EPI_BF16 && args.c_tma) prefetch_tmap(&tmC);
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
@@ -163,6 +189,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       uint32_t ready_mask = args.ag_world > 1 ? (1u << args.ag_rank) : 0xffffffffu;
+      PAIR_STAT_DECL(st_empty);
+      PAIR_STAT_T0(st_loop);
       for (int tile = pair_id; tile < tiles && ok; tile += num_pairs) {
         int split, mb, nb;
         tile_coords(tile, args, num_m, num_n, split, mb, nb);
@@ -179,7 +207,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         for (int kb = kb0; kb < kb1; ++kb) {
+          PAIR_STAT_T0(st_w);
           if (!mbar_wait(&empty[stage], phase ^ 1u, args.err, kErrTimeoutEmpty, abort_flag)) { ok = false; break; }
+          PAIR_STAT_ADD(st_empty, st_w);
           if (leader) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
           uint8_t* sa = smem + stage * C::STAGE_BYTES;
           uint8_t* sb = sa + C::A_BYTES;
@@ -199,6 +229,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
       }
+      PAIR_STAT_FLUSH(3, st_empty);
+      PAIR_STAT_FLUSH(7, clock64() - st_loop);
     }
   } else if (warp == 1) {
     if (lane == 0 && leader) {
@@ -209,15 +241,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
+      PAIR_STAT_DECL(st_tempty);
+      PAIR_STAT_DECL(st_full);
+      PAIR_STAT_DECL(st_tiles);
+      PAIR_STAT_T0(st_loop);
       for (int tile = pair_id; tile < tiles && ok; tile += num_pairs) {
         const int split = tile % args.splits;   // same in both tile orders
         const int kb0 = split * args.kb_per_split;
         const int kb1 = min(total_kb, kb0 + args.kb_per_split);
+        PAIR_STAT_T0(st_w0);
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, args.err, kErrTimeoutTmemEmpty, abort_flag)) { ok = false; break; }
+        PAIR_STAT_ADD(st_tempty, st_w0);
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
         for (int kb = kb0; kb < kb1; ++kb) {
+          PAIR_STAT_T0(st_w1);
           if (!mbar_wait(&full[stage], phase, args.err, kErrTimeoutFull, abort_flag)) { ok = false; break; }
+          PAIR_STAT_ADD(st_full, st_w1);
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES);
           const uint32_t sb = sa + C::A_BYTES;
@@ -236,7 +276,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma_commit_pair(&tfull[acc], 0x3);
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1u;
+#ifdef PCB_GEMM_STATS
+        ++st_tiles;
+#endif
       }
+      PAIR_STAT_FLUSH(0, clock64() - st_loop);
+      PAIR_STAT_FLUSH(1, st_tempty);
+      PAIR_STAT_FLUSH(2, st_full);
+      PAIR_STAT_FLUSH(6, st_tiles);
     }
   } else {
     // ---------------- epilogue warps (both CTAs, 128 rows each) ----------------
@@ -248,13 +295,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (args.ag_world > 1) gather_chunks(args, threadIdx.x - 64, 32 * kEpiWarps);
     int acc = 0;
     uint32_t acc_phase = 0;
+    PAIR_STAT_DECL(st_tfull);
+    PAIR_STAT_DECL(st_body);
     for (int tile = pair_id; tile < tiles; tile += num_pairs) {
       int split_unused, mb, nb;
       tile_coords(tile, args, num_m, num_n, split_unused, mb, nb);
       const int m = mb * 2 * kBM + rank * kBM + row;
       const int n0 = nb * BN;
       const bool row_ok = m < args.M;
+      PAIR_STAT_T0(st_w2);
       if (!mbar_wait(&tfull[acc], acc_phase, args.err, kErrTimeoutTmemFull, abort_flag)) break;
+      PAIR_STAT_ADD(st_tfull, st_w2);
+      PAIR_STAT_T0(st_b);
       tc_fence_after();
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
       if (EPI == EPI_SWIGLU) {
@@ -286,16 +338,86 @@ __global__ void __launch_bounds__(kThreads, 1)
             store_bf16x32(reinterpret_cast<__nv_bfloat16*>(args.D) + (long long)m * args.ldd + fcol, o, nvalid);
           }
         }
+      } else if (EPI == EPI_BF16 && args.c_tma) {
+        // 64-column blocks: two accumulator chunks -> alpha, bias, RoPE -> bf16 row of 128 bytes per
+        // lane, staged in the 128-byte-swizzled layout of a [32 x 64] box and written by one TMA store.
+        // The two boxes of a warp alternate; a box is rewritten only after its previous store has
+        // finished reading it.
+        uint8_t* stg = smem + C::EPI_OFF + (warp - 2) * C::EPI_WARP_BYTES;
+        const int row0 = mb * 2 * kBM + rank * kBM + q * 32;
+#pragma unroll 1
+        for (int c2 = half, bx = 0; c2 < BN / 64; c2 += 2, bx ^= 1) {
+          float v[64];
+          {
+            uint32_t r0[32], r1[32];
+            tmem_ld_32x32b_x32(tbase + c2 * 64, r0);
+            tmem_ld_32x32b_x32(tbase + c2 * 64 + 32, r1);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              v[j] = __uint_as_float(r0[j]);
+              v[32 + j] = __uint_as_float(r1[j]);
+            }
+          }
+          const int nb0 = n0 + c2 * 64;
+#pragma unroll
+          for (int j = 0; j < 64; ++j) v[j] *= args.alpha;
+          if (args.bias != nullptr) {
+#pragma unroll
+            for (int j = 0; j < 64; ++j) {
+              const int n = nb0 + j;
+              if (n < args.N)
+                v[j] += args.bias_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(args.bias)[n])
+                                       : reinterpret_cast<const float*>(args.bias)[n];
+            }
+          }
+          if (args.rope_cs != nullptr && nb0 < args.rope_cols && row_ok) {
+            const float2* cs = reinterpret_cast<const float2*>(args.rope_cs) + (long long)(m % args.rope_S) * (args.rope_hd >> 1);
+#pragma unroll
+            for (int j = 0; j < 64; j += 2) {
+              const int n = nb0 + j;
+              if (n < args.rope_cols) {
+                const float2 cv = cs[(n % args.rope_hd) >> 1];
+                const float x0 = v[j], x1 = v[j + 1];
+                v[j] = x0 * cv.x - x1 * cv.y;
+                v[j + 1] = x0 * cv.y + x1 * cv.x;
+              }
+            }
+          }
+          uint8_t* box = stg + bx * 4096;
+          if (lane == 0) bulk_group_wait_read<1>();   // the store that last read this box is done with it
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            uint4 u;
+            u.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
+            u.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+            u.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+            u.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+            *reinterpret_cast<uint4*>(box + lane * 128 + ((j ^ (lane & 7)) << 4)) = u;
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmC, box, nb0, row0);
+            bulk_group_commit();
+          }
+        }
       } else if (epi_coalesced<EPI>()) {
         // transpose each 32x32 chunk through this warp's shared scratch (16-byte cells, XOR-swizzled by
         // row) so that 8 lanes then cover one 128-byte row segment of the output
-        float4* scr = reinterpret_cast<float4*>(smem + C::EPI_OFF) + (warp - 2) * 32 * 8;
+        float4* scr = reinterpret_cast<float4*>(smem + C::EPI_OFF + (warp - 2) * C::EPI_WARP_BYTES);
         const int row0 = mb * 2 * kBM + rank * kBM + q * 32;
         float sq = 0.f;
+        PAIR_STAT_DECL(st_ld);
+        PAIR_STAT_DECL(st_st);
 #pragma unroll 1
         for (int c = half; c < BN / 32; c += 2) {
           float v[32];
+          PAIR_STAT_T0(st_l0);
           tmem_load_f32x32(tbase + c * 32, v);
+          PAIR_STAT_ADD(st_ld, st_l0);
+          PAIR_STAT_T0(st_s0);
 #pragma unroll
           for (int j = 0; j < 8; ++j)
             scr[lane * 8 + (j ^ (lane & 7))] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
@@ -315,6 +437,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             sq += epilogue_vec4<EPI>(args, row0 + rr, ncol, e, pf[it], row0 + rr < args.M);
           }
           __syncwarp();
+          PAIR_STAT_ADD(st_st, st_s0);
+        }
+        if (warp == 2 && lane == 0) {
+          PAIR_STAT_FLUSH(8, st_ld);
+          PAIR_STAT_FLUSH(9, st_st);
         }
         if (EPI == EPI_PC_PRED && args.pc_energy != nullptr) {
           sq = warp_sum(sq);
@@ -389,11 +516,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (leader) mbar_arrive(&tempty[acc]);
         else mbar_arrive_remote(acc ? tempty_leader1 : tempty_leader0);
       }
+      PAIR_STAT_ADD(st_body, st_b);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
+    if (warp == 2 && lane == 0) {
+      PAIR_STAT_FLUSH(4, st_tfull);
+      PAIR_STAT_FLUSH(5, st_body);
+    }
   }
 
+  if (EPI == EPI_BF16 && args.c_tma && warp >= 2 && lane == 0) bulk_group_wait_all();  // stores landed
   __syncwarp();
   tc_fence_before();
   cluster_sync_all();  // both CTAs done with TMEM and with each other's barriers
@@ -402,6 +535,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 }  // namespace pair
+
+// Copies the pair-kernel cycle counters into out[12] and clears them; -1 when built without them.
+int pcb_gemm_pair_stats(unsigned long long* out) {
+#ifdef PCB_GEMM_STATS
+  if (cudaMemcpyFromSymbol(out, pair::g_pair_stats, 12 * sizeof(unsigned long long)) != cudaSuccess) return -2;
+  unsigned long long zero[12] = {};
+  cudaMemcpyToSymbol(pair::g_pair_stats, zero, sizeof(zero));
+  return 0;
+#else
+  (void)out;
+  return -1;
+#endif
+}
 
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn2() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -430,7 +576,8 @@ static bool make_map2(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t 
 }
 
 template <int BN, int EPI>
-static int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int grid, cudaStream_t s) {
+static int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmArgs& a, int grid,
+                       cudaStream_t s) {
   using C = pair::Cfg<BN>;
   static bool attr_done = false;
   if (!attr_done) {
@@ -452,35 +599,35 @@ static int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmA
   attr[1].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = a.ag_world > 1 ? 2 : 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, pair::gemm_pair_kernel<BN, EPI>, ta, tb, a);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, pair::gemm_pair_kernel<BN, EPI>, ta, tb, tc, a);
   if (e != cudaSuccess && cfg.numAttrs == 2) {
     // cooperative + cluster refused: one CTA per SM with grid <= SM count is resident anyway on a
     // stream of its own; the chunk waits stay bounded either way
     cudaGetLastError();
     cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, pair::gemm_pair_kernel<BN, EPI>, ta, tb, a);
+    e = cudaLaunchKernelEx(&cfg, pair::gemm_pair_kernel<BN, EPI>, ta, tb, tc, a);
   }
   return e == cudaSuccess ? 0 : -3;
 }
 
 template <int BN>
-static int dispatch_pair(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int grid,
-                         cudaStream_t s) {
+static int dispatch_pair(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmArgs& a,
+                         int grid, cudaStream_t s) {
   switch (epi) {
-    case EPI_BF16: return launch_pair<BN, EPI_BF16>(ta, tb, a, grid, s);
-    case EPI_F32: return launch_pair<BN, EPI_F32>(ta, tb, a, grid, s);
-    case EPI_ACC_F32: return launch_pair<BN, EPI_ACC_F32>(ta, tb, a, grid, s);
-    case EPI_RED_F32: return launch_pair<BN, EPI_RED_F32>(ta, tb, a, grid, s);
-    case EPI_GELU: return launch_pair<BN, EPI_GELU>(ta, tb, a, grid, s);
-    case EPI_SWIGLU: return launch_pair<BN, EPI_SWIGLU>(ta, tb, a, grid, s);
-    case EPI_SWIGLU_BWD: return launch_pair<BN, EPI_SWIGLU_BWD>(ta, tb, a, grid, s);
-    case EPI_GELU_BWD: return launch_pair<BN, EPI_GELU_BWD>(ta, tb, a, grid, s);
-    case EPI_PC_PRED: return launch_pair<BN, EPI_PC_PRED>(ta, tb, a, grid, s);
-    case EPI_PC_STATE: return launch_pair<BN, EPI_PC_STATE>(ta, tb, a, grid, s);
-    case EPI_PC_WUPD: return launch_pair<BN, EPI_PC_WUPD>(ta, tb, a, grid, s);
-    case EPI_BF16_ACC: return launch_pair<BN, EPI_BF16_ACC>(ta, tb, a, grid, s);
-    case EPI_RESID_F32: return launch_pair<BN, EPI_RESID_F32>(ta, tb, a, grid, s);
-    case EPI_RS_BF16: return launch_pair<BN, EPI_RS_BF16>(ta, tb, a, grid, s);
+    case EPI_BF16: return launch_pair<BN, EPI_BF16>(ta, tb, tc, a, grid, s);
+    case EPI_F32: return launch_pair<BN, EPI_F32>(ta, tb, tc, a, grid, s);
+    case EPI_ACC_F32: return launch_pair<BN, EPI_ACC_F32>(ta, tb, tc, a, grid, s);
+    case EPI_RED_F32: return launch_pair<BN, EPI_RED_F32>(ta, tb, tc, a, grid, s);
+    case EPI_GELU: return launch_pair<BN, EPI_GELU>(ta, tb, tc, a, grid, s);
+    case EPI_SWIGLU: return launch_pair<BN, EPI_SWIGLU>(ta, tb, tc, a, grid, s);
+    case EPI_SWIGLU_BWD: return launch_pair<BN, EPI_SWIGLU_BWD>(ta, tb, tc, a, grid, s);
+    case EPI_GELU_BWD: return launch_pair<BN, EPI_GELU_BWD>(ta, tb, tc, a, grid, s);
+    case EPI_PC_PRED: return launch_pair<BN, EPI_PC_PRED>(ta, tb, tc, a, grid, s);
+    case EPI_PC_STATE: return launch_pair<BN, EPI_PC_STATE>(ta, tb, tc, a, grid, s);
+    case EPI_PC_WUPD: return launch_pair<BN, EPI_PC_WUPD>(ta, tb, tc, a, grid, s);
+    case EPI_BF16_ACC: return launch_pair<BN, EPI_BF16_ACC>(ta, tb, tc, a, grid, s);
+    case EPI_RESID_F32: return launch_pair<BN, EPI_RESID_F32>(ta, tb, tc, a, grid, s);
+    case EPI_RS_BF16: return launch_pair<BN, EPI_RS_BF16>(ta, tb, tc, a, grid, s);
     default: return -2;
   }
 }
@@ -523,9 +670,17 @@ int pcb_gemm_pair_launch(const void* A, int a_mn, long long lda, const void* B, 
   if (!ok) return -5;
   ok = b_mn == 0 ? make_map2(&tb, B, K, N, ldb, 64, bn / 2) : make_map2(&tb, B, N, K, ldb, 64, 64);
   if (!ok) return -5;
+  // bf16 output through TMA stores when C can be described by a tensor map (16-byte aligned base and
+  // row stride); [32 x 64] boxes, clipped by the hardware at the M / N edges
+  CUtensorMap tc;
+  memset(&tc, 0, sizeof(tc));
+  args.c_tma = 0;
+  if (epi == EPI_BF16 && (reinterpret_cast<uintptr_t>(args.C) & 15) == 0 && (args.ldc % 8) == 0 &&
+      make_map2(&tc, args.C, N, M, args.ldc, 64, 32))
+    args.c_tma = 1;
   const int tiles = num_m * num_n * splits;
   const int max_pairs = num_sms / 2;
   const int pairs = tiles < max_pairs ? tiles : max_pairs;
-  return bn == 256 ? dispatch_pair<256>(epi, ta, tb, args, 2 * pairs, stream)
-                   : dispatch_pair<128>(epi, ta, tb, args, 2 * pairs, stream);
+  return bn == 256 ? dispatch_pair<256>(epi, ta, tb, tc, args, 2 * pairs, stream)
+                   : dispatch_pair<128>(epi, ta, tb, tc, args, 2 * pairs, stream);
 }

@@ -67,7 +67,13 @@ struct GemmArgs {
   void* const* rs_peers;        // device table [world] of owners' slot buffers
   int rs_rows;
   int rs_rank;
+  // EPI_BF16 on the CTA-pair kernel: 1 when the launcher built a tensor map of C, so the epilogue
+  // stages 32 x 64 bf16 boxes in shared memory and writes them with TMA stores
+  int c_tma;
 };
+
+// Pair-kernel cycle counters (builds with PCB_GEMM_STATS): copies 12 counters to `out` and clears them.
+int pcb_gemm_pair_stats(unsigned long long* out);
 
 }  // namespace pcb
 

@@ -40,6 +40,8 @@ def _shared_libstdcxx() -> list:
 
 if os.environ.get("PCB_CHECKED") == "1":   # debug build: bounds-violation counters in the kernels
     NVCC_FLAGS.append("-DPCB_CHECKED")
+if os.environ.get("PCB_GEMM_STATS") == "1":   # profiling build: cycle counters in the pair GEMM roles
+    NVCC_FLAGS.append("-DPCB_GEMM_STATS")
 
 setup(
     name="predicitivecoding_b200",

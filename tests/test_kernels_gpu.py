@@ -66,13 +66,35 @@ def test_gemm_pair_epilogues(bn, gemm_mode):
 
 
 @pytest.mark.parametrize("bn", [128, 256])
-def test_gemm_bf16_out_and_bias(bn):
-    M, N, K = 512, 512, 256
+@pytest.mark.parametrize("shape", [(512, 512, 256), (200, 136, 72), (1000, 100, 128), (768, 2304, 192)])
+def test_gemm_bf16_out_and_bias(bn, shape, gemm_mode):
+    # (200, 136): TMA-store boxes clipped at the row and column edges; (1000, 100): a row stride that is
+    # not a multiple of 16 bytes, so the epilogue stores without a tensor map
+    M, N, K = shape
     a, b, ref = _operands(M, N, K, False, False, seed=1)
     bias = torch.randn(N, device=DEV)
-    out = ops.gemm(a, b, epi=ops.EPI_BF16, bias=bias, alpha=0.5, bn=bn)
+    padded = torch.full((M, N + 8), 7.0, device=DEV, dtype=torch.bfloat16)
+    out = padded[:, :N]
+    ops.gemm(a, b, epi=ops.EPI_BF16, c=out, bias=bias, alpha=0.5, bn=bn)
     torch.cuda.synchronize()
     assert rel_err(out, 0.5 * ref + bias) < 0.02
+    assert bool((padded[:, N:] == 7.0).all()), "bf16 epilogue wrote past the last column"
+
+
+@pytest.mark.parametrize("bn", [128, 256])
+def test_gemm_bf16_fused_rope(bn, gemm_mode):
+    # the q/k columns [0, 2D) of a fused qkv projection rotated in the epilogue, v columns untouched
+    from predicitivecoding_b200.models.decoder_lm import rope_tables
+    S, hd, D = 256, 64, 256
+    M, N, K = 2 * S, 3 * D, 192
+    a, b, ref = _operands(M, N, K, False, False, seed=4)
+    cos, sin = rope_tables(S, hd, device=DEV)
+    cs = torch.stack((cos, sin), -1).contiguous()
+    out = ops.gemm(a, b, epi=ops.EPI_BF16, bn=bn, rope=(cs, S, hd, 2 * D))
+    expect = ref.to(torch.bfloat16)
+    ops.rope(expect, cs, S, D, hd, 2, 1.0)
+    torch.cuda.synchronize()
+    assert rel_err(out, expect.float()) < 0.02
 
 
 def test_gemm_split_k_red():
