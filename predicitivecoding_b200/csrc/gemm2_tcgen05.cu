@@ -15,6 +15,7 @@
 // No TMA load uses .multicast::cluster: each CTA fetches the tiles it stores.
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -76,6 +77,9 @@ PCB_DEVICE void tile_coords(int tile, const GemmArgs& a, int num_m, int num_n, i
     const int r = rest % tpc;
     mb = c * mpc + r % mpc;
     nb = r / mpc;
+  } else if (a.n_fastest) {
+    nb = rest % num_n;
+    mb = rest / num_n;
   } else {
     mb = rest % num_m;
     nb = rest / num_m;
@@ -670,6 +674,15 @@ int pcb_gemm_pair_launch(const void* A, int a_mn, long long lda, const void* B, 
   if (!ok) return -5;
   ok = b_mn == 0 ? make_map2(&tb, B, K, N, ldb, 64, bn / 2) : make_map2(&tb, B, N, K, ldb, 64, 64);
   if (!ok) return -5;
+  // Tile order: the pairs running at once should share the operand with the larger footprint, so that
+  // it crosses from DRAM once per wave. With A larger (M > N) the column blocks of one row block run
+  // side by side; otherwise the row blocks of one column block do. PCB_GEMM_RASTER=1 / 2 forces
+  // row-fastest / column-fastest (measurement).
+  static const int raster_env = [] {
+    const char* e = getenv("PCB_GEMM_RASTER");
+    return e ? atoi(e) : 0;
+  }();
+  args.n_fastest = raster_env == 1 ? 0 : raster_env == 2 ? 1 : (M > N ? 1 : 0);
   // bf16 output through TMA stores when C can be described by a tensor map (16-byte aligned base and
   // row stride); [32 x 64] boxes, clipped by the hardware at the M / N edges
   CUtensorMap tc;
