@@ -451,6 +451,17 @@ __global__ void colsum_kernel(const T* __restrict__ x, long long ld, float* __re
 // wd applies to elements [0, n_decay); elements beyond it are not decayed.
 // hyper = [lr, wd, bc1, bc2, grad_scale] lives in device memory so a captured CUDA graph
 // replays the optimizer with the current schedule values.
+PCB_DEVICE void adamw_elem(float& wi, float gi, float& mi, float& vi, long long i, long long n_decay, float s,
+                           float lr, float wd, float bc1, float bc2, float b1, float b2, float eps) {
+  gi = isfinite(gi) ? gi * s : 0.f;
+  mi = b1 * mi + (1.f - b1) * gi;
+  vi = b2 * vi + (1.f - b2) * gi * gi;
+  wi -= lr * (mi / bc1) / (sqrtf(vi / bc2) + eps);
+  if (i < n_decay) wi -= lr * wd * wi;
+}
+
+// Four parameters per thread and step (16-byte loads of w, g, m, v; 8-byte bf16 store), two such
+// groups in flight per thread; the n % 4 tail (or an unaligned buffer) takes the scalar loop.
 __global__ void adamw_kernel(float* __restrict__ w, const float* __restrict__ g, float* __restrict__ m,
                              float* __restrict__ v, __nv_bfloat16* __restrict__ w16, long long n,
                              long long n_decay, const float* __restrict__ hyper, float b1, float b2, float eps,
@@ -462,16 +473,50 @@ __global__ void adamw_kernel(float* __restrict__ w, const float* __restrict__ g,
     const float norm = sqrtf(*clip_sumsq) * grad_scale;
     if (norm > max_norm) s *= max_norm / (norm + 1e-6f);
   }
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-    float gi = g[i];
-    gi = isfinite(gi) ? gi * s : 0.f;
-    const float mi = b1 * m[i] + (1.f - b1) * gi;
-    const float vi = b2 * v[i] + (1.f - b2) * gi * gi;
+  const bool vec = ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(g) | reinterpret_cast<uintptr_t>(m) |
+                     reinterpret_cast<uintptr_t>(v)) & 15) == 0 &&
+                   (w16 == nullptr || (reinterpret_cast<uintptr_t>(w16) & 7) == 0);
+  const long long tid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  long long done = 0;
+  if (vec) {
+    const long long n4 = n / 4;
+    float4* w4 = reinterpret_cast<float4*>(w);
+    const float4* g4 = reinterpret_cast<const float4*>(g);
+    float4* m4 = reinterpret_cast<float4*>(m);
+    float4* v4 = reinterpret_cast<float4*>(v);
+    for (long long i = tid; i < n4; i += 2 * stride) {
+      const long long j = i + stride;
+      const bool two = j < n4;
+      float4 wa = w4[i], ga = g4[i], ma = m4[i], va = v4[i];
+      float4 wb, gb, mb, vb;
+      if (two) { wb = w4[j]; gb = g4[j]; mb = m4[j]; vb = v4[j]; }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        if (h == 1 && !two) break;
+        const long long q = h ? j : i;
+        float4& wq = h ? wb : wa;
+        float4& gq = h ? gb : ga;
+        float4& mq = h ? mb : ma;
+        float4& vq = h ? vb : va;
+        adamw_elem(wq.x, gq.x, mq.x, vq.x, 4 * q + 0, n_decay, s, lr, wd, bc1, bc2, b1, b2, eps);
+        adamw_elem(wq.y, gq.y, mq.y, vq.y, 4 * q + 1, n_decay, s, lr, wd, bc1, bc2, b1, b2, eps);
+        adamw_elem(wq.z, gq.z, mq.z, vq.z, 4 * q + 2, n_decay, s, lr, wd, bc1, bc2, b1, b2, eps);
+        adamw_elem(wq.w, gq.w, mq.w, vq.w, 4 * q + 3, n_decay, s, lr, wd, bc1, bc2, b1, b2, eps);
+        m4[q] = mq;
+        v4[q] = vq;
+        w4[q] = wq;
+        if (w16 != nullptr)
+          reinterpret_cast<uint2*>(w16)[q] = make_uint2(pack_bf16x2(wq.x, wq.y), pack_bf16x2(wq.z, wq.w));
+      }
+    }
+    done = 4 * n4;
+  }
+  for (long long i = done + tid; i < n; i += stride) {
+    float wi = w[i], mi = m[i], vi = v[i];
+    adamw_elem(wi, g[i], mi, vi, i, n_decay, s, lr, wd, bc1, bc2, b1, b2, eps);
     m[i] = mi;
     v[i] = vi;
-    float wi = w[i];
-    wi -= lr * (mi / bc1) / (sqrtf(vi / bc2) + eps);
-    if (i < n_decay) wi -= lr * wd * wi;
     w[i] = wi;
     if (w16 != nullptr) w16[i] = __float2bfloat16_rn(wi);
   }

@@ -152,14 +152,50 @@ def decoder_gemm_table(iters: int = 20) -> list:
     return rows
 
 
+def step_breakdown(steps: int = 2) -> list:
+    """Device time per kernel of one step of the 124M decoder trainer (micro-batch 16 x 1024), from the
+    CUDA activity records of torch.profiler over `steps` steps after 3 warm-up steps; eager launches
+    (no CUDA graph) so that every kernel record is attributed. Returns rows sorted by time."""
+    from ..engine.fused_trainer import FusedDecoderTrainer
+    from ..models.config import DecoderLmConfig
+    from ..utils.data import zipf_windows
+    dev = torch.device("cuda", torch.cuda.current_device())
+    cfg = DecoderLmConfig.gpt2_small_swiglu()
+    B, S = 16, cfg.max_seq
+    tok, tgt = zipf_windows(B, S, cfg.vocab, 1.1, seed=1)
+    tok, tgt = tok.to(torch.int32).pin_memory(), tgt.to(torch.int32).pin_memory()
+    tr = FusedDecoderTrainer(cfg, B, S, device=dev, lr=3e-4, weight_decay=0.1, use_graph=False)
+    tr.stage(tok, tgt)
+    for _ in range(3):
+        tr.step(tok, tgt)
+    torch.cuda.synchronize()
+    with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA]) as prof:
+        for _ in range(steps):
+            tr.step(tok, tgt)
+        torch.cuda.synchronize()
+    rows = []
+    for e in prof.key_averages():
+        t = getattr(e, "device_time_total", 0.0)
+        if t > 0:
+            rows.append({"kernel": e.key[:120], "us_per_step": round(t / steps, 1), "launches_per_step": e.count // steps})
+    rows.sort(key=lambda r: -r["us_per_step"])
+    return rows
+
+
 def main() -> None:
     p = argparse.ArgumentParser()
-    p.add_argument("case", choices=CASES + ("all", "decoder_gemms"))
+    p.add_argument("case", choices=CASES + ("all", "decoder_gemms", "step_breakdown"))
     p.add_argument("--time", type=int, default=0, help="time N launches after warm-up")
     a = p.parse_args()
     ext()
     if a.case == "decoder_gemms":
         for row in decoder_gemm_table():
+            print(json.dumps(row))
+        return
+    if a.case == "step_breakdown":
+        rows = step_breakdown()
+        print(json.dumps({"kernel_us_per_step": round(sum(r["us_per_step"] for r in rows), 1)}))
+        for row in rows:
             print(json.dumps(row))
         return
     for c in (CASES if a.case == "all" else (a.case,)):
