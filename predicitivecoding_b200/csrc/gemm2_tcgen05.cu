@@ -137,7 +137,8 @@ PCB_DEVICE void gather_chunks(const GemmArgs& a, int tid, int nthreads) {
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const __grid_constant__ CUtensorMap tmC, const GemmArgs args) {
+                     const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmD,
+                     const GemmArgs args) {
   using C = Cfg<BN>;
   constexpr int STAGES = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -175,7 +176,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
-    if (EPI == EPI_BF16 && args.c_tma) prefetch_tmap(&tmC);
+    if ((EPI == EPI_BF16 || EPI == EPI_SWIGLU) && args.c_tma) prefetch_tmap(&tmC);
+    if (EPI == EPI_SWIGLU && args.c_tma) prefetch_tmap(&tmD);
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
@@ -313,7 +315,50 @@ __global__ void __launch_bounds__(kThreads, 1)
       PAIR_STAT_T0(st_b);
       tc_fence_after();
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      if (EPI == EPI_SWIGLU) {
+      if (EPI == EPI_SWIGLU && args.c_tma) {
+        // per 128-column group: this warp's 32 gate and 32 up columns of pre and the 32 act columns
+        // they make, each staged as a [32 x 32] bf16 box (64-byte rows, 64-byte swizzle: 16-byte
+        // chunk c of row r at c ^ ((r >> 1) & 3)) and written by TMA stores
+        uint8_t* stg = smem + C::EPI_OFF + (warp - 2) * C::EPI_WARP_BYTES;
+        const int row0 = mb * 2 * kBM + rank * kBM + q * 32;
+#pragma unroll 1
+        for (int g = 0; g < BN / 128; ++g) {
+          const int h = half;
+          uint32_t rg[32], ru[32];
+          tmem_ld_32x32b_x32(tbase + g * 128 + h * 32, rg);
+          tmem_ld_32x32b_x32(tbase + g * 128 + 64 + h * 32, ru);
+          tmem_ld_wait();
+          uint32_t pg[16], pu[16], pa[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float g0 = __uint_as_float(rg[2 * j]) * args.alpha, g1 = __uint_as_float(rg[2 * j + 1]) * args.alpha;
+            const float u0 = __uint_as_float(ru[2 * j]) * args.alpha, u1 = __uint_as_float(ru[2 * j + 1]) * args.alpha;
+            pg[j] = pack_bf16x2(g0, g1);
+            pu[j] = pack_bf16x2(u0, u1);
+            const float gb0 = bf16_lo(pg[j]), gb1 = bf16_hi(pg[j]);
+            const float ub0 = bf16_lo(pu[j]), ub1 = bf16_hi(pu[j]);
+            pa[j] = pack_bf16x2(__fdividef(gb0, 1.f + __expf(-gb0)) * ub0, __fdividef(gb1, 1.f + __expf(-gb1)) * ub1);
+          }
+          if (lane == 0) bulk_group_wait_read<0>();   // the previous group's stores have read the boxes
+          __syncwarp();
+          const int sw = (lane >> 1) & 3;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const int off = lane * 64 + ((c ^ sw) << 4);
+            *reinterpret_cast<uint4*>(stg + off) = make_uint4(pg[4 * c], pg[4 * c + 1], pg[4 * c + 2], pg[4 * c + 3]);
+            *reinterpret_cast<uint4*>(stg + 2048 + off) = make_uint4(pu[4 * c], pu[4 * c + 1], pu[4 * c + 2], pu[4 * c + 3]);
+            *reinterpret_cast<uint4*>(stg + 4096 + off) = make_uint4(pa[4 * c], pa[4 * c + 1], pa[4 * c + 2], pa[4 * c + 3]);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmC, stg, n0 + g * 128 + h * 32, row0);
+            tma_store_2d(&tmC, stg + 2048, n0 + g * 128 + 64 + h * 32, row0);
+            tma_store_2d(&tmD, stg + 4096, (n0 >> 1) + g * 64 + h * 32, row0);
+            bulk_group_commit();
+          }
+        }
+      } else if (EPI == EPI_SWIGLU) {
 #pragma unroll 1
         for (int g = 0; g < BN / 128; ++g) {
           const int h = half;
@@ -530,7 +575,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
-  if (EPI == EPI_BF16 && args.c_tma && warp >= 2 && lane == 0) bulk_group_wait_all();  // stores landed
+  if ((EPI == EPI_BF16 || EPI == EPI_SWIGLU) && args.c_tma && warp >= 2 && lane == 0)
+    bulk_group_wait_all();  // every TMA store has landed before the CTA exits
   __syncwarp();
   tc_fence_before();
   cluster_sync_all();  // both CTAs done with TMEM and with each other's barriers
@@ -567,7 +613,8 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn2() {
 }
 
 static bool make_map2(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld,
-                      uint32_t box_inner, uint32_t box_outer) {
+                      uint32_t box_inner, uint32_t box_outer,
+                      CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
   auto fn = encode_fn2();
   if (!fn) return false;
   cuuint64_t dims[2] = {inner, outer};
@@ -575,13 +622,13 @@ static bool make_map2(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t 
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t es[2] = {1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, es,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 template <int BN, int EPI>
-static int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmArgs& a, int grid,
-                       cudaStream_t s) {
+static int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const CUtensorMap& td,
+                       const GemmArgs& a, int grid, cudaStream_t s) {
   using C = pair::Cfg<BN>;
   static bool attr_done = false;
   if (!attr_done) {
@@ -603,35 +650,35 @@ static int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
   attr[1].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = a.ag_world > 1 ? 2 : 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, pair::gemm_pair_kernel<BN, EPI>, ta, tb, tc, a);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, pair::gemm_pair_kernel<BN, EPI>, ta, tb, tc, td, a);
   if (e != cudaSuccess && cfg.numAttrs == 2) {
     // cooperative + cluster refused: one CTA per SM with grid <= SM count is resident anyway on a
     // stream of its own; the chunk waits stay bounded either way
     cudaGetLastError();
     cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, pair::gemm_pair_kernel<BN, EPI>, ta, tb, tc, a);
+    e = cudaLaunchKernelEx(&cfg, pair::gemm_pair_kernel<BN, EPI>, ta, tb, tc, td, a);
   }
   return e == cudaSuccess ? 0 : -3;
 }
 
 template <int BN>
-static int dispatch_pair(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmArgs& a,
-                         int grid, cudaStream_t s) {
+static int dispatch_pair(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                         const CUtensorMap& td, const GemmArgs& a, int grid, cudaStream_t s) {
   switch (epi) {
-    case EPI_BF16: return launch_pair<BN, EPI_BF16>(ta, tb, tc, a, grid, s);
-    case EPI_F32: return launch_pair<BN, EPI_F32>(ta, tb, tc, a, grid, s);
-    case EPI_ACC_F32: return launch_pair<BN, EPI_ACC_F32>(ta, tb, tc, a, grid, s);
-    case EPI_RED_F32: return launch_pair<BN, EPI_RED_F32>(ta, tb, tc, a, grid, s);
-    case EPI_GELU: return launch_pair<BN, EPI_GELU>(ta, tb, tc, a, grid, s);
-    case EPI_SWIGLU: return launch_pair<BN, EPI_SWIGLU>(ta, tb, tc, a, grid, s);
-    case EPI_SWIGLU_BWD: return launch_pair<BN, EPI_SWIGLU_BWD>(ta, tb, tc, a, grid, s);
-    case EPI_GELU_BWD: return launch_pair<BN, EPI_GELU_BWD>(ta, tb, tc, a, grid, s);
-    case EPI_PC_PRED: return launch_pair<BN, EPI_PC_PRED>(ta, tb, tc, a, grid, s);
-    case EPI_PC_STATE: return launch_pair<BN, EPI_PC_STATE>(ta, tb, tc, a, grid, s);
-    case EPI_PC_WUPD: return launch_pair<BN, EPI_PC_WUPD>(ta, tb, tc, a, grid, s);
-    case EPI_BF16_ACC: return launch_pair<BN, EPI_BF16_ACC>(ta, tb, tc, a, grid, s);
-    case EPI_RESID_F32: return launch_pair<BN, EPI_RESID_F32>(ta, tb, tc, a, grid, s);
-    case EPI_RS_BF16: return launch_pair<BN, EPI_RS_BF16>(ta, tb, tc, a, grid, s);
+    case EPI_BF16: return launch_pair<BN, EPI_BF16>(ta, tb, tc, td, a, grid, s);
+    case EPI_F32: return launch_pair<BN, EPI_F32>(ta, tb, tc, td, a, grid, s);
+    case EPI_ACC_F32: return launch_pair<BN, EPI_ACC_F32>(ta, tb, tc, td, a, grid, s);
+    case EPI_RED_F32: return launch_pair<BN, EPI_RED_F32>(ta, tb, tc, td, a, grid, s);
+    case EPI_GELU: return launch_pair<BN, EPI_GELU>(ta, tb, tc, td, a, grid, s);
+    case EPI_SWIGLU: return launch_pair<BN, EPI_SWIGLU>(ta, tb, tc, td, a, grid, s);
+    case EPI_SWIGLU_BWD: return launch_pair<BN, EPI_SWIGLU_BWD>(ta, tb, tc, td, a, grid, s);
+    case EPI_GELU_BWD: return launch_pair<BN, EPI_GELU_BWD>(ta, tb, tc, td, a, grid, s);
+    case EPI_PC_PRED: return launch_pair<BN, EPI_PC_PRED>(ta, tb, tc, td, a, grid, s);
+    case EPI_PC_STATE: return launch_pair<BN, EPI_PC_STATE>(ta, tb, tc, td, a, grid, s);
+    case EPI_PC_WUPD: return launch_pair<BN, EPI_PC_WUPD>(ta, tb, tc, td, a, grid, s);
+    case EPI_BF16_ACC: return launch_pair<BN, EPI_BF16_ACC>(ta, tb, tc, td, a, grid, s);
+    case EPI_RESID_F32: return launch_pair<BN, EPI_RESID_F32>(ta, tb, tc, td, a, grid, s);
+    case EPI_RS_BF16: return launch_pair<BN, EPI_RS_BF16>(ta, tb, tc, td, a, grid, s);
     default: return -2;
   }
 }
@@ -685,15 +732,20 @@ int pcb_gemm_pair_launch(const void* A, int a_mn, long long lda, const void* B, 
   args.n_fastest = raster_env == 1 ? 0 : raster_env == 2 ? 1 : (M > N ? 1 : 0);
   // bf16 output through TMA stores when C can be described by a tensor map (16-byte aligned base and
   // row stride); [32 x 64] boxes, clipped by the hardware at the M / N edges
-  CUtensorMap tc;
+  CUtensorMap tc, td;
   memset(&tc, 0, sizeof(tc));
+  memset(&td, 0, sizeof(td));
   args.c_tma = 0;
-  if (epi == EPI_BF16 && (reinterpret_cast<uintptr_t>(args.C) & 15) == 0 && (args.ldc % 8) == 0 &&
-      make_map2(&tc, args.C, N, M, args.ldc, 64, 32))
+  const bool c_ok = (reinterpret_cast<uintptr_t>(args.C) & 15) == 0 && (args.ldc % 8) == 0;
+  if (epi == EPI_BF16 && c_ok && make_map2(&tc, args.C, N, M, args.ldc, 64, 32)) args.c_tma = 1;
+  // SwiGLU forward: pre (C, [M, N]) and act (D, [M, N / 2]) in [32 x 32] boxes with 64-byte swizzle
+  if (epi == EPI_SWIGLU && c_ok && args.D != nullptr && (reinterpret_cast<uintptr_t>(args.D) & 15) == 0 &&
+      (args.ldd % 8) == 0 && make_map2(&tc, args.C, N, M, args.ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B) &&
+      make_map2(&td, args.D, N / 2, M, args.ldd, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
     args.c_tma = 1;
   const int tiles = num_m * num_n * splits;
   const int max_pairs = num_sms / 2;
   const int pairs = tiles < max_pairs ? tiles : max_pairs;
-  return bn == 256 ? dispatch_pair<256>(epi, ta, tb, tc, args, 2 * pairs, stream)
-                   : dispatch_pair<128>(epi, ta, tb, tc, args, 2 * pairs, stream);
+  return bn == 256 ? dispatch_pair<256>(epi, ta, tb, tc, td, args, 2 * pairs, stream)
+                   : dispatch_pair<128>(epi, ta, tb, tc, td, args, 2 * pairs, stream);
 }

@@ -70,8 +70,8 @@ struct GemmArgs {
   // tile order of the CTA-pair kernel without a fused gather: 0 = row blocks vary fastest (concurrent
   // tiles share B tiles), 1 = column blocks vary fastest (concurrent tiles share A tiles)
   int n_fastest;
-  // EPI_BF16 on the CTA-pair kernel: 1 when the launcher built a tensor map of C, so the epilogue
-  // stages 32 x 64 bf16 boxes in shared memory and writes them with TMA stores
+  // EPI_BF16 / EPI_SWIGLU on the CTA-pair kernel: 1 when the launcher built tensor maps of the outputs,
+  // so the epilogue stages bf16 boxes in shared memory and writes them with TMA stores
   int c_tma;
 };
 
