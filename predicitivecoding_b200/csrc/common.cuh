@@ -27,6 +27,7 @@ enum ErrorCode : int {
   kErrTimeoutPeer = 5,      // a peer rank's flag never arrived
   kErrBadArg = 6,
   kErrTimeoutChunk = 7,     // a gathered chunk of A was never marked copied
+  kErrTimeoutAux = 8,       // GEMM epilogue waited too long for an auxiliary input tile
 };
 
 // ~2 s at 1.9 GHz.  A legitimate wait in these kernels is microseconds.

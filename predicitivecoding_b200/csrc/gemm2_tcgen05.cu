@@ -134,6 +134,12 @@ PCB_DEVICE void gather_chunks(const GemmArgs& a, int tid, int nthreads) {
   }
 }
 
+// Epilogues that read an input tile of the output's shape (the residual stream; the SwiGLU
+// pre-activations): with tensor maps, each warp loads its [32 x 32] input boxes by TMA into its
+// staging buffer, finishes them in place and stores them by TMA.
+template <int EPI>
+PCB_DEVICE constexpr bool aux_tma() { return EPI == EPI_RESID_F32 || EPI == EPI_SWIGLU_BWD; }
+
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -149,6 +155,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // two auxiliary-tile barriers per epilogue warp, 256 bytes into the 1 KB gap after the ring
+  uint64_t* aux_bar = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES + 256);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -170,6 +178,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tfull[s], 1);
       mbar_init(&tempty[s], 2 * kEpiWarps);
     }
+    if (aux_tma<EPI>() && args.c_tma)
+      for (int s = 0; s < 2 * kEpiWarps; ++s) mbar_init(aux_bar + s, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -177,7 +187,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
     if ((EPI == EPI_BF16 || EPI == EPI_SWIGLU) && args.c_tma) prefetch_tmap(&tmC);
-    if (EPI == EPI_SWIGLU && args.c_tma) prefetch_tmap(&tmD);
+    if ((EPI == EPI_SWIGLU || aux_tma<EPI>()) && args.c_tma) prefetch_tmap(&tmD);
+    if (aux_tma<EPI>() && args.c_tma) prefetch_tmap(&tmC);
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
@@ -303,19 +314,131 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t acc_phase = 0;
     PAIR_STAT_DECL(st_tfull);
     PAIR_STAT_DECL(st_body);
-    for (int tile = pair_id; tile < tiles; tile += num_pairs) {
+    uint8_t* aux_stage = smem + C::EPI_OFF + (warp - 2) * C::EPI_WARP_BYTES;
+    uint32_t aux_ph = 0u;   // bit b: parity of buffer b's next completion
+    bool aux_ok = true;
+    for (int tile = pair_id; tile < tiles && aux_ok; tile += num_pairs) {
       int split_unused, mb, nb;
       tile_coords(tile, args, num_m, num_n, split_unused, mb, nb);
       const int m = mb * 2 * kBM + rank * kBM + row;
       const int n0 = nb * BN;
       const bool row_ok = m < args.M;
+      const int row0_aux = mb * 2 * kBM + rank * kBM + q * 32;
+      // input boxes of chunk i (accumulator columns [32 (half + 2 i), +32)) into buffer buf
+      auto aux_request = [&](int i, int buf) {
+        uint64_t* bar = &aux_bar[(warp - 2) * 2 + buf];
+        uint8_t* box = aux_stage + buf * 4096;
+        const int n = n0 + (half + 2 * i) * 32;
+        mbar_arrive_expect_tx(bar, 4096);
+        if (EPI == EPI_RESID_F32) {
+          tma_load_2d(box, &tmD, bar, n, row0_aux);
+        } else {
+          const int gx = (n >> 6) * 128 + (n & 63);
+          tma_load_2d(box, &tmD, bar, gx, row0_aux);
+          tma_load_2d(box + 2048, &tmD, bar, gx + 64, row0_aux);
+        }
+      };
+      if (aux_tma<EPI>() && args.c_tma && lane == 0) {
+        bulk_group_wait_read<0>();   // the previous tile's stores have read both buffers
+        aux_request(0, 0);
+        if (BN / 64 > 1) aux_request(1, 1);
+      }
       PAIR_STAT_T0(st_w2);
       if (!mbar_wait(&tfull[acc], acc_phase, args.err, kErrTimeoutTmemFull, abort_flag)) break;
       PAIR_STAT_ADD(st_tfull, st_w2);
       PAIR_STAT_T0(st_b);
       tc_fence_after();
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      if (EPI == EPI_SWIGLU && args.c_tma) {
+      if (aux_tma<EPI>() && args.c_tma) {
+        // chunk i of this warp = accumulator columns [32 (half + 2 i), +32); input boxes of chunk i go
+        // to buffer i & 1 (4 KB: one fp32 box, or the gate and up bf16 boxes of 2 KB); the boxes of
+        // chunks 0 and 1 were requested before the accumulator wait, chunk i + 2 is requested as soon as
+        // the store of chunk i has read buffer i & 1
+        constexpr int NCH = BN / 64;
+#pragma unroll 1
+        for (int i = 0; i < NCH; ++i) {
+          const int c = half + 2 * i;
+          const int buf = i & 1;
+          uint8_t* box = aux_stage + buf * 4096;
+          float v[32];
+          tmem_load_f32x32(tbase + c * 32, v);
+          const bool got = mbar_wait(&aux_bar[(warp - 2) * 2 + buf], (aux_ph >> buf) & 1u, args.err, kErrTimeoutAux,
+                                     abort_flag);
+          if (!__all_sync(0xffffffffu, got)) {   // the warp leaves together
+            aux_ok = false;
+            break;
+          }
+          aux_ph ^= 1u << buf;
+          const int n = n0 + c * 32;
+          if (EPI == EPI_RESID_F32) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              float4* cell = reinterpret_cast<float4*>(box + lane * 128 + ((j ^ (lane & 7)) << 4));
+              float4 a = *cell;
+              float o[4] = {v[4 * j] * args.alpha, v[4 * j + 1] * args.alpha, v[4 * j + 2] * args.alpha,
+                            v[4 * j + 3] * args.alpha};
+              if (args.bias != nullptr) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const int col = n + 4 * j + e;
+                  if (col < args.N)
+                    o[e] += args.bias_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(args.bias)[col])
+                                           : reinterpret_cast<const float*>(args.bias)[col];
+                }
+              }
+              a.x += o[0];
+              a.y += o[1];
+              a.z += o[2];
+              a.w += o[3];
+              *cell = a;
+            }
+          } else {  // EPI_SWIGLU_BWD: gate box at box, up box at box + 2048 (64-byte rows, 64-byte swizzle)
+            const int sw = (lane >> 1) & 3;
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+              uint4* gp = reinterpret_cast<uint4*>(box + lane * 64 + ((cc ^ sw) << 4));
+              uint4* up = reinterpret_cast<uint4*>(box + 2048 + lane * 64 + ((cc ^ sw) << 4));
+              const uint4 g4 = *gp, u4 = *up;
+              const uint32_t gw[4] = {g4.x, g4.y, g4.z, g4.w};
+              const uint32_t uw[4] = {u4.x, u4.y, u4.z, u4.w};
+              uint32_t dgw[4], duw[4];
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                float dgv[2], duv[2];
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                  const float g = e ? bf16_hi(gw[k]) : bf16_lo(gw[k]);
+                  const float u = e ? bf16_hi(uw[k]) : bf16_lo(uw[k]);
+                  const float dh = args.alpha * v[8 * cc + 2 * k + e];
+                  const float sg = __fdividef(1.f, 1.f + __expf(-g));
+                  duv[e] = dh * g * sg;
+                  dgv[e] = dh * u * sg * (1.f + g * (1.f - sg));
+                }
+                dgw[k] = pack_bf16x2(dgv[0], dgv[1]);
+                duw[k] = pack_bf16x2(duv[0], duv[1]);
+              }
+              *gp = make_uint4(dgw[0], dgw[1], dgw[2], dgw[3]);
+              *up = make_uint4(duw[0], duw[1], duw[2], duw[3]);
+            }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if (EPI == EPI_RESID_F32) {
+              tma_store_2d(&tmC, box, n, row0_aux);
+            } else {
+              const int gx = (n >> 6) * 128 + (n & 63);
+              tma_store_2d(&tmC, box, gx, row0_aux);
+              tma_store_2d(&tmC, box + 2048, gx + 64, row0_aux);
+            }
+            bulk_group_commit();
+            if (i + 2 < NCH) {
+              bulk_group_wait_read<0>();
+              aux_request(i + 2, buf);
+            }
+          }
+        }
+      } else if (EPI == EPI_SWIGLU && args.c_tma) {
         // per 128-column group: this warp's 32 gate and 32 up columns of pre and the 32 act columns
         // they make, each staged as a [32 x 32] bf16 box (64-byte rows, 64-byte swizzle: 16-byte
         // chunk c of row r at c ^ ((r >> 1) & 3)) and written by TMA stores
@@ -575,7 +698,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
-  if ((EPI == EPI_BF16 || EPI == EPI_SWIGLU) && args.c_tma && warp >= 2 && lane == 0)
+  if ((EPI == EPI_BF16 || EPI == EPI_SWIGLU || aux_tma<EPI>()) && args.c_tma && warp >= 2 && lane == 0)
     bulk_group_wait_all();  // every TMA store has landed before the CTA exits
   __syncwarp();
   tc_fence_before();
@@ -614,14 +737,15 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn2() {
 
 static bool make_map2(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld,
                       uint32_t box_inner, uint32_t box_outer,
-                      CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
+                      CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B, bool f32 = false) {
   auto fn = encode_fn2();
   if (!fn) return false;
   cuuint64_t dims[2] = {inner, outer};
-  cuuint64_t strides[1] = {ld * 2};
+  cuuint64_t strides[1] = {ld * (f32 ? 4 : 2)};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t es[2] = {1, 1};
-  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, es,
+  return fn(m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr),
+            dims, strides, box, es,
             CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -742,6 +866,17 @@ int pcb_gemm_pair_launch(const void* A, int a_mn, long long lda, const void* B, 
   if (epi == EPI_SWIGLU && c_ok && args.D != nullptr && (reinterpret_cast<uintptr_t>(args.D) & 15) == 0 &&
       (args.ldd % 8) == 0 && make_map2(&tc, args.C, N, M, args.ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B) &&
       make_map2(&td, args.D, N / 2, M, args.ldd, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+    args.c_tma = 1;
+  // residual add (fp32 x_out = x_in + f(x)) and SwiGLU backward (bf16 pre in, bf16 d(pre) out): the
+  // input tile is loaded by TMA through the D map slot, the output stored by TMA through the C map
+  const bool aux_al = args.aux != nullptr && (reinterpret_cast<uintptr_t>(args.aux) & 15) == 0;
+  if (epi == EPI_RESID_F32 && aux_al && (reinterpret_cast<uintptr_t>(args.C) & 15) == 0 && (args.ldc % 4) == 0 &&
+      (args.ldaux % 4) == 0 && make_map2(&tc, args.C, N, M, args.ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B, true) &&
+      make_map2(&td, args.aux, N, M, args.ldaux, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B, true))
+    args.c_tma = 1;
+  if (epi == EPI_SWIGLU_BWD && aux_al && c_ok && (args.ldaux % 8) == 0 &&
+      make_map2(&tc, args.C, 2 * (long long)N, M, args.ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B) &&
+      make_map2(&td, args.aux, 2 * (long long)N, M, args.ldaux, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
     args.c_tma = 1;
   const int tiles = num_m * num_n * splits;
   const int max_pairs = num_sms / 2;

@@ -106,14 +106,21 @@ def test_gemm_split_k_red():
     assert rel_err(out, ref + 1.0) < 1e-3
 
 
-def test_gemm_resid():
-    M, N, K = 512, 256, 192
+@pytest.mark.parametrize("shape", [(512, 256, 192), (200, 136, 72), (300, 102, 64)])
+@pytest.mark.parametrize("with_bias", [False, True])
+def test_gemm_resid(shape, with_bias, gemm_mode):
+    # (200, 136): TMA boxes clipped at both edges; (300, 102): rows of 408 bytes, no tensor maps
+    M, N, K = shape
     a, b, ref = _operands(M, N, K, False, False, seed=3)
     x = torch.randn(M, N, device=DEV)
-    out = torch.empty_like(x)
-    ops.gemm(a, b, epi=ops.EPI_RESID_F32, c=out, aux=x)
+    bias = torch.randn(N, device=DEV) if with_bias else None
+    padded = torch.full((M, N + 4), 5.0, device=DEV)
+    out = padded[:, :N]
+    ops.gemm(a, b, epi=ops.EPI_RESID_F32, c=out, aux=x, bias=bias, alpha=0.5)
     torch.cuda.synchronize()
-    assert rel_err(out, ref + x) < 1e-3
+    expect = 0.5 * ref + x + (bias if with_bias else 0.0)
+    assert rel_err(out, expect) < 1e-3
+    assert bool((padded[:, N:] == 5.0).all())
 
 
 def _gelu(x):
