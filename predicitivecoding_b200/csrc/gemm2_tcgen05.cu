@@ -47,18 +47,23 @@ constexpr int kBK = 64;
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 
-template <int BN>
+template <int BN, int EPI>
 struct Cfg {
   static constexpr int A_BYTES = kBM * kBK * 2;
   static constexpr int B_BYTES = (BN / 2) * kBK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (BN == 256) ? 5 : 6;
   static constexpr int TMEM_COLS = 2 * BN;
-  // barriers in the first 256 bytes after the ring; then, 1024-aligned for the 128-byte swizzle of the
-  // TMA-store boxes, 8 KB per epilogue warp: two [32 x 64] bf16 store boxes, or one [32 x 32] fp32
-  // transpose scratch on the coalesced path
+  // per epilogue warp: 8 KB for the epilogues that stage two TMA boxes (bf16 output, SwiGLU, residual,
+  // SwiGLU backward), 4 KB for the [32 x 32] fp32 transpose scratch of the coalesced path
+  static constexpr bool kTwoBoxes =
+      EPI == EPI_BF16 || EPI == EPI_SWIGLU || EPI == EPI_RESID_F32 || EPI == EPI_SWIGLU_BWD;
+  static constexpr int EPI_WARP_BYTES = kTwoBoxes ? 8192 : 4096;
+  // the deepest operand ring that fits: 227 KB - 1 KB (barriers, alignment gap) - staging - 1 KB slack
+  static constexpr int STAGES_FIT = (232448 - 2048 - 8 * EPI_WARP_BYTES) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
+  // barriers in the first 256 bytes after the ring (then the auxiliary-tile barriers); the staging
+  // area starts 1024-aligned for the 128-byte swizzle of the TMA boxes
   static constexpr int EPI_OFF = STAGES * STAGE_BYTES + 1024;
-  static constexpr int EPI_WARP_BYTES = 8192;
   static constexpr int SMEM_BYTES = EPI_OFF + 8 * EPI_WARP_BYTES + 1024;
   static_assert(SMEM_BYTES <= 232448, "dynamic shared memory above the 227 KB per-block limit");
   static_assert(8 * (2 * STAGES + 4) + 8 <= 256, "barriers do not fit their 256-byte slot");
@@ -145,7 +150,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmD,
                      const GemmArgs args) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, EPI>;
   constexpr int STAGES = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -753,7 +758,7 @@ static bool make_map2(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t 
 template <int BN, int EPI>
 static int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const CUtensorMap& td,
                        const GemmArgs& a, int grid, cudaStream_t s) {
-  using C = pair::Cfg<BN>;
+  using C = pair::Cfg<BN, EPI>;
   static bool attr_done = false;
   if (!attr_done) {
     cudaFuncSetAttribute(pair::gemm_pair_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
