@@ -9,15 +9,17 @@ Cases (each timed with CUDA events on the launching stream after warm-up, max ov
 
 * ``rs_adamw_ag``: the data-parallel optimizer step of the 124M decoder (134,105,856 parameters):
   every rank reads its 1/T shard of every rank's fp32 gradients over NVLink, runs AdamW on it and
-  writes the bf16 weights of the shard into every rank's weight buffer.  Bytes that cross NVLink per
-  rank: in (T-1)/T * N * 4, out (T-1)/T * N * 2;
+  writes the bf16 weights of the shard into every rank's weight buffer;
 * ``pc_allreduce_update``: the PC data-parallel weight step (64 Mi fp32 weights): sum of every
-  rank's delta-W shard, weight update, fp32 + bf16 weights written to every rank.  In (T-1)/T * N * 4,
-  out (T-1)/T * N * 6;
+  rank's delta-W shard, weight update, fp32 + bf16 weights written to every rank;
 * ``all_reduce``: the Communicator's peer all-reduce (one-shot below 512 KiB, two-shot above).
 
-The roofline time is the slower direction's bytes at the measured 770 GB/s per direction per GPU;
-each line reports achieved / roofline.  Every case includes the device barriers it needs in the
+Bytes that must cross each GPU's links, per direction: a rank's inbound link carries what it pulls from
+the others and what the others push to it, and its outbound link the mirror image, so for T ranks the
+per-direction volume is (T-1)/T * N * 6 for ``rs_adamw_ag`` (4-byte gradients pulled, 2-byte weights
+pushed), (T-1)/T * N * 10 for ``pc_allreduce_update`` (4 pulled, 4 + 2 pushed) and 2 (T-1)/T * S for
+an all-reduce of S bytes. The roofline time is that volume at the measured 770 GB/s per direction per
+GPU; each line reports achieved / roofline. Every case includes the device barriers it needs in the
 trainer (before: all inputs written; after: all outputs written).
 """
 from __future__ import annotations
@@ -80,10 +82,10 @@ def main() -> None:
         peer.barrier()
 
     ms = _time(dp_step, 10, dev)
-    b_in, b_out = (T - 1) / T * N * 4, (T - 1) / T * N * 2
-    roof = max(b_in, b_out) / (LINK_GBS * 1e9) * 1e3
+    per_dir = (T - 1) / T * N * (4 + 2)
+    roof = per_dir / (LINK_GBS * 1e9) * 1e3
     out.append({"case": "rs_adamw_ag (124M params, fp32 grads in, bf16 weights out)", "world": T,
-                "ms": round(ms, 3), "nvlink_in_gb": round(b_in / 1e9, 3), "nvlink_out_gb": round(b_out / 1e9, 3),
+                "ms": round(ms, 3), "nvlink_gb_per_direction": round(per_dir / 1e9, 3),
                 "roofline_ms": round(roof, 3), "of_roofline": round(roof / ms, 3) if T > 1 else None})
     del grad, w16, w32, m, v
 
@@ -103,10 +105,10 @@ def main() -> None:
         peer.barrier()
 
     ms = _time(pc_step, 10, dev)
-    b_in, b_out = (T - 1) / T * N2 * 4, (T - 1) / T * N2 * 6
-    roof = max(b_in, b_out) / (LINK_GBS * 1e9) * 1e3
+    per_dir = (T - 1) / T * N2 * (4 + 6)
+    roof = per_dir / (LINK_GBS * 1e9) * 1e3
     out.append({"case": "pc_allreduce_update (64 Mi fp32 weights)", "world": T, "ms": round(ms, 3),
-                "nvlink_in_gb": round(b_in / 1e9, 3), "nvlink_out_gb": round(b_out / 1e9, 3),
+                "nvlink_gb_per_direction": round(per_dir / 1e9, 3),
                 "roofline_ms": round(roof, 3), "of_roofline": round(roof / ms, 3) if T > 1 else None})
     del dlt, wts, w16b
 
