@@ -58,6 +58,8 @@ int pcb_linear_scan_bwd(const float* a, const float* st, const float* ds, float*
 
 int pcb_coll_reduce(const void* const* in_peers, void* out, long long lo, long long hi, int world, int op,
                     float scale, int dtype, int num_sms, cudaStream_t s);
+int pcb_coll_reduce_push(const void* const* in_peers, void* const* out_peers, long long lo, long long hi, int world,
+                         int op, float scale, int dtype, int num_sms, cudaStream_t s);
 int pcb_coll_gather(const void* const* src_peers, void* out, long long chunk, long long src_stride, int world,
                     int dtype, int num_sms, cudaStream_t s);
 int pcb_rope_append(const void* qkv, const float* cs_table, const long long* pos, void* qo, void* kc, void* vc, int B,
@@ -511,6 +513,17 @@ void coll_reduce(const at::Tensor& in_ptrs, at::Tensor& out, int64_t lo, int64_t
                         world, op, (float)scale, coll_dtype(out), num_sms(), cur_stream()),
         "coll_reduce");
 }
+// `like`: a tensor of the payload dtype (the local symmetric buffer)
+void coll_reduce_push(const at::Tensor& in_ptrs, const at::Tensor& out_ptrs, const at::Tensor& like, int64_t lo,
+                      int64_t hi, int64_t world, int64_t op, double scale) {
+  req(in_ptrs, at::kLong, "in_ptrs");
+  req(out_ptrs, at::kLong, "out_ptrs");
+  PCB_CHECK(in_ptrs.numel() >= world && out_ptrs.numel() >= world, "coll_reduce_push: pointer tables too short");
+  check(pcb_coll_reduce_push(reinterpret_cast<const void* const*>(in_ptrs.data_ptr<int64_t>()),
+                             reinterpret_cast<void* const*>(out_ptrs.data_ptr<int64_t>()), lo, hi, world, op,
+                             (float)scale, coll_dtype(like), num_sms(), cur_stream()),
+        "coll_reduce_push");
+}
 void coll_gather(const at::Tensor& src_ptrs, at::Tensor& out, int64_t chunk, int64_t src_stride, int64_t world) {
   req(src_ptrs, at::kLong, "src_ptrs");
   PCB_CHECK(out.is_cuda() && out.is_contiguous() && out.numel() >= chunk * world, "coll_gather: out too small");
@@ -698,6 +711,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("swiglu_rows", &swiglu_rows);
   m.def("annotate", &annotate);
   m.def("coll_reduce", &coll_reduce);
+  m.def("coll_reduce_push", &coll_reduce_push);
   m.def("coll_gather", &coll_gather);
   m.def("dev_alloc", &dev_alloc);
   m.def("dev_record_stream", &dev_record_stream);

@@ -50,38 +50,65 @@ __device__ __forceinline__ T from_f(float x) {
   else return __float2bfloat16(x);
 }
 
-// out[i - lo + out_off] = scale * op_{p=0..world-1} in_peers[p][i] for i in [lo, hi)
-template <typename T, int OP>
+// r[i] = scale * op_{p=0..world-1} in_peers[p][i] for i in [lo, hi), written to out[i - lo] or, with
+// out_peers, to out_peers[q][i] of every rank q (the two-shot all-reduce pushes its reduced shard into
+// every rank's buffer at the shard's own offsets; each index is read and then overwritten by the same
+// thread, and no other rank touches this shard). WORLD > 0 fixes the rank count so that the loads of
+// all ranks are issued before the first combine; WORLD == 0 takes it at run time.
+template <typename T, int OP, int WORLD>
 __global__ void __launch_bounds__(256)
-coll_reduce_kernel(const T* const* __restrict__ in_peers, T* __restrict__ out, long long lo, long long hi,
-                   int world, float scale) {
+coll_reduce_kernel(const T* const* __restrict__ in_peers, T* __restrict__ out, T* const* __restrict__ out_peers,
+                   long long lo, long long hi, int world_rt, float scale) {
   using V = Vec<T>;
   constexpr int N = V::N;
+  const int world = WORLD > 0 ? WORLD : world_rt;
   const long long n = hi - lo;
-  const long long nv = (reinterpret_cast<uintptr_t>(out) % 16 == 0 && lo % N == 0) ? n / N : 0;
+  const bool out_al = out_peers != nullptr || reinterpret_cast<uintptr_t>(out) % 16 == 0;
+  const long long nv = (out_al && lo % N == 0) ? n / N : 0;
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long q = blockIdx.x * (long long)blockDim.x + threadIdx.x; q < nv; q += stride) {
     float acc[N];
     const long long i = lo + q * N;
-    {
+    if constexpr (WORLD > 0) {
+      V x[WORLD];
+#pragma unroll
+      for (int p = 0; p < WORLD; ++p) x[p] = *reinterpret_cast<const V*>(in_peers[p] + i);
+#pragma unroll
+      for (int e = 0; e < N; ++e) acc[e] = to_f(x[0].v[e]);
+#pragma unroll
+      for (int p = 1; p < WORLD; ++p)
+#pragma unroll
+        for (int e = 0; e < N; ++e) acc[e] = combine<OP>(acc[e], to_f(x[p].v[e]));
+    } else {
       V x = *reinterpret_cast<const V*>(in_peers[0] + i);
 #pragma unroll
       for (int e = 0; e < N; ++e) acc[e] = to_f(x.v[e]);
-    }
-    for (int p = 1; p < world; ++p) {
-      V x = *reinterpret_cast<const V*>(in_peers[p] + i);
+#pragma unroll 4
+      for (int p = 1; p < world; ++p) {
+        V y = *reinterpret_cast<const V*>(in_peers[p] + i);
 #pragma unroll
-      for (int e = 0; e < N; ++e) acc[e] = combine<OP>(acc[e], to_f(x.v[e]));
+        for (int e = 0; e < N; ++e) acc[e] = combine<OP>(acc[e], to_f(y.v[e]));
+      }
     }
     V o;
 #pragma unroll
     for (int e = 0; e < N; ++e) o.v[e] = from_f<T>(acc[e] * scale);
-    *reinterpret_cast<V*>(out + q * N) = o;
+    if (out_peers != nullptr) {
+#pragma unroll 8
+      for (int p = 0; p < world; ++p) *reinterpret_cast<V*>(out_peers[p] + i) = o;
+    } else {
+      *reinterpret_cast<V*>(out + q * N) = o;
+    }
   }
   for (long long j = nv * N + blockIdx.x * (long long)blockDim.x + threadIdx.x; j < n; j += stride) {
     float a = to_f(in_peers[0][lo + j]);
     for (int p = 1; p < world; ++p) a = combine<OP>(a, to_f(in_peers[p][lo + j]));
-    out[j] = from_f<T>(a * scale);
+    const T r = from_f<T>(a * scale);
+    if (out_peers != nullptr) {
+      for (int p = 0; p < world; ++p) out_peers[p][lo + j] = r;
+    } else {
+      out[j] = r;
+    }
   }
 }
 
@@ -116,17 +143,30 @@ int grid_for(long long work, int num_sms) {
   return static_cast<int>(g < 1 ? 1 : g);
 }
 
+template <typename T, int OP>
+void launch_reduce_op(int g, cudaStream_t s, const T* const* ip, T* o, T* const* op_peers, long long lo, long long hi,
+                      int world, float scale) {
+  switch (world) {
+    case 1: coll_reduce_kernel<T, OP, 1><<<g, 256, 0, s>>>(ip, o, op_peers, lo, hi, world, scale); break;
+    case 2: coll_reduce_kernel<T, OP, 2><<<g, 256, 0, s>>>(ip, o, op_peers, lo, hi, world, scale); break;
+    case 4: coll_reduce_kernel<T, OP, 4><<<g, 256, 0, s>>>(ip, o, op_peers, lo, hi, world, scale); break;
+    case 8: coll_reduce_kernel<T, OP, 8><<<g, 256, 0, s>>>(ip, o, op_peers, lo, hi, world, scale); break;
+    default: coll_reduce_kernel<T, OP, 0><<<g, 256, 0, s>>>(ip, o, op_peers, lo, hi, world, scale); break;
+  }
+}
+
 template <typename T>
-int launch_reduce(const void* const* in_peers, void* out, long long lo, long long hi, int world, int op, float scale,
-                  int num_sms, cudaStream_t s) {
+int launch_reduce(const void* const* in_peers, void* out, void* const* out_peers, long long lo, long long hi,
+                  int world, int op, float scale, int num_sms, cudaStream_t s) {
   auto ip = reinterpret_cast<const T* const*>(in_peers);
   auto o = reinterpret_cast<T*>(out);
+  auto opp = reinterpret_cast<T* const*>(out_peers);
   const int g = grid_for((hi - lo) / Vec<T>::N + 1, num_sms);
   switch (op) {
-    case kOpSum: coll_reduce_kernel<T, kOpSum><<<g, 256, 0, s>>>(ip, o, lo, hi, world, scale); break;
-    case kOpProd: coll_reduce_kernel<T, kOpProd><<<g, 256, 0, s>>>(ip, o, lo, hi, world, scale); break;
-    case kOpMax: coll_reduce_kernel<T, kOpMax><<<g, 256, 0, s>>>(ip, o, lo, hi, world, scale); break;
-    case kOpMin: coll_reduce_kernel<T, kOpMin><<<g, 256, 0, s>>>(ip, o, lo, hi, world, scale); break;
+    case kOpSum: launch_reduce_op<T, kOpSum>(g, s, ip, o, opp, lo, hi, world, scale); break;
+    case kOpProd: launch_reduce_op<T, kOpProd>(g, s, ip, o, opp, lo, hi, world, scale); break;
+    case kOpMax: launch_reduce_op<T, kOpMax>(g, s, ip, o, opp, lo, hi, world, scale); break;
+    case kOpMin: launch_reduce_op<T, kOpMin>(g, s, ip, o, opp, lo, hi, world, scale); break;
     default: return -2;
   }
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
@@ -139,8 +179,19 @@ int pcb_coll_reduce(const void* const* in_peers, void* out, long long lo, long l
                     float scale, int dtype, int num_sms, cudaStream_t s) {
   if (hi < lo || world < 1) return -2;
   if (hi == lo) return 0;
-  return dtype == 0 ? launch_reduce<float>(in_peers, out, lo, hi, world, op, scale, num_sms, s)
-                    : launch_reduce<__nv_bfloat16>(in_peers, out, lo, hi, world, op, scale, num_sms, s);
+  return dtype == 0 ? launch_reduce<float>(in_peers, out, nullptr, lo, hi, world, op, scale, num_sms, s)
+                    : launch_reduce<__nv_bfloat16>(in_peers, out, nullptr, lo, hi, world, op, scale, num_sms, s);
+}
+
+// Reduce [lo, hi) over the ranks' buffers and store the result into every rank's buffer (out_peers) at
+// the same offsets: the reduce-scatter and the all-gather halves of a two-shot all-reduce in one pass,
+// with the all-gather as pushes (peer stores) rather than pulls.
+int pcb_coll_reduce_push(const void* const* in_peers, void* const* out_peers, long long lo, long long hi, int world,
+                         int op, float scale, int dtype, int num_sms, cudaStream_t s) {
+  if (hi < lo || world < 1 || out_peers == nullptr) return -2;
+  if (hi == lo) return 0;
+  return dtype == 0 ? launch_reduce<float>(in_peers, nullptr, out_peers, lo, hi, world, op, scale, num_sms, s)
+                    : launch_reduce<__nv_bfloat16>(in_peers, nullptr, out_peers, lo, hi, world, op, scale, num_sms, s);
 }
 
 int pcb_coll_gather(const void* const* src_peers, void* out, long long chunk, long long src_stride, int world,

@@ -219,15 +219,15 @@ class Communicator:
                 ops.ext().coll_reduce(buf.ptrs, flat[lo:hi], 0, n, self.world, int(op), 1.0)
                 P.barrier()
             else:
-                # two-shot: rank r reduces shard r in place in its own buffer; after a barrier every
-                # rank gathers all shards (shard j sits at offset j*per of rank j's buffer)
+                # two-shot in one pass: rank r reduces shard r over every rank's buffer and stores the
+                # result into shard r of every rank's buffer (peer stores); after a barrier each rank's
+                # buffer holds the whole reduced vector
                 per = -(-n // self.world)
                 per += (-per) % 8
                 a, b = min(n, self.rank * per), min(n, (self.rank + 1) * per)
                 if b > a:
-                    ops.ext().coll_reduce(buf.ptrs, buf.local[a:b], a, b, self.world, int(op), 1.0)
+                    ops.ext().coll_reduce_push(buf.ptrs, buf.ptrs, buf.local, a, b, self.world, int(op), 1.0)
                 P.barrier()
-                ops.ext().coll_gather(buf.ptrs, buf.local, per, per, self.world)
                 flat[lo:hi].copy_(buf.local[:n])
                 P.barrier()
         return t
