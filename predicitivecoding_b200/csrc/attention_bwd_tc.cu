@@ -32,6 +32,24 @@
 namespace pcb {
 namespace fab {
 
+// Optional cycle counters (build with -DPCB_ATTN_STATS), read with pcb_attn_bwd_stats():
+//   0 MMA issuer loop   1 MMA waits Q/dO stage   2 MMA waits S/dP read (s_free)   3 MMA waits dS (ds_full)
+//   4 MMA waits dQ drained   5 gradient warp 0: waits stage + S/dP   6 gradient warp 0: waits P read / dS buffer
+//   7 gradient warp 0 loop   8 dQ warp: waits dQ   9 dQ warp: waits staging reads   10 dQ warp loop
+//   11 producer waits free stage   12 gradient warp 0 waits dK/dV   13 tiles issued by the MMA warps
+#ifdef PCB_ATTN_STATS
+__device__ unsigned long long g_attn_stats[16];
+#define AST_DECL(v) long long v = 0
+#define AST_T0(t) const long long t = clock64()
+#define AST_ADD(v, t) v += clock64() - t
+#define AST_FLUSH(i, v) atomicAdd(&g_attn_stats[i], (unsigned long long)(v))
+#else
+#define AST_DECL(v)
+#define AST_T0(t)
+#define AST_ADD(v, t)
+#define AST_FLUSH(i, v)
+#endif
+
 constexpr int kT = 128;            // keys per item, queries per tile
 constexpr int kHD = 64;
 constexpr int kThreads = 512;  // WG0/WG1 gradient (query columns 0-63 / 64-127), WG2 dQ, warp 12 TMA, warp 13 MMA
@@ -176,6 +194,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---------------- TMA producer ----------------
       int ic = 0, lc = 0;
       bool ok = true;
+      AST_DECL(a_pw);
       for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++ic) {
         const Item it = item_of(i, BH, H);
         if (!(ok = mbar_wait(kv_empty, (ic & 1) ^ 1u, err, kErrTimeoutEmpty, abort_flag))) break;
@@ -185,7 +204,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_2d(sV, &tm_qkv, kv_full, (2 * H + it.h) * kHD, krow);
         for (int qi = it.kb; qi < T; ++qi, ++lc) {
           const int st = lc & 1;
+          AST_T0(a_t);
           if (!(ok = mbar_wait(&ld_empty[st], ((lc >> 1) & 1) ^ 1u, err, kErrTimeoutEmpty, abort_flag))) break;
+          AST_ADD(a_pw, a_t);
           mbar_arrive_expect_tx(&ld_full[st], 2 * kAtom + 2 * kT * 4);
           const int qrow = it.b * S + qi * kT;
           tma_load_2d(sQ + st * kAtom, &tm_qkv, &ld_full[st], it.h * kHD, qrow);
@@ -194,6 +215,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           bulk_load(sVec + st * 2 * kT + kT, dvec + (long long)it.bh * S + qi * kT, kT * 4, &ld_full[st]);
         }
       }
+      AST_FLUSH(11, a_pw);
     }
    } else if (warp == kMmaWarp) {
     if (lane == 0) {
@@ -206,8 +228,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                      ds_addr = smem_u32(sDS);
       int ic = 0, lc = 0, tcount = 0;  // items, loaded tiles, tiles processed (phase counters)
       bool ok = true;
+      AST_DECL(a_ld);
+      AST_DECL(a_sf);
+      AST_DECL(a_ds);
+      AST_DECL(a_dq);
+      AST_T0(a_loop);
       auto grad = [&](int v, int st, bool first) -> bool {  // MMAs (3)(4)(5) of the tile with counter v
+        AST_T0(a_t1);
         if (!mbar_wait(ds_full, v & 1, err, kErrTimeoutTmemEmpty, abort_flag)) return false;
+        AST_ADD(a_ds, a_t1);
         tc_fence_after();
         const uint64_t bdo = make_smem_desc(do_addr + st * kAtom, kAtom, 1024, 2);
         const uint64_t bq = make_smem_desc(q_addr + st * kAtom, kAtom, 1024, 2);
@@ -224,7 +253,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t off = (k >> 2) * kAtom + (k & 3) * 32;
           umma_bf16(tmem + TM_DK, ads + (off >> 4), bq + (k * 2048 >> 4), idesc_dk, (!first || k > 0) ? 1u : 0u);
         }
+        AST_T0(a_t2);
         if (v > 0 && !mbar_wait(dq_empty, (v - 1) & 1, err, kErrTimeoutTmemEmpty, abort_flag)) return false;
+        AST_ADD(a_dq, a_t2);
         tc_fence_after();
         const uint64_t adq = make_smem_desc(dsb, kAtom, 1024, 2);
         const uint64_t bk = make_smem_desc(k_addr, kAtom, 1024, 2);
@@ -243,9 +274,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         int prev_st = 0;
         for (int qi = it.kb; qi < T && ok; ++qi, ++lc, ++tcount) {
           const int st = lc & 1;
+          AST_T0(a_t3);
           if (!(ok = mbar_wait(&ld_full[st], (lc >> 1) & 1, err, kErrTimeoutFull, abort_flag))) break;
+          AST_ADD(a_ld, a_t3);
+          AST_T0(a_t4);
           // S/dP may be overwritten once the gradient warpgroup has read the previous tile's
           if (tcount > 0 && !(ok = mbar_wait(s_free, (tcount - 1) & 1, err, kErrTimeoutTmemEmpty, abort_flag))) break;
+          AST_ADD(a_sf, a_t4);
           tc_fence_after();
           const uint64_t bq = make_smem_desc(q_addr + st * kAtom, 16, 1024, 2);
           const uint64_t bdo = make_smem_desc(do_addr + st * kAtom, 16, 1024, 2);
@@ -264,6 +299,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma_commit(acc_full);
         umma_commit(kv_empty);
       }
+      AST_FLUSH(0, clock64() - a_loop);
+      AST_FLUSH(1, a_ld);
+      AST_FLUSH(2, a_sf);
+      AST_FLUSH(3, a_ds);
+      AST_FLUSH(4, a_dq);
+      AST_FLUSH(13, tcount);
     }
    }
   } else if (warp < 8) {
@@ -275,12 +316,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float c = scale * kLog2e;
     int ic = 0, lc = 0, tcount = 0;
     bool ok = true;
+    AST_DECL(g_w1);
+    AST_DECL(g_w2);
+    AST_DECL(g_w3);
+    AST_T0(g_loop);
     for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++ic) {
       const Item it = item_of(i, BH, H);
       for (int qi = it.kb; qi < T; ++qi, ++lc, ++tcount) {
         const int st = lc & 1;
+        AST_T0(g_t1);
         ok = mbar_wait(&ld_full[st], (lc >> 1) & 1, err, kErrTimeoutFull, abort_flag) &&
              mbar_wait(s_full, tcount & 1, err, kErrTimeoutTmemFull, abort_flag);
+        AST_ADD(g_w1, g_t1);
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
         tc_fence_after();
         const float* sl = sVec + st * 2 * kT;
@@ -317,9 +364,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (qt == 2 * gw) {
             // P of the previous tile must have been read by its (3); this tile's dS buffer by (4)(5)
             // of the tile two back (each barrier is waited once per phase, in order)
+            AST_T0(g_t2);
             if (tcount > 0) ok = mbar_wait(p_done, (tcount - 1) & 1, err, kErrTimeoutTmemFull, abort_flag);
             if (ok && tcount > 1)
               ok = mbar_wait(&grad_done[tcount & 1], ((tcount - 2) >> 1) & 1, err, kErrTimeoutTmemFull, abort_flag);
+            AST_ADD(g_w2, g_t2);
             if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
             tc_fence_after();
           }
@@ -361,7 +410,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) break;
       // ---- dK, dV of this key tile ----
+      AST_T0(g_t3);
       ok = mbar_wait(acc_full, ic & 1, err, kErrTimeoutTmemFull, abort_flag);
+      AST_ADD(g_w3, g_t3);
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
       // warpgroup 0 writes dK * scale (rotated back by -theta with a RoPE table), warpgroup 1 writes dV
@@ -397,6 +448,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
     }
+    if (threadIdx.x == 0) {
+      AST_FLUSH(5, g_w1);
+      AST_FLUSH(6, g_w2);
+      AST_FLUSH(7, clock64() - g_loop);
+      AST_FLUSH(12, g_w3);
+    }
   } else if (warp < 12) {
     // ---------------- dQ warpgroup: thread = query row = TMEM lane ----------------
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsDq));
@@ -404,10 +461,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     int tcount = 0;
     bool ok = true;
+    AST_DECL(q_w1);
+    AST_DECL(q_w2);
+    AST_T0(q_loop);
     for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
       const Item it = item_of(i, BH, H);
       for (int qi = it.kb; qi < T; ++qi, ++tcount) {
+        AST_T0(q_t1);
         ok = dq_wg_all(mbar_wait(dq_full, tcount & 1, err, kErrTimeoutTmemFull, abort_flag));
+        AST_ADD(q_w1, q_t1);
         if (!ok) break;
         tc_fence_after();
         uint32_t qu[64];
@@ -419,8 +481,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(dq_empty);
         // stage dQ * scale in shared memory (two 128B-swizzled boxes of 32 columns), then one thread
         // adds both boxes into the fp32 accumulator with TMA reductions
+        AST_T0(q_t2);
         if (r == 0) bulk_wait_read0();  // the previous tile's reductions have read the staging buffer
         dq_wg_sync();
+        AST_ADD(q_w2, q_t2);
 #pragma unroll
         for (int bx = 0; bx < 2; ++bx) {
           uint8_t* row = sDQ + bx * kAtom + r * 128;
@@ -443,6 +507,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if (r == 0) bulk_wait0();  // every reduction has landed before the CTA exits
+    if (r == 0) {
+      AST_FLUSH(8, q_w1);
+      AST_FLUSH(9, q_w2);
+      AST_FLUSH(10, clock64() - q_loop);
+    }
   }
 
   __syncwarp();
@@ -535,6 +604,19 @@ static bool encode_rows(PFN_cuTensorMapEncodeTiled_v12000 fn, CUtensorMap* tm, c
 
 // Same contract as pcb_attn_bwd_rope, on tcgen05: S % 128 == 0, HD == 64, row strides % 8 == 0.
 // Returns 0, -1 (unsupported shape), -5 (tensor-map encode) or -(1000 + cudaError) (launch).
+// Copies the attention-backward cycle counters into out[16] and clears them; -1 when built without them.
+int pcb_attn_bwd_stats(unsigned long long* out) {
+#ifdef PCB_ATTN_STATS
+  if (cudaMemcpyFromSymbol(out, pcb::fab::g_attn_stats, 16 * sizeof(unsigned long long)) != cudaSuccess) return -2;
+  unsigned long long zero[16] = {};
+  cudaMemcpyToSymbol(pcb::fab::g_attn_stats, zero, sizeof(zero));
+  return 0;
+#else
+  (void)out;
+  return -1;
+#endif
+}
+
 int pcb_attn_bwd_tc(const void* qkv, long long ld, const void* out, const void* dout, long long ld_o,
                     const float* lse, float* dvec, float* dq_acc, void* dqkv, long long ld_d, int B, int S, int H,
                     int HD, float scale, const float* rope_cs, int* err, cudaStream_t s) {

@@ -42,6 +42,8 @@ if os.environ.get("PCB_CHECKED") == "1":   # debug build: bounds-violation count
     NVCC_FLAGS.append("-DPCB_CHECKED")
 if os.environ.get("PCB_GEMM_STATS") == "1":   # profiling build: cycle counters in the pair GEMM roles
     NVCC_FLAGS.append("-DPCB_GEMM_STATS")
+if os.environ.get("PCB_ATTN_STATS") == "1":   # profiling build: cycle counters in the attention backward roles
+    NVCC_FLAGS.append("-DPCB_ATTN_STATS")
 
 setup(
     name="predicitivecoding_b200",
