@@ -65,12 +65,12 @@ constexpr float kLog2e = 1.4426950408889634f;
 // shared memory
 constexpr int K_OFF = 0;                        // K tile (1 atom)
 constexpr int V_OFF = K_OFF + kAtom;            // V tile
-constexpr int Q_OFF = V_OFF + kAtom;            // 2 stages
-constexpr int DO_OFF = Q_OFF + 2 * kAtom;       // 2 stages
-constexpr int DS_OFF = DO_OFF + 2 * kAtom;      // dS^T, 2 buffers x 2 atoms (queries 0-63, 64-127)
-constexpr int DQ_OFF = DS_OFF + 4 * kAtom;      // dQ staging: 2 boxes of [128 rows x 32 fp32], swizzled
-constexpr int VEC_OFF = DQ_OFF + 2 * kAtom;     // per stage: lse[128], delta[128] fp32
-constexpr int BAR_OFF = VEC_OFF + 2 * 2 * kT * 4;
+constexpr int kQStages = 3;  // Q / dO ring: the loads of tile i+2 overlap tile i (lse / delta come from L2)
+constexpr int Q_OFF = V_OFF + kAtom;                   // kQStages stages
+constexpr int DO_OFF = Q_OFF + kQStages * kAtom;       // kQStages stages
+constexpr int DS_OFF = DO_OFF + kQStages * kAtom;      // dS^T, 2 buffers x 2 atoms (queries 0-63, 64-127)
+constexpr int DQ_OFF = DS_OFF + 4 * kAtom;             // dQ staging: 2 boxes of [128 rows x 32 fp32], swizzled
+constexpr int BAR_OFF = DQ_OFF + 2 * kAtom;
 constexpr int SMEM = BAR_OFF + 256 + 1024;
 static_assert(SMEM <= 232448, "shared memory budget");
 
@@ -134,21 +134,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sDO = smem + DO_OFF;
   uint8_t* sDS = smem + DS_OFF;
   uint8_t* sDQ = smem + DQ_OFF;
-  float* sVec = reinterpret_cast<float*>(smem + VEC_OFF);  // [stage][lse 128 | delta 128]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BAR_OFF);
   uint64_t* kv_full = bars + 0;
   uint64_t* kv_empty = bars + 1;
-  uint64_t* ld_full = bars + 2;    // [2]
-  uint64_t* ld_empty = bars + 4;   // [2]
-  uint64_t* s_full = bars + 6;
-  uint64_t* s_free = bars + 7;
-  uint64_t* ds_full = bars + 8;
-  uint64_t* grad_done = bars + 13;  // [2]: per dS buffer, after (4)(5) of a tile read it
-  uint64_t* p_done = bars + 9;      // after (3) read P
-  uint64_t* dq_full = bars + 10;
-  uint64_t* dq_empty = bars + 11;
-  uint64_t* acc_full = bars + 12;  // dK / dV of the item complete
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
+  uint64_t* ld_full = bars + 2;    // [kQStages]
+  uint64_t* ld_empty = bars + 5;   // [kQStages]
+  uint64_t* s_full = bars + 8;
+  uint64_t* s_free = bars + 9;
+  uint64_t* ds_full = bars + 10;
+  uint64_t* p_done = bars + 11;     // after (3) read P
+  uint64_t* dq_full = bars + 12;
+  uint64_t* dq_empty = bars + 13;
+  uint64_t* acc_full = bars + 14;   // dK / dV of the item complete
+  uint64_t* grad_done = bars + 15;  // [2]: per dS buffer, after (4)(5) of a tile read it
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -159,11 +158,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
     mbar_init(kv_empty, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kQStages; ++i) {
       mbar_init(&ld_full[i], 1);
-      mbar_init(&ld_empty[i], 1 + 8);  // MMA commit + the 8 gradient warps (lse / delta read)
-      mbar_init(&grad_done[i], 1);
+      mbar_init(&ld_empty[i], 1 + 8);  // MMA commit + the 8 gradient warps (done with the tile)
     }
+    for (int i = 0; i < 2; ++i) mbar_init(&grad_done[i], 1);
     mbar_init(s_full, 1);
     mbar_init(s_free, 8);
     mbar_init(ds_full, 8);
@@ -203,16 +202,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_2d(sK, &tm_qkv, kv_full, (H + it.h) * kHD, krow);
         tma_load_2d(sV, &tm_qkv, kv_full, (2 * H + it.h) * kHD, krow);
         for (int qi = it.kb; qi < T; ++qi, ++lc) {
-          const int st = lc & 1;
+          const int st = lc % kQStages;
           AST_T0(a_t);
-          if (!(ok = mbar_wait(&ld_empty[st], ((lc >> 1) & 1) ^ 1u, err, kErrTimeoutEmpty, abort_flag))) break;
+          if (!(ok = mbar_wait(&ld_empty[st], ((lc / kQStages) & 1) ^ 1u, err, kErrTimeoutEmpty, abort_flag))) break;
           AST_ADD(a_pw, a_t);
-          mbar_arrive_expect_tx(&ld_full[st], 2 * kAtom + 2 * kT * 4);
+          mbar_arrive_expect_tx(&ld_full[st], 2 * kAtom);
           const int qrow = it.b * S + qi * kT;
           tma_load_2d(sQ + st * kAtom, &tm_qkv, &ld_full[st], it.h * kHD, qrow);
           tma_load_2d(sDO + st * kAtom, &tm_do, &ld_full[st], it.h * kHD, qrow);
-          bulk_load(sVec + st * 2 * kT, lse + (long long)it.bh * S + qi * kT, kT * 4, &ld_full[st]);
-          bulk_load(sVec + st * 2 * kT + kT, dvec + (long long)it.bh * S + qi * kT, kT * 4, &ld_full[st]);
         }
       }
       AST_FLUSH(11, a_pw);
@@ -273,9 +270,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint64_t ak = make_smem_desc(k_addr, 16, 1024, 2), av = make_smem_desc(v_addr, 16, 1024, 2);
         int prev_st = 0;
         for (int qi = it.kb; qi < T && ok; ++qi, ++lc, ++tcount) {
-          const int st = lc & 1;
+          const int st = lc % kQStages;
           AST_T0(a_t3);
-          if (!(ok = mbar_wait(&ld_full[st], (lc >> 1) & 1, err, kErrTimeoutFull, abort_flag))) break;
+          if (!(ok = mbar_wait(&ld_full[st], (lc / kQStages) & 1, err, kErrTimeoutFull, abort_flag))) break;
           AST_ADD(a_ld, a_t3);
           AST_T0(a_t4);
           // S/dP may be overwritten once the gradient warpgroup has read the previous tile's
@@ -323,21 +320,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++ic) {
       const Item it = item_of(i, BH, H);
       for (int qi = it.kb; qi < T; ++qi, ++lc, ++tcount) {
-        const int st = lc & 1;
+        const int st = lc % kQStages;
         AST_T0(g_t1);
-        ok = mbar_wait(&ld_full[st], (lc >> 1) & 1, err, kErrTimeoutFull, abort_flag) &&
+        ok = mbar_wait(&ld_full[st], (lc / kQStages) & 1, err, kErrTimeoutFull, abort_flag) &&
              mbar_wait(s_full, tcount & 1, err, kErrTimeoutTmemFull, abort_flag);
         AST_ADD(g_w1, g_t1);
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
         tc_fence_after();
-        const float* sl = sVec + st * 2 * kT;
-        const float* sd = sl + kT;
+        const float* sl = lse + (long long)it.bh * S + qi * kT;   // read through L1 / L2
+        const float* sd = dvec + (long long)it.bh * S + qi * kT;
         const bool diag = qi == it.kb;
         uint8_t* ds_buf = sDS + (tcount & 1) * 2 * kAtom;
 #pragma unroll 1
         for (int qt = 2 * gw; qt < 2 * gw + 2; ++qt) {  // 32 query columns at a time
-          // this quarter's lse / delta first: once the next tile's MMAs stream operands out of shared
-          // memory, loads issued in the arithmetic below would queue behind them
+          // this quarter's lse / delta first (32 values each, the same for every thread of the warpgroup,
+          // so the loads hit L1 after the first warp), ahead of the TMEM loads they overlap
           float lv[32], dv[32];
 #pragma unroll
           for (int e = 0; e < 32; e += 4) {
