@@ -203,6 +203,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated in both
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Programmatic dependent launch: everything above (barriers, tensor-map prefetch, TMEM) may overlap
+  // the tail of the previous kernel in the stream; no global memory is touched before the previous
+  // grid has completed and its writes are visible. The next kernel may be scheduled from here on (it
+  // waits the same way before touching memory). Both are no-ops when the launch is not programmatic.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == 0) {
     if (lane == 0) {
@@ -755,6 +761,15 @@ static bool make_map2(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t 
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Programmatic dependent launch of the pair kernel (PCB_PDL=0 turns it off).
+static bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("PCB_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 template <int BN, int EPI>
 static int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const CUtensorMap& td,
                        const GemmArgs& a, int grid, cudaStream_t s) {
@@ -774,13 +789,19 @@ static int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  // with a fused gather, CTAs wait on each other's copies: all of them must be resident at once
-  attr[1].id = cudaLaunchAttributeCooperative;
-  attr[1].val.cooperative = 1;
+  if (a.ag_world > 1) {
+    // with a fused gather, CTAs wait on each other's copies: all of them must be resident at once
+    attr[1].id = cudaLaunchAttributeCooperative;
+    attr[1].val.cooperative = 1;
+  } else {
+    // the prologue may overlap the previous kernel's tail (the kernel waits before touching memory)
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = a.ag_world > 1 ? 2 : 1;
+  cfg.numAttrs = 2;
   cudaError_t e = cudaLaunchKernelEx(&cfg, pair::gemm_pair_kernel<BN, EPI>, ta, tb, tc, td, a);
-  if (e != cudaSuccess && cfg.numAttrs == 2) {
+  if (e != cudaSuccess && a.ag_world > 1) {
     // cooperative + cluster refused: one CTA per SM with grid <= SM count is resident anyway on a
     // stream of its own; the chunk waits stay bounded either way
     cudaGetLastError();
