@@ -89,13 +89,6 @@ PCB_DEVICE Item item_of(int i, int BH, int H) {
   return it;
 }
 
-PCB_DEVICE void bulk_load(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   smem_u32(smem_dst)),
-               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
-               : "memory");
-}
-
 // TMA reduce-add of a shared-memory box into global fp32 (x, y non-negative, x * 4 bytes 16-aligned)
 PCB_DEVICE void tma_reduce_add_2d(const CUtensorMap* map, const void* smem_src, int x, int y) {
   asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
@@ -402,7 +395,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(ds_full);
-          mbar_arrive(&ld_empty[st]);  // lse / delta of this stage are no longer read
+          mbar_arrive(&ld_empty[st]);  // the gradient warps are done with this stage's tile
         }
       }
       if (!ok) break;
