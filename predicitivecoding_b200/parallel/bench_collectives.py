@@ -34,6 +34,22 @@ import torch.distributed as dist
 LINK_GBS = 770.0   # measured peer copy per direction per GPU on this pool
 
 
+def nvlink_bytes_per_direction(case: str, n: int, world: int) -> float:
+    """Bytes that must cross each rank's links in one direction for one call.
+
+    ``n`` is the parameter count for ``rs_adamw_ag`` (fp32 gradients pulled, bf16 weights pushed) and
+    ``pc_allreduce_update`` (fp32 deltas pulled, fp32 + bf16 weights pushed), and the message size in
+    bytes for ``all_reduce``. What a rank pulls and what the others push to it share its inbound link.
+    """
+    if world <= 1:
+        return 0.0
+    f = (world - 1) / world
+    per_elem = {"rs_adamw_ag": 4 + 2, "pc_allreduce_update": 4 + 6, "all_reduce": 2}
+    if case not in per_elem:
+        raise ValueError(f"unknown case {case!r}")
+    return f * n * per_elem[case]
+
+
 def _time(fn, iters: int, dev) -> float:
     for _ in range(3):
         fn()
@@ -82,7 +98,7 @@ def main() -> None:
         peer.barrier()
 
     ms = _time(dp_step, 10, dev)
-    per_dir = (T - 1) / T * N * (4 + 2)
+    per_dir = nvlink_bytes_per_direction("rs_adamw_ag", N, T)
     roof = per_dir / (LINK_GBS * 1e9) * 1e3
     out.append({"case": "rs_adamw_ag (124M params, fp32 grads in, bf16 weights out)", "world": T,
                 "ms": round(ms, 3), "nvlink_gb_per_direction": round(per_dir / 1e9, 3),
@@ -105,7 +121,7 @@ def main() -> None:
         peer.barrier()
 
     ms = _time(pc_step, 10, dev)
-    per_dir = (T - 1) / T * N2 * (4 + 6)
+    per_dir = nvlink_bytes_per_direction("pc_allreduce_update", N2, T)
     roof = per_dir / (LINK_GBS * 1e9) * 1e3
     out.append({"case": "pc_allreduce_update (64 Mi fp32 weights)", "world": T, "ms": round(ms, 3),
                 "nvlink_gb_per_direction": round(per_dir / 1e9, 3),
@@ -117,8 +133,7 @@ def main() -> None:
     for nbytes in (256 << 10, 32 << 20, 256 << 20):
         x = torch.randn(nbytes // 4, device=dev)
         ms = _time(lambda: comm.all_reduce(x), 10, dev)
-        # ring-equivalent bytes per direction: 2 (T-1)/T * size
-        roof = 2 * (T - 1) / T * nbytes / (LINK_GBS * 1e9) * 1e3
+        roof = nvlink_bytes_per_direction("all_reduce", nbytes, T) / (LINK_GBS * 1e9) * 1e3
         out.append({"case": f"all_reduce fp32 {nbytes >> 10} KiB", "world": T, "ms": round(ms, 4),
                     "bus_gbs": round(2 * (T - 1) / T * nbytes / (ms * 1e-3) / 1e9, 1),
                     "roofline_ms": round(roof, 4), "of_roofline": round(roof / ms, 3) if T > 1 else None})

@@ -119,3 +119,16 @@ def test_communicator_gloo_matches_host_semantics():
         assert torch.equal(got[r]["bcast"], torch.ones(3))
         assert torch.equal(got[r]["ag"], torch.tensor([0.0, 10.0, 1.0, 11.0]))
     assert torch.equal(got[0]["rs"], torch.tensor([0.0, 3.0])) and torch.equal(got[1]["rs"], torch.tensor([6.0, 9.0]))
+
+
+def test_collective_roofline_counts_both_directions():
+    from predicitivecoding_b200.parallel.bench_collectives import nvlink_bytes_per_direction as vol
+    n = 134_105_856
+    # 2 ranks: half of the gradients pulled in (4 B) and half of the weights pushed in (2 B) per parameter
+    assert vol("rs_adamw_ag", n, 2) == 0.5 * n * 6
+    assert abs(vol("rs_adamw_ag", n, 8) - 7 / 8 * n * 6) < 1
+    assert vol("pc_allreduce_update", 64 << 20, 8) == 7 / 8 * (64 << 20) * 10
+    assert vol("all_reduce", 1 << 28, 4) == 2 * 3 / 4 * (1 << 28)
+    assert vol("rs_adamw_ag", n, 1) == 0.0
+    with pytest.raises(ValueError):
+        vol("broadcast", 1, 2)
