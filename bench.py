@@ -57,7 +57,7 @@ def main():
     if args.impl == "reference":
         emit({"impl": "reference",
               "unavailable": "the reference is C#/.NET 10 with no Python package or NCCL build; no dotnet SDK "
-                             "on this image, so `pip install /root/reference` cannot build it"})
+                             "on this image, so a pip install of the reference source tree cannot build it"})
         return 0
 
     import torch
@@ -239,7 +239,7 @@ def run_decoder_bench(args, dev, rank, world, pg):
         "scaling": "strong" if (tp_mode and dp == 1) else "weak",
         "vs_baseline": round(tok_s / REF_DECODER_TOKS, 2),
         "vs_baseline_basis": "closest published reference figure: Base preset (135M, ctx 1024) bf16 mixed, "
-                             "2680 tok/s on one RTX 4070 SUPER (ROADMAP-Scale.md:69); BASELINE.md lists no "
+                             "2680 tok/s on one RTX 4070 SUPER (ROADMAP-Scale.md:69); the reference publishes no "
                              "number for this exact config",
         "dtype": "bf16",
         "data": "synthetic (seeded Zipf(1.1) token ids, random-init weights)",
