@@ -19,7 +19,7 @@ Three implementations with one contract:
 from __future__ import annotations
 
 import enum
-from typing import List, Optional, Sequence
+from typing import Tuple, List, Optional, Sequence
 
 import torch
 import torch.distributed as dist
@@ -154,6 +154,18 @@ class MultiDeviceCollectives(HostCollectives):
 
 
 # ------------------------------------------------------------------------------------ one process per GPU
+def two_shot_shard(n: int, world: int, rank: int) -> Tuple[int, int]:
+    """[a, b) of an n-element message that `rank` reduces in the two-shot all-reduce.
+
+    Shards are ceil(n / world) rounded up to a multiple of 8 elements, so every shard starts on a
+    16-byte boundary for both fp32 and bf16 (the kernel's vector path); the last shards may be short or
+    empty. Together the shards of ranks 0..world-1 cover [0, n) exactly once.
+    """
+    per = -(-n // world)
+    per += (-per) % 8
+    return min(n, rank * per), min(n, (rank + 1) * per)
+
+
 class Communicator:
     """Collectives among the ranks of a process group (one rank per GPU, or gloo ranks on CPU)."""
 
@@ -222,9 +234,7 @@ class Communicator:
                 # two-shot in one pass: rank r reduces shard r over every rank's buffer and stores the
                 # result into shard r of every rank's buffer (peer stores); after a barrier each rank's
                 # buffer holds the whole reduced vector
-                per = -(-n // self.world)
-                per += (-per) % 8
-                a, b = min(n, self.rank * per), min(n, (self.rank + 1) * per)
+                a, b = two_shot_shard(n, self.world, self.rank)
                 if b > a:
                     ops.ext().coll_reduce_push(buf.ptrs, buf.ptrs, buf.local, a, b, self.world, int(op), 1.0)
                 P.barrier()

@@ -132,3 +132,19 @@ def test_collective_roofline_counts_both_directions():
     assert vol("rs_adamw_ag", n, 1) == 0.0
     with pytest.raises(ValueError):
         vol("broadcast", 1, 2)
+
+
+def test_two_shot_shards_cover_message_once_and_align():
+    from predicitivecoding_b200.parallel.collectives import two_shot_shard
+    for world in (1, 2, 3, 4, 8):
+        for n in (1, 7, 8, 9, 63, 64, 1000, 4097, 1 << 20, (1 << 20) + 5):
+            shards = [two_shot_shard(n, world, r) for r in range(world)]
+            covered = []
+            for a, b in shards:
+                assert 0 <= a <= b <= n
+                if b > a:
+                    assert a % 8 == 0          # 16-byte aligned start for fp32 and bf16
+                covered.extend(range(a, b)) if n < 5000 else None
+            if n < 5000:
+                assert covered == list(range(n))
+            assert sum(b - a for a, b in shards) == n
