@@ -327,6 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     PAIR_STAT_DECL(st_body);
     uint8_t* aux_stage = smem + C::EPI_OFF + (warp - 2) * C::EPI_WARP_BYTES;
     uint32_t aux_ph = 0u;   // bit b: parity of buffer b's next completion
+    int store_box = 0;      // bf16 TMA-store path: the staging box used next (alternates across tiles too)
     bool aux_ok = true;
     for (int tile = pair_id; tile < tiles && aux_ok; tile += num_pairs) {
       int split_unused, mb, nb;
@@ -524,12 +525,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else if (EPI == EPI_BF16 && args.c_tma) {
         // 64-column blocks: two accumulator chunks -> alpha, bias, RoPE -> bf16 row of 128 bytes per
         // lane, staged in the 128-byte-swizzled layout of a [32 x 64] box and written by one TMA store.
-        // The two boxes of a warp alternate; a box is rewritten only after its previous store has
-        // finished reading it.
+        // The two boxes of a warp alternate over all of its blocks, across tiles too (with BN = 128 a
+        // tile has one block per warp); before a box is rewritten every store but the latest, which
+        // read the other box, has finished reading.
         uint8_t* stg = smem + C::EPI_OFF + (warp - 2) * C::EPI_WARP_BYTES;
         const int row0 = mb * 2 * kBM + rank * kBM + q * 32;
 #pragma unroll 1
-        for (int c2 = half, bx = 0; c2 < BN / 64; c2 += 2, bx ^= 1) {
+        for (int c2 = half; c2 < BN / 64; c2 += 2) {
+          const int bx = store_box;
+          store_box ^= 1;
           float v[64];
           {
             uint32_t r0[32], r1[32];
