@@ -606,13 +606,17 @@ int pcb_attn_bwd(const void* qkv, long long ld, const void* out, const void* dou
 
 // ------------------------------------------------------------------------------------------
 // Allocation-free variant (see attention_noalloc.h for who needs it and the contract).
-// Same kernels as pcb_attn_bwd; the two fp32 scratch buffers come from a file-scope device
-// array instead of the caller.
+// Same kernels as the regular backward (tcgen05 for head dim 64, the mma.sync kernels for 128);
+// the two fp32 scratch buffers come from a file-scope device array instead of the caller.
 // ------------------------------------------------------------------------------------------
 #include <cstdio>
 #include <mutex>
 
 #include "attention_noalloc.h"
+
+int pcb_attn_bwd_tc(const void* qkv, long long ld, const void* out, const void* dout, long long ld_o,
+                    const float* lse, float* dvec, float* dq_acc, void* dqkv, long long ld_d, int B, int S, int H,
+                    int HD, float scale, const float* rope_cs, int* err, cudaStream_t s);
 
 namespace {
 
@@ -643,6 +647,21 @@ int noalloc_scratch(float** base) {
   return 0;
 }
 
+// Scratch floats the problem needs: the dQ accumulator (rounded up to 64 floats, so the row
+// dot-products that follow it start on a 256-byte boundary) plus B*H*S row dot-products.
+// Returns false when a product overflows 64 bits; the caller treats that as "too large".
+bool noalloc_need(int B, int S, int H, int HD, size_t* dq_floats, size_t* need) {
+  size_t bs, bsh, bshd, bhs;
+  if (__builtin_mul_overflow((size_t)B, (size_t)S, &bs) || __builtin_mul_overflow(bs, (size_t)H, &bsh) ||
+      __builtin_mul_overflow(bsh, (size_t)HD, &bshd) || bshd > SIZE_MAX - 63)
+    return false;
+  bhs = bsh;  // B*H*S
+  *dq_floats = (bshd + 63) / 64 * 64;
+  if (*dq_floats > SIZE_MAX - bhs) return false;
+  *need = *dq_floats + bhs;
+  return true;
+}
+
 }  // namespace
 
 extern "C" int pcb_attn_bwd_noalloc(const void* qkv, long long ld, const void* out, const void* dout, long long ld_o,
@@ -650,20 +669,28 @@ extern "C" int pcb_attn_bwd_noalloc(const void* qkv, long long ld, const void* o
                                     float scale, cudaStream_t s) {
   if (B <= 0 || H <= 0 || S <= 0 || S % 128 != 0 || ld % 8 || ld_o % 8 || ld_d % 8) return -1;
   if (HD != 64 && HD != 128) return -1;
-  const size_t dq_floats = ((size_t)B * S * H * HD + 63) / 64 * 64;
-  const size_t need = dq_floats + (size_t)B * H * S;
-  if (need > kNoAllocFloats) {
+  size_t dq_floats = 0, need = 0;
+  if (!noalloc_need(B, S, H, HD, &dq_floats, &need) || need > kNoAllocFloats) {
     fprintf(stderr,
-            "pcb_attn_bwd_noalloc: problem needs %zu scratch floats (B=%d S=%d H=%d HD=%d) but the built-in "
-            "scratch holds %zu (%u bytes); use pcb_attn_bwd with caller-provided buffers\n",
-            need, B, S, H, HD, kNoAllocFloats, (unsigned)PCB_ATTN_NOALLOC_SCRATCH_BYTES);
+            "pcb_attn_bwd_noalloc: problem B=%d S=%d H=%d HD=%d needs more than the built-in scratch of %zu "
+            "floats (%u bytes); use pcb_attn_bwd with caller-provided buffers\n",
+            B, S, H, HD, kNoAllocFloats, (unsigned)PCB_ATTN_NOALLOC_SCRATCH_BYTES);
     return PCB_ATTN_NOALLOC_E_TOO_LARGE;
   }
+  // tensor-core loads and 16-byte vector stores need every operand on a 16-byte boundary
+  if ((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(dout) |
+       reinterpret_cast<uintptr_t>(lse) | reinterpret_cast<uintptr_t>(dqkv)) & 15)
+    return PCB_ATTN_NOALLOC_E_ALIGN;
   float* base = nullptr;
   const int rc = noalloc_scratch(&base);
   if (rc != 0) return rc;
   float* dq_acc = base;
   float* dvec = base + dq_floats;
-  // the preprocess kernel zeroes dq_acc, so stale contents of an earlier call never leak in
+  // both paths clear dq_acc before accumulating, so an earlier call's partial sums never leak in
+  if (HD == 64) {
+    const int r = pcb_attn_bwd_tc(qkv, ld, out, dout, ld_o, lse, dvec, dq_acc, dqkv, ld_d, B, S, H, HD, scale,
+                                  nullptr, nullptr, s);
+    return r <= -1000 ? -3 : r;
+  }
   return pcb_attn_bwd(qkv, ld, out, dout, ld_o, lse, dvec, dq_acc, dqkv, ld_d, B, S, H, HD, scale, s);
 }

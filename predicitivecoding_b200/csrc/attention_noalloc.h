@@ -25,6 +25,9 @@
 //   * Set-up: the first call on each device, with that device current, looks up
 //     the array's device address (cudaGetSymbolAddress) and caches it for that
 //     device.  Make that first call on a device before any stream capture on it.
+//     The cached address belongs to the device's primary context: after
+//     cudaDeviceReset (or any teardown of that context) it is stale and the
+//     process must not call this entry point on that device again.
 //   * No allocation: the call performs no cudaMalloc, cudaFree or allocating
 //     library call.
 //   * Shared state: every call uses the same array, which keeps the previous
@@ -35,17 +38,24 @@
 //   * Inputs/outputs are exactly those of pcb_attn_bwd: qkv [B*S, ld] bf16
 //     (q | k | v at column offsets 0, H*HD, 2*H*HD), out and dout [B*S, ld_o]
 //     bf16, lse [B*H, S] fp32 from the forward; dqkv [B*S, ld_d] bf16 receives
-//     dq | dk | dv.  S must be a multiple of 128 and HD 64 or 128.
+//     dq | dk | dv.  S must be a multiple of 128 and HD 64 or 128; qkv, out,
+//     dout, lse and dqkv must start on 16-byte boundaries and every row stride
+//     must be a multiple of 8 elements.  Head dim 64 runs the tcgen05 backward,
+//     head dim 128 the mma.sync backward, exactly as the regular entry point.
+//   * Size arithmetic is overflow-checked: shapes whose element counts do not
+//     fit in 64 bits are rejected like any other oversized problem.
 //
 // Return codes: 0 success; -1 unsupported shape/stride; -3 launch failure;
-// PCB_ATTN_NOALLOC_E_TOO_LARGE (-7) scratch too small; -8 no current device;
-// -9 the scratch address lookup failed.
+// -5 tensor-map encoding failed; PCB_ATTN_NOALLOC_E_TOO_LARGE (-7) scratch too
+// small; -8 no current device; -9 the scratch address lookup failed;
+// PCB_ATTN_NOALLOC_E_ALIGN (-10) an operand is not 16-byte aligned.
 #pragma once
 
 #include <cuda_runtime.h>
 
 #define PCB_ATTN_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
 #define PCB_ATTN_NOALLOC_E_TOO_LARGE (-7)
+#define PCB_ATTN_NOALLOC_E_ALIGN (-10)
 
 #ifdef __cplusplus
 extern "C" {

@@ -20,7 +20,8 @@ from predicitivecoding_b200.models.config import DecoderLmConfig
 from predicitivecoding_b200.models.decoder_lm import DecoderLM
 from predicitivecoding_b200.optim.adam import LrSchedule
 
-REF = "/root/reference/PredictiveCoding.Translate.Cli"
+# directory of the reference project's Translate.Cli (its out-sample fixture); the test skips when unset
+REF = os.environ.get("PCB_REFERENCE_TRANSLATE_CLI", "")
 TEXT = ("the cat sat on the mat.\nthe dog sat on the log.\na bird sang in the tree.\n" * 6).strip()
 
 
@@ -183,7 +184,8 @@ def test_opt1_and_dam1_roundtrip():
         assert t2 == 3 and b2[0][0].sum() == 4
 
 
-@pytest.mark.skipif(not os.path.exists(REF + "/out-sample/model.ckpt"), reason="reference fixture not mounted")
+@pytest.mark.skipif(not REF or not os.path.exists(REF + "/out-sample/model.ckpt"),
+                    reason="PCB_REFERENCE_TRANSLATE_CLI does not point at the reference fixture")
 def test_golden_reference_translation_model():
     """The reference's own trained LLM1 model + BPE1 tokenizer, run through our DecoderLM,
     reproduces every translation pair it was trained on (LayerNorm, sinusoidal positions, GELU)."""
