@@ -94,6 +94,13 @@ int pcb_ipc_handle(void* ptr, void* out64);
 int pcb_ipc_open(const void* in64, void** ptr);
 int pcb_ipc_close(void* ptr);
 int pcb_peer_barrier(void* const* peer_flags_dev, unsigned int* ctr, int rank, int world, int* err, cudaStream_t s);
+int pcb_dp_reduce_sumsq(const float* grad, const float* staging, long long shard, const long long* tab, int nb,
+                        int rank, int world, float* gshard, double* sumsq, int num_sms, cudaStream_t s);
+int pcb_dp_norm_push(const double* sumsq, void* const* slot_peers, int rank, int world, cudaStream_t s);
+int pcb_dp_adamw_ag(const float* gshard, float* w32, float* m, float* v, void* const* w16_peers, long long shard,
+                    const long long* tab, int nb, const float* hyper, float b1, float b2, float eps,
+                    const double* norm_slots, float max_norm, int world, int num_sms, cudaStream_t s);
+int pcb_memcpy_d2d(void* dst, const void* src, size_t bytes, cudaStream_t s);
 int pcb_rs_adamw_ag(void* const* grad_peers, void* const* w16_peers, float* w32, float* m, float* v, long long lo,
                     long long hi, long long n_decay, const float* hyper, float b1, float b2, float eps, int world,
                     int num_sms, cudaStream_t s);
@@ -419,6 +426,50 @@ void rs_adamw_ag(const at::Tensor& grad_ptrs, const at::Tensor& w16_ptrs, at::Te
                         hyper.data_ptr<float>(), (float)b1, (float)b2, (float)eps, (int)world, num_sms(), cur_stream()),
         "rs_adamw_ag");
 }
+void dp_reduce_sumsq(const at::Tensor& grad, const at::Tensor& staging, int64_t shard, const at::Tensor& tab,
+                     int64_t rank, int64_t world, at::Tensor& gshard, at::Tensor& sumsq) {
+  req(grad, at::kFloat, "grad");
+  req(staging, at::kFloat, "staging");
+  req(gshard, at::kFloat, "gshard");
+  PCB_CHECK(sumsq.is_cuda() && sumsq.scalar_type() == at::kDouble, "dp_reduce_sumsq: sumsq must be a CUDA float64");
+  PCB_CHECK(tab.is_cuda() && tab.scalar_type() == at::kLong && tab.dim() == 2 && tab.size(1) == 4,
+            "dp_reduce_sumsq: tab must be a CUDA int64 [buckets, 4] table");
+  PCB_CHECK(staging.numel() >= world * shard && gshard.numel() >= shard, "dp_reduce_sumsq: buffers too small");
+  check(pcb_dp_reduce_sumsq(grad.data_ptr<float>(), staging.data_ptr<float>(), shard, reinterpret_cast<const long long*>(tab.data_ptr<int64_t>()),
+                            (int)tab.size(0), (int)rank, (int)world, gshard.data_ptr<float>(),
+                            sumsq.data_ptr<double>(), num_sms(), cur_stream()),
+        "dp_reduce_sumsq");
+}
+void dp_norm_push(const at::Tensor& sumsq, const at::Tensor& slot_ptrs, int64_t rank, int64_t world) {
+  PCB_CHECK(sumsq.is_cuda() && sumsq.scalar_type() == at::kDouble, "dp_norm_push: sumsq must be a CUDA float64");
+  check(pcb_dp_norm_push(sumsq.data_ptr<double>(), ptr_table(slot_ptrs, world, "slot_ptrs"), (int)rank, (int)world,
+                         cur_stream()),
+        "dp_norm_push");
+}
+void dp_adamw_ag(const at::Tensor& gshard, at::Tensor& w32, at::Tensor& m, at::Tensor& v, const at::Tensor& w16_ptrs,
+                 int64_t shard, const at::Tensor& tab, const at::Tensor& hyper, double b1, double b2, double eps,
+                 const c10::optional<at::Tensor>& norm_slots, double max_norm, int64_t world) {
+  req(gshard, at::kFloat, "gshard");
+  req(w32, at::kFloat, "w32");
+  PCB_CHECK(gshard.numel() >= shard && w32.numel() >= shard && m.numel() >= shard && v.numel() >= shard,
+            "dp_adamw_ag: state too small");
+  PCB_CHECK(tab.is_cuda() && tab.scalar_type() == at::kLong && tab.dim() == 2 && tab.size(1) == 4,
+            "dp_adamw_ag: tab must be a CUDA int64 [buckets, 4] table");
+  if (norm_slots) PCB_CHECK(norm_slots->is_cuda() && norm_slots->scalar_type() == at::kDouble &&
+                                norm_slots->numel() >= world, "dp_adamw_ag: norm_slots must be CUDA float64 [world]");
+  check(pcb_dp_adamw_ag(gshard.data_ptr<float>(), w32.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
+                        ptr_table(w16_ptrs, world, "w16_ptrs"), shard, reinterpret_cast<const long long*>(tab.data_ptr<int64_t>()), (int)tab.size(0),
+                        hyper.data_ptr<float>(), (float)b1, (float)b2, (float)eps,
+                        norm_slots ? norm_slots->data_ptr<double>() : nullptr, (float)max_norm, (int)world, num_sms(),
+                        cur_stream()),
+        "dp_adamw_ag");
+}
+void memcpy_d2d(int64_t dst, int64_t src, int64_t bytes) {
+  PCB_CHECK(bytes >= 0, "memcpy_d2d: negative size");
+  if (bytes == 0) return;
+  check(pcb_memcpy_d2d(reinterpret_cast<void*>(dst), reinterpret_cast<const void*>(src), (size_t)bytes, cur_stream()),
+        "memcpy_d2d", 0);   // a copy-engine transfer, not a kernel
+}
 void pc_allreduce_update(const at::Tensor& delta_ptrs, const at::Tensor& w_ptrs, const c10::optional<at::Tensor>& w16_ptrs,
                          int64_t lo, int64_t hi, double alpha, double decay, int64_t world, int64_t rank) {
   check(pcb_pc_allreduce_update(ptr_table(delta_ptrs, world, "delta_ptrs"), ptr_table(w_ptrs, world, "w_ptrs"),
@@ -735,5 +786,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_barrier", &peer_barrier);
   m.def("rs_adamw_ag", &rs_adamw_ag);
   m.def("pc_allreduce_update", &pc_allreduce_update);
+  m.def("dp_reduce_sumsq", &dp_reduce_sumsq);
+  m.def("dp_norm_push", &dp_norm_push);
+  m.def("dp_adamw_ag", &dp_adamw_ag);
+  m.def("memcpy_d2d", &memcpy_d2d);
   m.def("peer_reduce", &peer_reduce);
 }

@@ -151,6 +151,131 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// ---------------------------------------------------------------------------------------------
+// Bucketed data-parallel optimizer step (gradient reduce-scatter overlapped with the backward).
+//
+// Every rank owns piece `rank` of every gradient bucket.  During the backward each rank's copy
+// engines push its gradient pieces into the owners' staging buffers (slot = source rank, in the
+// owner's local order), so the transfer costs no SM time and overlaps the remaining backward.
+// After one barrier the owner runs
+//   dp_reduce_sumsq: g = own gradient + sum of the staged slots, non-finite -> 0, kept in gshard,
+//                    and the sum of squares accumulated in double (for global-norm clipping);
+//   dp_norm_push:    its partial sum of squares stored into every rank's slot table;
+//   dp_adamw_ag:     clip scale from the summed table, AdamW on the local master shard (decay only
+//                    below each bucket's decay end), bf16 weights stored into every rank's copy.
+// The table `tab` holds one row per bucket: (local offset, flat start of my piece, length, flat
+// decay end); lengths and offsets are multiples of 64 elements.
+constexpr int kDpMaxBuckets = 128;
+
+PCB_DEVICE int dp_find(const long long* tab, int nb, long long j) {
+  int lo = 0, hi = nb - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (tab[4 * mid] <= j) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
+
+template <int WORLD>
+__global__ void __launch_bounds__(256)
+    dp_reduce_sumsq_kernel(const float* __restrict__ grad, const float* __restrict__ staging, long long shard,
+                           const long long* __restrict__ tab_g, int nb, int rank, int world_rt,
+                           float* __restrict__ gshard, double* __restrict__ sumsq) {
+  const int world = WORLD > 0 ? WORLD : world_rt;
+  __shared__ long long tab[4 * kDpMaxBuckets];
+  __shared__ float part[8];
+  for (int t = threadIdx.x; t < 4 * nb; t += blockDim.x) tab[t] = tab_g[t];
+  __syncthreads();
+  float acc = 0.f;
+  const long long n4 = shard / 4;
+  for (long long q = blockIdx.x * (long long)blockDim.x + threadIdx.x; q < n4; q += (long long)gridDim.x * blockDim.x) {
+    const long long j = 4 * q;
+    const int b = dp_find(tab, nb, j);
+    const long long i = tab[4 * b + 1] + (j - tab[4 * b]);
+    float4 g = __ldcs(reinterpret_cast<const float4*>(grad + i));
+#pragma unroll 8
+    for (int p = 0; p < world; ++p) {
+      if (p == rank) continue;
+      const float4 x = __ldcs(reinterpret_cast<const float4*>(staging + (long long)p * shard + j));
+      g.x += x.x; g.y += x.y; g.z += x.z; g.w += x.w;
+    }
+    g.x = isfinite(g.x) ? g.x : 0.f;
+    g.y = isfinite(g.y) ? g.y : 0.f;
+    g.z = isfinite(g.z) ? g.z : 0.f;
+    g.w = isfinite(g.w) ? g.w : 0.f;
+    *reinterpret_cast<float4*>(gshard + j) = g;
+    acc += g.x * g.x + g.y * g.y + g.z * g.z + g.w * g.w;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += part[w];
+    atomicAdd(sumsq, (double)t);
+  }
+}
+
+__global__ void dp_norm_push_kernel(const double* __restrict__ sumsq, double* const* __restrict__ slot_peers, int rank,
+                                    int world) {
+  const int p = threadIdx.x;
+  if (p < world) {
+    *reinterpret_cast<volatile double*>(slot_peers[p] + rank) = *sumsq;
+    __threadfence_system();
+  }
+}
+
+template <int WORLD>
+__global__ void __launch_bounds__(256)
+    dp_adamw_ag_kernel(const float* __restrict__ gshard, float* __restrict__ w32, float* __restrict__ m,
+                       float* __restrict__ v, __nv_bfloat16* const* __restrict__ w16_peers, long long shard,
+                       const long long* __restrict__ tab_g, int nb, const float* __restrict__ hyper, float b1,
+                       float b2, float eps, const double* __restrict__ norm_slots, float max_norm, int world_rt) {
+  const int world = WORLD > 0 ? WORLD : world_rt;
+  __shared__ long long tab[4 * kDpMaxBuckets];
+  for (int t = threadIdx.x; t < 4 * nb; t += blockDim.x) tab[t] = tab_g[t];
+  __syncthreads();
+  const float lr = hyper[0], wd = hyper[1], bc1 = hyper[2], bc2 = hyper[3];
+  float s = hyper[4];
+  if (norm_slots != nullptr && max_norm > 0.f) {   // global norm of the mean gradient, as the reference clips
+    double t = 0.0;
+    for (int p = 0; p < world; ++p) t += norm_slots[p];
+    const float norm = static_cast<float>(sqrt(t)) * s;
+    if (norm > max_norm) s *= max_norm / (norm + 1e-6f);
+  }
+  const long long n4 = shard / 4;
+  for (long long q = blockIdx.x * (long long)blockDim.x + threadIdx.x; q < n4; q += (long long)gridDim.x * blockDim.x) {
+    const long long j = 4 * q;
+    const int b = dp_find(tab, nb, j);
+    const long long i = tab[4 * b + 1] + (j - tab[4 * b]);
+    const long long dend = tab[4 * b + 3];
+    const float4 g = __ldcs(reinterpret_cast<const float4*>(gshard + j));
+    float4 w = *reinterpret_cast<float4*>(w32 + j);
+    float4 mm = *reinterpret_cast<float4*>(m + j);
+    float4 vv = *reinterpret_cast<float4*>(v + j);
+    float gg[4] = {g.x, g.y, g.z, g.w}, ww[4] = {w.x, w.y, w.z, w.w};
+    float m4[4] = {mm.x, mm.y, mm.z, mm.w}, v4[4] = {vv.x, vv.y, vv.z, vv.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float gi = gg[k] * s;
+      m4[k] = b1 * m4[k] + (1.f - b1) * gi;
+      v4[k] = b2 * v4[k] + (1.f - b2) * gi * gi;
+      ww[k] -= lr * (m4[k] / bc1) / (sqrtf(v4[k] / bc2) + eps);
+      if (i + k < dend) ww[k] -= lr * wd * ww[k];
+    }
+    *reinterpret_cast<float4*>(w32 + j) = make_float4(ww[0], ww[1], ww[2], ww[3]);
+    *reinterpret_cast<float4*>(m + j) = make_float4(m4[0], m4[1], m4[2], m4[3]);
+    *reinterpret_cast<float4*>(v + j) = make_float4(v4[0], v4[1], v4[2], v4[3]);
+    uint2 packed;
+    packed.x = pack_bf16x2(ww[0], ww[1]);
+    packed.y = pack_bf16x2(ww[2], ww[3]);
+#pragma unroll 8
+    for (int p = 0; p < world; ++p) *reinterpret_cast<uint2*>(w16_peers[p] + i) = packed;
+  }
+}
+
 }  // namespace pcb
 
 using namespace pcb;
@@ -223,4 +348,45 @@ int pcb_peer_reduce(void* const* in_peers, void* const* out_peers, long long lo,
   peer_reduce_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const float* const*>(in_peers),
                                           reinterpret_cast<float* const*>(out_peers), lo, hi, scale, world);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+// ------------------------------------------------------------------ bucketed data-parallel step
+int pcb_dp_reduce_sumsq(const float* grad, const float* staging, long long shard, const long long* tab, int nb,
+                        int rank, int world, float* gshard, double* sumsq, int num_sms, cudaStream_t s) {
+  if (nb <= 0 || nb > kDpMaxBuckets || (shard % 4)) return -1;
+  const int grid = grid_for_n4(shard / 4, num_sms);
+  switch (world) {
+    case 2: dp_reduce_sumsq_kernel<2><<<grid, 256, 0, s>>>(grad, staging, shard, tab, nb, rank, world, gshard, sumsq); break;
+    case 4: dp_reduce_sumsq_kernel<4><<<grid, 256, 0, s>>>(grad, staging, shard, tab, nb, rank, world, gshard, sumsq); break;
+    case 8: dp_reduce_sumsq_kernel<8><<<grid, 256, 0, s>>>(grad, staging, shard, tab, nb, rank, world, gshard, sumsq); break;
+    default: dp_reduce_sumsq_kernel<0><<<grid, 256, 0, s>>>(grad, staging, shard, tab, nb, rank, world, gshard, sumsq);
+  }
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+int pcb_dp_norm_push(const double* sumsq, void* const* slot_peers, int rank, int world, cudaStream_t s) {
+  if (world > 1024) return -1;
+  dp_norm_push_kernel<<<1, 32 * ((world + 31) / 32), 0, s>>>(sumsq, reinterpret_cast<double* const*>(slot_peers),
+                                                             rank, world);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+int pcb_dp_adamw_ag(const float* gshard, float* w32, float* m, float* v, void* const* w16_peers, long long shard,
+                    const long long* tab, int nb, const float* hyper, float b1, float b2, float eps,
+                    const double* norm_slots, float max_norm, int world, int num_sms, cudaStream_t s) {
+  if (nb <= 0 || nb > kDpMaxBuckets || (shard % 4)) return -1;
+  const int grid = grid_for_n4(shard / 4, num_sms);
+  auto wp = reinterpret_cast<__nv_bfloat16* const*>(w16_peers);
+  switch (world) {
+    case 2: dp_adamw_ag_kernel<2><<<grid, 256, 0, s>>>(gshard, w32, m, v, wp, shard, tab, nb, hyper, b1, b2, eps, norm_slots, max_norm, world); break;
+    case 4: dp_adamw_ag_kernel<4><<<grid, 256, 0, s>>>(gshard, w32, m, v, wp, shard, tab, nb, hyper, b1, b2, eps, norm_slots, max_norm, world); break;
+    case 8: dp_adamw_ag_kernel<8><<<grid, 256, 0, s>>>(gshard, w32, m, v, wp, shard, tab, nb, hyper, b1, b2, eps, norm_slots, max_norm, world); break;
+    default: dp_adamw_ag_kernel<0><<<grid, 256, 0, s>>>(gshard, w32, m, v, wp, shard, tab, nb, hyper, b1, b2, eps, norm_slots, max_norm, world);
+  }
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+// Copy-engine copy between two device addresses (either may be a peer's IPC-mapped buffer) on `s`.
+int pcb_memcpy_d2d(void* dst, const void* src, size_t bytes, cudaStream_t s) {
+  return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, s) == cudaSuccess ? 0 : -3;
 }

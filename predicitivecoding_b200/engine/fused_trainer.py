@@ -117,18 +117,29 @@ class FusedDecoderTrainer:
                 specs.append(ParamSpec(f"b{l}.b1", (F_,), decay_all))
                 specs.append(ParamSpec(f"b{l}.b2", (D,), decay_all))
         specs.append(ParamSpec("lnf", (D,), decay_all))
-        self.arena = ParamArena(specs, self.world)
+        # fused data parallel: one bucket per group of tensors whose gradients become final together,
+        # in backward order; every rank owns an equal piece of every bucket
+        self.arena = ParamArena(specs, self.world, buckets=self._bucket_names() if grad_sync == "fused" else None)
         A = self.arena
         dev = self.device
         f32, bf16 = torch.float32, torch.bfloat16
         if grad_sync == "fused":
-            # gradients and bf16 weights live in IPC-shared buffers: the fused optimizer kernel
-            # reduce-scatters gradients and all-gathers weights by loading/storing peer memory
+            # bf16 weights, gradient staging and the clip-norm slots live in IPC-shared buffers: during the
+            # backward the copy engines push each finished bucket's pieces into their owners' staging slots;
+            # after it, each owner reduces its pieces, clips, runs AdamW and stores bf16 weights to every peer
             from ..parallel.peer import PeerGroup
             self.peer = PeerGroup(self.pg, dev)
             self._w16_sym = self.peer.symmetric(A.total, bf16)
-            self._grad_sym = self.peer.symmetric(A.total, f32)
-            self.w16, self.grad = self._w16_sym.local, self._grad_sym.local
+            self._stage_sym = self.peer.symmetric(self.world * A.shard, f32)
+            self._norm_sym = self.peer.symmetric(self.world, torch.float64)
+            self.w16 = self._w16_sym.local
+            self.grad = torch.zeros(A.total, device=dev, dtype=f32)      # this rank's full local gradient
+            self.gshard = torch.zeros(A.shard, device=dev, dtype=f32)    # reduced gradient of the owned pieces
+            self.sumsq = torch.zeros(1, device=dev, dtype=torch.float64)
+            self._tab = torch.tensor([list(p) for p in A.pieces(self.rank)], dtype=torch.int64, device=dev)
+            self._plans = [self.push_plan(A, self.rank, b) for b in range(len(A.buckets))]
+            self._push_stream = torch.cuda.Stream(dev, priority=-1)
+            self._bucket_events = [torch.cuda.Event() for _ in A.buckets]
         else:
             self.w16 = torch.zeros(A.total, device=dev, dtype=bf16)      # full bf16 working copy (replicated)
             self.grad = torch.zeros(A.total, device=dev, dtype=f32)      # full gradient (local, then reduced)
@@ -188,6 +199,48 @@ class FusedDecoderTrainer:
         self.attn_scale = 1.0 / math.sqrt(hd)
         self.launches_per_step = None
 
+    def _bucket_names(self) -> List[List[str]]:
+        """Tensor groups in the order the backward finishes their gradients: LM head + final norm,
+        then the blocks from last to first, then the embedding."""
+        cfg = self.cfg
+        out = [["wout", "lnf"]]
+        for l in reversed(range(cfg.num_blocks)):
+            names = [f"b{l}.wqkv", f"b{l}.wo", f"b{l}.w2", f"b{l}.ln1", f"b{l}.ln2"]
+            names += [f"b{l}.w13"] if cfg.ffn == "swiglu" else [f"b{l}.w1", f"b{l}.b1", f"b{l}.b2"]
+            out.append(names)
+        out.append(["wemb"])
+        return out
+
+    @staticmethod
+    def push_plan(arena: ParamArena, rank: int, b: int):
+        """Copies that send this rank's finished bucket ``b`` to the other ranks:
+        (owner rank q, element offset in q's staging buffer, element offset in the local gradient,
+        element count).  Owner q's staging buffer holds one slot of ``arena.shard`` elements per source
+        rank, in q's local (pieces) order."""
+        world = arena.world
+        start, end, _ = arena.buckets[b]
+        c = (end - start) // world
+        loff = arena.pieces(rank)[b][0]
+        plan = []
+        for k in range(1, world):          # start with the next rank, so the ranks spread their pushes
+            q = (rank + k) % world
+            plan.append((q, rank * arena.shard + loff, start + q * c, c))
+        return plan
+
+    def _bucket_done(self, b: int) -> None:
+        """Bucket ``b``'s gradient is final on this rank: push its pieces to their owners (copy engines,
+        on the push stream, ordered after the kernels that produced them)."""
+        if self.grad_sync != "fused":
+            return
+        ev = self._bucket_events[b]
+        ev.record(torch.cuda.current_stream(self.device))
+        s = self._push_stream
+        s.wait_event(ev)
+        base = self.grad.data_ptr()
+        with torch.cuda.stream(s):
+            for q, dst, src, n in self._plans[b]:
+                ops.ext().memcpy_d2d(self._stage_sym.host_ptrs[q] + 4 * dst, base + 4 * src, 4 * n)
+
     # ------------------------------------------------------------------ weights in/out
     def _model_to_flat(self, model: DecoderLM) -> torch.Tensor:
         """DecoderLM tensors (reference [in,out] layout) -> flat fp32 arena (cpu)."""
@@ -215,7 +268,7 @@ class FusedDecoderTrainer:
     def import_model(self, model: DecoderLM) -> None:
         """Copy a DecoderLM's weights (reference [in,out] layout) into the arena."""
         full_d = self._model_to_flat(model).to(self.device)
-        self.w32.copy_(full_d[self.shard_lo:self.shard_hi])
+        self.w32.copy_(self.arena.gather_local(full_d, self.rank))
         self.w16.copy_(full_d.to(torch.bfloat16))
         self.m.zero_()
         self.v.zero_()
@@ -224,12 +277,7 @@ class FusedDecoderTrainer:
     @torch.no_grad()
     def master_weights(self) -> torch.Tensor:
         """Full fp32 master buffer (all-gathered across ranks)."""
-        if self.world == 1:
-            return self.w32.clone()
-        import torch.distributed as dist
-        out = torch.empty(self.arena.total, device=self.device, dtype=torch.float32)
-        dist.all_gather_into_tensor(out, self.w32, group=self.pg)
-        return out
+        return self._gather_full(self.w32)
 
     @torch.no_grad()
     def _flat_to_model(self, flat: torch.Tensor, model: DecoderLM) -> DecoderLM:
@@ -264,12 +312,19 @@ class FusedDecoderTrainer:
         return self._flat_to_model(self.master_weights(), model if model is not None else DecoderLM(self.cfg))
 
     def _gather_full(self, shard: torch.Tensor) -> torch.Tensor:
+        """Full flat buffer from every rank's local shard (the ranks' pieces put back in place)."""
         if self.world == 1:
             return shard.clone()
         import torch.distributed as dist
-        out = torch.empty(self.arena.total, device=self.device, dtype=torch.float32)
-        dist.all_gather_into_tensor(out, shard, group=self.pg)
-        return out
+        A = self.arena
+        out = torch.empty(self.world * A.shard, device=self.device, dtype=torch.float32)
+        dist.all_gather_into_tensor(out, shard.contiguous(), group=self.pg)
+        if not A.buckets:
+            return out
+        full = torch.zeros(A.total, device=self.device, dtype=torch.float32)
+        for r in range(self.world):
+            A.scatter_local(out[r * A.shard:(r + 1) * A.shard], r, full)
+        return full
 
     @torch.no_grad()
     def save_state(self, path: str) -> None:
@@ -293,7 +348,7 @@ class FusedDecoderTrainer:
             tensors = [torch.from_numpy(mv[k].copy()).view_as(p) for mv, p in zip(moms, ref.reference_parameters())]
             ref.load_reference_parameters([x.numpy() for x in tensors])
             full = self._model_to_flat(ref).to(self.device)
-            buf.copy_(full[self.shard_lo:self.shard_hi])
+            buf.copy_(self.arena.gather_local(full, self.rank))
         self.t = int(t)
 
     # ------------------------------------------------------------------ the step
@@ -334,6 +389,7 @@ class FusedDecoderTrainer:
         ops.gemm(dl, self.nf, a_mn=True, b_mn=True, epi=RED, c=G["wout"])           # dWout = dL^T nf
         ops.gemm(dl, W["wout"], b_mn=True, epi=ops.EPI_F32, c=self.dn)              # dnf = dL Wout
         ops.rmsnorm_bwd(self.dn, self.x[L], W["lnf"], self.invf, self.dx, G["lnf"], False, self.dx16)
+        self._bucket_done(0)
         for l in reversed(range(L)):
             # ---- FFN: x_{l+1} = xmid + ffn(norm2(xmid))
             ops.gemm(self.dx16, self.act[l], a_mn=True, b_mn=True, epi=RED, c=G[f"b{l}.w2"])
@@ -358,19 +414,28 @@ class FusedDecoderTrainer:
             ops.gemm(self.dqkv, W[f"b{l}.wqkv"], b_mn=True, epi=ops.EPI_F32, c=self.dn)
             ops.rmsnorm_bwd(self.dn, self.x[l], W[f"b{l}.ln1"], self.inv1[l], self.dx, G[f"b{l}.ln1"], True,
                             self.dx16)
+            self._bucket_done(L - l)
         ops.embed_bwd(self.tok, self.dx, G["wemb"])
+        self._bucket_done(L + 1)
 
     def _optimizer(self) -> None:
         """Gradient sync (data parallel) + AdamW on this rank's shard + bf16 weight refresh."""
         self.hyper.copy_(self.hyper_host, non_blocking=True)
         if self.grad_sync == "fused":
+            A = self.arena
+            torch.cuda.current_stream(self.device).wait_stream(self._push_stream)
+            self.peer.barrier()   # every rank's pushes into every staging buffer are complete
+            self.sumsq.zero_()
+            ops.ext().dp_reduce_sumsq(self.grad, self._stage_sym.local, A.shard, self._tab, self.rank, self.world,
+                                      self.gshard, self.sumsq)
+            slots = None
             if self.clip_norm > 0:
-                raise NotImplementedError("global-norm clipping is not fused into the peer optimizer; "
-                                          "use grad_sync='zero' with clip_norm")
-            self.peer.barrier()   # every rank's gradients are complete
-            ops.ext().rs_adamw_ag(self._grad_sym.ptrs, self._w16_sym.ptrs, self.w32, self.m, self.v,
-                                  self.shard_lo, self.shard_hi, self.arena.n_decay, self.hyper,
-                                  self.betas[0], self.betas[1], self.eps, self.world)
+                ops.ext().dp_norm_push(self.sumsq, self._norm_sym.ptrs, self.rank, self.world)
+                self.peer.barrier()   # every rank's partial sum of squares has arrived
+                slots = self._norm_sym.local
+            ops.ext().dp_adamw_ag(self.gshard, self.w32, self.m, self.v, self._w16_sym.ptrs, A.shard, self._tab,
+                                  self.hyper, self.betas[0], self.betas[1], self.eps, slots, float(self.clip_norm),
+                                  self.world)
             self.peer.barrier()   # every rank's weights are written before anyone's next forward
             return
         if self.world > 1:

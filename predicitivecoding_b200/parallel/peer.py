@@ -21,13 +21,14 @@ import torch.distributed as dist
 
 from .. import ops
 
-_ELT = {torch.float32: 4, torch.bfloat16: 2, torch.int32: 4, torch.uint8: 1, torch.int64: 8}
+_ELT = {torch.float32: 4, torch.bfloat16: 2, torch.int32: 4, torch.uint8: 1, torch.int64: 8, torch.float64: 8}
 
 
 @dataclass
 class SymmetricBuffer:
     local: torch.Tensor        # this rank's buffer (typed view)
     ptrs: torch.Tensor         # device int64 [world]: every rank's buffer address, as seen from this rank
+    host_ptrs: List[int]       # the same addresses on the host (for copy-engine transfers)
 
 
 class PeerGroup:
@@ -64,7 +65,7 @@ class PeerGroup:
                 ptrs.append(p)
         table = torch.tensor(ptrs, dtype=torch.int64, device=self.device)
         local = raw.view(dtype)[:numel]
-        return SymmetricBuffer(local, table)
+        return SymmetricBuffer(local, table, ptrs)
 
     def barrier(self) -> None:
         """Device-side barrier over all ranks, ordered on the current stream (bounded wait)."""

@@ -1,8 +1,9 @@
 """Data-parallel fused trainer on 2 GPUs (skipped with fewer devices).
 
-Each rank trains on half of a global batch; the fused peer-memory path (gradient
-reduce-scatter + AdamW + bf16 all-gather in one kernel) and the NCCL ZeRO-1
-baseline must both track a single-GPU trainer that sees the whole batch.
+Each rank trains on half of a global batch; the fused peer-memory path (bucketed
+gradient pushes overlapped with the backward, then reduce + clip + AdamW + bf16
+all-gather) and the NCCL ZeRO-1 baseline must both track a single-GPU trainer
+that sees the whole batch, with global-norm clipping off and on.
 """
 import os
 import socket
@@ -34,7 +35,7 @@ def _data(step):
     return t[:, :-1].contiguous(), t[:, 1:].contiguous()
 
 
-def _worker(rank, world, port, mode, out_q):
+def _worker(rank, world, port, mode, clip, out_q):
     import torch.distributed as dist
     from datetime import timedelta
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -46,7 +47,7 @@ def _worker(rank, world, port, mode, out_q):
         from predicitivecoding_b200.engine.fused_trainer import FusedDecoderTrainer
         from predicitivecoding_b200.models.decoder_lm import DecoderLM
         cfg = _cfg()
-        tr = FusedDecoderTrainer(cfg, batch=2, model=DecoderLM(cfg, seed=7), device=dev, lr=1e-3,
+        tr = FusedDecoderTrainer(cfg, batch=2, model=DecoderLM(cfg, seed=7), device=dev, lr=1e-3, clip_norm=clip,
                                  process_group=dist.group.WORLD, grad_sync=mode, use_graph=(mode == "fused"))
         losses = []
         for s in range(4):
@@ -56,7 +57,7 @@ def _worker(rank, world, port, mode, out_q):
         # mean loss over ranks = loss of the whole batch
         t = torch.tensor(losses, device=dev)
         dist.all_reduce(t)
-        w = tr.master_weights()
+        w = torch.cat([p.detach().reshape(-1) for p in tr.export_model().reference_parameters()])
         if rank == 0:
             out_q.put(((t / world).tolist(), w.cpu()))
         if tr.peer is not None:
@@ -67,11 +68,11 @@ def _worker(rank, world, port, mode, out_q):
         dist.destroy_process_group()
 
 
-def _run(mode):
+def _run(mode, clip):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, mode, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, mode, clip, q)) for r in range(2)]
     for p in procs:
         p.start()
     res = q.get(timeout=300)
@@ -82,18 +83,19 @@ def _run(mode):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("clip", [0.0, 0.05])
 @pytest.mark.parametrize("mode", ["fused", "zero"])
-def test_dp_matches_single_gpu(mode):
+def test_dp_matches_single_gpu(mode, clip):
+    """clip 0.05 is far below this model's gradient norm, so the clip scale is active on every step."""
     from predicitivecoding_b200.engine.fused_trainer import FusedDecoderTrainer
     from predicitivecoding_b200.models.decoder_lm import DecoderLM
-    dp_losses, dp_w = _run(mode)
+    dp_losses, dp_w = _run(mode, clip)
     cfg = _cfg()
     single = FusedDecoderTrainer(cfg, batch=4, model=DecoderLM(cfg, seed=7), device="cuda:0", lr=1e-3,
-                                 use_graph=False)
+                                 clip_norm=clip, use_graph=False)
     ref = [single.step(*_data(s)) for s in range(4)]
     for a, b in zip(dp_losses, ref):
         assert abs(a - b) / b < 5e-3, (dp_losses, ref)
-    w = single.master_weights().cpu()
-    n = single.arena.used
-    rel = float((dp_w[:n] - w[:n]).norm() / w[:n].norm())
+    w = torch.cat([p.detach().reshape(-1) for p in single.export_model().reference_parameters()]).cpu()
+    rel = float((dp_w - w).norm() / w.norm())
     assert rel < 2e-3, rel
