@@ -110,11 +110,12 @@ def page_size_bits_for(max_payload_len: int) -> int:
 class CheckpointStore:
     """Keyed blob store over a directory (``weights.log`` + ``checkpoints/``)."""
 
-    def __init__(self, directory: str, page_size_bits: int = 22, recover: bool = True):
+    def __init__(self, directory: str, page_size_bits: int = 22, recover: bool = True, segment_bits: int = 0):
         os.makedirs(directory, exist_ok=True)
         self.dir = directory
         self.page_size_bits = page_size_bits
-        self.kv = FasterKV(os.path.join(directory, LOG_NAME), os.path.join(directory, "checkpoints"), recover=recover)
+        self.kv = FasterKV(os.path.join(directory, LOG_NAME), os.path.join(directory, "checkpoints"), recover=recover,
+                           page_bits=page_size_bits, segment_bits=segment_bits or max(30, page_size_bits))
 
     def put_blob(self, key: int, data: bytes) -> None:
         self.kv.upsert(key, bytes(data))

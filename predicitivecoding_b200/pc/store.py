@@ -18,8 +18,38 @@ from ..io import layer_serializer as ser
 from .layer import Layer
 
 
+def page_size_bits(layer_sizes) -> int:
+    """LayerStore.cs:354-369: the smallest page (>= 2^22 bytes) that holds the largest layer record
+    plus ~32 bytes of record header, for records without diagonal precision or prior."""
+    biggest = 0
+    for l, size in enumerate(layer_sizes):
+        lower = layer_sizes[l - 1] if l > 0 else 0
+        biggest = max(biggest, ser.byte_length(size, lower, False, False))
+    bits = 22
+    while (1 << bits) < biggest + 32:
+        bits += 1
+    return bits
+
+
+def _open_kv(path: str, sizes, page_bits: int = 0, segment_bits: int = 0) -> "object":
+    from ..io.faster import DEFAULT_SEGMENT_BITS, FasterKV
+    if page_bits:
+        return FasterKV(os.path.join(path, "layers.log"), os.path.join(path, "checkpoints"), page_bits=page_bits,
+                        segment_bits=segment_bits or max(DEFAULT_SEGMENT_BITS, page_bits))
+    # records with a diagonal precision or prior are larger than the reference's sizing assumes:
+    # grow the page until the largest possible record fits
+    bits = page_size_bits(sizes)
+    biggest = max(ser.byte_length(s, sizes[l - 1] if l else 0, True, True) for l, s in enumerate(sizes))
+    while (1 << bits) < biggest + 40:
+        bits += 1
+    return FasterKV(os.path.join(path, "layers.log"), os.path.join(path, "checkpoints"), page_bits=bits)
+
+
 class LayerStore:
-    def __init__(self, layers: List[Layer], path: Optional[str] = None, lazy: bool = False):
+    def __init__(self, layers: List[Layer], path: Optional[str] = None, lazy: bool = False, page_bits: int = 0,
+                 segment_bits: int = 0):
+        """``page_bits`` / ``segment_bits`` override the log geometry (0 = the reference's sizing:
+        pages just large enough for the largest layer, 1 GiB segments)."""
         self._layers = [L.clone() for L in layers]
         self._dirty = set()
         self._lock = threading.RLock()
@@ -28,9 +58,8 @@ class LayerStore:
         self._kv = None
         self._quantized = {}
         if path is not None:
-            from ..io.faster import FasterKV
             os.makedirs(path, exist_ok=True)
-            self._kv = FasterKV(os.path.join(path, "layers.log"), os.path.join(path, "checkpoints"))
+            self._kv = _open_kv(path, [L.size for L in self._layers], page_bits, segment_bits)
             if self._kv.count() > 0:
                 self._recover()
             else:
@@ -39,10 +68,13 @@ class LayerStore:
                 self._kv.checkpoint()
 
     @classmethod
-    def open(cls, path: str, activation: str, lazy: bool = False) -> "LayerStore":
-        """Recover a store written earlier at ``path``."""
-        from ..io.faster import FasterKV
-        kv = FasterKV(os.path.join(path, "layers.log"), os.path.join(path, "checkpoints"))
+    def open(cls, path: str, activation: str, lazy: bool = False, page_bits: int = 0,
+             segment_bits: int = 0) -> "LayerStore":
+        """Recover a store written earlier at ``path`` (``page_bits`` 0 = find the page size from the log)."""
+        from ..io.faster import DEFAULT_SEGMENT_BITS, FasterKV, probe_page_bits
+        bits = page_bits or probe_page_bits(os.path.join(path, "layers.log"))
+        kv = FasterKV(os.path.join(path, "layers.log"), os.path.join(path, "checkpoints"), page_bits=bits,
+                      segment_bits=segment_bits or max(DEFAULT_SEGMENT_BITS, bits))
         recs = kv.items()
         layers = [ser.deserialize(recs[k], k, activation) for k in sorted(recs)]
         st = cls.__new__(cls)
