@@ -4,23 +4,28 @@
 // block per (query, head), fp32 SIMT).  One CTA owns two consecutive 128-query tiles (A and B) of
 // one (batch, head) and streams the 128-key tiles they need once:
 //
-//   warp 8      TMA producer: Q_A and Q_B once, then K_j / V_j into a 3-stage ring
-//   warp 9      MMA issuer (one thread), per key tile j, in this order:
-//                 PV_A(j-1), S_A(j), PV_B(j-1), S_B(j)
-//               S_w = Q_w K_j^T lands in TMEM (128 columns per tile); O_w += P_w V_j accumulates
-//               in TMEM.  Because one commit covers every earlier MMA of the issuing thread, the
-//               commit that announces S_w(j) also proves PV_w(j-1) finished: softmax warpgroup w
-//               may then rewrite P_w and rescale O_w without another barrier.
+//   warp 8      TMA producer: Q_A and Q_B, then K_j / V_j into a ring
+//   warp 9      MMA issuer (one thread): S_w = Q_w K_j^T into TMEM (128 columns per tile) and
+//               O_w += P_w V_j accumulating in TMEM
 //   warps 0-3   softmax of tile A, warps 4-7 softmax of tile B (thread = query row = TMEM lane):
 //               the whole 128-key row is read from TMEM at once, p = 2^(s*c - m*c) with
 //               c = scale*log2(e) on the SFU, and bf16 P is written back to TMEM (two keys per
 //               column), where the PV MMA reads its A operand; P never touches shared memory.
 //               The running max is only moved (and O rescaled in TMEM) when a warp sees a row max
-//               grow by more than 2^8, so most tiles skip the O round trip.  The two warpgroups alternate: one computes exponentials while the
-//               tensor cores run the other's MMAs.
+//               grow by more than 2^8, so most tiles skip the O round trip.
 //   epilogue    O / l in bf16, lse = m*scale + ln(l) (the backward's convention)
 //
-// Heavy (late) tile pairs are scheduled first.  Every wait is bounded and unwinds on timeout.
+// Head dim 64 (TMEM: S 2x128 + O 2x64 + P 2x64 = 512 columns): S and P live in separate columns,
+// so a softmax warpgroup releases S (s_free) as soon as the row is in registers and the MMA issuer
+// starts S_w(j+1) while the exponentials of tile j run; P_w(j+1) is stored only after the MMA that
+// read P_w(j) has completed (pv_done).  Issue order per key tile: S_A(j+1), S_B(j+1), PV_A(j),
+// PV_B(j).
+// Head dim 128 (TMEM: S 2x128 + O 2x128): P is written over the first half of its own S columns,
+// so S_w(j+1) is issued after PV_w(j) (the tensor pipe runs one thread's MMAs in order, so it
+// reads P before the next S lands there).  Issue order: PV_A(j), S_A(j+1), PV_B(j), S_B(j+1).
+// Either way the two warpgroups alternate: one computes exponentials while the tensor cores run the
+// other's MMAs.  Heavy (late) tile pairs are scheduled first.  Every wait is bounded and unwinds on
+// timeout.
 #include <cudaTypedefs.h>
 
 #include <mutex>
@@ -32,12 +37,11 @@ namespace fa {
 
 constexpr int kBQ = 128;
 constexpr int kBKV = 128;
-constexpr int kStages = 3;
 constexpr int kThreads = 384;  // warpgroups 0, 1: softmax; warpgroup 2: TMA warp, MMA warp, two idle warps
 // Register split (setmaxnreg): launched at 168 per thread (384 x 168 = 64512); warpgroup 2 drops to
-// 72 (frees 4 x 32 x 96 = 12288), the softmax warpgroups rise to 216 (take 2 x 4 x 32 x 48 = 12288).
-constexpr int kRegsCtl = 72;
-constexpr int kRegsSoftmax = 216;
+// 96 (frees 4 x 32 x 72 = 9216), the softmax warpgroups rise to 200 (take 2 x 4 x 32 x 32 = 8192).
+constexpr int kRegsCtl = 96;
+constexpr int kRegsSoftmax = 200;
 static_assert(4 * 32 * (2 * kRegsSoftmax + kRegsCtl) <= kThreads * 168, "register split exceeds the launch");
 constexpr int kAtom = 128 * 128;  // bytes of one [128 rows x 64 bf16] swizzled atom
 constexpr float kLog2e = 1.4426950408889634f;
@@ -46,17 +50,21 @@ constexpr float kRescaleLog2 = 8.f;  // move the running max only when it grows 
 template <int HD>
 struct Cfg {
   static constexpr int ATOMS = HD / 64;
-  static constexpr int Q_OFF = 0;                                   // 2 buffers x tiles A, B
-  static constexpr int K_OFF = Q_OFF + 2 * 2 * ATOMS * kAtom;       // kStages stages
-  static constexpr int V_OFF = K_OFF + kStages * ATOMS * kAtom;     // kStages stages
-  static constexpr int BAR_OFF = V_OFF + kStages * ATOMS * kAtom;
+  static constexpr bool EARLY_S = HD == 64;                         // S released before P is written
+  static constexpr int QBUF = HD == 64 ? 2 : 1;                     // Q buffers (tiles A, B each)
+  static constexpr int STAGES = HD == 64 ? 3 : 2;                   // K/V ring depth
+  static constexpr int Q_OFF = 0;
+  static constexpr int K_OFF = Q_OFF + QBUF * 2 * ATOMS * kAtom;
+  static constexpr int V_OFF = K_OFF + STAGES * ATOMS * kAtom;
+  static constexpr int BAR_OFF = V_OFF + STAGES * ATOMS * kAtom;
   static constexpr int SMEM = BAR_OFF + 256 + 1024;
   static constexpr int TM_S = 0;                                    // + w * 128
   static constexpr int TM_O = 2 * kBKV;                             // + w * HD
-  static constexpr int TM_P = TM_O + 2 * HD;                        // + w * 64: bf16 P, two keys per column
-  static_assert(TM_P + 2 * 64 <= 512, "TMEM budget");
+  static constexpr int TM_P = EARLY_S ? TM_O + 2 * HD : TM_S;       // + w * (EARLY_S ? 64 : 128)
+  static constexpr int P_STRIDE = EARLY_S ? 64 : kBKV;
+  static_assert(TM_O + 2 * HD <= 512 && (!EARLY_S || TM_P + 2 * 64 <= 512), "TMEM budget");
+  static_assert(SMEM <= 232448, "shared memory budget");
 };
-static_assert(Cfg<64>::SMEM <= 232448, "shared memory budget");
 
 // Work item i of the heavy-first list: tile pair t (query rows 256t..256t+255), batch-head bh.
 struct Item {
@@ -71,11 +79,57 @@ PCB_DEVICE Item item_of(int i, int BH, int T, int H) {
   return it;
 }
 
+// Elementwise helpers of the softmax loop.  The SFU pipe (16 lanes per SM per clock) runs both the
+// exponentials and float->bf16 conversions, and it is the busiest unit of this loop, so part of the work
+// moves to the FMA and ALU pipes:
+//  * ex2_fma: 2^x (x <= 0) with x = n + f, n = rint(x) read from the mantissa of x + 1.5*2^23,
+//    f in [-0.5, 0.5]; 2^f by a degree-3 polynomial whose coefficients were fitted here for minimum
+//    relative error on that interval (Lawson's iteratively reweighted least squares; max relative
+//    error 7.5e-5, far below the 2^-9 rounding of P to bf16), and n added to the exponent bits;
+//  * pack_pos: two non-negative floats to a bf16 pair by adding half an ulp of bf16 and keeping the
+//    high halves (round half up, which differs from round-to-nearest-even only on exact ties);
+//  * ffma2 / fadd2: two fp32 lanes per instruction (fma.rn.f32x2 / add.rn.f32x2).
+PCB_DEVICE float ex2_fma(float x) {
+  x = fmaxf(x, -126.f);
+  const float t = x + 12582912.f;
+  const float f = x - (t - 12582912.f);
+  const float p = fmaf(fmaf(fmaf(0.05517132f, f, 0.24261054f), f, 0.69326097f), f, 0.99992812f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+PCB_DEVICE uint32_t pack_pos(float lo, float hi) {
+  return __byte_perm(__float_as_uint(lo) + 0x8000u, __float_as_uint(hi) + 0x8000u, 0x7632);
+}
+PCB_DEVICE void ffma2(float& d0, float& d1, float a0, float a1, float b, float c) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %4};\n\t"
+      "mov.b64 rc, {%5, %5};\n\tfma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b), "f"(c));
+}
+PCB_DEVICE void fadd2(float& a0, float& a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%0, %1};\n\tmov.b64 rb, {%2, %3};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(b0), "f"(b1));
+}
+// Exponentials of one pair of keys: pairs e % 8 == 6 (a quarter of them) on the FMA pipe.
+PCB_DEVICE void exp_pair(int e, float s0, float s1, float c, float msc, float& p0, float& p1) {
+  float x0, x1;
+  ffma2(x0, x1, s0, s1, c, -msc);
+  if ((e & 7) == 6) {
+    p0 = ex2_fma(x0);
+    p1 = ex2_fma(x1);
+  } else {
+    p0 = ex2_approx(x0);
+    p1 = ex2_approx(x1);
+  }
+}
+
 template <int HD>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm, __nv_bfloat16* __restrict__ out, long long ld_o,
                        float* __restrict__ lse, int S, int H, int BH, float scale, int* err) {
   using C = Cfg<HD>;
+  constexpr int ST = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem + C::Q_OFF;
@@ -84,12 +138,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   uint64_t* q_full = bars + 0;                 // [2]
   uint64_t* q_empty = bars + 2;                // [2]
-  uint64_t* kv_full = bars + 4;                // [kStages]
-  uint64_t* kv_empty = kv_full + kStages;      // [kStages]
-  uint64_t* s_full = kv_empty + kStages;       // [2]
+  uint64_t* kv_full = bars + 4;                // [ST]
+  uint64_t* kv_empty = kv_full + ST;           // [ST]
+  uint64_t* s_full = kv_empty + ST;            // [2]
   uint64_t* p_full = s_full + 2;               // [2]
   uint64_t* o_final = p_full + 2;              // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_final + 2);
+  uint64_t* s_free = o_final + 2;              // [2] (EARLY_S) softmax warpgroup w has S_w in registers
+  uint64_t* pv_done = s_free + 2;              // [2] (EARLY_S) the PV MMA of warpgroup w has read P_w
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -103,8 +159,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 4);
       mbar_init(&o_final[i], 1);
+      mbar_init(&s_free[i], 4);
+      mbar_init(&pv_done[i], 1);
     }
-    for (int i = 0; i < kStages; ++i) {
+    for (int i = 0; i < ST; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
     }
@@ -129,8 +187,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++qc) {
         const Item it = item_of(i, BH, T, H);
-        const int qb = qc & 1;
-        if (!(ok = mbar_wait(&q_empty[qb], ((qc >> 1) & 1) ^ 1u, err, kErrTimeoutEmpty, abort_flag))) break;
+        const int qb = C::QBUF == 2 ? (qc & 1) : 0;
+        const uint32_t qpar = C::QBUF == 2 ? (((qc >> 1) & 1) ^ 1u) : ((qc & 1) ^ 1u);
+        if (!(ok = mbar_wait(&q_empty[qb], qpar, err, kErrTimeoutEmpty, abort_flag))) break;
         mbar_arrive_expect_tx(&q_full[qb], 2 * C::ATOMS * kAtom);
         const int row0 = it.b * S + it.t * 2 * kBQ;
 #pragma unroll
@@ -141,8 +200,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         row0 + w * kBQ);
         const int n_kv = 2 * it.t + 2;
         for (int j = 0; j < n_kv; ++j, ++kc) {
-          const int st = kc % kStages;
-          if (!(ok = mbar_wait(&kv_empty[st], ((kc / kStages) & 1) ^ 1u, err, kErrTimeoutEmpty, abort_flag))) break;
+          const int st = kc % ST;
+          if (!(ok = mbar_wait(&kv_empty[st], ((kc / ST) & 1) ^ 1u, err, kErrTimeoutEmpty, abort_flag))) break;
           mbar_arrive_expect_tx(&kv_full[st], 2 * C::ATOMS * kAtom);
           const int krow = it.b * S + j * kBKV;
 #pragma unroll
@@ -158,10 +217,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc_o = make_idesc_bf16(kBQ, HD, 0, 1);
       const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV);
       auto kv_ready = [&](int n) -> bool {
-        return mbar_wait(&kv_full[n % kStages], (n / kStages) & 1, err, kErrTimeoutFull, abort_flag);
+        return mbar_wait(&kv_full[n % ST], (n / ST) & 1, err, kErrTimeoutFull, abort_flag);
       };
-      auto issue_s = [&](int w, int qb, int n) {
-        const uint32_t kb = k_addr + (n % kStages) * C::ATOMS * kAtom;
+      int n_s[2] = {0, 0}, n_pv[2] = {0, 0};     // S / PV MMAs issued per warpgroup (phase counters)
+      auto issue_s = [&](int w, int qb, int n) -> bool {
+        if (C::EARLY_S && n_s[w] > 0 &&
+            !mbar_wait(&s_free[w], (n_s[w] - 1) & 1, err, kErrTimeoutTmemEmpty, abort_flag))
+          return false;
+        ++n_s[w];
+        const uint32_t kb = k_addr + (n % ST) * C::ATOMS * kAtom;
         const uint32_t qa = q_addr + (qb * 2 + w) * C::ATOMS * kAtom;
         const uint64_t ad = make_smem_desc(qa, 16, 1024, 2), bd = make_smem_desc(kb, 16, 1024, 2);
         tc_fence_after();
@@ -171,49 +235,67 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_bf16(tmem + C::TM_S + w * kBKV, ad + off, bd + off, idesc_s, k > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[w]);
+        return true;
       };
-      auto issue_pv = [&](int w, int n, bool first) {  // A = P from TMEM (16 keys = 8 columns per step)
-        const uint32_t vb = v_addr + (n % kStages) * C::ATOMS * kAtom;
+      auto issue_pv = [&](int w, int n, bool first) -> bool {  // A = P from TMEM (16 keys = 8 columns per step)
+        if (!mbar_wait(&p_full[w], n_pv[w] & 1, err, kErrTimeoutTmemEmpty, abort_flag)) return false;
+        ++n_pv[w];
+        const uint32_t vb = v_addr + (n % ST) * C::ATOMS * kAtom;
         const uint64_t bd = make_smem_desc(vb, kAtom, 1024, 2);
         tc_fence_after();
 #pragma unroll
         for (int k = 0; k < kBKV / 16; ++k)
-          umma_bf16_ts(tmem + C::TM_O + w * HD, tmem + C::TM_P + w * 64 + k * 8, bd + (k * 2048 >> 4), idesc_o,
-                       (!first || k > 0) ? 1u : 0u);
+          umma_bf16_ts(tmem + C::TM_O + w * HD, tmem + C::TM_P + w * C::P_STRIDE + k * 8, bd + (k * 2048 >> 4),
+                       idesc_o, (!first || k > 0) ? 1u : 0u);
+        if (C::EARLY_S) umma_commit(&pv_done[w]);
+        return true;
       };
-      int qc = 0, kc = 0, ta = 0, tb = 0;
+      int qc = 0, kc = 0;
       bool ok = true;
       for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++qc) {
         const Item it = item_of(i, BH, T, H);
-        const int qb = qc & 1;
+        const int qb = C::QBUF == 2 ? (qc & 1) : 0;
+        const uint32_t qpar = C::QBUF == 2 ? ((qc >> 1) & 1) : (qc & 1);
         const int last_a = 2 * it.t, n_kv = 2 * it.t + 2;
-        // S_w(0) may overwrite S_w: the previous item's last p_full_w (waited below) proved it was read
-        if (!(ok = mbar_wait(&q_full[qb], (qc >> 1) & 1, err, kErrTimeoutFull, abort_flag) && kv_ready(kc))) break;
-        issue_s(0, qb, kc);
-        issue_s(1, qb, kc);
-        for (int j = 0; j < n_kv; ++j) {
+        // S_w(0) may overwrite S_w: (EARLY_S) the s_free wait inside issue_s; (otherwise) the previous
+        // item's last p_full_w, waited below, proved the softmax had read it
+        if (!(ok = mbar_wait(&q_full[qb], qpar, err, kErrTimeoutFull, abort_flag) && kv_ready(kc))) break;
+        if (!(ok = issue_s(0, qb, kc) && issue_s(1, qb, kc))) break;
+        for (int j = 0; j < n_kv && ok; ++j) {
           const int n = kc + j;
-          if (j <= last_a) {
-            if (!(ok = mbar_wait(&p_full[0], ta & 1, err, kErrTimeoutTmemEmpty, abort_flag))) break;
-            ++ta;
-            issue_pv(0, n, j == 0);
-            if (j + 1 <= last_a) {
+          if (C::EARLY_S) {
+            if (j + 1 < n_kv) {
               if (!(ok = kv_ready(n + 1))) break;
-              issue_s(0, qb, n + 1);
-            } else {
-              umma_commit(&o_final[0]);
+              if (j + 1 <= last_a && !(ok = issue_s(0, qb, n + 1))) break;
+              if (!(ok = issue_s(1, qb, n + 1))) break;
             }
-          }
-          if (!(ok = mbar_wait(&p_full[1], tb & 1, err, kErrTimeoutTmemEmpty, abort_flag))) break;
-          ++tb;
-          issue_pv(1, n, j == 0);
-          umma_commit(&kv_empty[n % kStages]);
-          if (j + 1 < n_kv) {
-            if (!(ok = kv_ready(n + 1))) break;
-            issue_s(1, qb, n + 1);
+            if (j <= last_a) {
+              if (!(ok = issue_pv(0, n, j == 0))) break;
+              if (j == last_a) umma_commit(&o_final[0]);
+            }
+            if (!(ok = issue_pv(1, n, j == 0))) break;
+            umma_commit(&kv_empty[n % ST]);
+            if (j + 1 == n_kv) {
+              umma_commit(&q_empty[qb]);
+              umma_commit(&o_final[1]);
+            }
           } else {
-            umma_commit(&q_empty[qb]);
-            umma_commit(&o_final[1]);
+            if (j <= last_a) {
+              if (!(ok = issue_pv(0, n, j == 0))) break;
+              if (j + 1 <= last_a) {
+                if (!(ok = kv_ready(n + 1) && issue_s(0, qb, n + 1))) break;
+              } else {
+                umma_commit(&o_final[0]);
+              }
+            }
+            if (!(ok = issue_pv(1, n, j == 0))) break;
+            umma_commit(&kv_empty[n % ST]);
+            if (j + 1 < n_kv) {
+              if (!(ok = kv_ready(n + 1) && issue_s(1, qb, n + 1))) break;
+            } else {
+              umma_commit(&q_empty[qb]);
+              umma_commit(&o_final[1]);
+            }
           }
         }
         kc += n_kv;
@@ -227,7 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     const uint32_t s_col = lane_base + C::TM_S + w * kBKV;
     const uint32_t o_col = lane_base + C::TM_O + w * HD;
-    const uint32_t p_col = lane_base + C::TM_P + w * 64;
+    const uint32_t p_col = lane_base + C::TM_P + w * C::P_STRIDE;
     const float c = scale * kLog2e;
     int tc = 0, ic = 0;
     bool ok = true;
@@ -244,6 +326,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int cc = 0; cc < 4; ++cc)
           tmem_ld_32x32b_x32(s_col + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(sv_u + cc * 32));
         tmem_ld_wait();
+        if (C::EARLY_S) {  // S_w is in registers: the next S_w MMA may overwrite it
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s_free[w]);
+        }
 #define SV(e) __uint_as_float(sv_u[e])
         if (j == last) {  // diagonal tile: key column e is visible to row r iff e <= r
 #pragma unroll
@@ -267,21 +354,42 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const float msc = m * c;
         float rsv[4] = {0.f, 0.f, 0.f, 0.f};
+        if constexpr (C::EARLY_S) {
+          // all of P in registers first; it may be stored only after PV_w of the previous tile read P_w
+          uint32_t pk[64];
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {  // keys 32*q4 .. 32*q4+31 -> 16 TMEM columns of bf16 pairs
-          uint32_t pk[16];
-#pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            const float p0 = ex2_approx(fmaf(SV(q4 * 32 + e), c, -msc));
-            const float p1 = ex2_approx(fmaf(SV(q4 * 32 + e + 1), c, -msc));
-            rsv[(e >> 1) & 3] += p0 + p1;
-            pk[e >> 1] = pack_bf16x2(p0, p1);
+          for (int e = 0; e < 128; e += 2) {
+            float p0, p1;
+            exp_pair(e, SV(e), SV(e + 1), c, msc, p0, p1);
+            fadd2(rsv[(e >> 1) & 1], rsv[((e >> 1) & 1) + 2], p0, p1);
+            pk[e >> 1] = pack_pos(p0, p1);
           }
-          tmem_st_32x32b_x16(p_col + q4 * 16, pk);
+          if (tc > 0) {
+            ok = mbar_wait(&pv_done[w], (tc - 1) & 1, err, kErrTimeoutTmemEmpty, abort_flag);
+            if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+            tc_fence_after();
+          }
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4)
+            tmem_st_32x32b_x16(p_col + q4 * 16, *reinterpret_cast<const uint32_t(*)[16]>(pk + q4 * 16));
+        } else {
+          // P over its own S columns, a quarter at a time (S is already in registers)
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+              float p0, p1;
+              exp_pair(e, SV(q4 * 32 + e), SV(q4 * 32 + e + 1), c, msc, p0, p1);
+              fadd2(rsv[(e >> 1) & 1], rsv[((e >> 1) & 1) + 2], p0, p1);
+              pk[e >> 1] = pack_pos(p0, p1);
+            }
+            tmem_st_32x32b_x16(p_col + q4 * 16, pk);
+          }
         }
 #undef SV
         l += (rsv[0] + rsv[1]) + (rsv[2] + rsv[3]);
-        if (rescale && j > 0) {  // O holds PV(0..j-1): scale it in place (PV_w(j-1) is complete, see above)
+        if (rescale && j > 0) {  // O holds PV(0..j-1): scale it in place (PV_w(j-1) is complete)
 #pragma unroll 1
           for (int cc = 0; cc < HD / 32; ++cc) {
             uint32_t ov[32];
@@ -306,7 +414,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int q = it.t * 2 * kBQ + w * kBQ + r;
       const float inv = l > 0.f ? 1.f / l : 0.f;
       __nv_bfloat16* orow = out + (long long)(it.b * S + q) * ld_o + it.h * HD;
-#pragma unroll
+#pragma unroll 1
       for (int cc = 0; cc < HD / 32; ++cc) {
         uint32_t ov[32];
         tmem_ld_32x32b_x32(o_col + cc * 32, ov);
@@ -386,11 +494,12 @@ static int fa_launch(const void* qkv, long long ld, void* out, long long ld_o, f
 }  // namespace pcb
 
 // Same contract as pcb_attn_fwd (qkv [B*S, 3*H*HD] bf16 with q|k|v column blocks, out [B*S, H*HD]
-// bf16, lse [B*H, S] fp32), on tcgen05.  S % 256 == 0, HD == 64, row strides % 8 == 0.
+// bf16, lse [B*H, S] fp32), on tcgen05.  S % 256 == 0, HD 64 or 128, row strides % 8 == 0.
 int pcb_attn_fwd_tc(const void* qkv, long long ld, void* out, long long ld_o, float* lse, int B, int S, int H,
                     int HD, float scale, int* err, cudaStream_t s) {
   if (S % 256 != 0 || ld % 8 || ld_o % 8) return -1;
   if (reinterpret_cast<uintptr_t>(qkv) & 15) return -1;
   if (HD == 64) return pcb::fa_launch<64>(qkv, ld, out, ld_o, lse, B, S, H, scale, err, s);
+  if (HD == 128) return pcb::fa_launch<128>(qkv, ld, out, ld_o, lse, B, S, H, scale, err, s);
   return -1;
 }

@@ -268,3 +268,31 @@ def pro_eval(llm, reference_text: str, domains: Dict[str, str], serve_tokens: in
     llm.generate(prompt, max_new_tokens=serve_tokens)
     dt = time.perf_counter() - t0
     return ProEvalReport(bpb, per, probes, serve_tokens / dt if dt > 0 else 0.0)
+
+
+# --------------------------------------------------------------------------- KV-cache model loss
+def token_loss(logits: torch.Tensor, target: int) -> float:
+    """-log softmax(logits)[target] with a max-shifted log-sum-exp (CrossEntropy.cs:17-27)."""
+    l = logits.detach().double().reshape(-1)
+    return float(torch.logsumexp(l, 0) - l[target])
+
+
+@torch.no_grad()
+def evaluate_gpt(model, tokens) -> tuple:
+    """Teacher-forced mean next-token cross-entropy and perplexity exp(loss) of a KV-cache model
+    (``GptModel.step``) over one token sequence, stopping at the context limit (CrossEntropy.cs:33-52).
+    Returns (0, 1) for fewer than two tokens."""
+    tokens = list(tokens)
+    if len(tokens) < 2:
+        return 0.0, 1.0
+    cache = model.create_cache()
+    total, count, pos = 0.0, 0, 0
+    for i in range(len(tokens) - 1):
+        if pos >= model.max_seq_len:
+            break
+        logits = model.step(tokens[i], pos, cache)
+        pos += 1
+        total += token_loss(logits, tokens[i + 1])
+        count += 1
+    loss = total / count if count else 0.0
+    return loss, math.exp(loss)

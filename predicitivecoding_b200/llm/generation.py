@@ -231,3 +231,94 @@ class ContinuousBatcher:
         while self.queue or self.active:
             self.step()
         return self.finished
+
+
+def _prefill(model, prompt: Sequence[int], cache, bos: int):
+    """Feed the prompt (a lone BOS when empty) one position at a time; returns (logits, next position)."""
+    prompt = list(prompt) if len(prompt) > 0 else [bos]
+    pos = 0
+    logits = model.step(prompt[0], pos, cache)
+    pos += 1
+    for t in prompt[1:]:
+        if pos >= model.max_seq_len:
+            break
+        logits = model.step(t, pos, cache)
+        pos += 1
+    return logits, pos, prompt
+
+
+class TextGenerator:
+    """Autoregressive generation over a KV-cache model (TextGenerator.cs:16-70): prefill the prompt, then
+    sample, append and decode-step until EOS, ``max_new_tokens`` or the context is full."""
+
+    def __init__(self, model, tokenizer):
+        self.model, self.tokenizer = model, tokenizer
+
+    def generate(self, prompt: str, options: SamplingOptions, on_token: Optional[Callable[[int], None]] = None) -> str:
+        ids = self.generate_tokens(self.tokenizer.encode(prompt, add_bos=True), options, on_token)
+        return self.tokenizer.decode(ids)
+
+    @torch.no_grad()
+    def generate_tokens(self, prompt: Sequence[int], options: SamplingOptions,
+                        on_token: Optional[Callable[[int], None]] = None) -> List[int]:
+        m = self.model
+        cache = m.create_cache()
+        sampler = Sampler(options.seed)
+        logits, pos, ctx = _prefill(m, prompt, cache, self.tokenizer.bos)
+        context = list(ctx)
+        out: List[int] = []
+        for _ in range(options.max_new_tokens):
+            if pos >= m.max_seq_len:
+                break
+            nxt = sampler.sample(logits, context, options)
+            if nxt == self.tokenizer.eos:
+                break
+            out.append(nxt)
+            context.append(nxt)
+            if on_token is not None:
+                on_token(nxt)
+            logits = m.step(nxt, pos, cache)
+            pos += 1
+        return out
+
+
+class BatchedGenerator:
+    """Several independent prompts decoded in lockstep (BatchedGenerator.cs:16-83): every sequence has its
+    own KV cache and sampler (seed + i), and the loop advances all live sequences one token per step until
+    each hits EOS, ``max_new_tokens`` or the context limit."""
+
+    def __init__(self, model, tokenizer):
+        self.model, self.tokenizer = model, tokenizer
+
+    def generate(self, prompts: Sequence[str], options: SamplingOptions) -> List[str]:
+        enc = [self.tokenizer.encode(p, add_bos=True) for p in prompts]
+        return [self.tokenizer.decode(t) for t in self.generate_batch(enc, options)]
+
+    @torch.no_grad()
+    def generate_batch(self, prompts: Sequence[Sequence[int]], options: SamplingOptions) -> List[List[int]]:
+        m, n = self.model, len(prompts)
+        caches = [m.create_cache() for _ in range(n)]
+        samplers = [Sampler(None if options.seed is None else options.seed + i) for i in range(n)]
+        logits, pos, context = [None] * n, [0] * n, [None] * n
+        for i in range(n):
+            logits[i], pos[i], ctx = _prefill(m, prompts[i], caches[i], self.tokenizer.bos)
+            context[i] = list(ctx)
+        out: List[List[int]] = [[] for _ in range(n)]
+        done = [False] * n
+        for _ in range(options.max_new_tokens):
+            active = False
+            for i in range(n):
+                if done[i]:
+                    continue
+                active = True
+                nxt = samplers[i].sample(logits[i], context[i], options)
+                if nxt == self.tokenizer.eos or pos[i] >= m.max_seq_len:
+                    done[i] = True
+                    continue
+                out[i].append(nxt)
+                context[i].append(nxt)
+                logits[i] = m.step(nxt, pos[i], caches[i])
+                pos[i] += 1
+            if not active:
+                break
+        return out

@@ -53,8 +53,9 @@ class InferenceModel:
     def __init__(self, model: DecoderLM, device=None, dtype: Optional[torch.dtype] = None,
                  kv_dtype: Optional[torch.dtype] = None):
         cfg = model.cfg
-        if cfg.block_pattern is not None or cfg.num_loops != 1 or cfg.use_plan:
-            raise NotImplementedError("InferenceModel exports dense attention stacks (no T blocks, loops or plan).")
+        if cfg.block_pattern is not None or cfg.num_loops != 1:
+            raise NotImplementedError("InferenceModel runs dense attention stacks; recurrent 'T' blocks are served "
+                                      "by export_gpt (step-by-step), looped models cannot be exported.")
         self.cfg = cfg
         self.device = torch.device(device) if device is not None else model.wemb.device
         self.dtype = dtype or (torch.bfloat16 if self.device.type == "cuda" else torch.float32)
@@ -65,7 +66,8 @@ class InferenceModel:
         self._fast_decode = (self.device.type == "cuda" and self.kv_dtype == torch.bfloat16
                              and cfg.head_dim in (64, 128))
         cast = lambda t: None if t is None else t.detach().to(self.device, self.dtype)
-        self.wemb = cast(model.wemb)
+        # the plan vector conditions every position identically: fold it into the embedding rows
+        self.wemb = cast(model.wemb + model.plan if cfg.use_plan else model.wemb)
         self.wout = cast(model.wout)
         self.lnf = (cast(model.lnf_g), cast(model.lnf_b))
         self.blocks = []
@@ -178,9 +180,41 @@ class InferenceModel:
         return out
 
 
-def export(model: DecoderLM, device=None, dtype=None) -> InferenceModel:
-    """GptExporter.Export: a trained DecoderLM becomes a KV-cache inference model."""
+def export(model: DecoderLM, device=None, dtype=None):
+    """GptExporter.Export: a trained DecoderLM becomes a KV-cache inference model.  Dense attention
+    stacks (with or without plan and MoE) get the batched device model; stacks with recurrent 'T'
+    blocks get the step-by-step ``GptModel`` behind the same ``generate`` interface."""
+    if model.cfg.block_pattern is not None and "T" in model.cfg.block_pattern:
+        return StepModelServer(export_gpt(model), device)
     return InferenceModel(model, device, dtype)
+
+
+class StepModelServer:
+    """Batched ``generate`` over a step-by-step KV-cache model (each sequence keeps its own cache)."""
+
+    def __init__(self, gpt, device=None):
+        self.gpt = gpt.to(device) if device is not None else gpt
+        self.cfg = gpt.cfg
+
+    @torch.no_grad()
+    def generate(self, prompts: Sequence[Sequence[int]], max_new_tokens: int, eos: int = -1) -> List[List[int]]:
+        outs = []
+        for p in prompts:
+            cache = self.gpt.create_cache()
+            pos, logits = 0, None
+            for t in p:
+                logits = self.gpt.step(int(t), pos, cache)
+                pos += 1
+            out = []
+            while len(out) < max_new_tokens and pos < self.cfg.max_seq_len:
+                nxt = int(torch.argmax(logits.reshape(-1)))
+                out.append(nxt)
+                if nxt == eos:
+                    break
+                logits = self.gpt.step(nxt, pos, cache)
+                pos += 1
+            outs.append(out)
+        return outs
 
 
 class LlmServer:
@@ -204,3 +238,102 @@ class LlmServer:
         ids = [self.tok.encode(p, add_bos=True) for p in prompts]
         outs = self.model.generate(ids, max_new_tokens, self.tok.eos)
         return [self.tok.decode([t for t in o if t != self.tok.eos]) for o in outs]
+
+
+@torch.no_grad()
+def export_gpt(model: DecoderLM):
+    """GptExporter.Export (Serving/GptExporter.cs:32-150): a trained DecoderLM becomes the step-by-step
+    KV-cache ``GptModel`` of ``llm.gpt``, by walking the reference parameter order.
+
+    Covers every block family the trainer has: attention blocks (per-head q/k/v/o slices), recurrent
+    'T' blocks (wa/wi/wu/wo with biases, LayerNorm, GELU FFN), MoE FFNs (router + GELU experts) and the
+    plan vector, which conditions every position identically and is therefore added into every row of
+    the embedding table.  The multi-token head is skipped (the main head serves).  Looped models are
+    refused, as in the reference (the serving stack is single-pass).
+    """
+    from .gpt import FeedForward, GptModel, Norm, TransformerConfig
+    c = model.cfg
+    if c.num_loops > 1:
+        raise NotImplementedError("looped models (num_loops > 1) cannot be exported: serving is single-pass")
+    tc = TransformerConfig(vocab_size=c.vocab, max_seq_len=c.max_seq, embed_dim=c.dim, num_heads=c.num_heads,
+                           num_layers=c.num_blocks, feed_forward_dim=c.ff_dim, layer_norm_eps=c.eps,
+                           tie_embeddings=False, positional="rotary" if c.use_rope else "sinusoidal",
+                           norm="rmsnorm" if c.use_rms_norm else "layernorm", ffn=c.ffn,
+                           block_pattern=c.block_pattern, num_experts=c.num_experts, moe_top_k=c.moe_top_k)
+    gpt = GptModel(tc, seed=0)
+    ps = [p.detach().float().cpu() for p in model.reference_parameters()]
+    cur = [0]
+
+    def nxt(rows, cols, what):
+        if cur[0] >= len(ps):
+            raise ValueError(f"exporter ran out of parameters at {what!r} (layout drift)")
+        t = ps[cur[0]]
+        cur[0] += 1
+        t2 = t.view(1, -1) if t.dim() == 1 else t
+        if tuple(t2.shape) != (rows, cols):
+            raise ValueError(f"exporter shape mismatch at {what!r}: expected [{rows},{cols}], found {list(t2.shape)}")
+        return t2
+
+    def linear(lin, w, b=None):            # trainable y = x W ([in, out]) -> Linear weight [out, in]
+        lin.weight.copy_(w.T)
+        if b is not None:
+            lin.bias.copy_(b.reshape(-1))
+
+    def norm(n, g, b):
+        if (b is None) != n.rms:
+            raise ValueError("norm import mismatch: trained and served configs disagree")
+        n.gamma.copy_(g.reshape(-1))
+        if b is not None:
+            n.beta.copy_(b.reshape(-1))
+
+    D, hd, F_, H = c.dim, c.head_dim, c.ff_dim, c.num_heads
+    rms = c.use_rms_norm
+    wemb = nxt(c.vocab, D, "wemb")
+    for bi, blk in enumerate(gpt.blocks):
+        temporal = c.block_pattern is not None and c.block_pattern[bi] == "T"
+        if temporal:
+            # the trained recurrent block always uses LayerNorm and a GELU FFN with biases
+            ln = TransformerConfig(**{**tc.__dict__, "norm": "layernorm"})
+            blk.ln1, blk.ln2 = Norm(ln), Norm(ln)
+            blk.ffn = FeedForward(tc, torch.Generator().manual_seed(0))
+            norm(blk.ln1, nxt(1, D, "ln1G"), nxt(1, D, "ln1B"))
+            for name in ("wa", "wi", "wu", "wo"):
+                linear(getattr(blk.attn, name), nxt(D, D, name), nxt(1, D, "b" + name[1]))
+        else:
+            norm(blk.ln1, nxt(1, D, "ln1G"), None if rms else nxt(1, D, "ln1B"))
+            a = blk.attn
+            for h in range(H):
+                s = slice(h * hd, (h + 1) * hd)
+                a.q.weight[s].copy_(nxt(D, hd, "wq").T)
+                a.k.weight[s].copy_(nxt(D, hd, "wk").T)
+                a.v.weight[s].copy_(nxt(D, hd, "wv").T)
+                a.o.weight[:, s].copy_(nxt(hd, D, "wo").T)
+            for lin in (a.q, a.k, a.v, a.o):
+                lin.bias.zero_()
+        norm(blk.ln2, nxt(1, D, "ln2G"), None if (rms and not temporal) else nxt(1, D, "ln2B"))
+        if c.num_experts > 0 and not temporal:
+            linear(blk.ffn.router, nxt(D, c.num_experts, "router"))
+            blk.ffn.router.bias.zero_()
+            for ex in blk.ffn.experts:
+                linear(ex.fc1, nxt(D, F_, "ew1"), nxt(1, F_, "eb1"))
+                linear(ex.fc2, nxt(F_, D, "ew2"), nxt(1, D, "eb2"))
+        elif temporal or c.ffn == "gelu":
+            linear(blk.ffn.fc1, nxt(D, F_, "w1"), nxt(1, F_, "b1"))
+            linear(blk.ffn.fc2, nxt(F_, D, "w2"), nxt(1, D, "b2"))
+        else:
+            f = blk.ffn
+            linear(f.gate, nxt(D, F_, "w1"))
+            linear(f.up, nxt(D, F_, "w3"))
+            linear(f.down, nxt(F_, D, "w2"))
+            for lin in (f.gate, f.up, f.down):
+                lin.bias.zero_()
+    norm(gpt.ln_final, nxt(1, D, "lnFG"), None if rms else nxt(1, D, "lnFB"))
+    linear(gpt.lm_head, nxt(D, c.vocab, "wout"))
+    gpt.lm_head.bias.zero_()
+    if c.mtp_weight > 0:
+        nxt(D, c.vocab, "woutMtp")
+    plan = nxt(1, D, "plan").reshape(-1) if c.use_plan else torch.zeros(D)
+    if cur[0] != len(ps):
+        raise ValueError(f"exporter left {len(ps) - cur[0]} parameter(s) unconsumed (layout drift)")
+    gpt.embedding.copy_(wemb + plan)
+    return gpt

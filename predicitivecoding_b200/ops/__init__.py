@@ -177,8 +177,8 @@ _ATTN_IMPL = os.environ.get("PCB_ATTN", "tc")     # "tc" (tcgen05, where the sha
 
 
 def tc_attention_supported(S: int, HD: int) -> bool:
-    """Shapes the tcgen05 attention kernels take (two 128-query tiles per CTA, head dim 64)."""
-    return S % 256 == 0 and HD == 64
+    """Shapes the tcgen05 attention forward takes (two 128-query tiles per CTA, head dim 64 or 128)."""
+    return S % 256 == 0 and HD in (64, 128)
 
 
 def attn_fwd(qkv, out, lse, B, S, H, HD, scale, impl: Optional[str] = None):

@@ -16,7 +16,8 @@ import torch
 from . import (ext, gemm, gemm_pc, attn_fwd, attn_bwd, EPI_BF16, EPI_F32, EPI_RESID_F32, EPI_SWIGLU, EPI_SWIGLU_BWD,
                EPI_RED_F32, EPI_PC_PRED, EPI_PC_STATE)
 
-CASES = ("gemm_swiglu", "gemm_lmhead", "gemm_dw", "pc_pred", "pc_state", "attn_fwd", "attn_fwd_mma", "attn_bwd")
+CASES = ("gemm_swiglu", "gemm_lmhead", "gemm_dw", "pc_pred", "pc_state", "attn_fwd", "attn_fwd_mma", "attn_bwd",
+         "attn_fwd_d128", "attn_fwd_mma_d128", "attn_bwd_d128")
 
 
 def build(which: str, dev: str = "cuda"):
@@ -57,22 +58,26 @@ def build(which: str, dev: str = "cuda"):
             mu16 = torch.empty(B, S, device=dev, dtype=bf)
             fn = lambda: gemm_pc(d, w, b_mn=True, epi=EPI_PC_STATE, c=mu, d=mu16, aux=e, eta=0.1)
         return fn, 2 * B * S * S
-    if which in ("attn_fwd", "attn_fwd_mma", "attn_bwd"):  # causal attention, 8 x 1024 tokens, 12 heads of 64
-        B, S, H, hd = 8, 1024, 12, 64
+    if which.startswith("attn_"):
+        # causal attention: 8 x 1024 tokens, 12 heads of 64 (the 124M decoder), or with the _d128 suffix
+        # 8 x 2048 tokens, 16 heads of 128 (the 1.3B decoder)
+        B, S, H, hd = (8, 2048, 16, 128) if which.endswith("_d128") else (8, 1024, 12, 64)
+        which = which.replace("_d128", "")
         D = H * hd
         qkv = rn(B * S, 3 * D).to(bf)
         o = torch.empty(B * S, D, device=dev, dtype=bf)
         lse = torch.empty(B * H, S, device=dev)
         causal_mm = B * H * S * S * hd          # one causal S x S x hd matmul = 2 * (S^2 / 2) * hd per head
-        attn_fwd(qkv, o, lse, B, S, H, hd, 0.125)
+        sc = hd ** -0.5
+        attn_fwd(qkv, o, lse, B, S, H, hd, sc)
         if which in ("attn_fwd", "attn_fwd_mma"):
             impl = "mma" if which == "attn_fwd_mma" else "tc"
-            return (lambda: attn_fwd(qkv, o, lse, B, S, H, hd, 0.125, impl=impl)), 2 * causal_mm
+            return (lambda: attn_fwd(qkv, o, lse, B, S, H, hd, sc, impl=impl)), 2 * causal_mm
         do = rn(B * S, D).to(bf)
         dq = torch.empty(B * S, D, device=dev)
         dv = torch.empty(B * H, S, device=dev)
         dqkv = torch.empty_like(qkv)
-        return (lambda: attn_bwd(qkv, o, do, lse, dv, dq, dqkv, B, S, H, hd, 0.125)), 5 * causal_mm
+        return (lambda: attn_bwd(qkv, o, do, lse, dv, dq, dqkv, B, S, H, hd, sc)), 5 * causal_mm
     raise ValueError(f"unknown case {which!r}; one of {CASES}")
 
 

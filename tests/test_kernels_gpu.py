@@ -300,11 +300,14 @@ def test_attention_fwd_bwd(hd, impl):
         assert rel_err(dqkv[:, i * D:(i + 1) * D], ref_g) < 0.03, ("qkv"[i], rel_err(dqkv[:, i * D:(i + 1) * D], ref_g))
 
 
+@pytest.mark.parametrize("hd", [64, 128])
 @pytest.mark.parametrize("S,mag", [(1024, 1.5), (512, 4.0), (2048, 0.5)])
-def test_attention_tc_long_sequence(S, mag):
-    """Many key tiles per tile pair: the 3-stage K/V ring, both softmax warpgroups, diagonal masking,
-    and (large magnitudes) the lazy rescaling of O in tensor memory."""
-    hd, B, H = 64, 2, 3
+def test_attention_tc_long_sequence(S, mag, hd):
+    """Many key tiles per tile pair: the K/V ring, both softmax warpgroups, diagonal masking, the early
+    release of S (head dim 64) or P over S (head dim 128), and (large magnitudes) the lazy rescaling of O
+    in tensor memory; several items per CTA (B * H * S / 256 > 148 for S = 2048 at B = 2, H = 3 is not,
+    so the persistent loop is covered by the decoder-shaped case below)."""
+    B, H = 2, 3
     D = H * hd
     g = torch.Generator(device=DEV).manual_seed(S)
     qkv = (torch.randn(B * S, 3 * D, device=DEV, generator=g) * mag).to(torch.bfloat16)
@@ -313,6 +316,29 @@ def test_attention_tc_long_sequence(S, mag):
     err = torch.zeros(1, dtype=torch.int32, device=DEV)
     scale = 1 / math.sqrt(hd)
     assert ops.tc_attention_supported(S, hd)
+    assert ops.ext().attn_fwd_tc(qkv, out, lse, B, S, H, hd, scale, err) == 0
+    q, k, v = (qkv.float()[:, i * D:(i + 1) * D].view(B, S, H, hd).transpose(1, 2) for i in range(3))
+    s = (q @ k.transpose(-1, -2)) * scale
+    s = s.masked_fill(torch.ones(S, S, dtype=torch.bool, device=DEV).triu(1), float("-inf"))
+    ref = (torch.softmax(s, -1) @ v).transpose(1, 2).reshape(B * S, D)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert rel_err(out, ref) < 0.02
+    assert rel_err(lse.view(B, H, S), torch.logsumexp(s, -1)) < 1e-3
+
+
+@pytest.mark.parametrize("hd", [64, 128])
+def test_attention_fwd_tc_persistent_items(hd):
+    """More tile pairs than CTAs (B * H * S / 256 = 384 > 148): each persistent CTA runs several items,
+    reusing Q buffers, the K/V ring and the TMEM accumulators across them."""
+    B, S, H = 16, 1024, 6
+    D = H * hd
+    g = torch.Generator(device=DEV).manual_seed(hd)
+    qkv = torch.randn(B * S, 3 * D, device=DEV, generator=g).to(torch.bfloat16)
+    out = torch.empty(B * S, D, device=DEV, dtype=torch.bfloat16)
+    lse = torch.empty(B * H, S, device=DEV)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    scale = 1 / math.sqrt(hd)
     assert ops.ext().attn_fwd_tc(qkv, out, lse, B, S, H, hd, scale, err) == 0
     q, k, v = (qkv.float()[:, i * D:(i + 1) * D].view(B, S, H, hd).transpose(1, 2) for i in range(3))
     s = (q @ k.transpose(-1, -2)) * scale
