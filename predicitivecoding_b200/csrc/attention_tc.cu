@@ -47,6 +47,21 @@ constexpr int kAtom = 128 * 128;  // bytes of one [128 rows x 64 bf16] swizzled 
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleLog2 = 8.f;  // move the running max only when it grows by more than 2^8
 
+// Optional cycle counters (build with -DPCB_ATTN_STATS), read with pcb_attn_fwd_stats():
+//   0 softmax warp 0 loop   1 waits S   2 TMEM load of S   3 max / exp / pack   4 waits PV (P buffer free)
+//   5 P store + arrive   6 O rescale   7 tiles   8 epilogue   9 MMA loop   10 MMA waits K/V   11 MMA waits
+//   S read   12 MMA waits P   13 producer waits free stage
+#ifdef PCB_ATTN_STATS
+__device__ unsigned long long g_fwd_stats[16];
+#define FST_T0(t) long long t = clock64()
+#define FST_ADD(v, t) v += clock64() - t
+#define FST_FLUSH(i, v) atomicAdd(&g_fwd_stats[i], (unsigned long long)(v))
+#else
+#define FST_T0(t)
+#define FST_ADD(v, t)
+#define FST_FLUSH(i, v)
+#endif
+
 template <int HD>
 struct Cfg {
   static constexpr int ATOMS = HD / 64;
@@ -77,51 +92,6 @@ PCB_DEVICE Item item_of(int i, int BH, int T, int H) {
   it.b = it.bh / H;
   it.h = it.bh % H;
   return it;
-}
-
-// Elementwise helpers of the softmax loop.  The SFU pipe (16 lanes per SM per clock) runs both the
-// exponentials and float->bf16 conversions, and it is the busiest unit of this loop, so part of the work
-// moves to the FMA and ALU pipes:
-//  * ex2_fma: 2^x (x <= 0) with x = n + f, n = rint(x) read from the mantissa of x + 1.5*2^23,
-//    f in [-0.5, 0.5]; 2^f by a degree-3 polynomial whose coefficients were fitted here for minimum
-//    relative error on that interval (Lawson's iteratively reweighted least squares; max relative
-//    error 7.5e-5, far below the 2^-9 rounding of P to bf16), and n added to the exponent bits;
-//  * pack_pos: two non-negative floats to a bf16 pair by adding half an ulp of bf16 and keeping the
-//    high halves (round half up, which differs from round-to-nearest-even only on exact ties);
-//  * ffma2 / fadd2: two fp32 lanes per instruction (fma.rn.f32x2 / add.rn.f32x2).
-PCB_DEVICE float ex2_fma(float x) {
-  x = fmaxf(x, -126.f);
-  const float t = x + 12582912.f;
-  const float f = x - (t - 12582912.f);
-  const float p = fmaf(fmaf(fmaf(0.05517132f, f, 0.24261054f), f, 0.69326097f), f, 0.99992812f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
-}
-PCB_DEVICE uint32_t pack_pos(float lo, float hi) {
-  return __byte_perm(__float_as_uint(lo) + 0x8000u, __float_as_uint(hi) + 0x8000u, 0x7632);
-}
-PCB_DEVICE void ffma2(float& d0, float& d1, float a0, float a1, float b, float c) {
-  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %4};\n\t"
-      "mov.b64 rc, {%5, %5};\n\tfma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d0), "=f"(d1)
-      : "f"(a0), "f"(a1), "f"(b), "f"(c));
-}
-PCB_DEVICE void fadd2(float& a0, float& a1, float b0, float b1) {
-  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%0, %1};\n\tmov.b64 rb, {%2, %3};\n\t"
-      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "+f"(a0), "+f"(a1)
-      : "f"(b0), "f"(b1));
-}
-// Exponentials of one pair of keys: pairs e % 8 == 6 (a quarter of them) on the FMA pipe.
-PCB_DEVICE void exp_pair(int e, float s0, float s1, float c, float msc, float& p0, float& p1) {
-  float x0, x1;
-  ffma2(x0, x1, s0, s1, c, -msc);
-  if ((e & 7) == 6) {
-    p0 = ex2_fma(x0);
-    p1 = ex2_fma(x1);
-  } else {
-    p0 = ex2_approx(x0);
-    p1 = ex2_approx(x1);
-  }
 }
 
 template <int HD>
@@ -185,6 +155,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---------------- TMA producer: runs ahead into the next item ----------------
       int qc = 0, kc = 0;
       bool ok = true;
+      long long st_pw = 0;
+      (void)st_pw;
       for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++qc) {
         const Item it = item_of(i, BH, T, H);
         const int qb = C::QBUF == 2 ? (qc & 1) : 0;
@@ -201,7 +173,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int n_kv = 2 * it.t + 2;
         for (int j = 0; j < n_kv; ++j, ++kc) {
           const int st = kc % ST;
+          FST_T0(t0);
           if (!(ok = mbar_wait(&kv_empty[st], ((kc / ST) & 1) ^ 1u, err, kErrTimeoutEmpty, abort_flag))) break;
+          FST_ADD(st_pw, t0);
           mbar_arrive_expect_tx(&kv_full[st], 2 * C::ATOMS * kAtom);
           const int krow = it.b * S + j * kBKV;
 #pragma unroll
@@ -211,19 +185,28 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      FST_FLUSH(13, st_pw);
     } else if (warp == 9 && lane == 0) {
       // ---------------- MMA issuer ----------------
       constexpr uint32_t idesc_s = make_idesc_bf16(kBQ, kBKV, 0, 0);
       constexpr uint32_t idesc_o = make_idesc_bf16(kBQ, HD, 0, 1);
       const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV);
+      long long st_kv = 0, st_sf = 0, st_pf = 0;
+      (void)st_kv; (void)st_sf; (void)st_pf;
+      FST_T0(st_loop);
       auto kv_ready = [&](int n) -> bool {
-        return mbar_wait(&kv_full[n % ST], (n / ST) & 1, err, kErrTimeoutFull, abort_flag);
+        FST_T0(t0);
+        const bool r = mbar_wait(&kv_full[n % ST], (n / ST) & 1, err, kErrTimeoutFull, abort_flag);
+        FST_ADD(st_kv, t0);
+        return r;
       };
       int n_s[2] = {0, 0}, n_pv[2] = {0, 0};     // S / PV MMAs issued per warpgroup (phase counters)
       auto issue_s = [&](int w, int qb, int n) -> bool {
+        FST_T0(t0);
         if (C::EARLY_S && n_s[w] > 0 &&
             !mbar_wait(&s_free[w], (n_s[w] - 1) & 1, err, kErrTimeoutTmemEmpty, abort_flag))
           return false;
+        FST_ADD(st_sf, t0);
         ++n_s[w];
         const uint32_t kb = k_addr + (n % ST) * C::ATOMS * kAtom;
         const uint32_t qa = q_addr + (qb * 2 + w) * C::ATOMS * kAtom;
@@ -238,7 +221,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         return true;
       };
       auto issue_pv = [&](int w, int n, bool first) -> bool {  // A = P from TMEM (16 keys = 8 columns per step)
+        FST_T0(t0);
         if (!mbar_wait(&p_full[w], n_pv[w] & 1, err, kErrTimeoutTmemEmpty, abort_flag)) return false;
+        FST_ADD(st_pf, t0);
         ++n_pv[w];
         const uint32_t vb = v_addr + (n % ST) * C::ATOMS * kAtom;
         const uint64_t bd = make_smem_desc(vb, kAtom, 1024, 2);
@@ -300,6 +285,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         kc += n_kv;
       }
+      FST_FLUSH(9, clock64() - st_loop);
+      FST_FLUSH(10, st_kv);
+      FST_FLUSH(11, st_sf);
+      FST_FLUSH(12, st_pf);
     }
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
@@ -313,19 +302,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float c = scale * kLog2e;
     int tc = 0, ic = 0;
     bool ok = true;
+    long long sx[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
+    (void)sx;
+    FST_T0(sx_loop);
     for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++ic) {
       const Item it = item_of(i, BH, T, H);
       const int last = 2 * it.t + w;           // tile A: key tiles 0..2t, tile B: 0..2t+1
       float m = -INFINITY, l = 0.f;
       for (int j = 0; j <= last; ++j, ++tc) {
+        FST_T0(t1);
         ok = mbar_wait(&s_full[w], tc & 1, err, kErrTimeoutTmemFull, abort_flag);
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+        FST_ADD(sx[1], t1);
         tc_fence_after();
+        FST_T0(t2);
         uint32_t sv_u[128];
 #pragma unroll
         for (int cc = 0; cc < 4; ++cc)
           tmem_ld_32x32b_x32(s_col + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(sv_u + cc * 32));
         tmem_ld_wait();
+        FST_ADD(sx[2], t2);
+        FST_T0(t3);
         if (C::EARLY_S) {  // S_w is in registers: the next S_w MMA may overwrite it
           tc_fence_before();
           __syncwarp();
@@ -359,16 +356,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t pk[64];
 #pragma unroll
           for (int e = 0; e < 128; e += 2) {
-            float p0, p1;
-            exp_pair(e, SV(e), SV(e + 1), c, msc, p0, p1);
-            fadd2(rsv[(e >> 1) & 1], rsv[((e >> 1) & 1) + 2], p0, p1);
-            pk[e >> 1] = pack_pos(p0, p1);
+            const float p0 = ex2_approx(fmaf(SV(e), c, -msc));
+            const float p1 = ex2_approx(fmaf(SV(e + 1), c, -msc));
+            rsv[(e >> 1) & 3] += p0 + p1;
+            pk[e >> 1] = pack_bf16x2(p0, p1);
           }
+          FST_ADD(sx[3], t3);
+          FST_T0(t4);
           if (tc > 0) {
             ok = mbar_wait(&pv_done[w], (tc - 1) & 1, err, kErrTimeoutTmemEmpty, abort_flag);
             if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
             tc_fence_after();
           }
+          FST_ADD(sx[4], t4);
 #pragma unroll
           for (int q4 = 0; q4 < 4; ++q4)
             tmem_st_32x32b_x16(p_col + q4 * 16, *reinterpret_cast<const uint32_t(*)[16]>(pk + q4 * 16));
@@ -379,16 +379,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t pk[16];
 #pragma unroll
             for (int e = 0; e < 32; e += 2) {
-              float p0, p1;
-              exp_pair(e, SV(q4 * 32 + e), SV(q4 * 32 + e + 1), c, msc, p0, p1);
-              fadd2(rsv[(e >> 1) & 1], rsv[((e >> 1) & 1) + 2], p0, p1);
-              pk[e >> 1] = pack_pos(p0, p1);
+              const float p0 = ex2_approx(fmaf(SV(q4 * 32 + e), c, -msc));
+              const float p1 = ex2_approx(fmaf(SV(q4 * 32 + e + 1), c, -msc));
+              rsv[(e >> 1) & 3] += p0 + p1;
+              pk[e >> 1] = pack_bf16x2(p0, p1);
             }
             tmem_st_32x32b_x16(p_col + q4 * 16, pk);
           }
         }
 #undef SV
         l += (rsv[0] + rsv[1]) + (rsv[2] + rsv[3]);
+        FST_T0(t6);
         if (rescale && j > 0) {  // O holds PV(0..j-1): scale it in place (PV_w(j-1) is complete)
 #pragma unroll 1
           for (int cc = 0; cc < HD / 32; ++cc) {
@@ -400,12 +401,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_st_32x32b_x32(o_col + cc * 32, ov);
           }
         }
+        FST_ADD(sx[6], t6);
+        FST_T0(t5);
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[w]);
+        FST_ADD(sx[5], t5);
+        ++sx[7];
       }
       if (!ok) break;
+      FST_T0(t8);
       ok = mbar_wait(&o_final[w], ic & 1, err, kErrTimeoutTmemFull, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
@@ -431,6 +437,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       lse[(long long)it.bh * S + q] = m * scale + logf(l);
       tc_fence_before();
+      FST_ADD(sx[8], t8);
+    }
+    if (threadIdx.x == 0) {
+      FST_FLUSH(0, clock64() - sx_loop);
+      for (int k = 1; k < 9; ++k) FST_FLUSH(k, sx[k]);
     }
   }
 
@@ -492,6 +503,19 @@ static int fa_launch(const void* qkv, long long ld, void* out, long long ld_o, f
 }
 
 }  // namespace pcb
+
+// Copies the forward's cycle counters into out[16] and clears them; -1 when built without them.
+int pcb_attn_fwd_stats(unsigned long long* out) {
+#ifdef PCB_ATTN_STATS
+  if (cudaMemcpyFromSymbol(out, pcb::fa::g_fwd_stats, 16 * sizeof(unsigned long long)) != cudaSuccess) return -2;
+  unsigned long long zero[16] = {};
+  cudaMemcpyToSymbol(pcb::fa::g_fwd_stats, zero, sizeof(zero));
+  return 0;
+#else
+  (void)out;
+  return -1;
+#endif
+}
 
 // Same contract as pcb_attn_fwd (qkv [B*S, 3*H*HD] bf16 with q|k|v column blocks, out [B*S, H*HD]
 // bf16, lse [B*H, S] fp32), on tcgen05.  S % 256 == 0, HD 64 or 128, row strides % 8 == 0.

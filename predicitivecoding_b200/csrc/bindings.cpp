@@ -67,6 +67,7 @@ int pcb_rope_append(const void* qkv, const float* cs_table, const long long* pos
 int pcb_swiglu_rows(const void* gu, void* a, int rows, int F, cudaStream_t s);
 long long pcb_checked_violations();
 int pcb_attn_bwd_stats(unsigned long long* out);
+int pcb_attn_fwd_stats(unsigned long long* out);
 int pcb_tp_allreduce_norm(const void* peers, int world, int rows, int D, float* x, const void* gamma, void* y,
                           float eps, cudaStream_t s);
 int pcb_tp_reduce_norm(const void* slots, int world, int rows, int D, const float* resid, float* x_out,
@@ -757,6 +758,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     unsigned long long v[16] = {};
     std::vector<int64_t> out;
     if (pcb_attn_bwd_stats(v) == 0)
+      for (int i = 0; i < 16; ++i) out.push_back((int64_t)v[i]);
+    return out;
+  });
+  m.def("attn_fwd_stats", []() {
+    unsigned long long v[16] = {};
+    std::vector<int64_t> out;
+    if (pcb_attn_fwd_stats(v) == 0)
       for (int i = 0; i < 16; ++i) out.push_back((int64_t)v[i]);
     return out;
   });

@@ -607,6 +607,13 @@ class MultiColumnSystem:
                 break
         return r
 
+    def propagate_constraint(self, external_candidates: Sequence[int]) -> None:
+        """Restrict every column's hypotheses to candidates another area holds (MultiColumnSystem.cs:141-148)."""
+        ext = list(external_candidates)
+        if ext:
+            for c in self.columns:
+                c.constrain(ext)
+
     def reset(self) -> None:
         for c in self.columns:
             c.reset()
