@@ -35,7 +35,7 @@ def test_translate_usage_errors():
     assert translate.main([]) == 0
 
 
-@pytest.mark.parametrize("key", ["1", "5", "7", "9"])
+@pytest.mark.parametrize("key", ["1", "2", "3", "4", "5", "6", "7", "8", "9", "10", "11", "12"])
 def test_demos_run(key):
     assert isinstance(demos.DEMOS[key][1](), str)
 
@@ -45,3 +45,7 @@ def test_mixed_precision_rows():
     names = [r[0] for r in rows]
     assert names.count("MatVec") == 2 and "GEMM" in names
     assert all(r[2] > 0 and r[3] > 0 for r in rows)
+
+
+def test_demo_menu_covers_the_reference_thirteen():
+    assert sorted(demos.DEMOS, key=int) == [str(i) for i in range(1, 14)]

@@ -146,3 +146,13 @@ def test_device_state_roundtrip_and_gpu_pretrainer(tmp_path):
                                          checkpoint_dir=str(tmp_path / "ck"), checkpoint_every_steps=3))
     assert rep.steps == 6 and rep.final_eval_loss < 6.0
     assert (tmp_path / "ck" / "adam-device.bin").exists()
+
+
+def test_web_pretrain_demo_trains_on_the_device_and_resumes(tmp_path):
+    """Demo 13: corpus shards -> BPE -> Small preset trained by the fused device trainer with checkpoints;
+    the second run finds the checkpoint by its own format marker and resumes."""
+    from predicitivecoding_b200.cli import demos
+    first = demos.web_pretrain(str(tmp_path), max_steps=4)
+    assert "fresh" in first and "4 steps" in first
+    second = demos.web_pretrain(str(tmp_path), max_steps=4)
+    assert "resumed" in second
