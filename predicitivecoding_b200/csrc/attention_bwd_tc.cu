@@ -592,7 +592,8 @@ static bool encode_rows(PFN_cuTensorMapEncodeTiled_v12000 fn, CUtensorMap* tm, c
 }  // namespace pcb
 
 
-// Same contract as pcb_attn_bwd_rope, on tcgen05: S % 128 == 0, HD == 64, row strides % 8 == 0.
+// Same contract as pcb_attn_bwd_rope, on tcgen05: S % 128 == 0, HD 64 (this file) or 128
+// (attention_bwd_tc128.cu), row strides % 8 == 0.
 // Returns 0, -1 (unsupported shape), -5 (tensor-map encode) or -(1000 + cudaError) (launch).
 // Copies the attention-backward cycle counters into out[16] and clears them; -1 when built without them.
 int pcb_attn_bwd_stats(unsigned long long* out) {
@@ -607,10 +608,16 @@ int pcb_attn_bwd_stats(unsigned long long* out) {
 #endif
 }
 
+int pcb_attn_bwd_tc128(const void* qkv, long long ld, const void* out, const void* dout, long long ld_o,
+                       const float* lse, float* dvec, float* dq_acc, void* dqkv, long long ld_d, int B, int S, int H,
+                       float scale, const float* rope_cs, int* err, cudaStream_t s);
+
 int pcb_attn_bwd_tc(const void* qkv, long long ld, const void* out, const void* dout, long long ld_o,
                     const float* lse, float* dvec, float* dq_acc, void* dqkv, long long ld_d, int B, int S, int H,
                     int HD, float scale, const float* rope_cs, int* err, cudaStream_t s) {
   using namespace pcb;
+  if (HD == 128)
+    return pcb_attn_bwd_tc128(qkv, ld, out, dout, ld_o, lse, dvec, dq_acc, dqkv, ld_d, B, S, H, scale, rope_cs, err, s);
   if (HD != 64 || S % 128 != 0 || ld % 8 || ld_o % 8 || ld_d % 8) return -1;
   if ((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(dout) | reinterpret_cast<uintptr_t>(lse) |
        reinterpret_cast<uintptr_t>(dvec) | reinterpret_cast<uintptr_t>(dq_acc)) & 15)

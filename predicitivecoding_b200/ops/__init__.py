@@ -193,7 +193,7 @@ def attn_fwd(qkv, out, lse, B, S, H, HD, scale, impl: Optional[str] = None):
 
 def attn_bwd(qkv, out, dout, lse, dvec, dq_acc, dqkv, B, S, H, HD, scale, rope_cs=None, impl: Optional[str] = None):
     """Attention backward; with ``rope_cs`` the dq/dk written are w.r.t. the pre-RoPE q/k."""
-    if (impl or _ATTN_IMPL) == "tc" and HD == 64 and S % 128 == 0:
+    if (impl or _ATTN_IMPL) == "tc" and HD in (64, 128) and S % 128 == 0:
         rc = ext().attn_bwd_tc(qkv, out, dout, lse, dvec, dq_acc, dqkv, int(B), int(S), int(H), int(HD),
                                float(scale), rope_cs, None)
         if rc != 0:

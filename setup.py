@@ -60,6 +60,7 @@ setup(
                 os.path.join(CSRC, "attention.cu"),
                 os.path.join(CSRC, "attention_tc.cu"),
                 os.path.join(CSRC, "attention_bwd_tc.cu"),
+                os.path.join(CSRC, "attention_bwd_tc128.cu"),
                 os.path.join(CSRC, "peer.cu"),
                 os.path.join(CSRC, "decode.cu"),
                 os.path.join(CSRC, "collectives.cu"),

@@ -350,11 +350,12 @@ def test_attention_fwd_tc_persistent_items(hd):
     assert rel_err(lse.view(B, H, S), torch.logsumexp(s, -1)) < 1e-3
 
 
+@pytest.mark.parametrize("hd", [64, 128])
 @pytest.mark.parametrize("S,B,H", [(1024, 2, 3), (384, 3, 2)])
-def test_attention_bwd_tc_matches_autograd(S, B, H):
-    """tcgen05 backward over many key/query tiles (persistent CTAs, 2-stage Q/dO ring, dQ reductions),
-    with and without the RoPE rotation of dq/dk."""
-    hd = 64
+def test_attention_bwd_tc_matches_autograd(S, B, H, hd):
+    """tcgen05 backward over many key/query tiles (persistent CTAs, the Q/dO ring, dQ reductions),
+    with and without the RoPE rotation of dq/dk; head dim 128 uses 64-query tiles and the transposed
+    dQ product."""
     D = H * hd
     g = torch.Generator(device=DEV).manual_seed(S + B)
     qkv = torch.randn(B * S, 3 * D, device=DEV, generator=g).to(torch.bfloat16)
