@@ -187,7 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int ic = 0, lc = 0;
       bool ok = true;
       AST_DECL(a_pw);
-      for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++ic) {
+      for (int i = snake_item(0); i < n_items && ok; i = snake_item(++ic)) {
         const Item it = item_of(i, BH, H);
         if (!(ok = mbar_wait(kv_empty, (ic & 1) ^ 1u, err, kErrTimeoutEmpty, abort_flag))) break;
         mbar_arrive_expect_tx(kv_full, 2 * kAtom);
@@ -257,7 +257,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma_commit(&ld_empty[st]);
         return true;
       };
-      for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++ic) {
+      for (int i = snake_item(0); i < n_items && ok; i = snake_item(++ic)) {
         const Item it = item_of(i, BH, H);
         if (!(ok = mbar_wait(kv_full, ic & 1, err, kErrTimeoutFull, abort_flag))) break;
         const uint64_t ak = make_smem_desc(k_addr, 16, 1024, 2), av = make_smem_desc(v_addr, 16, 1024, 2);
@@ -310,7 +310,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     AST_DECL(g_w2);
     AST_DECL(g_w3);
     AST_T0(g_loop);
-    for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++ic) {
+    for (int i = snake_item(0); i < n_items && ok; i = snake_item(++ic)) {
       const Item it = item_of(i, BH, H);
       for (int qi = it.kb; qi < T; ++qi, ++lc, ++tcount) {
         const int st = lc % kQStages;
@@ -454,7 +454,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     AST_DECL(q_w1);
     AST_DECL(q_w2);
     AST_T0(q_loop);
-    for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
+    for (int r = 0, i = snake_item(0); i < n_items && ok; i = snake_item(++r)) {
       const Item it = item_of(i, BH, H);
       for (int qi = it.kb; qi < T; ++qi, ++tcount) {
         AST_T0(q_t1);

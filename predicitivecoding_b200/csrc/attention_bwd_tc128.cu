@@ -157,7 +157,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---------------- TMA producer ----------------
       int ic = 0, lc = 0;
       bool ok = true;
-      for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++ic) {
+      for (int i = snake_item(0); i < n_items && ok; i = snake_item(++ic)) {
         const Item it = item_of(i, BH, H);
         if (!(ok = mbar_wait(kv_empty, (ic & 1) ^ 1u, err, kErrTimeoutEmpty, abort_flag))) break;
         mbar_arrive_expect_tx(kv_full, 4 * kAtom);
@@ -215,7 +215,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma_commit(&ld_empty[st]);
         return true;
       };
-      for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++ic) {
+      for (int i = snake_item(0); i < n_items && ok; i = snake_item(++ic)) {
         const Item it = item_of(i, BH, H);
         if (!(ok = mbar_wait(kv_full, ic & 1, err, kErrTimeoutFull, abort_flag))) break;
         const uint64_t ak = make_smem_desc(k_addr, 16, 1024, 2), av = make_smem_desc(v_addr, 16, 1024, 2);
@@ -251,9 +251,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = threadIdx.x & 127;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     const float c = scale * kLog2e;
-    int lc = 0, tcount = 0;
+    int lc = 0, tcount = 0, ic = 0;
     bool ok = true;
-    for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
+    for (int i = snake_item(0); i < n_items && ok; i = snake_item(++ic)) {
       const Item it = item_of(i, BH, H);
       for (int qi = 2 * it.kb; qi < TQ; ++qi, ++lc, ++tcount) {
         const int st = lc % kQStages;
@@ -326,7 +326,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       // ---- dK, dV of this key tile: warpgroup 0 writes dK * scale (rotated back by -theta with a RoPE
       // table), warpgroup 1 writes dV ----
-      ok = mbar_wait(acc_full, (i - blockIdx.x) / gridDim.x & 1, err, kErrTimeoutTmemFull, abort_flag);
+      ok = mbar_wait(acc_full, ic & 1, err, kErrTimeoutTmemFull, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
       const long long row = (long long)it.b * S + it.kb * kKT + r;
@@ -368,7 +368,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     int tcount = 0;
     bool ok = true;
-    for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
+    for (int r = 0, i = snake_item(0); i < n_items && ok; i = snake_item(++r)) {
       const Item it = item_of(i, BH, H);
       for (int qi = 2 * it.kb; qi < TQ; ++qi, ++tcount) {
         ok = dq_wg_all(mbar_wait(dq_full, tcount & 1, err, kErrTimeoutTmemFull, abort_flag));

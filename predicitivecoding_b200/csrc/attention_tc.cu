@@ -94,6 +94,28 @@ PCB_DEVICE Item item_of(int i, int BH, int T, int H) {
   return it;
 }
 
+// Elementwise helpers of the softmax loop.  Exponentials and float->bf16 conversions share the SFU
+// pipe (16 lanes per SM per clock), the busiest unit of the loop, so the conversions move to the ALU
+// and the scale / row-sum arithmetic to paired fp32 instructions:
+//  * pack_pos: two non-negative floats to a bf16 pair by adding half a bf16 ulp to the bit pattern and
+//    keeping the high halves (round half up, which differs from round-to-nearest-even only on exact ties);
+//  * ffma2 / fadd2: two fp32 lanes per instruction (fma.rn.f32x2 / add.rn.f32x2).
+PCB_DEVICE uint32_t pack_pos(float lo, float hi) {
+  return __byte_perm(__float_as_uint(lo) + 0x8000u, __float_as_uint(hi) + 0x8000u, 0x7632);
+}
+PCB_DEVICE void ffma2(float& d0, float& d1, float a0, float a1, float b, float c) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %4};\n\t"
+      "mov.b64 rc, {%5, %5};\n\tfma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b), "f"(c));
+}
+PCB_DEVICE void fadd2(float& a0, float& a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%0, %1};\n\tmov.b64 rb, {%2, %3};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(b0), "f"(b1));
+}
+
 template <int HD>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm, __nv_bfloat16* __restrict__ out, long long ld_o,
@@ -157,7 +179,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       long long st_pw = 0;
       (void)st_pw;
-      for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++qc) {
+      for (int i = snake_item(0); i < n_items && ok; i = snake_item(++qc)) {
         const Item it = item_of(i, BH, T, H);
         const int qb = C::QBUF == 2 ? (qc & 1) : 0;
         const uint32_t qpar = C::QBUF == 2 ? (((qc >> 1) & 1) ^ 1u) : ((qc & 1) ^ 1u);
@@ -237,7 +259,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       int qc = 0, kc = 0;
       bool ok = true;
-      for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++qc) {
+      for (int i = snake_item(0); i < n_items && ok; i = snake_item(++qc)) {
         const Item it = item_of(i, BH, T, H);
         const int qb = C::QBUF == 2 ? (qc & 1) : 0;
         const uint32_t qpar = C::QBUF == 2 ? ((qc >> 1) & 1) : (qc & 1);
@@ -305,7 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     long long sx[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
     (void)sx;
     FST_T0(sx_loop);
-    for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++ic) {
+    for (int i = snake_item(0); i < n_items && ok; i = snake_item(++ic)) {
       const Item it = item_of(i, BH, T, H);
       const int last = 2 * it.t + w;           // tile A: key tiles 0..2t, tile B: 0..2t+1
       float m = -INFINITY, l = 0.f;
@@ -356,10 +378,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t pk[64];
 #pragma unroll
           for (int e = 0; e < 128; e += 2) {
-            const float p0 = ex2_approx(fmaf(SV(e), c, -msc));
-            const float p1 = ex2_approx(fmaf(SV(e + 1), c, -msc));
-            rsv[(e >> 1) & 3] += p0 + p1;
-            pk[e >> 1] = pack_bf16x2(p0, p1);
+            float x0, x1;
+            ffma2(x0, x1, SV(e), SV(e + 1), c, -msc);
+            const float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
+            fadd2(rsv[(e >> 1) & 1], rsv[((e >> 1) & 1) + 2], p0, p1);
+            pk[e >> 1] = pack_pos(p0, p1);
           }
           FST_ADD(sx[3], t3);
           FST_T0(t4);
@@ -379,10 +402,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t pk[16];
 #pragma unroll
             for (int e = 0; e < 32; e += 2) {
-              const float p0 = ex2_approx(fmaf(SV(q4 * 32 + e), c, -msc));
-              const float p1 = ex2_approx(fmaf(SV(q4 * 32 + e + 1), c, -msc));
-              rsv[(e >> 1) & 3] += p0 + p1;
-              pk[e >> 1] = pack_bf16x2(p0, p1);
+              float x0, x1;
+              ffma2(x0, x1, SV(q4 * 32 + e), SV(q4 * 32 + e + 1), c, -msc);
+              const float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
+              fadd2(rsv[(e >> 1) & 1], rsv[((e >> 1) & 1) + 2], p0, p1);
+              pk[e >> 1] = pack_pos(p0, p1);
             }
             tmem_st_32x32b_x16(p_col + q4 * 16, pk);
           }

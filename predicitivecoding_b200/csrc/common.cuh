@@ -84,6 +84,15 @@ PCB_DEVICE bool mbar_try_wait(uint32_t bar_addr, uint32_t parity) {
   return ok != 0;
 }
 
+// Persistent work lists ordered heaviest first: round r of CTA c takes item r*G + c on even rounds and
+// r*G + (G-1-c) on odd rounds (G = grid size).  Against plain round-robin this evens out the per-CTA sum
+// of work when item sizes fall off along the list (causal attention tiles), and every role of a CTA
+// walks the same sequence.
+PCB_DEVICE int snake_item(int r) {
+  const int G = static_cast<int>(gridDim.x), c = static_cast<int>(blockIdx.x);
+  return r * G + ((r & 1) ? (G - 1 - c) : c);
+}
+
 // Bounded wait on an mbarrier phase.  Returns false (and records `code`) when
 // the budget runs out, or immediately when another role already failed.
 PCB_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,

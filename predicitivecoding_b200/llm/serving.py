@@ -65,7 +65,8 @@ class InferenceModel:
         # the decode kernel reads bf16 caches with head_dim 64 or 128 on the GPU
         self._fast_decode = (self.device.type == "cuda" and self.kv_dtype == torch.bfloat16
                              and cfg.head_dim in (64, 128))
-        cast = lambda t: None if t is None else t.detach().to(self.device, self.dtype)
+        cast = lambda t: None if t is None else t.detach().to(self.device, self.dtype).contiguous()
+        self._tc = self.device.type == "cuda" and self.dtype == torch.bfloat16 and ops.available()
         # the plan vector conditions every position identically: fold it into the embedding rows
         self.wemb = cast(model.wemb + model.plan if cfg.use_plan else model.wemb)
         self.wout = cast(model.wout)
@@ -83,13 +84,17 @@ class InferenceModel:
         c = self.cfg
         return rms_norm(x, g, c.eps) if c.use_rms_norm else layer_norm(x, g, b, c.eps)
 
+    def _mm(self, x, w):
+        """Projection on the tcgen05 GEMM when the shapes allow it (bf16 on the GPU), else torch."""
+        return ops.linear(x, w) if self._tc and ops.linear_ok(x, w) else x @ w
+
     def _ffn(self, blk, h):
         c = self.cfg
         if c.num_experts > 0:
             return blk["_ref"].moe_ffn(h.float(), None).to(h.dtype)
         if c.ffn == "gelu":
-            return gelu_tanh(h @ blk["w1"] + blk["b1"]) @ blk["w2"] + blk["b2"]
-        return (F.silu(h @ blk["w1"]) * (h @ blk["w3"])) @ blk["w2"]
+            return self._mm(gelu_tanh(self._mm(h, blk["w1"]) + blk["b1"]), blk["w2"]) + blk["b2"]
+        return self._mm(F.silu(self._mm(h, blk["w1"])) * self._mm(h, blk["w3"]), blk["w2"])
 
     def new_cache(self, batch: int, max_len: Optional[int] = None, window: Optional[int] = None,
                   sinks: int = 0) -> KvCache:
@@ -121,9 +126,9 @@ class InferenceModel:
         lens = None
         for l, blk in enumerate(self.blocks):
             h = self._norm(x, blk["ln1_g"], blk.get("ln1_b"))
-            q = (h @ blk["wq"]).view(B, T, H, hd).transpose(1, 2)
-            k = (h @ blk["wk"]).view(B, T, H, hd).transpose(1, 2)
-            v = (h @ blk["wv"]).view(B, T, H, hd).transpose(1, 2)
+            q = self._mm(h, blk["wq"]).view(B, T, H, hd).transpose(1, 2)
+            k = self._mm(h, blk["wk"]).view(B, T, H, hd).transpose(1, 2)
+            v = self._mm(h, blk["wv"]).view(B, T, H, hd).transpose(1, 2)
             if rope is not None:
                 q = apply_rope(q, *rope)
                 k = apply_rope(k, *rope)
@@ -134,17 +139,26 @@ class InferenceModel:
                 if lens is None:
                     lens = torch.full((B,), pos0 + 1, dtype=torch.int32, device=self.device)
                 o = ops.decode_attn(q[:, :, 0].contiguous(), cache.k[l], cache.v[l], lens, scale)[:, :, None]
+            elif pos0 == 0 and self._tc and T % 128 == 0 and hd in (64, 128):
+                # prompt prefill on an empty cache: causal flash attention over the prompt
+                qkv = torch.cat([t.transpose(1, 2).reshape(B * T, c.dim) for t in (q, k, v)], 1).contiguous()
+                o2 = torch.empty(B * T, c.dim, device=self.device, dtype=torch.bfloat16)
+                lse_buf = torch.empty(B * H, T, device=self.device)
+                ops.attn_fwd(qkv, o2, lse_buf, B, T, H, hd, scale)
+                o = o2.view(B, T, H, hd).transpose(1, 2)
             else:
                 K = cache.k[l, :, :, :pos0 + T].to(self.dtype)
                 V = cache.v[l, :, :, :pos0 + T].to(self.dtype)
                 # causal over the new positions, full over the cached prefix
                 mask = torch.ones(T, pos0 + T, dtype=torch.bool, device=self.device).tril(pos0)
                 o = F.scaled_dot_product_attention(q, K, V, attn_mask=mask, scale=scale)
-            x = x + o.transpose(1, 2).reshape(B, T, c.dim) @ blk["wo"]
+            x = x + self._mm(o.transpose(1, 2).reshape(B, T, c.dim).contiguous(), blk["wo"])
             x = x + self._ffn(blk, self._norm(x, blk["ln2_g"], blk.get("ln2_b")))
         cache.length = pos0 + T
         cache.position += T
         x = self._norm(x, *self.lnf)
+        if self._tc and ops.linear_ok(x, self.wout):
+            return ops.linear(x, self.wout, fp32=True)
         return (x @ self.wout).float()
 
     def prefill(self, tokens: torch.Tensor, cache: KvCache) -> torch.Tensor:

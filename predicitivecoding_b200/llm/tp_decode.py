@@ -141,7 +141,7 @@ class TensorParallelDecoder:
         buf = bufs[self._flip]
         self._flip ^= 1
         rows = a.shape[0]
-        torch.matmul(a, w, out=buf.local[:rows * self.cfg.dim].view(rows, self.cfg.dim))
+        ops.linear(a, w, out=buf.local[:rows * self.cfg.dim].view(rows, self.cfg.dim))
         if self.T > 1:
             self.peer.barrier()
         y = torch.empty(x.shape, device=self.device, dtype=torch.bfloat16)
@@ -153,9 +153,9 @@ class TensorParallelDecoder:
     def _layer(self, x: torch.Tensor, h: torch.Tensor, l: int, attn, bufs) -> torch.Tensor:
         """One block on normalised input h (residual x updated in place); returns the next norm's output."""
         W, L = self.W, self.cfg.num_blocks
-        o = attn(h @ W[f"b{l}.wqkv"], l)
+        o = attn(ops.linear(h, W[f"b{l}.wqkv"]), l)
         h2 = self._row_parallel(o, W[f"b{l}.wo"], x, W[f"b{l}.ln2"], bufs)
-        gu = h2 @ W[f"b{l}.w13"]
+        gu = ops.linear(h2, W[f"b{l}.w13"])
         a = torch.empty(gu.shape[0], self.Fl, device=self.device, dtype=torch.bfloat16)
         ops.ext().swiglu_rows(gu, a)
         nxt = W[f"b{l + 1}.ln1"] if l + 1 < L else W["lnf"]
@@ -163,7 +163,7 @@ class TensorParallelDecoder:
 
     def _argmax_tokens(self, hf: torch.Tensor) -> torch.Tensor:
         """Greedy next tokens from the final normalised rows [B, D] (vocabulary split over ranks)."""
-        logits = (hf @ self.W["wout"]).float()                  # [B, V/T]
+        logits = ops.linear(hf, self.W["wout"], fp32=True)      # [B, V/T]
         val, idx = logits.max(dim=-1)
         if self.comm is None:
             return idx

@@ -122,6 +122,28 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = F
     return c
 
 
+def linear(x: torch.Tensor, w_kn: torch.Tensor, out: Optional[torch.Tensor] = None, fp32: bool = False,
+           bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """x [..., K] @ w [K, N] on the tcgen05 GEMM (the weight read N-major, no transpose), bf16 operands,
+    fp32 accumulation; bf16 result (or fp32 with ``fp32``), written into ``out`` when given.  Inference
+    projections (serving, tensor-parallel decode) call this instead of a library GEMM."""
+    shape = x.shape
+    x2 = x.reshape(-1, shape[-1])
+    if not x2.is_contiguous():
+        x2 = x2.contiguous()
+    N = w_kn.shape[1]
+    if out is None:
+        out = torch.empty(x2.shape[0], N, device=x.device, dtype=torch.float32 if fp32 else torch.bfloat16)
+    gemm(x2, w_kn, b_mn=True, epi=EPI_F32 if fp32 else EPI_BF16, c=out.view(x2.shape[0], N), bias=bias)
+    return out.view(*shape[:-1], N)
+
+
+def linear_ok(x: torch.Tensor, w_kn: torch.Tensor) -> bool:
+    """Shapes and dtypes the tcgen05 projection path takes (16-byte rows)."""
+    return (x.is_cuda and x.dtype == torch.bfloat16 and w_kn.dtype == torch.bfloat16 and w_kn.dim() == 2
+            and w_kn.is_contiguous() and x.shape[-1] % 8 == 0 and w_kn.shape[1] % 8 == 0)
+
+
 def gemm_pc(a, b, *, a_mn=False, b_mn=False, epi, c=None, d=None, aux=None, bias=None, alpha=1.0, act="tanh",
             pi=1.0, eta=0.1, actreg=0.0, decay=1.0, energy=None, pred_out=None, pred_bf16=None, err=None):
     """GEMM with a predictive-coding epilogue (prediction/error, state update or weight update)."""
