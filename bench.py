@@ -3,7 +3,8 @@
 
 Default workload is the GPT-2-small-shaped decoder (12 layers, d 768, 12 heads,
 ctx 1024, vocab 32000, RMSNorm, RoPE, SwiGLU 2048), bf16 compute with fp32 master
-weights, AdamW (lr 3e-4, wd 0.1) with ZeRO-sharded optimizer state, micro-batch 16
+weights, AdamW (lr 3e-4, wd 0.1, global-norm clipping 1.0 as the reference trains by default) with
+ZeRO-sharded optimizer state, micro-batch 16
 sequences per GPU, data parallel over all ranks.  Tokens are seeded Zipf(1.1) over
 32000 ids; weights are random-init.
 
@@ -174,7 +175,7 @@ def run_decoder_bench(args, dev, rank, world, pg):
             return ops.launch_count()
     else:
         from predicitivecoding_b200.engine.fused_trainer import FusedDecoderTrainer
-        tr = FusedDecoderTrainer(cfg, B, S, device=dev, lr=3e-4, weight_decay=0.1, process_group=pg,
+        tr = FusedDecoderTrainer(cfg, B, S, device=dev, lr=3e-4, weight_decay=0.1, clip_norm=1.0, process_group=pg,
                                  use_graph=not args.no_graph)
         info = {"params": tr.arena.numel, "grad_sync": tr.grad_sync if world > 1 else "none"}
 
@@ -246,7 +247,8 @@ def run_decoder_bench(args, dev, rank, world, pg):
         "impl": args.impl,
         "config": {"model": name, "global_batch": B * groups, "seq_len": S,
                    "parallelism": (f"tp{T}" + (f"xdp{dp}" if dp > 1 else "")) if tp_mode else f"dp{world}",
-                   "micro_batch_per_gpu": B, "optimizer": "AdamW lr 3e-4 wd 0.1 (ZeRO-1 sharded states)",
+                   "micro_batch_per_gpu": B,
+                   "optimizer": "AdamW lr 3e-4 wd 0.1, global-norm clipping 1.0 (ZeRO-1 sharded states)",
                    "l2": "no flush needed: per-step working set (~3 GB of activations, 1 GB logits) >> 126 MB L2",
                    **info},
         "clocks": clk.summary(),
@@ -360,6 +362,7 @@ def _torch_baseline(cfg, B, dev, world, pg):
             logits = model(tok) if world == 1 else model(tok)
             loss = torch.nn.functional.cross_entropy(logits.float().view(-1, cfg.vocab), tgt.view(-1))
         loss.backward()
+        torch.nn.utils.clip_grad_norm_(model.parameters(), 1.0, foreach=True)
         opt.step()
         opt.zero_grad(set_to_none=True)
         return float(loss) if sync else None

@@ -454,7 +454,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     AST_DECL(q_w1);
     AST_DECL(q_w2);
     AST_T0(q_loop);
-    for (int r = 0, i = snake_item(0); i < n_items && ok; i = snake_item(++r)) {
+    for (int ic = 0, i = snake_item(0); i < n_items && ok; i = snake_item(++ic)) {
       const Item it = item_of(i, BH, H);
       for (int qi = it.kb; qi < T; ++qi, ++tcount) {
         AST_T0(q_t1);

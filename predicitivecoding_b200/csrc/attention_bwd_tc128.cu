@@ -368,7 +368,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     int tcount = 0;
     bool ok = true;
-    for (int r = 0, i = snake_item(0); i < n_items && ok; i = snake_item(++r)) {
+    for (int ic = 0, i = snake_item(0); i < n_items && ok; i = snake_item(++ic)) {
       const Item it = item_of(i, BH, H);
       for (int qi = 2 * it.kb; qi < TQ; ++qi, ++tcount) {
         ok = dq_wg_all(mbar_wait(dq_full, tcount & 1, err, kErrTimeoutTmemFull, abort_flag));

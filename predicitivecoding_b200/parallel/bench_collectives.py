@@ -12,7 +12,12 @@ Cases (each timed with CUDA events on the launching stream after warm-up, max ov
   writes the bf16 weights of the shard into every rank's weight buffer;
 * ``pc_allreduce_update``: the PC data-parallel weight step (64 Mi fp32 weights): sum of every
   rank's delta-W shard, weight update, fp32 + bf16 weights written to every rank;
-* ``all_reduce``: the Communicator's peer all-reduce (one-shot below 512 KiB, two-shot above).
+* ``all_reduce``: the Communicator's peer all-reduce (one-shot below 512 KiB, two-shot above);
+* ``dp_bucket_push`` / ``dp_post_backward``: the trainer's bucketed data-parallel step on the same
+  124M arena, split as it runs: the copy-engine pushes of every bucket's pieces to their owners (in the
+  trainer they overlap the backward; here they are timed alone), and what runs after the backward
+  (barrier, owner reduce + sum of squares, clip-norm exchange, AdamW + bf16 weights to every rank,
+  barrier).
 
 Bytes that must cross each GPU's links, per direction: a rank's inbound link carries what it pulls from
 the others and what the others push to it, and its outbound link the mirror image, so for T ranks the
@@ -44,7 +49,8 @@ def nvlink_bytes_per_direction(case: str, n: int, world: int) -> float:
     if world <= 1:
         return 0.0
     f = (world - 1) / world
-    per_elem = {"rs_adamw_ag": 4 + 2, "pc_allreduce_update": 4 + 6, "all_reduce": 2}
+    per_elem = {"rs_adamw_ag": 4 + 2, "pc_allreduce_update": 4 + 6, "all_reduce": 2, "dp_bucket_push": 4,
+                "dp_post_backward": 2}
     if case not in per_elem:
         raise ValueError(f"unknown case {case!r}")
     return f * n * per_elem[case]
@@ -104,6 +110,57 @@ def main() -> None:
                 "ms": round(ms, 3), "nvlink_gb_per_direction": round(per_dir / 1e9, 3),
                 "roofline_ms": round(roof, 3), "of_roofline": round(roof / ms, 3) if T > 1 else None})
     del grad, w16, w32, m, v
+
+    # ---- bucketed data-parallel step (the trainer's path): pushes, then the post-backward kernels
+    from ..engine.arena import ParamArena, ParamSpec
+    from ..engine.fused_trainer import FusedDecoderTrainer
+    from ..models.config import DecoderLmConfig
+    cfg = DecoderLmConfig.gpt2_small_swiglu()
+    D, F_, L, V = cfg.dim, cfg.ff_dim, cfg.num_blocks, cfg.vocab
+    specs = [ParamSpec("wemb", (V, D)), ParamSpec("wout", (V, D)), ParamSpec("lnf", (D,))]
+    buckets = [["wout", "lnf"]]
+    for l in reversed(range(L)):
+        names = [f"b{l}.wqkv", f"b{l}.wo", f"b{l}.w13", f"b{l}.w2", f"b{l}.ln1", f"b{l}.ln2"]
+        shapes = [(3 * D, D), (D, D), (2 * F_, D), (D, F_), (D,), (D,)]
+        specs += [ParamSpec(n, sh) for n, sh in zip(names, shapes)]
+        buckets.append(names)
+    buckets.append(["wemb"])
+    A = ParamArena(specs, T, buckets=buckets)
+    gradb = torch.randn(A.total, device=dev)
+    stage = peer.symmetric(T * A.shard, torch.float32)
+    w16c = peer.symmetric(A.total, torch.bfloat16)
+    norm = peer.symmetric(T, torch.float64)
+    tab = torch.tensor([list(p) for p in A.pieces(rank)], dtype=torch.int64, device=dev)
+    plans = [FusedDecoderTrainer.push_plan(A, rank, b) for b in range(len(A.buckets))]
+    gsh, w32b = torch.zeros(A.shard, device=dev), torch.randn(A.shard, device=dev)
+    mb, vb = torch.zeros(A.shard, device=dev), torch.zeros(A.shard, device=dev)
+    sumsq = torch.zeros(1, device=dev, dtype=torch.float64)
+
+    def pushes():
+        base = gradb.data_ptr()
+        for plan in plans:
+            for q, dst, src, n in plan:
+                ops.ext().memcpy_d2d(stage.host_ptrs[q] + 4 * dst, base + 4 * src, 4 * n)
+        peer.barrier()
+
+    def post_backward():
+        peer.barrier()
+        sumsq.zero_()
+        ops.ext().dp_reduce_sumsq(gradb, stage.local, A.shard, tab, rank, T, gsh, sumsq)
+        ops.ext().dp_norm_push(sumsq, norm.ptrs, rank, T)
+        peer.barrier()
+        ops.ext().dp_adamw_ag(gsh, w32b, mb, vb, w16c.ptrs, A.shard, tab, hyper, 0.9, 0.999, 1e-8, norm.local, 1.0, T)
+        peer.barrier()
+
+    for name, fn in (("dp_bucket_push", pushes), ("dp_post_backward", post_backward)):
+        ms = _time(fn, 10, dev)
+        per_dir = nvlink_bytes_per_direction(name, A.total, T)
+        roof = per_dir / (LINK_GBS * 1e9) * 1e3
+        label = ("dp_bucket_push (copy engines, all buckets, timed alone)" if name == "dp_bucket_push" else
+                 "dp_post_backward (reduce + clip + AdamW + bf16 all-gather)")
+        out.append({"case": label, "world": T, "ms": round(ms, 3), "nvlink_gb_per_direction": round(per_dir / 1e9, 3),
+                    "roofline_ms": round(roof, 3), "of_roofline": round(roof / ms, 3) if T > 1 else None})
+    del gradb, stage, w16c, norm, gsh, w32b, mb, vb
 
     # ---- PC data-parallel delta-W all-reduce + update
     N2 = 64 << 20
