@@ -110,6 +110,23 @@ int pcb_pc_allreduce_update(void* const* delta_peers, void* const* w_peers, void
 int pcb_peer_reduce(void* const* in_peers, void* const* out_peers, long long lo, long long hi, float scale, int world,
                     int num_sms, cudaStream_t s);
 
+int pcb_moe_route(const void* x, long long ldx, const void* router, int M, int D, int E, int k, float* gates,
+                  int* topi, cudaStream_t s);
+int pcb_moe_dispatch(const int* topi, const float* gates, int M, int k, int E, int cap, int* seg, int* pos, int* src,
+                     float* rgate, float* coef, float* loss_acc, float weight, cudaStream_t s);
+int pcb_moe_gather(const void* x, long long ldx, const int* src, const int* seg, int E, int D, int cap, void* xs,
+                   cudaStream_t s);
+int pcb_moe_combine(const float* res, const float* ys, const int* pos, const float* rgate, int M, int k, int D,
+                    float* out, cudaStream_t s);
+int pcb_moe_combine_bwd(const float* dx, const float* ys, const int* src, const float* rgate, const int* seg, int E,
+                        int D, int cap, void* dys, float* dgate, cudaStream_t s);
+int pcb_moe_router_bwd(const float* gates, const int* topi, const int* pos, const float* dgate, const float* coef,
+                       float weight, const float* dxs, const void* router, int M, int k, int E, int D, float* dlogits,
+                       float* dn, cudaStream_t s);
+int pcb_moe_router_wgrad(const float* dlogits, const void* x, long long ldx, int M, int E, int D, float* dR,
+                         cudaStream_t s);
+int pcb_moe_seg_colsum(const void* x, const int* seg, int E, int N, int cap, float* db, cudaStream_t s);
+
 extern "C" void pcb_set_gemm_mode(int mode);
 
 namespace {
@@ -217,6 +234,159 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, int64_
   check(pcb_gemm_launch(a.data_ptr(), a_mn, lda, b.data_ptr(), b_mn, ldb, (int)epi, args, (int)force_bn,
                         (int)force_splits, num_sms(), cur_stream()),
         "gemm");
+}
+
+// Grouped (mixture-of-experts) GEMM.  mode 1: a [cap, K] sorted activations, b stacks `count` expert
+// blocks ([count*N, K], or [count*K, N] with b_mn), bias [count*N]; mode 2 (weight gradients): a [cap, m_per]
+// and b [cap, N] read MN-major, c [count*m_per, N] fp32 accumulated.  seg: device int32 [count + 1].
+void gemm_grouped(const at::Tensor& a, const at::Tensor& b, bool b_mn, int64_t epi, const at::Tensor& seg,
+                  int64_t count, int64_t mode, const c10::optional<at::Tensor>& c, const c10::optional<at::Tensor>& d,
+                  const c10::optional<at::Tensor>& aux, const c10::optional<at::Tensor>& bias,
+                  const c10::optional<at::Tensor>& err) {
+  req(a, at::kBFloat16, "a");
+  req(b, at::kBFloat16, "b");
+  req(seg, at::kInt, "seg");
+  PCB_CHECK(seg.numel() == count + 1, "gemm_grouped: seg must have count + 1 entries");
+  PCB_CHECK(mode == 1 || mode == 2, "gemm_grouped: mode 1 (rows) or 2 (weight gradients)");
+  const long long lda = row_stride(a, "a"), ldb = row_stride(b, "b");
+  pcb::GemmArgs args{};
+  int a_mn = 0;
+  if (mode == 1) {
+    args.M = a.size(0);
+    args.K = a.size(1);
+    if (b_mn) {
+      PCB_CHECK(b.size(0) == count * args.K, "gemm_grouped: b must be [count*K, N]");
+      args.N = b.size(1);
+    } else {
+      PCB_CHECK(b.size(1) == args.K && b.size(0) % count == 0, "gemm_grouped: b must be [count*N, K]");
+      args.N = b.size(0) / count;
+    }
+  } else {
+    a_mn = 1;
+    PCB_CHECK(b_mn, "gemm_grouped: mode 2 reads b MN-major");
+    PCB_CHECK(a.size(0) == b.size(0), "gemm_grouped: a and b must share the sorted rows");
+    args.grp_m = a.size(1);
+    args.M = count * a.size(1);
+    args.K = a.size(0);
+    args.N = b.size(1);
+  }
+  args.alpha = 1.f;
+  if (c) { args.C = c->data_ptr(); args.ldc = row_stride(*c, "c"); }
+  if (d) { args.D = d->data_ptr(); args.ldd = row_stride(*d, "d"); }
+  if (aux) { args.aux = aux->data_ptr(); args.ldaux = row_stride(*aux, "aux"); }
+  if (bias) {
+    PCB_CHECK(bias->scalar_type() == at::kFloat || bias->scalar_type() == at::kBFloat16, "bias: fp32 or bf16");
+    PCB_CHECK(bias->numel() == count * args.N, "gemm_grouped: bias must have count*N entries");
+    args.bias = bias->data_ptr();
+    args.bias_bf16 = bias->scalar_type() == at::kBFloat16 ? 1 : 0;
+  }
+  if (err) args.err = err->data_ptr<int>();
+  args.grp_seg = seg.data_ptr<int>();
+  args.grp_count = (int)count;
+  args.grp_mode = (int)mode;
+  const at::cuda::CUDAGuard guard(a.device());
+  check(pcb_gemm_grouped_launch(a.data_ptr(), a_mn, lda, b.data_ptr(), b_mn ? 1 : 0, ldb, (int)epi, args, num_sms(),
+                                cur_stream()),
+        "gemm_grouped");
+}
+
+// ---------------------------------------------------------------- mixture of experts
+void moe_route(const at::Tensor& x, const at::Tensor& router, int64_t k, at::Tensor& gates, at::Tensor& topi) {
+  req(x, at::kBFloat16, "x");
+  req(router, at::kBFloat16, "router");
+  req(gates, at::kFloat, "gates");
+  req(topi, at::kInt, "topi");
+  const int M = x.size(0), D = x.size(1), E = router.size(0);
+  PCB_CHECK(router.size(1) == D && router.is_contiguous(), "moe_route: router must be [E, D] contiguous");
+  PCB_CHECK(gates.numel() == (long long)M * E && topi.numel() == (long long)M * k, "moe_route: output sizes");
+  check(pcb_moe_route(x.data_ptr(), row_stride(x, "x"), router.data_ptr(), M, D, E, (int)k, gates.data_ptr<float>(),
+                      topi.data_ptr<int>(), cur_stream()),
+        "moe_route");
+}
+void moe_dispatch(const at::Tensor& topi, const at::Tensor& gates, int64_t k, at::Tensor& seg, at::Tensor& pos,
+                  at::Tensor& src, at::Tensor& rgate, at::Tensor& coef, const c10::optional<at::Tensor>& loss_acc,
+                  double weight) {
+  req(topi, at::kInt, "topi");
+  req(gates, at::kFloat, "gates");
+  req(seg, at::kInt, "seg");
+  req(pos, at::kInt, "pos");
+  req(src, at::kInt, "src");
+  req(rgate, at::kFloat, "rgate");
+  req(coef, at::kFloat, "coef");
+  const int M = gates.size(0), E = gates.size(1);
+  PCB_CHECK(seg.numel() == E + 1 && coef.numel() == E && pos.numel() == topi.numel() && topi.numel() == (long long)M * k,
+            "moe_dispatch: sizes");
+  PCB_CHECK(rgate.numel() == src.numel(), "moe_dispatch: src / rgate sizes");
+  check(pcb_moe_dispatch(topi.data_ptr<int>(), gates.data_ptr<float>(), M, (int)k, E, (int)src.numel(),
+                         seg.data_ptr<int>(), pos.data_ptr<int>(), src.data_ptr<int>(), rgate.data_ptr<float>(),
+                         coef.data_ptr<float>(), loss_acc ? loss_acc->data_ptr<float>() : nullptr, (float)weight,
+                         cur_stream()),
+        "moe_dispatch");
+}
+void moe_gather(const at::Tensor& x, const at::Tensor& src, const at::Tensor& seg, at::Tensor& xs) {
+  req(x, at::kBFloat16, "x");
+  req(xs, at::kBFloat16, "xs");
+  req(src, at::kInt, "src");
+  req(seg, at::kInt, "seg");
+  PCB_CHECK(xs.is_contiguous() && xs.size(1) == x.size(1) && xs.size(0) == src.numel(), "moe_gather: xs shape");
+  check(pcb_moe_gather(x.data_ptr(), row_stride(x, "x"), src.data_ptr<int>(), seg.data_ptr<int>(),
+                       (int)seg.numel() - 1, x.size(1), (int)src.numel(), xs.data_ptr(), cur_stream()),
+        "moe_gather");
+}
+void moe_combine(const at::Tensor& res, const at::Tensor& ys, const at::Tensor& pos, const at::Tensor& rgate,
+                 int64_t k, at::Tensor& out) {
+  req(res, at::kFloat, "res");
+  req(ys, at::kFloat, "ys");
+  req(out, at::kFloat, "out");
+  PCB_CHECK(res.is_contiguous() && ys.is_contiguous() && out.is_contiguous(), "moe_combine: contiguous operands");
+  check(pcb_moe_combine(res.data_ptr<float>(), ys.data_ptr<float>(), pos.data_ptr<int>(), rgate.data_ptr<float>(),
+                        res.size(0), (int)k, res.size(1), out.data_ptr<float>(), cur_stream()),
+        "moe_combine");
+}
+void moe_combine_bwd(const at::Tensor& dx, const at::Tensor& ys, const at::Tensor& src, const at::Tensor& rgate,
+                     const at::Tensor& seg, at::Tensor& dys, at::Tensor& dgate) {
+  req(dx, at::kFloat, "dx");
+  req(ys, at::kFloat, "ys");
+  req(dys, at::kBFloat16, "dys");
+  req(dgate, at::kFloat, "dgate");
+  PCB_CHECK(dx.is_contiguous() && ys.is_contiguous() && dys.is_contiguous(), "moe_combine_bwd: contiguous operands");
+  check(pcb_moe_combine_bwd(dx.data_ptr<float>(), ys.data_ptr<float>(), src.data_ptr<int>(), rgate.data_ptr<float>(),
+                            seg.data_ptr<int>(), (int)seg.numel() - 1, dx.size(1), (int)src.numel(), dys.data_ptr(),
+                            dgate.data_ptr<float>(), cur_stream()),
+        "moe_combine_bwd");
+}
+void moe_router_bwd(const at::Tensor& gates, const at::Tensor& topi, const at::Tensor& pos, const at::Tensor& dgate,
+                    const at::Tensor& coef, double weight, const at::Tensor& dxs, const at::Tensor& router, int64_t k,
+                    at::Tensor& dlogits, at::Tensor& dn) {
+  req(gates, at::kFloat, "gates");
+  req(dxs, at::kFloat, "dxs");
+  req(router, at::kBFloat16, "router");
+  req(dlogits, at::kFloat, "dlogits");
+  req(dn, at::kFloat, "dn");
+  PCB_CHECK(dxs.is_contiguous() && dn.is_contiguous() && router.is_contiguous(), "moe_router_bwd: contiguous operands");
+  const int M = gates.size(0), E = gates.size(1), D = dn.size(1);
+  check(pcb_moe_router_bwd(gates.data_ptr<float>(), topi.data_ptr<int>(), pos.data_ptr<int>(), dgate.data_ptr<float>(),
+                           coef.data_ptr<float>(), (float)weight, dxs.data_ptr<float>(), router.data_ptr(), M, (int)k, E,
+                           D, dlogits.data_ptr<float>(), dn.data_ptr<float>(), cur_stream()),
+        "moe_router_bwd");
+}
+void moe_router_wgrad(const at::Tensor& dlogits, const at::Tensor& x, at::Tensor& dR) {
+  req(dlogits, at::kFloat, "dlogits");
+  req(x, at::kBFloat16, "x");
+  req(dR, at::kFloat, "dR");
+  check(pcb_moe_router_wgrad(dlogits.data_ptr<float>(), x.data_ptr(), row_stride(x, "x"), x.size(0), dlogits.size(1),
+                             x.size(1), dR.data_ptr<float>(), cur_stream()),
+        "moe_router_wgrad");
+}
+void moe_seg_colsum(const at::Tensor& x, const at::Tensor& seg, at::Tensor& db) {
+  req(x, at::kBFloat16, "x");
+  req(db, at::kFloat, "db");
+  PCB_CHECK(x.is_contiguous(), "moe_seg_colsum: contiguous input");
+  const int E = seg.numel() - 1;
+  PCB_CHECK(db.numel() == (long long)E * x.size(1), "moe_seg_colsum: db must have E*N entries");
+  check(pcb_moe_seg_colsum(x.data_ptr(), seg.data_ptr<int>(), E, x.size(1), x.size(0), db.data_ptr<float>(),
+                           cur_stream()),
+        "moe_seg_colsum");
 }
 
 // PC-specific GEMM entry (epilogues 8..10), scalar knobs passed explicitly.
@@ -726,6 +896,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "predicitivecoding_b200 sm_100a kernels";
   m.def("gemm", &gemm);
   m.def("gemm_pc", &gemm_pc);
+  m.def("gemm_grouped", &gemm_grouped);
+  m.def("moe_route", &moe_route);
+  m.def("moe_dispatch", &moe_dispatch);
+  m.def("moe_gather", &moe_gather);
+  m.def("moe_combine", &moe_combine);
+  m.def("moe_combine_bwd", &moe_combine_bwd);
+  m.def("moe_router_bwd", &moe_router_bwd);
+  m.def("moe_router_wgrad", &moe_router_wgrad);
+  m.def("moe_seg_colsum", &moe_seg_colsum);
   m.def("embed_fwd", &embed_fwd);
   m.def("embed_bwd", &embed_bwd);
   m.def("rmsnorm_fwd", &rmsnorm_fwd);

@@ -91,6 +91,26 @@ PCB_DEVICE void tile_coords(int tile, const GemmArgs& a, int num_m, int num_n, i
   }
 }
 
+// Grouped GEMM: the expert of a 256-row tile and its k-block range; false when the tile is skipped
+// (mode 1: past the rows in use; mode 2: an expert that received no rows).  The producer, the MMA
+// issuer and the epilogue read the same segment table, so they skip the same tiles.
+PCB_DEVICE bool grp_tile(const GemmArgs& a, int mb, int total_kb, int& e, int& kb0, int& kb1) {
+  const int row0 = mb * 2 * kBM;
+  if (a.grp_mode == 1) {
+    if (row0 >= a.grp_seg[a.grp_count]) return false;
+    int x = 0;
+    while (x + 1 < a.grp_count && a.grp_seg[x + 1] <= row0) ++x;
+    e = x;
+    kb0 = 0;
+    kb1 = total_kb;
+    return true;
+  }
+  e = row0 / a.grp_m;
+  kb0 = a.grp_seg[e] / kBK;
+  kb1 = a.grp_seg[e + 1] / kBK;
+  return kb1 > kb0;
+}
+
 PCB_DEVICE unsigned int ld_acquire_gpu(const unsigned int* p) {
   unsigned int v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -222,10 +242,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int tile = pair_id; tile < tiles && ok; tile += num_pairs) {
         int split, mb, nb;
         tile_coords(tile, args, num_m, num_n, split, mb, nb);
-        const int m0 = mb * 2 * kBM + rank * kBM;
-        const int n0 = nb * BN + rank * (BN / 2);
-        const int kb0 = split * args.kb_per_split;
-        const int kb1 = min(total_kb, kb0 + args.kb_per_split);
+        int m0 = mb * 2 * kBM + rank * kBM;
+        int n0 = nb * BN + rank * (BN / 2);
+        int kb0 = split * args.kb_per_split;
+        int kb1 = min(total_kb, kb0 + args.kb_per_split);
+        int bk_off = 0;   // grouped, MN-major B: this expert's block along B's K coordinate
+        if (args.grp_mode) {
+          int e;
+          if (!grp_tile(args, mb, total_kb, e, kb0, kb1)) continue;
+          if (args.grp_mode == 1) {
+            if (args.b_mn == 0) n0 += e * (int)args.grp_b_off;
+            else bk_off = e * (int)args.grp_b_off;
+          } else {
+            m0 -= e * args.grp_m;   // A holds one expert's columns: local row coordinate
+          }
+        }
         if (args.ag_world > 1) {
           const int c = m0 / args.ag_rows;
           if (!((ready_mask >> c) & 1u)) {
@@ -252,7 +283,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_2d_pair(sb, &tmB, &full[stage], k0, n0);
           } else {
 #pragma unroll
-            for (int p = 0; p < BN / 128; ++p) tma_load_2d_pair(sb + p * 8192, &tmB, &full[stage], n0 + 64 * p, k0);
+            for (int p = 0; p < BN / 128; ++p)
+              tma_load_2d_pair(sb + p * 8192, &tmB, &full[stage], n0 + 64 * p, k0 + bk_off);
           }
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
@@ -275,8 +307,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       PAIR_STAT_T0(st_loop);
       for (int tile = pair_id; tile < tiles && ok; tile += num_pairs) {
         const int split = tile % args.splits;   // same in both tile orders
-        const int kb0 = split * args.kb_per_split;
-        const int kb1 = min(total_kb, kb0 + args.kb_per_split);
+        int kb0 = split * args.kb_per_split;
+        int kb1 = min(total_kb, kb0 + args.kb_per_split);
+        if (args.grp_mode) {
+          int sp, mb, nb, e;
+          tile_coords(tile, args, num_m, num_n, sp, mb, nb);
+          if (!grp_tile(args, mb, total_kb, e, kb0, kb1)) continue;
+        }
         PAIR_STAT_T0(st_w0);
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, args.err, kErrTimeoutTmemEmpty, abort_flag)) { ok = false; break; }
         PAIR_STAT_ADD(st_tempty, st_w0);
@@ -332,6 +369,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int tile = pair_id; tile < tiles && aux_ok; tile += num_pairs) {
       int split_unused, mb, nb;
       tile_coords(tile, args, num_m, num_n, split_unused, mb, nb);
+      long long boff = 0;   // grouped, mode 1: this expert's bias block
+      if (args.grp_mode) {
+        int e, g0, g1;
+        if (!grp_tile(args, mb, total_kb, e, g0, g1)) continue;
+        if (args.grp_mode == 1) boff = (long long)e * args.grp_bias_off;
+      }
       const int m = mb * 2 * kBM + rank * kBM + row;
       const int n0 = nb * BN;
       const bool row_ok = m < args.M;
@@ -621,7 +664,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int rr = it * 4 + (lane >> 3);
             const float4 x = scr[rr * 8 + (c4 ^ (rr & 7))];
             float e[4] = {x.x, x.y, x.z, x.w};
-            sq += epilogue_vec4<EPI>(args, row0 + rr, ncol, e, pf[it], row0 + rr < args.M);
+            sq += epilogue_vec4<EPI>(args, row0 + rr, ncol, e, pf[it], row0 + rr < args.M, boff);
           }
           __syncwarp();
           PAIR_STAT_ADD(st_st, st_s0);
@@ -681,7 +724,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             store_bf16x32(out + gcol_of(c), dg, 32);
             store_bf16x32(out + gcol_of(c) + 64, du, 32);
           } else {
-            epilogue_chunk<EPI>(args, m, n, v, row_ok);
+            epilogue_chunk<EPI>(args, m, n, v, row_ok, boff);
           }
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
@@ -694,7 +737,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = half; c < BN / 32; c += 2) {
           float v[32];
           tmem_load_f32x32(tbase + c * 32, v);
-          epilogue_chunk<EPI>(args, m, n0 + c * 32, v, row_ok);
+          epilogue_chunk<EPI>(args, m, n0 + c * 32, v, row_ok, boff);
         }
       }
       tc_fence_before();
@@ -870,10 +913,14 @@ int pcb_gemm_pair_launch(const void* A, int a_mn, long long lda, const void* B, 
   splits = (total_kb + kbps - 1) / kbps;
   args.splits = splits;
   args.kb_per_split = kbps;
+  // grouped GEMM: A of a weight gradient holds one expert's columns (grp_m); B of the rows mode
+  // stacks grp_count expert blocks
+  const long long a_rows = args.grp_mode == 2 ? args.grp_m : M;
+  const long long b_ext = (args.grp_mode == 1 ? args.grp_count : 1) * (long long)(b_mn ? K : N);
   CUtensorMap ta, tb;
-  bool ok = a_mn == 0 ? make_map2(&ta, A, K, M, lda, 64, 128) : make_map2(&ta, A, M, K, lda, 64, 64);
+  bool ok = a_mn == 0 ? make_map2(&ta, A, K, a_rows, lda, 64, 128) : make_map2(&ta, A, a_rows, K, lda, 64, 64);
   if (!ok) return -5;
-  ok = b_mn == 0 ? make_map2(&tb, B, K, N, ldb, 64, bn / 2) : make_map2(&tb, B, N, K, ldb, 64, 64);
+  ok = b_mn == 0 ? make_map2(&tb, B, K, b_ext, ldb, 64, bn / 2) : make_map2(&tb, B, N, b_ext, ldb, 64, 64);
   if (!ok) return -5;
   // Tile order: the pairs running at once should share the operand with the larger footprint, so that
   // it crosses from DRAM once per wave. With A larger (M > N) the column blocks of one row block run
@@ -913,4 +960,33 @@ int pcb_gemm_pair_launch(const void* A, int a_mn, long long lda, const void* B, 
   const int pairs = tiles < max_pairs ? tiles : max_pairs;
   return bn == 256 ? dispatch_pair<256>(epi, ta, tb, tc, td, args, 2 * pairs, stream)
                    : dispatch_pair<128>(epi, ta, tb, tc, td, args, 2 * pairs, stream);
+}
+
+// Grouped (mixture-of-experts) GEMM: validates the group description and runs the CTA-pair kernel
+// with one split.  Mode 1 (rows): A is the expert-sorted activation buffer [M = capacity, K], K-major;
+// B stacks grp_count expert blocks ([grp_count * N, K] K-major or [grp_count * K, N] MN-major, K a
+// multiple of 64 so that no k-block reaches into the next expert); the bias, if any, stacks grp_count
+// blocks of N.  Mode 2 (K, weight gradients): A [capacity, grp_m] and B [capacity, N] are both MN-major
+// over the sorted buffer, C is [grp_count * grp_m, N] fp32 accumulated with EPI_RED_F32.
+int pcb_gemm_grouped_launch(const void* A, int a_mn, long long lda, const void* B, int b_mn, long long ldb, int epi,
+                            GemmArgs args, int num_sms, cudaStream_t stream) {
+  if (args.grp_seg == nullptr || args.grp_count < 1 || args.grp_count > 4096) return -6;
+  if ((reinterpret_cast<uintptr_t>(args.grp_seg) & 3) != 0) return -6;
+  if (args.grp_mode == 1) {
+    if (a_mn != 0 || args.M % 256 != 0) return -6;
+    if (b_mn != 0 && args.K % 64 != 0) return -6;
+    if (!(epi == EPI_F32 || epi == EPI_GELU || epi == EPI_GELU_BWD)) return -6;
+    args.grp_b_off = b_mn ? args.K : args.N;
+    args.grp_bias_off = args.N;
+  } else if (args.grp_mode == 2) {
+    if (a_mn != 1 || b_mn != 1 || args.grp_m <= 0 || args.grp_m % 256 != 0 ||
+        (long long)args.M != (long long)args.grp_count * args.grp_m || args.K % 256 != 0)
+      return -6;
+    if (epi != EPI_RED_F32 || args.bias != nullptr) return -6;
+  } else {
+    return -6;
+  }
+  if (args.ag_world > 1 || args.rope_cs != nullptr) return -6;
+  const int bn = args.N >= 256 ? 256 : 128;
+  return pcb_gemm_pair_launch(A, a_mn, lda, B, b_mn, ldb, epi, args, bn, 1, num_sms, stream);
 }

@@ -73,6 +73,21 @@ struct GemmArgs {
   // EPI_BF16 / EPI_SWIGLU on the CTA-pair kernel: 1 when the launcher built tensor maps of the outputs,
   // so the epilogue stages bf16 boxes in shared memory and writes them with TMA stores
   int c_tma;
+  // grouped GEMM (CTA-pair kernel only; mixture-of-experts FFNs).  grp_seg[0..grp_count] are the row
+  // offsets of the experts' segments in a token buffer sorted by expert, each a multiple of 256 (the
+  // pair tile); grp_seg[grp_count] is the number of rows in use.
+  //   grp_mode 1 (rows): the M rows are the sorted buffer; a 256-row tile belongs to the expert whose
+  //     segment holds it and reads that expert's block of B (B's N coordinate + e * grp_b_off when B is
+  //     K-major, its K coordinate + e * grp_b_off when MN-major) and bias (+ e * grp_bias_off); tiles
+  //     past the rows in use are skipped
+  //   grp_mode 2 (K): weight gradients; the output stacks grp_count blocks of grp_m rows, block e
+  //     contracts over the rows of segment e only (A and B MN-major over the sorted buffer)
+  const int* grp_seg;
+  int grp_count;
+  int grp_mode;
+  int grp_m;
+  long long grp_b_off;
+  long long grp_bias_off;
 };
 
 // Pair-kernel cycle counters (builds with PCB_GEMM_STATS): copies 12 counters to `out` and clears them.
@@ -86,3 +101,9 @@ int pcb_gemm_pair_stats(unsigned long long* out);
 int pcb_gemm_launch(const void* A, int a_mn, long long lda, const void* B, int b_mn, long long ldb,
                     int epi, pcb::GemmArgs args, int force_bn, int force_splits, int num_sms,
                     cudaStream_t stream);
+
+// Grouped (mixture-of-experts) GEMM on the CTA-pair kernel: `args` carries the grp_* fields (see
+// GemmArgs); M, N, K are per expert except M in mode 1 (the sorted buffer's capacity) and K in mode 2
+// (likewise).  Returns 0 on success, -1 bad operands, -6 bad group description.
+int pcb_gemm_grouped_launch(const void* A, int a_mn, long long lda, const void* B, int b_mn, long long ldb,
+                            int epi, pcb::GemmArgs args, int num_sms, cudaStream_t stream);

@@ -108,7 +108,7 @@ PCB_DEVICE void tmem_load_f32x32(uint32_t taddr, float (&v)[32]) {
 
 // One 32-column chunk of a "plain" epilogue (everything except the SwiGLU pairs).
 template <int EPI>
-PCB_DEVICE void epilogue_chunk(const GemmArgs& a, int m, int n, float (&v)[32], bool row_ok) {
+PCB_DEVICE void epilogue_chunk(const GemmArgs& a, int m, int n, float (&v)[32], bool row_ok, long long boff = 0) {
   const int nvalid = min(32, a.N - n);
   if (!row_ok || nvalid <= 0) return;
   if (EPI == EPI_BF16 || EPI == EPI_F32 || EPI == EPI_ACC_F32 || EPI == EPI_GELU || EPI == EPI_RESID_F32) {
@@ -116,8 +116,8 @@ PCB_DEVICE void epilogue_chunk(const GemmArgs& a, int m, int n, float (&v)[32], 
     for (int j = 0; j < 32; ++j) v[j] *= a.alpha;
     if (a.bias != nullptr) {
       float b[32];
-      if (a.bias_bf16) load_bf16x32(reinterpret_cast<const __nv_bfloat16*>(a.bias) + n, b, nvalid);
-      else load_f32x32(reinterpret_cast<const float*>(a.bias) + n, b, nvalid);
+      if (a.bias_bf16) load_bf16x32(reinterpret_cast<const __nv_bfloat16*>(a.bias) + boff + n, b, nvalid);
+      else load_f32x32(reinterpret_cast<const float*>(a.bias) + boff + n, b, nvalid);
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] += b[j];
     }
@@ -350,7 +350,8 @@ PCB_DEVICE void epi_prefetch(const GemmArgs& a, int m, int n, float (&p)[8], boo
 }
 
 template <int EPI>
-PCB_DEVICE float epilogue_vec4(const GemmArgs& a, int m, int n, float (&v)[4], const float (&p)[8], bool row_ok) {
+PCB_DEVICE float epilogue_vec4(const GemmArgs& a, int m, int n, float (&v)[4], const float (&p)[8], bool row_ok,
+                                long long boff = 0) {
   const int nv = min(4, a.N - n);
   if (!row_ok || nv <= 0) return 0.f;
   if (EPI == EPI_BF16 || EPI == EPI_F32 || EPI == EPI_ACC_F32 || EPI == EPI_GELU || EPI == EPI_RESID_F32) {
@@ -358,8 +359,8 @@ PCB_DEVICE float epilogue_vec4(const GemmArgs& a, int m, int n, float (&v)[4], c
     for (int j = 0; j < 4; ++j) v[j] *= a.alpha;
     if (a.bias != nullptr) {
       float b[4];
-      if (a.bias_bf16) ld_bf16x4(reinterpret_cast<const __nv_bfloat16*>(a.bias) + n, b, nv);
-      else ld_f32x4(reinterpret_cast<const float*>(a.bias) + n, b, nv);
+      if (a.bias_bf16) ld_bf16x4(reinterpret_cast<const __nv_bfloat16*>(a.bias) + boff + n, b, nv);
+      else ld_f32x4(reinterpret_cast<const float*>(a.bias) + boff + n, b, nv);
 #pragma unroll
       for (int j = 0; j < 4; ++j) v[j] += b[j];
     }

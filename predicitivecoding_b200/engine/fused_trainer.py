@@ -30,6 +30,7 @@ from typing import Dict, List, Optional, Sequence
 import torch
 
 from .. import ops
+from ..ops import moe as moe_ops
 from ..utils.trace import nvtx_range
 from ..models.config import DecoderLmConfig
 from ..models.decoder_lm import DecoderLM, rope_tables
@@ -39,7 +40,8 @@ from .arena import ParamArena, ParamSpec
 def supports(cfg: DecoderLmConfig, seq: Optional[int] = None) -> bool:
     """True when ``cfg`` can run on the fused device path."""
     s = seq or cfg.max_seq
-    return (cfg.use_rms_norm and cfg.use_rope and cfg.block_pattern is None and cfg.num_experts == 0
+    moe_ok = cfg.num_experts == 0 or moe_ops.supported(cfg.dim, cfg.ff_dim, cfg.num_experts, cfg.moe_top_k)
+    return (cfg.use_rms_norm and cfg.use_rope and cfg.block_pattern is None and moe_ok
             and cfg.num_loops == 1 and cfg.mtp_weight == 0 and not cfg.use_plan and cfg.dropout == 0
             and cfg.head_dim in (64, 128) and s % 128 == 0 and cfg.dim % 64 == 0 and cfg.ff_dim % 64 == 0)
 
@@ -67,8 +69,9 @@ class FusedDecoderTrainer:
                  decay_all: bool = True, process_group=None, grad_sync: str = "auto", use_graph: bool = True):
         seq = seq or cfg.max_seq
         if not supports(cfg, seq):
-            raise NotImplementedError("FusedDecoderTrainer needs a dense RMSNorm+RoPE config "
-                                      "(head_dim 64/128, seq % 128 == 0); use the autograd path.")
+            raise NotImplementedError("FusedDecoderTrainer needs an RMSNorm+RoPE config (head_dim 64/128, "
+                                      "seq % 128 == 0; with experts: dim and ff_dim % 256 == 0, <= 64 experts, "
+                                      "top-k <= 8); use the autograd path.")
         self.cfg, self.B, self.S = cfg, batch, seq
         self.M = batch * seq
         self.device = torch.device(device)
@@ -104,6 +107,13 @@ class FusedDecoderTrainer:
         for l in range(L):
             specs.append(ParamSpec(f"b{l}.wqkv", (3 * D, D)))
             specs.append(ParamSpec(f"b{l}.wo", (D, D)))
+            if cfg.num_experts > 0:
+                # expert e's blocks: router row e, W1_e^T rows [e F, (e+1) F), W2_e^T rows [e D, (e+1) D)
+                E = cfg.num_experts
+                specs.append(ParamSpec(f"b{l}.router", (E, D)))
+                specs.append(ParamSpec(f"b{l}.ew1", (E * F_, D)))
+                specs.append(ParamSpec(f"b{l}.ew2", (E * D, F_)))
+                continue
             if cfg.ffn == "swiglu":
                 specs.append(ParamSpec(f"b{l}.w13", (2 * F_, D)))
             else:
@@ -113,7 +123,10 @@ class FusedDecoderTrainer:
         for l in range(L):
             specs.append(ParamSpec(f"b{l}.ln1", (D,), decay_all))
             specs.append(ParamSpec(f"b{l}.ln2", (D,), decay_all))
-            if cfg.ffn == "gelu":
+            if cfg.num_experts > 0:
+                specs.append(ParamSpec(f"b{l}.eb1", (cfg.num_experts * F_,), decay_all))
+                specs.append(ParamSpec(f"b{l}.eb2", (cfg.num_experts * D,), decay_all))
+            elif cfg.ffn == "gelu":
                 specs.append(ParamSpec(f"b{l}.b1", (F_,), decay_all))
                 specs.append(ParamSpec(f"b{l}.b2", (D,), decay_all))
         specs.append(ParamSpec("lnf", (D,), decay_all))
@@ -178,8 +191,16 @@ class FusedDecoderTrainer:
         self.ao = [z(M, D) for _ in range(L)]
         self.lse = [z(batch * H, S, dt=f32) for _ in range(L)]
         fpre = 2 * F_ if cfg.ffn == "swiglu" else F_
-        self.pre = [z(M, fpre) for _ in range(L)]
-        self.act = [z(M, F_) for _ in range(L)]
+        if cfg.num_experts > 0:
+            E, k = cfg.num_experts, cfg.moe_top_k
+            self.moe = [moe_ops.MoEBuffers.allocate(M, D, F_, E, k, dev) for _ in range(L)]
+            self.moe_scr = moe_ops.MoEScratch.allocate(M, D, F_, E, k, dev)
+            self.moe_aux = z(1, dt=f32)   # weighted balance losses of the step (in summed-row units)
+            self.pre, self.act = [], []
+        else:
+            self.moe = None
+            self.pre = [z(M, fpre) for _ in range(L)]
+            self.act = [z(M, F_) for _ in range(L)]
         self.nf = z(M, D)
         self.invf = z(M, dt=f32)
         self.logits = z(M, V)
@@ -189,7 +210,7 @@ class FusedDecoderTrainer:
         self.dx = z(M, D, dt=f32)
         self.dx16 = z(M, D)
         self.dn = z(M, D, dt=f32)
-        self.dpre = z(M, fpre)
+        self.dpre = z(M, fpre) if cfg.num_experts == 0 else None
         self.dao = z(M, D)
         self.dqkv = z(M, 3 * D)
         self.dq_acc = z(M, D, dt=f32)
@@ -205,8 +226,13 @@ class FusedDecoderTrainer:
         cfg = self.cfg
         out = [["wout", "lnf"]]
         for l in reversed(range(cfg.num_blocks)):
-            names = [f"b{l}.wqkv", f"b{l}.wo", f"b{l}.w2", f"b{l}.ln1", f"b{l}.ln2"]
-            names += [f"b{l}.w13"] if cfg.ffn == "swiglu" else [f"b{l}.w1", f"b{l}.b1", f"b{l}.b2"]
+            names = [f"b{l}.wqkv", f"b{l}.wo", f"b{l}.ln1", f"b{l}.ln2"]
+            if cfg.num_experts > 0:
+                names += [f"b{l}.router", f"b{l}.ew1", f"b{l}.ew2", f"b{l}.eb1", f"b{l}.eb2"]
+            elif cfg.ffn == "swiglu":
+                names += [f"b{l}.w2", f"b{l}.w13"]
+            else:
+                names += [f"b{l}.w2", f"b{l}.w1", f"b{l}.b1", f"b{l}.b2"]
             out.append(names)
         out.append(["wemb"])
         return out
@@ -253,6 +279,15 @@ class FusedDecoderTrainer:
             V[f"b{l}.wo"].copy_(blk.wo.detach().T.cpu())
             V[f"b{l}.ln1"].copy_(blk.ln1_g.detach().cpu())
             V[f"b{l}.ln2"].copy_(blk.ln2_g.detach().cpu())
+            if cfg.num_experts > 0:
+                E, D, F_ = cfg.num_experts, cfg.dim, cfg.ff_dim
+                V[f"b{l}.router"].copy_(blk.router.detach().T.cpu())
+                for e in range(E):
+                    V[f"b{l}.ew1"][e * F_:(e + 1) * F_].copy_(blk.ew1[e].detach().T.cpu())
+                    V[f"b{l}.ew2"][e * D:(e + 1) * D].copy_(blk.ew2[e].detach().T.cpu())
+                    V[f"b{l}.eb1"][e * F_:(e + 1) * F_].copy_(blk.eb1[e].detach().cpu())
+                    V[f"b{l}.eb2"][e * D:(e + 1) * D].copy_(blk.eb2[e].detach().cpu())
+                continue
             if cfg.ffn == "swiglu":
                 V[f"b{l}.w13"].copy_(_interleave_gate_up(blk.w1.detach().T.cpu(), blk.w3.detach().T.cpu()))
             else:
@@ -293,6 +328,15 @@ class FusedDecoderTrainer:
             blk.wo.copy_(V[f"b{l}.wo"].T)
             blk.ln1_g.copy_(V[f"b{l}.ln1"])
             blk.ln2_g.copy_(V[f"b{l}.ln2"])
+            if cfg.num_experts > 0:
+                E, F_ = cfg.num_experts, cfg.ff_dim
+                blk.router.copy_(V[f"b{l}.router"].T)
+                for e in range(E):
+                    blk.ew1[e].copy_(V[f"b{l}.ew1"][e * F_:(e + 1) * F_].T)
+                    blk.ew2[e].copy_(V[f"b{l}.ew2"][e * D:(e + 1) * D].T)
+                    blk.eb1[e].copy_(V[f"b{l}.eb1"][e * F_:(e + 1) * F_])
+                    blk.eb2[e].copy_(V[f"b{l}.eb2"][e * D:(e + 1) * D])
+                continue
             if cfg.ffn == "swiglu":
                 g, u = _split_gate_up(V[f"b{l}.w13"])
                 blk.w1.copy_(g.T)
@@ -357,6 +401,8 @@ class FusedDecoderTrainer:
         W = self.W
         B, S, M, D, H, hd = self.B, self.S, self.M, cfg.dim, cfg.num_heads, cfg.head_dim
         ops.embed_fwd(self.tok, W["wemb"], self.x[0])
+        if self.moe is not None:
+            self.moe_aux.zero_()
         for l in range(cfg.num_blocks):
             ops.rmsnorm_fwd(self.x[l], W[f"b{l}.ln1"], self.n1[l], self.inv1[l], cfg.eps)
             ops.gemm(self.n1[l], W[f"b{l}.wqkv"], epi=ops.EPI_BF16, c=self.qkv[l],
@@ -364,7 +410,11 @@ class FusedDecoderTrainer:
             ops.attn_fwd(self.qkv[l], self.ao[l], self.lse[l], B, S, H, hd, self.attn_scale)
             ops.gemm(self.ao[l], W[f"b{l}.wo"], epi=ops.EPI_RESID_F32, c=self.xmid[l], aux=self.x[l])
             ops.rmsnorm_fwd(self.xmid[l], W[f"b{l}.ln2"], self.n2[l], self.inv2[l], cfg.eps)
-            if cfg.ffn == "swiglu":
+            if self.moe is not None:
+                moe_ops.forward(self.n2[l], self.xmid[l], self.x[l + 1], W[f"b{l}.router"], W[f"b{l}.ew1"],
+                                W[f"b{l}.eb1"], W[f"b{l}.ew2"], W[f"b{l}.eb2"], cfg.moe_top_k, self.moe[l],
+                                self.moe_aux, cfg.moe_balance_weight * M)
+            elif cfg.ffn == "swiglu":
                 ops.gemm(self.n2[l], W[f"b{l}.w13"], epi=ops.EPI_SWIGLU, c=self.pre[l], d=self.act[l])
                 ops.gemm(self.act[l], W[f"b{l}.w2"], epi=ops.EPI_RESID_F32, c=self.x[l + 1], aux=self.xmid[l])
             else:
@@ -378,6 +428,8 @@ class FusedDecoderTrainer:
         ops.cross_entropy(self.logits[:, :self.Vr], self.tgt, self.loss_rows, 1.0 / M, write_grad)
         self.loss_sum.zero_()
         ops.sumsq(self.loss_rows, self.loss_sum, square=False)
+        if self.moe is not None:
+            ops.sumsq(self.moe_aux, self.loss_sum, square=False)
 
     def _backward(self) -> None:
         cfg = self.cfg
@@ -392,12 +444,17 @@ class FusedDecoderTrainer:
         self._bucket_done(0)
         for l in reversed(range(L)):
             # ---- FFN: x_{l+1} = xmid + ffn(norm2(xmid))
-            ops.gemm(self.dx16, self.act[l], a_mn=True, b_mn=True, epi=RED, c=G[f"b{l}.w2"])
-            if cfg.ffn == "swiglu":
+            if self.moe is not None:
+                moe_ops.backward(self.dx, self.n2[l], self.dn, W[f"b{l}.router"], W[f"b{l}.ew1"], W[f"b{l}.ew2"],
+                                 cfg.moe_top_k, self.moe[l], self.moe_scr, G[f"b{l}.router"], G[f"b{l}.ew1"],
+                                 G[f"b{l}.eb1"], G[f"b{l}.ew2"], G[f"b{l}.eb2"], cfg.moe_balance_weight)
+            elif cfg.ffn == "swiglu":
+                ops.gemm(self.dx16, self.act[l], a_mn=True, b_mn=True, epi=RED, c=G[f"b{l}.w2"])
                 ops.gemm(self.dx16, W[f"b{l}.w2"], b_mn=True, epi=ops.EPI_SWIGLU_BWD, c=self.dpre, aux=self.pre[l])
                 ops.gemm(self.dpre, self.n2[l], a_mn=True, b_mn=True, epi=RED, c=G[f"b{l}.w13"])
                 ops.gemm(self.dpre, W[f"b{l}.w13"], b_mn=True, epi=ops.EPI_F32, c=self.dn)
             else:
+                ops.gemm(self.dx16, self.act[l], a_mn=True, b_mn=True, epi=RED, c=G[f"b{l}.w2"])
                 ops.colsum(self.dx16, G[f"b{l}.b2"])
                 ops.gemm(self.dx16, W[f"b{l}.w2"], b_mn=True, epi=ops.EPI_GELU_BWD, c=self.dpre, aux=self.pre[l])
                 ops.colsum(self.dpre, G[f"b{l}.b1"])
@@ -542,7 +599,10 @@ class FusedDecoderTrainer:
         """Model FLOPs of one step (6*N*T for the matmuls + causal attention fwd/bwd)."""
         cfg = self.cfg
         D, F_, V, L = cfg.dim, cfg.ff_dim, cfg.vocab, cfg.num_blocks
-        ffn = (3 if cfg.ffn == "swiglu" else 2) * D * F_
+        if cfg.num_experts > 0:
+            ffn = cfg.moe_top_k * 2 * D * F_ + D * cfg.num_experts   # k routed experts + the router
+        else:
+            ffn = (3 if cfg.ffn == "swiglu" else 2) * D * F_
         mat = L * (4 * D * D + ffn) + V * D
         attn = L * 2 * 2 * self.S * D / 2  # QK^T and PV, causal half, per token
         return 6.0 * mat * self.M + 3.0 * attn * self.M

@@ -17,7 +17,7 @@ from . import (ext, gemm, gemm_pc, attn_fwd, attn_bwd, EPI_BF16, EPI_F32, EPI_RE
                EPI_RED_F32, EPI_PC_PRED, EPI_PC_STATE)
 
 CASES = ("gemm_swiglu", "gemm_lmhead", "gemm_dw", "pc_pred", "pc_state", "attn_fwd", "attn_fwd_mma", "attn_bwd",
-         "attn_fwd_d128", "attn_fwd_mma_d128", "attn_bwd_d128")
+         "attn_fwd_d128", "attn_fwd_mma_d128", "attn_bwd_d128", "moe_fwd", "moe_layer")
 
 
 def build(which: str, dev: str = "cuda"):
@@ -78,6 +78,27 @@ def build(which: str, dev: str = "cuda"):
         dv = torch.empty(B * H, S, device=dev)
         dqkv = torch.empty_like(qkv)
         return (lambda: attn_bwd(qkv, o, do, lse, dv, dq, dqkv, B, S, H, hd, sc)), 5 * causal_mm
+    if which in ("moe_fwd", "moe_layer"):
+        # mixture-of-experts FFN layer: 16 x 1024 tokens, d 768, 8 GELU experts of 3072, top-2
+        from . import moe
+        M, D, F_, E, k = 16384, 768, 3072, 8, 2
+        x = rn(M, D).to(bf)
+        router, w1, w2 = rn(E, D, scale=0.05).to(bf), rn(E * F_, D, scale=0.03).to(bf), rn(E * D, F_, scale=0.02).to(bf)
+        b1, b2 = torch.zeros(E * F_, device=dev), torch.zeros(E * D, device=dev)
+        res, out = rn(M, D), torch.empty(M, D, device=dev)
+        buf = moe.MoEBuffers.allocate(M, D, F_, E, k, dev)
+        flops = k * M * 2 * 2 * D * F_
+        if which == "moe_fwd":
+            return (lambda: moe.forward(x, res, out, router, w1, b1, w2, b2, k, buf)), flops
+        scr = moe.MoEScratch.allocate(M, D, F_, E, k, dev)
+        dx, dn = rn(M, D), torch.empty(M, D, device=dev)
+        grads = [torch.zeros(E, D, device=dev), torch.zeros(E * F_, D, device=dev), torch.zeros(E * F_, device=dev),
+                 torch.zeros(E * D, F_, device=dev), torch.zeros(E * D, device=dev)]
+
+        def layer():
+            moe.forward(x, res, out, router, w1, b1, w2, b2, k, buf)
+            moe.backward(dx, x, dn, router, w1, w2, k, buf, scr, *grads, 0.01)
+        return layer, 3 * flops
     raise ValueError(f"unknown case {which!r}; one of {CASES}")
 
 
