@@ -250,7 +250,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int gw = warp >> 2;
     const int r = threadIdx.x & 127;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
-    const float c = scale * kLog2e;
+    const float cl = scale * kLog2e;
     int lc = 0, tcount = 0, ic = 0;
     bool ok = true;
     for (int i = snake_item(0); i < n_items && ok; i = snake_item(++ic)) {
@@ -265,24 +265,41 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float* sd = dvec + (long long)it.bh * S + qi * kQT + 32 * gw;
         // key r is visible to query column q of this tile iff r <= q + 64 * (qi - 2 kb)
         const int lim = r - 64 * (qi - 2 * it.kb);
-        float lv[32], dv[32];
-#pragma unroll
-        for (int e = 0; e < 32; e += 4) {
-          const float4 l4 = *reinterpret_cast<const float4*>(sl + e);
-          const float4 d4 = *reinterpret_cast<const float4*>(sd + e);
-          lv[e] = l4.x * kLog2e;
-          lv[e + 1] = l4.y * kLog2e;
-          lv[e + 2] = l4.z * kLog2e;
-          lv[e + 3] = l4.w * kLog2e;
-          dv[e] = d4.x;
-          dv[e + 1] = d4.y;
-          dv[e + 2] = d4.z;
-          dv[e + 3] = d4.w;
+        {   // pull the next tile's lse / delta line (this warpgroup's 32 queries) into L1 meanwhile
+          int nbh = it.bh, nq = qi + 1;
+          if (nq >= TQ) {
+            const int ni = snake_item(ic + 1);
+            nbh = ni < n_items ? ni % BH : -1;
+            nq = ni < n_items ? 2 * (ni / BH) : 0;
+          }
+          if (nbh >= 0 && lane < 2)
+            prefetch_l1((lane == 0 ? lse : dvec) + (long long)nbh * S + nq * kQT + 32 * gw);
         }
-        uint32_t su[32], du[32];
-        tmem_ld_32x32b_x32(lane_base + TM_S + 32 * gw, su);
-        tmem_ld_32x32b_x32(lane_base + TM_DP + 32 * gw, du);
-        tmem_ld_wait();
+        // this warpgroup's 32 query columns in two chunks of 16: chunk 1's TMEM and L1 loads are in flight
+        // while chunk 0 is finished
+        uint32_t su[2][16], du[2][16];
+        float lv[2][16], dv[2][16];
+        auto fetch = [&](int c, int b) {
+          tmem_ld_32x32b_x16(lane_base + TM_S + 32 * gw + 16 * c, su[b]);
+          tmem_ld_32x32b_x16(lane_base + TM_DP + 32 * gw + 16 * c, du[b]);
+#pragma unroll
+          for (int e = 0; e < 16; e += 4) {
+            const float4 l4 = *reinterpret_cast<const float4*>(sl + 16 * c + e);
+            const float4 d4 = *reinterpret_cast<const float4*>(sd + 16 * c + e);
+            lv[b][e] = -l4.x * kLog2e;
+            lv[b][e + 1] = -l4.y * kLog2e;
+            lv[b][e + 2] = -l4.z * kLog2e;
+            lv[b][e + 3] = -l4.w * kLog2e;
+            dv[b][e] = -d4.x;
+            dv[b][e + 1] = -d4.y;
+            dv[b][e + 2] = -d4.z;
+            dv[b][e + 3] = -d4.w;
+          }
+        };
+        fetch(0, 0);
+        fetch(1, 1);
+        tmem_ld_wait_regs(su[0], du[0]);
+        tmem_ld_wait_regs(su[1], du[1]);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(s_free);   // S/dP of this warp are in registers: the next tile's MMAs may start
@@ -292,27 +309,30 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = mbar_wait(&grad_done[tcount & 1], ((tcount - 2) >> 1) & 1, err, kErrTimeoutTmemFull, abort_flag);
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
         tc_fence_after();
-        uint32_t pk[16], dk[16];
-#pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          float p[2], ds[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int q = 32 * gw + e + u;
-            p[u] = q >= lim ? ex2_approx(fmaf(__uint_as_float(su[e + u]), c, -lv[e + u])) : 0.f;
-            ds[u] = p[u] * (__uint_as_float(du[e + u]) - dv[e + u]);
-          }
-          pk[e >> 1] = pack_bf16x2(p[0], p[1]);
-          dk[e >> 1] = pack_bf16x2(ds[0], ds[1]);
-        }
-        tmem_st_32x32b_x16(lane_base + TM_P + 16 * gw, pk);
         // dS^T row r: 16-byte chunk j (8 queries) at ((j ^ (r & 7)) << 4); this warpgroup owns chunks 4gw..4gw+3
         uint8_t* drow = sDS + (tcount & 1) * kAtom + r * 128;
 #pragma unroll
-        for (int ch = 0; ch < 4; ++ch) {
-          const int chunk = 4 * gw + ch;
-          *reinterpret_cast<uint4*>(drow + ((chunk ^ (r & 7)) << 4)) =
-              make_uint4(dk[4 * ch], dk[4 * ch + 1], dk[4 * ch + 2], dk[4 * ch + 3]);
+        for (int c = 0; c < 2; ++c) {
+          uint32_t pk[8], dk[8];
+#pragma unroll
+          for (int e = 0; e < 16; e += 2) {
+            const int q = 32 * gw + 16 * c + e;
+            float x0, x1, p0, p1, g0, g1;
+            ffma2v(x0, x1, __uint_as_float(su[c][e]), __uint_as_float(su[c][e + 1]), cl, lv[c][e], lv[c][e + 1]);
+            p0 = q >= lim ? ex2_approx(x0) : 0.f;
+            p1 = q + 1 >= lim ? ex2_approx(x1) : 0.f;
+            fmul_add2(g0, g1, p0, p1, __uint_as_float(du[c][e]), __uint_as_float(du[c][e + 1]), dv[c][e],
+                      dv[c][e + 1]);
+            pk[e >> 1] = pack_bf16_alu(p0, p1);
+            dk[e >> 1] = pack_bf16_alu(g0, g1);
+          }
+          tmem_st_32x32b_x8(lane_base + TM_P + 16 * gw + 8 * c, pk);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int chunk = 4 * gw + 2 * c + h;
+            *reinterpret_cast<uint4*>(drow + ((chunk ^ (r & 7)) << 4)) =
+                make_uint4(dk[4 * h], dk[4 * h + 1], dk[4 * h + 2], dk[4 * h + 3]);
+          }
         }
         tmem_st_wait();
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

@@ -281,6 +281,47 @@ PCB_DEVICE uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// Elementwise helpers of the attention backward's gradient warpgroups.  Exponentials share the SFU pipe with float -> bf16 conversions, so the
+// bf16 packing runs on the ALU (round half away from zero on the bit pattern: adding half a bf16 ulp
+// and keeping the high halves; differs from round-to-nearest-even only on exact ties, keeps signs,
+// infinities and NaNs) and the scale / difference / product arithmetic on paired fp32 instructions.
+// Bring the 128-byte line holding p into this SM's L1 (no register result, nothing to wait for).
+PCB_DEVICE void prefetch_l1(const void* p) { asm volatile("prefetch.global.L1 [%0];" ::"l"(p)); }
+PCB_DEVICE uint32_t pack_bf16_alu(float lo, float hi) {
+  return __byte_perm(__float_as_uint(lo) + 0x8000u, __float_as_uint(hi) + 0x8000u, 0x7632);
+}
+PCB_DEVICE void ffma2v(float& d0, float& d1, float a0, float a1, float b, float c0, float c1) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %4};\n\t"
+      "mov.b64 rc, {%5, %6};\n\tfma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b), "f"(c0), "f"(c1));
+}
+// (d0, d1) = (p0 * (a0 + b0), p1 * (a1 + b1))
+PCB_DEVICE void fmul_add2(float& d0, float& d1, float p0, float p1, float a0, float a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rp, rs, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mov.b64 rp, {%6, %7};\n\tadd.rn.f32x2 rs, ra, rb;\n\tmul.rn.f32x2 rd, rp, rs;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(p0), "f"(p1));
+}
+PCB_DEVICE void tmem_st_32x32b_x8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
+               "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+// tcgen05.wait::ld that names the registers of the loads it completes, so the compiler cannot move a use
+// of them above the wait (loads into the other buffer stay in flight across the arithmetic)
+PCB_DEVICE void tmem_ld_wait_regs(uint32_t (&a)[16], uint32_t (&b)[16]) {
+  asm volatile(
+      "tcgen05.wait::ld.sync.aligned;"
+      : "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(a[4]), "+r"(a[5]), "+r"(a[6]), "+r"(a[7]),
+        "+r"(a[8]), "+r"(a[9]), "+r"(a[10]), "+r"(a[11]), "+r"(a[12]), "+r"(a[13]), "+r"(a[14]), "+r"(a[15]),
+        "+r"(b[0]), "+r"(b[1]), "+r"(b[2]), "+r"(b[3]), "+r"(b[4]), "+r"(b[5]), "+r"(b[6]), "+r"(b[7]),
+        "+r"(b[8]), "+r"(b[9]), "+r"(b[10]), "+r"(b[11]), "+r"(b[12]), "+r"(b[13]), "+r"(b[14]), "+r"(b[15])
+      :
+      : "memory");
+}
+
 PCB_DEVICE float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

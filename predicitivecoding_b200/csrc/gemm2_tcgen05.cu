@@ -56,7 +56,7 @@ struct Cfg {
   // per epilogue warp: 8 KB for the epilogues that stage two TMA boxes (bf16 output, SwiGLU, residual,
   // SwiGLU backward), 4 KB for the [32 x 32] fp32 transpose scratch of the coalesced path
   static constexpr bool kTwoBoxes =
-      EPI == EPI_BF16 || EPI == EPI_SWIGLU || EPI == EPI_RESID_F32 || EPI == EPI_SWIGLU_BWD;
+      EPI == EPI_BF16 || EPI == EPI_SWIGLU || EPI == EPI_RESID_F32 || EPI == EPI_SWIGLU_BWD || EPI == EPI_GELU_BWD;
   static constexpr int EPI_WARP_BYTES = kTwoBoxes ? 8192 : 4096;
   // the deepest operand ring that fits: 227 KB - 1 KB (barriers, alignment gap) - staging - 1 KB slack
   static constexpr int STAGES_FIT = (232448 - 2048 - 8 * EPI_WARP_BYTES) / STAGE_BYTES;
@@ -163,7 +163,7 @@ PCB_DEVICE void gather_chunks(const GemmArgs& a, int tid, int nthreads) {
 // pre-activations): with tensor maps, each warp loads its [32 x 32] input boxes by TMA into its
 // staging buffer, finishes them in place and stores them by TMA.
 template <int EPI>
-PCB_DEVICE constexpr bool aux_tma() { return EPI == EPI_RESID_F32 || EPI == EPI_SWIGLU_BWD; }
+PCB_DEVICE constexpr bool aux_tma() { return EPI == EPI_RESID_F32 || EPI == EPI_SWIGLU_BWD || EPI == EPI_GELU_BWD; }
 
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -384,8 +384,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint64_t* bar = &aux_bar[(warp - 2) * 2 + buf];
         uint8_t* box = aux_stage + buf * 4096;
         const int n = n0 + (half + 2 * i) * 32;
-        mbar_arrive_expect_tx(bar, 4096);
-        if (EPI == EPI_RESID_F32) {
+        mbar_arrive_expect_tx(bar, EPI == EPI_GELU_BWD ? 2048 : 4096);
+        if (EPI == EPI_RESID_F32 || EPI == EPI_GELU_BWD) {
           tma_load_2d(box, &tmD, bar, n, row0_aux);
         } else {
           const int gx = (n >> 6) * 128 + (n & 63);
@@ -447,6 +447,20 @@ __global__ void __launch_bounds__(kThreads, 1)
               a.w += o[3];
               *cell = a;
             }
+          } else if (EPI == EPI_GELU_BWD) {  // pre box [32 rows x 32] bf16, 64-byte rows, 64-byte swizzle
+            const int sw = (lane >> 1) & 3;
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+              uint4* pp = reinterpret_cast<uint4*>(box + lane * 64 + ((cc ^ sw) << 4));
+              const uint4 p4 = *pp;
+              const uint32_t pw[4] = {p4.x, p4.y, p4.z, p4.w};
+              uint32_t ow[4];
+#pragma unroll
+              for (int k = 0; k < 4; ++k)
+                ow[k] = pack_bf16x2(args.alpha * v[8 * cc + 2 * k] * gelu_tanh_grad_fast(bf16_lo(pw[k])),
+                                    args.alpha * v[8 * cc + 2 * k + 1] * gelu_tanh_grad_fast(bf16_hi(pw[k])));
+              *pp = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+            }
           } else {  // EPI_SWIGLU_BWD: gate box at box, up box at box + 2048 (64-byte rows, 64-byte swizzle)
             const int sw = (lane >> 1) & 3;
 #pragma unroll
@@ -479,7 +493,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            if (EPI == EPI_RESID_F32) {
+            if (EPI == EPI_RESID_F32 || EPI == EPI_GELU_BWD) {
               tma_store_2d(&tmC, box, n, row0_aux);
             } else {
               const int gx = (n >> 6) * 128 + (n & 63);
@@ -950,6 +964,10 @@ int pcb_gemm_pair_launch(const void* A, int a_mn, long long lda, const void* B, 
   if (epi == EPI_RESID_F32 && aux_al && (reinterpret_cast<uintptr_t>(args.C) & 15) == 0 && (args.ldc % 4) == 0 &&
       (args.ldaux % 4) == 0 && make_map2(&tc, args.C, N, M, args.ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B, true) &&
       make_map2(&td, args.aux, N, M, args.ldaux, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B, true))
+    args.c_tma = 1;
+  if (epi == EPI_GELU_BWD && aux_al && c_ok && (args.ldaux % 8) == 0 &&
+      make_map2(&tc, args.C, N, M, args.ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B) &&
+      make_map2(&td, args.aux, N, M, args.ldaux, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
     args.c_tma = 1;
   if (epi == EPI_SWIGLU_BWD && aux_al && c_ok && (args.ldaux % 8) == 0 &&
       make_map2(&tc, args.C, 2 * (long long)N, M, args.ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B) &&

@@ -119,15 +119,28 @@ __global__ void __launch_bounds__(1024, 1)
   const unsigned lt = (1u << lane) - 1u;
   for (int e = lane; e <= kMaxE; e += 32) cnt[w][e] = 0;
   __syncwarp();
+  // the warp's expert ids, 8 batches of 32 at a time so that eight loads are in flight per lane
+  // (clamped: a bad id cannot index out of range)
+  auto load8 = [&](int b0, int (&ex)[8]) {
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int a = b0 + 32 * u + lane;
+      ex[u] = a < a1 ? min(max(topi[a], 0), E - 1) : -1;
+    }
+  };
   // pass 1: counts
-  for (int b = a0; b < a1; b += 32) {
-    const int a = b + lane;
-    const bool v = a < a1;
-    const int ex = v ? min(max(topi[a], 0), E - 1) : -1;   // clamped: a bad id cannot index out of range
-    const unsigned act = __ballot_sync(0xffffffffu, v);
-    const unsigned peers = __match_any_sync(0xffffffffu, ex) & act;
-    if (v && (peers & lt) == 0) cnt[w][ex] += __popc(peers);   // one leader per expert group
-    __syncwarp();
+  for (int b0 = a0; b0 < a1; b0 += 256) {
+    int exv[8];
+    load8(b0, exv);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int ex = exv[u];
+      const bool v = ex >= 0;
+      const unsigned act = __ballot_sync(0xffffffffu, v);
+      const unsigned peers = __match_any_sync(0xffffffffu, ex) & act;
+      if (v && (peers & lt) == 0) cnt[w][ex] += __popc(peers);   // one leader per expert group
+      __syncwarp();
+    }
   }
   // gate sums for the balance loss (fixed order: per thread, then per warp, then over warps)
   {
@@ -190,22 +203,27 @@ __global__ void __launch_bounds__(1024, 1)
   }
   __syncthreads();
   // pass 2: positions, source rows and gates of the sorted rows
-  for (int b = a0; b < a1; b += 32) {
-    const int a = b + lane;
-    const bool v = a < a1;
-    const int ex = v ? min(max(topi[a], 0), E - 1) : -1;
-    const unsigned act = __ballot_sync(0xffffffffu, v);
-    const unsigned peers = __match_any_sync(0xffffffffu, ex) & act;
-    if (v) {
-      const int p = cnt[w][ex] + __popc(peers & lt);
-      const int t = a / k;
-      pos[a] = p;
-      src[p] = t;
-      rgate[p] = gates[(long long)t * E + ex];
+  for (int b0 = a0; b0 < a1; b0 += 256) {
+    int exv[8];
+    load8(b0, exv);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int a = b0 + 32 * u + lane;
+      const int ex = exv[u];
+      const bool v = ex >= 0;
+      const unsigned act = __ballot_sync(0xffffffffu, v);
+      const unsigned peers = __match_any_sync(0xffffffffu, ex) & act;
+      if (v) {
+        const int p = cnt[w][ex] + __popc(peers & lt);
+        const int t = a / k;
+        pos[a] = p;
+        src[p] = t;
+        rgate[p] = gates[(long long)t * E + ex];
+      }
+      __syncwarp();
+      if (v && (peers & lt) == 0) cnt[w][ex] += __popc(peers);
+      __syncwarp();
     }
-    __syncwarp();
-    if (v && (peers & lt) == 0) cnt[w][ex] += __popc(peers);
-    __syncwarp();
   }
   // padding rows of every segment and the rows past the last one
   for (int e = 0; e < E; ++e) {

@@ -127,7 +127,7 @@ def _gelu(x):
     return 0.5 * x * (1 + torch.tanh(0.7978845608 * (x + 0.044715 * x ** 3)))
 
 
-def test_gemm_gelu_and_bwd():
+def test_gemm_gelu_and_bwd(gemm_mode):
     M, N, K = 512, 512, 256
     a, b, ref = _operands(M, N, K, False, False, seed=4)
     ref = ref / 16
