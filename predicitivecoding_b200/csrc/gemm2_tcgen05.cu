@@ -56,7 +56,8 @@ struct Cfg {
   // per epilogue warp: 8 KB for the epilogues that stage two TMA boxes (bf16 output, SwiGLU, residual,
   // SwiGLU backward), 4 KB for the [32 x 32] fp32 transpose scratch of the coalesced path
   static constexpr bool kTwoBoxes =
-      EPI == EPI_BF16 || EPI == EPI_SWIGLU || EPI == EPI_RESID_F32 || EPI == EPI_SWIGLU_BWD || EPI == EPI_GELU_BWD;
+      EPI == EPI_BF16 || EPI == EPI_SWIGLU || EPI == EPI_RESID_F32 || EPI == EPI_SWIGLU_BWD || EPI == EPI_GELU_BWD ||
+      EPI == EPI_GELU;
   static constexpr int EPI_WARP_BYTES = kTwoBoxes ? 8192 : 4096;
   // the deepest operand ring that fits: 227 KB - 1 KB (barriers, alignment gap) - staging - 1 KB slack
   static constexpr int STAGES_FIT = (232448 - 2048 - 8 * EPI_WARP_BYTES) / STAGE_BYTES;
@@ -211,8 +212,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
-    if ((EPI == EPI_BF16 || EPI == EPI_SWIGLU) && args.c_tma) prefetch_tmap(&tmC);
-    if ((EPI == EPI_SWIGLU || aux_tma<EPI>()) && args.c_tma) prefetch_tmap(&tmD);
+    if ((EPI == EPI_BF16 || EPI == EPI_SWIGLU || EPI == EPI_GELU) && args.c_tma) prefetch_tmap(&tmC);
+    if ((EPI == EPI_SWIGLU || EPI == EPI_GELU || aux_tma<EPI>()) && args.c_tma) prefetch_tmap(&tmD);
     if (aux_tma<EPI>() && args.c_tma) prefetch_tmap(&tmC);
   }
   if (warp == 1) {
@@ -507,6 +508,52 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
+      } else if (EPI == EPI_GELU && args.c_tma) {
+        // per 32-column chunk: pre = alpha acc + bias and act = gelu(bf16(pre)), staged as two [32 x 32]
+        // bf16 boxes (64-byte rows, 64-byte swizzle: 16-byte chunk c of row r at c ^ ((r >> 1) & 3)) and
+        // written by TMA stores into C and D; the two box pairs of the staging area alternate
+        uint8_t* stg = smem + C::EPI_OFF + (warp - 2) * C::EPI_WARP_BYTES;
+        const int row0 = mb * 2 * kBM + rank * kBM + q * 32;
+        const int sw = (lane >> 1) & 3;
+#pragma unroll 1
+        for (int i = 0; i < BN / 64; ++i) {
+          const int c = half + 2 * i;
+          const int n = n0 + c * 32;
+          float v[32], bv[32];
+          tmem_load_f32x32(tbase + c * 32, v);
+          if (args.bias != nullptr) {
+            const int nvalid = min(32, args.N - n);
+            if (args.bias_bf16) load_bf16x32(reinterpret_cast<const __nv_bfloat16*>(args.bias) + boff + n, bv, nvalid);
+            else load_f32x32(reinterpret_cast<const float*>(args.bias) + boff + n, bv, nvalid);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) bv[j] = 0.f;
+          }
+          uint32_t pp[16], pa[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            pp[j] = pack_bf16x2(fmaf(v[2 * j], args.alpha, bv[2 * j]), fmaf(v[2 * j + 1], args.alpha, bv[2 * j + 1]));
+            pa[j] = pack_bf16x2(gelu_tanh_fast(bf16_lo(pp[j])), gelu_tanh_fast(bf16_hi(pp[j])));
+          }
+          uint8_t* box = stg + store_box * 4096;
+          if (lane == 0) bulk_group_wait_read<1>();   // the stores that last read this box pair are done
+          __syncwarp();
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            const int off = lane * 64 + ((cc ^ sw) << 4);
+            *reinterpret_cast<uint4*>(box + off) = make_uint4(pp[4 * cc], pp[4 * cc + 1], pp[4 * cc + 2], pp[4 * cc + 3]);
+            *reinterpret_cast<uint4*>(box + 2048 + off) =
+                make_uint4(pa[4 * cc], pa[4 * cc + 1], pa[4 * cc + 2], pa[4 * cc + 3]);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmC, box, n, row0);
+            tma_store_2d(&tmD, box + 2048, n, row0);
+            bulk_group_commit();
+          }
+          store_box ^= 1;
+        }
       } else if (EPI == EPI_SWIGLU && args.c_tma) {
         // per 128-column group: this warp's 32 gate and 32 up columns of pre and the 32 act columns
         // they make, each staged as a [32 x 32] bf16 box (64-byte rows, 64-byte swizzle: 16-byte
@@ -770,7 +817,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
-  if ((EPI == EPI_BF16 || EPI == EPI_SWIGLU || aux_tma<EPI>()) && args.c_tma && warp >= 2 && lane == 0)
+  if ((EPI == EPI_BF16 || EPI == EPI_SWIGLU || EPI == EPI_GELU || aux_tma<EPI>()) && args.c_tma && warp >= 2 &&
+      lane == 0)
     bulk_group_wait_all();  // every TMA store has landed before the CTA exits
   __syncwarp();
   tc_fence_before();
@@ -964,6 +1012,10 @@ int pcb_gemm_pair_launch(const void* A, int a_mn, long long lda, const void* B, 
   if (epi == EPI_RESID_F32 && aux_al && (reinterpret_cast<uintptr_t>(args.C) & 15) == 0 && (args.ldc % 4) == 0 &&
       (args.ldaux % 4) == 0 && make_map2(&tc, args.C, N, M, args.ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B, true) &&
       make_map2(&td, args.aux, N, M, args.ldaux, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B, true))
+    args.c_tma = 1;
+  if (epi == EPI_GELU && c_ok && args.D != nullptr && (reinterpret_cast<uintptr_t>(args.D) & 15) == 0 &&
+      (args.ldd % 8) == 0 && make_map2(&tc, args.C, N, M, args.ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B) &&
+      make_map2(&td, args.D, N, M, args.ldd, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
     args.c_tma = 1;
   if (epi == EPI_GELU_BWD && aux_al && c_ok && (args.ldaux % 8) == 0 &&
       make_map2(&tc, args.C, N, M, args.ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B) &&
