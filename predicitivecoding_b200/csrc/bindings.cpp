@@ -127,6 +127,10 @@ int pcb_moe_router_wgrad(const float* dlogits, const void* x, long long ldx, int
                          cudaStream_t s);
 int pcb_moe_seg_colsum(const void* x, const int* seg, int E, int N, int cap, float* db, cudaStream_t s);
 
+int pcb_skinny_splits(int N, int K, int num_sms);
+int pcb_skinny_gemm(const void* x, long long ldx, const void* w, long long ldw, void* y, long long ldy, int y_f32,
+                    int M, int N, int K, int splits, int* err, unsigned long long* trace, cudaStream_t stream);
+
 extern "C" void pcb_set_gemm_mode(int mode);
 
 namespace {
@@ -288,6 +292,30 @@ void gemm_grouped(const at::Tensor& a, const at::Tensor& b, bool b_mn, int64_t e
   check(pcb_gemm_grouped_launch(a.data_ptr(), a_mn, lda, b.data_ptr(), b_mn ? 1 : 0, ldb, (int)epi, args, num_sms(),
                                 cur_stream()),
         "gemm_grouped");
+}
+
+// ---------------------------------------------------------------- decode-sized products
+// y [M, N] = x [M, K] @ w [K, N] (row-major weight) for M <= 32 on the tcgen05 skinny kernel (K split over
+// the CTAs of a cluster, reduced through distributed shared memory; deterministic).
+// `trace` (int64, optional) receives 8 globaltimer stamps per CTA: start, weights requested, dependency
+// wait over, first tile landed, accumulator read, partials visible, rows stored, end.
+void skinny_gemm(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, const c10::optional<at::Tensor>& err,
+                 const c10::optional<at::Tensor>& trace) {
+  req(x, at::kBFloat16, "x");
+  req(w, at::kBFloat16, "w");
+  PCB_CHECK(y.scalar_type() == at::kBFloat16 || y.scalar_type() == at::kFloat, "skinny_gemm: y bf16 or fp32");
+  PCB_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(0), "skinny_gemm: x [M, K], w [K, N]");
+  PCB_CHECK(x.size(0) <= 32 && y.size(0) == x.size(0) && y.size(1) == w.size(1), "skinny_gemm: M <= 32, y [M, N]");
+  const int M = x.size(0), K = x.size(1), N = w.size(1);
+  PCB_CHECK(K % 8 == 0 && N % 8 == 0, "skinny_gemm: K and N must be multiples of 8 (16-byte rows)");
+  const at::cuda::CUDAGuard guard(x.device());
+  const int splits = pcb_skinny_splits(N, K, num_sms());
+  check(pcb_skinny_gemm(x.data_ptr(), row_stride(x, "x"), w.data_ptr(), row_stride(w, "w"), y.data_ptr(),
+                        row_stride(y, "y"), y.scalar_type() == at::kFloat ? 1 : 0, M, N, K, splits,
+                        err ? err->data_ptr<int>() : nullptr,
+                        trace ? reinterpret_cast<unsigned long long*>(trace->data_ptr<int64_t>()) : nullptr,
+                        cur_stream()),
+        "skinny_gemm");
 }
 
 // ---------------------------------------------------------------- mixture of experts
@@ -897,6 +925,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm);
   m.def("gemm_pc", &gemm_pc);
   m.def("gemm_grouped", &gemm_grouped);
+  m.def("skinny_gemm", &skinny_gemm, py::arg("x"), py::arg("w"), py::arg("y"), py::arg("err") = py::none(),
+        py::arg("trace") = py::none());
   m.def("moe_route", &moe_route);
   m.def("moe_dispatch", &moe_dispatch);
   m.def("moe_gather", &moe_gather);

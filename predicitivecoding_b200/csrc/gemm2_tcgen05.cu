@@ -150,7 +150,20 @@ PCB_DEVICE void gather_chunks(const GemmArgs& a, int tid, int nthreads) {
     const int c = (a.ag_rank + j) % a.ag_world;
     const uint4* src = reinterpret_cast<const uint4*>(a.ag_peers[c]) + c * chunk_vec;
     uint4* dst = reinterpret_cast<uint4*>(a.ag_local) + c * chunk_vec;
-    for (long long v = v0 + tid; v < v1; v += nthreads) dst[v] = __ldcg(src + v);
+    // four independent 16-byte peer loads in flight per thread (NVLink latency is microseconds)
+    for (long long v = v0 + tid; v < v1; v += 4LL * nthreads) {
+      uint4 a[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const long long idx = v + (long long)u * nthreads;
+        if (idx < v1) a[u] = __ldcg(src + idx);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const long long idx = v + (long long)u * nthreads;
+        if (idx < v1) dst[idx] = a[u];
+      }
+    }
     fence_proxy_async_global();
     asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
     if (tid == 0) {

@@ -274,7 +274,7 @@ PCB_DEVICE void epilogue_chunk(const GemmArgs& a, int m, int n, float (&v)[32], 
 template <int EPI>
 PCB_DEVICE constexpr bool epi_coalesced() {
   return EPI == EPI_BF16 || EPI == EPI_F32 || EPI == EPI_ACC_F32 || EPI == EPI_RESID_F32 || EPI == EPI_RED_F32 ||
-         EPI == EPI_GELU || EPI == EPI_GELU_BWD || EPI == EPI_BF16_ACC ||
+         EPI == EPI_GELU || EPI == EPI_GELU_BWD || EPI == EPI_BF16_ACC || EPI == EPI_RS_BF16 ||
          EPI == EPI_PC_PRED || EPI == EPI_PC_STATE || EPI == EPI_PC_WUPD;
 }
 
@@ -379,6 +379,14 @@ PCB_DEVICE float epilogue_vec4(const GemmArgs& a, int m, int n, float (&v)[4], c
     st_bf16x4(reinterpret_cast<__nv_bfloat16*>(a.C) + (long long)m * a.ldc + n, v, nv);
   } else if (EPI == EPI_F32) {
     st_f32x4(reinterpret_cast<float*>(a.C) + (long long)m * a.ldc + n, v, nv);
+  } else if (EPI == EPI_RS_BF16) {
+    // row m goes to slot rs_rank of its owner c = m / rs_rows (plain 8-byte stores, over NVLink when remote)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] *= a.alpha;
+    const int c = m / a.rs_rows;
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.rs_peers[c]) +
+                         (long long)(a.rs_rank * a.rs_rows + (m - c * a.rs_rows)) * a.ldc + n;
+    st_bf16x4(dst, v, nv);
   } else if (EPI == EPI_ACC_F32) {
     float o[4];
 #pragma unroll

@@ -1,0 +1,382 @@
+// Skinny GEMM for decode-sized batches on the tcgen05 tensor cores: y[M, N] = x[M, K] @ W[K, N] with
+// M <= 32 activation rows and a row-major [K, N] bf16 weight (the inference projection layout).
+//
+// A decode step is bound by reading the weights, so the kernel is laid out for HBM, not for the MMA:
+// it computes the transposed product y^T = W^T x^T, so the weight's 128-column slice is the MMA's M (128
+// TMEM lanes) and the activations are its N (32 columns), and it splits K over the S CTAs of a
+// thread-block cluster (S = 1, 2, 4, 8 or 16) until about one CTA per SM streams a disjoint weight slab.
+// Each CTA: one TMA producer thread loads [64 k x 128 n] weight tiles (MN-major, two 64-column boxes)
+// and the matching [32 m x 64 k] activation tile into a 9-stage ring (the bytes in flight per SM bound a
+// weight stream), one thread issues tcgen05.mma (M 128, N 32, K 16 x 4) into 32 TMEM columns, and the
+// four warps read the accumulator back (thread = weight column, registers = the 32 rows).  With S = 1 the
+// rows are stored directly.  Otherwise CTA c of the cluster owns rows [c R, (c + 1) R), R = 32 / S:
+// every CTA pushes each owner its R rows with vector stores into the owner's shared memory (fire and
+// forget), one cluster barrier makes them visible, and each owner sums its S partials in a fixed order
+// and stores its rows -- no global workspace, no atomics, the same bits on every run, one barrier.
+//
+// Launched as a programmatic dependent: the weights are not written by the kernels before it, so the
+// first ring of weight tiles is requested (right after the barriers are initialised, while TMEM is being
+// allocated) before griddepcontrol.wait and streams in while the previous kernel drains; activations
+// and outputs are touched only after the wait.  Every mbarrier wait is bounded.
+//
+// Reference counterpart: PredictiveCoding.LLM/Infrastructure/GemmProvider.cs (the MatVec / MatMul used by
+// GptModel.Step for each token) and PredictiveCoding.Device/Kernels/DeviceMath.cs (device GEMV).
+#include <cudaTypedefs.h>
+
+#include <cstdlib>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace pcb {
+namespace skinny {
+
+constexpr int kBN = 128;                 // weight columns per CTA (MMA M)
+constexpr int kBM = 32;                  // activation rows (MMA N)
+constexpr int kBK = 64;
+constexpr int kStages = 9;               // 144 KB of weights in flight per CTA, one CTA per SM
+constexpr int kMaxSplits = 16;           // cluster size (above 8 where the GPU allows it)
+constexpr int W_BYTES = kBK * kBN * 2;   // two [64 n x 64 k] boxes, 128B swizzle
+constexpr int X_BYTES = kBM * kBK * 2;   // [32 m x 64 k], 128B swizzle
+constexpr int STAGE = W_BYTES + X_BYTES;
+// receive buffer of an owner: [S sources][128 columns][stride] fp32, stride = R padded so that the
+// vector accesses of eight consecutive columns hit disjoint banks
+__host__ __device__ constexpr int recv_stride(int S) { return (kBM / S) <= 4 ? kBM / S : kBM / S + 4; }
+__host__ __device__ constexpr int recv_bytes(int S) { return S == 1 ? 0 : S * kBN * recv_stride(S) * 4; }
+constexpr int RECV_OFF = kStages * STAGE;
+constexpr int RECV_MAX = 4 * kBN * 12 * 4;   // the largest of recv_bytes(2, 4, 8, 16)
+static_assert(recv_bytes(2) <= RECV_MAX && recv_bytes(4) <= RECV_MAX && recv_bytes(8) <= RECV_MAX &&
+                  recv_bytes(16) <= RECV_MAX, "receive buffer");
+constexpr int BAR_OFF = RECV_OFF + RECV_MAX;
+constexpr int SMEM = BAR_OFF + 256 + 1024;
+constexpr int kThreads = 128;
+static_assert(SMEM <= 232448, "shared memory budget");
+
+struct Args {
+  void* y;                 // [M, N] bf16 or fp32
+  long long ldy;
+  int M, N, K;
+  int y_f32;
+  int* err;
+  unsigned long long* trace;  // optional: 8 globaltimer stamps (ns) per CTA at the phase boundaries
+};
+
+PCB_DEVICE unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+PCB_DEVICE void st_dsmem_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
+PCB_DEVICE void st_dsmem_v2(uint32_t addr, uint32_t a, uint32_t b) {
+  asm volatile("st.shared::cluster.v2.b32 [%0], {%1, %2};" ::"r"(addr), "r"(a), "r"(b) : "memory");
+}
+
+PCB_DEVICE void store_out(const Args& a, int m, int n, float v) {
+  if (a.y_f32) reinterpret_cast<float*>(a.y)[(long long)m * a.ldy + n] = v;
+  else reinterpret_cast<__nv_bfloat16*>(a.y)[(long long)m * a.ldy + n] = __float2bfloat16_rn(v);
+}
+
+template <int S>
+__global__ void __launch_bounds__(kThreads, 1)
+    skinny_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, const Args a) {
+  constexpr int R = kBM / S;                 // rows each CTA of the cluster stores
+  constexpr int STRIDE = recv_stride(S);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + BAR_OFF);
+  uint64_t* empty = full + kStages;
+  uint64_t* done = empty + kStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* recv = reinterpret_cast<float*>(smem + RECV_OFF);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ntile = blockIdx.x, split = blockIdx.y;   // the cluster spans blockIdx.y: rank == split
+  const int n0 = ntile * kBN;
+  const int total_kb = (a.K + kBK - 1) / kBK;
+  const int kb0 = split * total_kb / S;
+  const int kb1 = (split + 1) * total_kb / S;
+  const int nkb = kb1 - kb0;
+  const int pre = min(nkb, kStages);
+  unsigned long long* tr = a.trace ? a.trace + 8ull * (blockIdx.y * gridDim.x + blockIdx.x) : nullptr;
+  if (tr && threadIdx.x == 0) tr[0] = global_ns();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tmap(&tmW);
+    prefetch_tmap(&tmX);
+    // the first ring of weight tiles does not depend on the previous kernel: request it now
+    for (int i = 0; i < pre; ++i) {
+      uint8_t* sw = smem + i * STAGE;
+      mbar_arrive_expect_tx(&full[i], STAGE);
+      tma_load_2d(sw, &tmW, &full[i], n0, (kb0 + i) * kBK);
+      tma_load_2d(sw + 8192, &tmW, &full[i], n0 + 64, (kb0 + i) * kBK);
+    }
+    if (tr) tr[1] = global_ns();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 32);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (tr && threadIdx.x == 0) tr[2] = global_ns();
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer ----------------
+    for (int i = 0; i < pre; ++i) tma_load_2d(smem + i * STAGE + W_BYTES, &tmX, &full[i], (kb0 + i) * kBK, 0);
+    for (int i = pre; i < nkb; ++i) {
+      const int s = i % kStages, kb = kb0 + i;
+      if (!mbar_wait(&empty[s], ((i / kStages) & 1) ^ 1u, a.err, kErrTimeoutEmpty, abort_flag)) break;
+      uint8_t* sw = smem + s * STAGE;
+      mbar_arrive_expect_tx(&full[s], STAGE);
+      tma_load_2d(sw, &tmW, &full[s], n0, kb * kBK);
+      tma_load_2d(sw + 8192, &tmW, &full[s], n0 + 64, kb * kBK);
+      tma_load_2d(sw + W_BYTES, &tmX, &full[s], kb * kBK, 0);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer ----------------
+    constexpr uint32_t idesc = make_idesc_bf16(kBN, kBM, 1, 0);   // A = W^T (MN-major), B = x (K-major)
+    for (int i = 0; i < nkb; ++i) {
+      const int s = i % kStages;
+      if (!mbar_wait(&full[s], (i / kStages) & 1, a.err, kErrTimeoutFull, abort_flag)) break;
+      if (tr && i == 0) tr[3] = global_ns();
+      tc_fence_after();
+      const uint32_t sw = smem_u32(smem + s * STAGE);
+      const uint32_t sx = sw + W_BYTES;
+#pragma unroll
+      for (int k = 0; k < kBK / 16; ++k)
+        umma_bf16(tmem, make_smem_desc(sw + k * 2048, 8192, 1024, 2), make_smem_desc(sx + k * 32, 16, 1024, 2),
+                  idesc, (i > 0 || k > 0) ? 1u : 0u);
+      umma_commit(&empty[s]);
+    }
+    umma_commit(done);
+  }
+  __syncwarp();
+
+  // ---------------- epilogue: thread = weight column n0 + threadIdx.x, registers = the 32 rows ----------------
+  const bool got = mbar_wait(done, 0, a.err, kErrTimeoutTmemFull, abort_flag) && !*abort_flag && nkb > 0;
+  tc_fence_after();
+  uint32_t r[32];
+  tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(warp * 32) << 16), r);
+  tmem_ld_wait();
+  if (!got) {
+#pragma unroll
+    for (int m = 0; m < kBM; ++m) r[m] = 0u;   // no k-blocks (or an abort): this split adds nothing
+  }
+  if (tr && threadIdx.x == 0) tr[4] = global_ns();
+  const int n = n0 + threadIdx.x;
+  if constexpr (S == 1) {
+    if (n < a.N) {
+#pragma unroll
+      for (int m = 0; m < kBM; ++m)
+        if (m < a.M) store_out(a, m, n, __uint_as_float(r[m]));
+    }
+  } else {
+    // push rows [c R, (c + 1) R) to owner c, at [split][column][row - c R] of its receive buffer
+    const uint32_t mine = smem_u32(recv) + (uint32_t)((split * kBN + threadIdx.x) * STRIDE * 4);
+#pragma unroll
+    for (int c = 0; c < S; ++c) {
+      if (c * R < a.M) {
+        const uint32_t dst = mapa_shared(mine, (uint32_t)c);
+#pragma unroll
+        for (int j = 0; j < R; j += (R >= 4 ? 4 : 2)) {
+          if constexpr (R >= 4) st_dsmem_v4(dst + j * 4, r[c * R + j], r[c * R + j + 1], r[c * R + j + 2], r[c * R + j + 3]);
+          else st_dsmem_v2(dst + j * 4, r[c * R + j], r[c * R + j + 1]);
+        }
+      }
+    }
+    cluster_sync_all();   // release the pushes / acquire the partials addressed to this CTA
+    if (tr && threadIdx.x == 0) tr[5] = global_ns();
+    if (split * R < a.M && n < a.N) {
+      float acc[R];
+#pragma unroll
+      for (int j = 0; j < R; ++j) acc[j] = 0.f;
+#pragma unroll
+      for (int q = 0; q < S; ++q) {                            // source CTAs in order: deterministic
+        const float* src = recv + (q * kBN + threadIdx.x) * STRIDE;
+#pragma unroll
+        for (int j = 0; j < R; j += (R >= 4 ? 4 : 2)) {
+          if constexpr (R >= 4) {
+            const float4 v = *reinterpret_cast<const float4*>(src + j);
+            acc[j] += v.x;
+            acc[j + 1] += v.y;
+            acc[j + 2] += v.z;
+            acc[j + 3] += v.w;
+          } else {
+            const float2 v = *reinterpret_cast<const float2*>(src + j);
+            acc[j] += v.x;
+            acc[j + 1] += v.y;
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < R; ++j)
+        if (split * R + j < a.M) store_out(a, split * R + j, n, acc[j]);
+    }
+    if (tr && threadIdx.x == 0) tr[6] = global_ns();
+  }
+  if (tr && threadIdx.x == 0) tr[7] = global_ns();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 32);
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+static bool make_map(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t bi,
+                     uint32_t bo) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {bi, bo};
+  cuuint32_t es[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace skinny
+}  // namespace pcb
+
+using namespace pcb;
+
+using KernelFn = void (*)(const CUtensorMap, const CUtensorMap, const skinny::Args);
+
+static KernelFn skinny_fn(int S) {
+  switch (S) {
+    case 1: return skinny::skinny_kernel<1>;
+    case 2: return skinny::skinny_kernel<2>;
+    case 4: return skinny::skinny_kernel<4>;
+    case 8: return skinny::skinny_kernel<8>;
+    default: return skinny::skinny_kernel<16>;
+  }
+}
+
+static void skinny_attrs() {
+  static std::once_flag once;
+  std::call_once(once, [] {
+    for (int S = 1; S <= skinny::kMaxSplits; S *= 2) {
+      cudaFuncSetAttribute(skinny_fn(S), cudaFuncAttributeMaxDynamicSharedMemorySize, skinny::SMEM);
+      cudaFuncSetAttribute(skinny_fn(S), cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    }
+    cudaGetLastError();
+  });
+}
+
+// Clusters of `S` CTAs (with this kernel's shared memory) the GPU can hold at once; cached per device.
+static int skinny_max_clusters(int S) {
+  static int cache[64][skinny::kMaxSplits + 1] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 0;
+  int& c = cache[dev][S];
+  if (c == 0) {
+    skinny_attrs();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, S, 1);
+    cfg.blockDim = dim3(skinny::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = skinny::SMEM;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 1;
+    at[0].val.clusterDim.y = S;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, skinny_fn(S), &cfg) != cudaSuccess) {
+      cudaGetLastError();
+      n = 0;
+    }
+    c = n > 0 ? n : -1;
+  }
+  return c;
+}
+
+// Split count (cluster size) for a skinny product: a power of two up to 16 so that column tiles x splits
+// fill about one wave of one CTA per SM, each split has at least two k-blocks, and all the clusters (one
+// per column tile) are resident together.
+int pcb_skinny_splits(int N, int K, int num_sms) {
+  const int ntiles = (N + skinny::kBN - 1) / skinny::kBN;
+  const int total_kb = (K + skinny::kBK - 1) / skinny::kBK;
+  const int cap = min(min(max(1, num_sms / ntiles), max(1, total_kb / 2)), skinny::kMaxSplits);
+  int s = 1;
+  while (s * 2 <= cap) s *= 2;
+  while (s > 1 && skinny_max_clusters(s) < ntiles) s /= 2;
+  return s;
+}
+
+// Programmatic dependent launch (PCB_PDL=0 turns it off).
+static bool skinny_pdl() {
+  static const bool on = [] {
+    const char* e = getenv("PCB_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+// y [M, N] (bf16, or fp32 with y_f32) = x [M, K] bf16 @ W [K, N] bf16 (row-major), M <= 32, K split over
+// `splits` CTAs of a cluster (1, 2, 4, 8 or 16); `trace` (optional) receives 8 timestamps per CTA.
+// Returns 0, -1 bad arguments, -5 tensor-map encode, -(1000 + cudaError) launch.
+int pcb_skinny_gemm(const void* x, long long ldx, const void* w, long long ldw, void* y, long long ldy, int y_f32,
+                    int M, int N, int K, int splits, int* err, unsigned long long* trace, cudaStream_t stream) {
+  if (M < 1 || M > skinny::kBM || N < 1 || K < 1) return -1;
+  if (splits != 1 && splits != 2 && splits != 4 && splits != 8 && splits != 16) return -1;
+  if (ldx % 8 || ldw % 8 || ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15)) return -1;
+  CUtensorMap tw, tx;
+  if (!skinny::make_map(&tw, w, (uint64_t)N, (uint64_t)K, (uint64_t)ldw, 64, 64)) return -5;
+  if (!skinny::make_map(&tx, x, (uint64_t)K, (uint64_t)M, (uint64_t)ldx, 64, skinny::kBM)) return -5;
+  skinny::Args a{};
+  a.y = y;
+  a.ldy = ldy;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.y_f32 = y_f32;
+  a.err = err;
+  a.trace = trace;
+  skinny_attrs();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((N + skinny::kBN - 1) / skinny::kBN, splits, 1);
+  cfg.blockDim = dim3(skinny::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = skinny::SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr_v[2];
+  attr_v[0].id = cudaLaunchAttributeClusterDimension;
+  attr_v[0].val.clusterDim.x = 1;
+  attr_v[0].val.clusterDim.y = splits;
+  attr_v[0].val.clusterDim.z = 1;
+  attr_v[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr_v[1].val.programmaticStreamSerializationAllowed = skinny_pdl() ? 1 : 0;
+  cfg.attrs = attr_v;
+  cfg.numAttrs = 2;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, skinny_fn(splits), tw, tx, a);
+  return e == cudaSuccess ? 0 : -(1000 + (int)e);
+}

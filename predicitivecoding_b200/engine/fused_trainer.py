@@ -164,6 +164,10 @@ class FusedDecoderTrainer:
         self.grad_shard = self.grad[lo:hi] if self.world == 1 else torch.zeros(A.shard, device=dev, dtype=f32)
         self.n_decay_local = max(0, min(A.n_decay - lo, A.shard))
         self.hyper_host = torch.zeros(8, dtype=f32).pin_memory()
+        self._hyper_np = self.hyper_host.numpy()   # host writes through numpy: no torch op per field
+        # the pinned staging buffers are rewritten only after the copies that read them have run
+        self._h2d_ev = torch.cuda.Event() if torch.device(device).type == "cuda" else None
+        self._h2d_pending = False
         self.hyper = torch.zeros(8, device=dev, dtype=f32)
         self.clip_buf = torch.zeros(1, device=dev, dtype=f32)
         self.W = A.views(self.w16)   # bf16 views by name
@@ -477,7 +481,6 @@ class FusedDecoderTrainer:
 
     def _optimizer(self) -> None:
         """Gradient sync (data parallel) + AdamW on this rank's shard + bf16 weight refresh."""
-        self.hyper.copy_(self.hyper_host, non_blocking=True)
         if self.grad_sync == "fused":
             A = self.arena
             torch.cuda.current_stream(self.device).wait_stream(self._push_stream)
@@ -513,9 +516,27 @@ class FusedDecoderTrainer:
             import torch.distributed as dist
             dist.all_gather_into_tensor(self.w16, w16_shard, group=self.pg)
 
-    def _step_body(self) -> None:
+    def _upload(self) -> None:
+        """Enqueue the host-to-device copies of the staged step (tokens, targets, hyper-parameters)."""
         self.tok.copy_(self.tok_pin, non_blocking=True)
         self.tgt.copy_(self.tgt_pin, non_blocking=True)
+        self.hyper.copy_(self.hyper_host, non_blocking=True)
+        if self._h2d_ev is not None:
+            self._h2d_ev.record(torch.cuda.current_stream(self.device))
+            self._h2d_pending = True
+
+    def _host_writable(self) -> None:
+        """Wait until the last upload has read the pinned buffers (the GPU may be a step behind)."""
+        if self._h2d_pending:
+            self._h2d_ev.synchronize()
+            self._h2d_pending = False
+
+    def _step_body(self) -> None:
+        self._upload()
+        self._device_step()
+
+    def _device_step(self) -> None:
+        """Everything of a step after the uploads: captured as one CUDA graph."""
         self.grad.zero_()
         with nvtx_range("forward"):
             self._forward(True)
@@ -526,19 +547,22 @@ class FusedDecoderTrainer:
         self.loss_pin.copy_(self.loss_sum, non_blocking=True)
 
     def _set_hyper(self, lr: float) -> None:
+        self._host_writable()
         self.t += 1
         b1, b2 = self.betas
-        self.hyper_host[0] = lr
-        self.hyper_host[1] = self.wd
-        self.hyper_host[2] = 1.0 - b1 ** self.t
-        self.hyper_host[3] = 1.0 - b2 ** self.t
+        h = self._hyper_np
+        h[0] = lr
+        h[1] = self.wd
+        h[2] = 1.0 - b1 ** self.t
+        h[3] = 1.0 - b2 ** self.t
         # gradients are sums over ranks of per-rank means: fold the 1/world mean here
-        self.hyper_host[4] = 1.0 / self.world
+        h[4] = 1.0 / self.world
 
     def stage(self, tokens: torch.Tensor, targets: torch.Tensor) -> None:
         """Copy one step's [B, S] int tokens/targets into the pinned staging buffers."""
-        self.tok_pin.copy_(tokens.reshape(-1).to(torch.int32))
-        self.tgt_pin.copy_(targets.reshape(-1).to(torch.int32))
+        self._host_writable()
+        self.tok_pin.copy_(tokens.reshape(-1))      # copy_ converts the dtype in place
+        self.tgt_pin.copy_(targets.reshape(-1))
 
     def launch(self, lr: Optional[float] = None) -> None:
         """Enqueue one full training step on the current stream (no host sync)."""
@@ -546,6 +570,7 @@ class FusedDecoderTrainer:
         if self.use_graph and self.grad_sync in ("none", "fused"):
             if self.graph is None:
                 self._capture()
+            self._upload()
             self.graph.replay()
         else:
             self._step_body()
@@ -566,7 +591,7 @@ class FusedDecoderTrainer:
         s.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(s):
             with torch.cuda.graph(self.graph, stream=s):
-                self._step_body()
+                self._device_step()
         torch.cuda.current_stream(self.device).wait_stream(s)
         torch.cuda.synchronize(self.device)
 
@@ -585,8 +610,7 @@ class FusedDecoderTrainer:
     def evaluate_loss(self, tokens: torch.Tensor, targets: torch.Tensor) -> float:
         """Mean CE without touching gradients or weights (DeviceDecoderTrainer.EvaluateLoss)."""
         self.stage(tokens, targets)
-        self.tok.copy_(self.tok_pin, non_blocking=True)
-        self.tgt.copy_(self.tgt_pin, non_blocking=True)
+        self._upload()
         self._forward(write_grad=False)
         self.loss_pin.copy_(self.loss_sum, non_blocking=True)
         return self.read_loss()

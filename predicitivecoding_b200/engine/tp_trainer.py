@@ -103,7 +103,11 @@ class TensorParallelTrainer:
         self.W = {**self.rep.views(self.w16["rep"]), **self.shd.views(self.w16["shd"])}
         self.G = {**self.rep.views(self.grad["rep"]), **self.shd.views(self.grad["shd"])}
         self.hyper_host = torch.zeros(8, dtype=f32).pin_memory()
+        self._hyper_np = self.hyper_host.numpy()
         self.hyper = torch.zeros(8, device=dev, dtype=f32)
+        # the pinned staging buffers are rewritten only after the copies that read them have run
+        self._h2d_ev = torch.cuda.Event()
+        self._h2d_pending = False
 
         # ---------------- peer memory: gather buffers, reduce-scatter slots, barrier, all-reduce
         self.peer = PeerGroup(self.pg, dev)
@@ -291,7 +295,6 @@ class TensorParallelTrainer:
         ops.embed_bwd(self.tok[sl], self.dx, G["wemb"])
 
     def _optimizer(self) -> None:
-        self.hyper.copy_(self.hyper_host, non_blocking=True)
         if self.comm is not None:
             self.comm.all_reduce(self.grad["rep"])       # replicated parameters: sum of row partials
         if self.dp_comm is not None:                     # data-parallel replicas: sum, AdamW scales by 1/DP
@@ -302,9 +305,26 @@ class TensorParallelTrainer:
                       self.hyper, self.betas[0], self.betas[1], self.eps)
         self._barrier()   # nobody's next forward reads a weight before every rank has written its own
 
-    def _step_body(self) -> None:
+    def _upload(self) -> None:
+        """Enqueue the host-to-device copies of the staged step (tokens, targets, hyper-parameters)."""
         self.tok.copy_(self.tok_pin, non_blocking=True)
         self.tgt.copy_(self.tgt_pin, non_blocking=True)
+        self.hyper.copy_(self.hyper_host, non_blocking=True)
+        self._h2d_ev.record(torch.cuda.current_stream(self.device))
+        self._h2d_pending = True
+
+    def _host_writable(self) -> None:
+        """Wait until the last upload has read the pinned buffers (the GPU may be a step behind)."""
+        if self._h2d_pending:
+            self._h2d_ev.synchronize()
+            self._h2d_pending = False
+
+    def _step_body(self) -> None:
+        self._upload()
+        self._device_step()
+
+    def _device_step(self) -> None:
+        """Everything of a step after the uploads: captured as one CUDA graph."""
         self.grad["rep"].zero_()
         self.grad["shd"].zero_()
         with nvtx_range("tp_forward"):
@@ -316,23 +336,27 @@ class TensorParallelTrainer:
         self.loss_pin.copy_(self.loss_sum, non_blocking=True)
 
     def _set_hyper(self, lr: float) -> None:
+        self._host_writable()
         self.step_count += 1
         b1, b2 = self.betas
-        self.hyper_host[0] = lr
-        self.hyper_host[1] = self.wd
-        self.hyper_host[2] = 1.0 - b1 ** self.step_count
-        self.hyper_host[3] = 1.0 - b2 ** self.step_count
-        self.hyper_host[4] = 1.0 / self.dp
+        h = self._hyper_np
+        h[0] = lr
+        h[1] = self.wd
+        h[2] = 1.0 - b1 ** self.step_count
+        h[3] = 1.0 - b2 ** self.step_count
+        h[4] = 1.0 / self.dp
 
     def stage(self, tokens: torch.Tensor, targets: torch.Tensor) -> None:
-        self.tok_pin.copy_(tokens.reshape(-1).to(torch.int32))
-        self.tgt_pin.copy_(targets.reshape(-1).to(torch.int32))
+        self._host_writable()
+        self.tok_pin.copy_(tokens.reshape(-1))      # copy_ converts the dtype in place
+        self.tgt_pin.copy_(targets.reshape(-1))
 
     def launch(self, lr: Optional[float] = None) -> None:
         self._set_hyper(self.lr if lr is None else lr)
         if self.use_graph:
             if self.graph is None:
                 self._capture()
+            self._upload()
             self.graph.replay()
         else:
             self._step_body()
@@ -353,7 +377,7 @@ class TensorParallelTrainer:
         s.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(s):
             with torch.cuda.graph(self.graph, stream=s):
-                self._step_body()
+                self._device_step()
         torch.cuda.current_stream(self.device).wait_stream(s)
         torch.cuda.synchronize(self.device)
 

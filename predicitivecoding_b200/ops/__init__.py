@@ -122,11 +122,16 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = F
     return c
 
 
+SKINNY_MAX_ROWS = 32 if os.environ.get("PCB_SKINNY", "1") != "0" else 0   # PCB_SKINNY=0: regular GEMM only
+
+
 def linear(x: torch.Tensor, w_kn: torch.Tensor, out: Optional[torch.Tensor] = None, fp32: bool = False,
            bias: Optional[torch.Tensor] = None) -> torch.Tensor:
     """x [..., K] @ w [K, N] on the tcgen05 GEMM (the weight read N-major, no transpose), bf16 operands,
     fp32 accumulation; bf16 result (or fp32 with ``fp32``), written into ``out`` when given.  Inference
-    projections (serving, tensor-parallel decode) call this instead of a library GEMM."""
+    projections (serving, tensor-parallel decode) call this instead of a library GEMM.  Up to 32 rows
+    (decode batches) take the skinny kernel, which splits K over a thread-block cluster so the SMs stream
+    disjoint weight slabs and sums the partials in distributed shared memory (deterministic)."""
     shape = x.shape
     x2 = x.reshape(-1, shape[-1])
     if not x2.is_contiguous():
@@ -134,7 +139,13 @@ def linear(x: torch.Tensor, w_kn: torch.Tensor, out: Optional[torch.Tensor] = No
     N = w_kn.shape[1]
     if out is None:
         out = torch.empty(x2.shape[0], N, device=x.device, dtype=torch.float32 if fp32 else torch.bfloat16)
-    gemm(x2, w_kn, b_mn=True, epi=EPI_F32 if fp32 else EPI_BF16, c=out.view(x2.shape[0], N), bias=bias)
+    y = out.view(x2.shape[0], N)
+    skinny_ok = (bias is None and x2.shape[0] <= SKINNY_MAX_ROWS and N <= 1024 * 128 and w_kn.is_contiguous()
+                 and y.is_contiguous() and x2.shape[1] % 8 == 0 and N % 8 == 0)
+    if skinny_ok:
+        ext().skinny_gemm(x2, w_kn, y, None)
+    else:
+        gemm(x2, w_kn, b_mn=True, epi=EPI_F32 if fp32 else EPI_BF16, c=y, bias=bias)
     return out.view(*shape[:-1], N)
 
 

@@ -38,7 +38,9 @@ class PeerGroup:
         self.pg = pg
         self.world = dist.get_world_size(pg) if dist.is_initialized() else 1
         self.rank = dist.get_rank(pg) if dist.is_initialized() else 0
-        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.device = torch.device(device) if device is not None else torch.device("cuda")
+        if self.device.index is None:   # "cuda" means the current device
+            self.device = torch.device("cuda", torch.cuda.current_device())
         self._opened: List[int] = []
         self._keep: List[torch.Tensor] = []
         self.flags = self.symmetric(64, torch.int32)

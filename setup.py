@@ -67,6 +67,7 @@ setup(
                 os.path.join(CSRC, "tp.cu"),
                 os.path.join(CSRC, "vision.cu"),
                 os.path.join(CSRC, "moe.cu"),
+                os.path.join(CSRC, "skinny.cu"),
                 os.path.join(CSRC, "runtime.cpp"),
             ],
             include_dirs=[os.path.join(HERE, CSRC)],

@@ -408,3 +408,23 @@ def test_embed_fwd_bwd():
     torch.cuda.synchronize()
     assert torch.equal(x, W.float()[tok.long()])
     assert rel_err(dW, ref) < 1e-5
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 2048, 768), (32, 2048, 768), (7, 688, 2048), (32, 2048, 1376), (32, 5504, 2048),
+                                   (32, 104, 1000), (16, 2048, 32000), (2, 256, 512), (5, 1216, 512),
+                                   (32, 1216, 512)])
+@pytest.mark.parametrize("fp32", [False, True])
+def test_skinny_linear_matches_fp32(M, K, N, fp32):
+    """Decode-sized projections (<= 32 rows) on the tcgen05 skinny kernel against an fp32 matmul, including
+    K and N tails and K split over clusters of 1 to 16 CTAs (with few rows, some CTAs of the cluster own
+    no rows to store); repeated runs give the same bits (fixed-order cluster reduction)."""
+    g = torch.Generator(device=DEV).manual_seed(M * 7 + K)
+    x = torch.randn(M, K, device=DEV, generator=g).to(torch.bfloat16)
+    w = (torch.randn(K, N, device=DEV, generator=g) * K ** -0.5).to(torch.bfloat16)
+    ref = x.float() @ w.float()
+    ys = [ops.linear(x, w, fp32=fp32) for _ in range(3)]
+    torch.cuda.synchronize()
+    for y in ys:
+        assert y.dtype == (torch.float32 if fp32 else torch.bfloat16)
+        assert rel_err(y, ref) < (1e-3 if fp32 else 1e-2)
+        assert torch.equal(y, ys[0])
