@@ -168,7 +168,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncwarp();
 
   // ---------------- epilogue: thread = weight column n0 + threadIdx.x, registers = the 32 rows ----------------
-  const bool got = mbar_wait(done, 0, a.err, kErrTimeoutTmemFull, abort_flag) && !*abort_flag && nkb > 0;
+  // lanes spin independently: agree on the outcome (and reconverge) before the warp-collective tcgen05.ld
+  const bool got = __all_sync(0xffffffffu, mbar_wait(done, 0, a.err, kErrTimeoutTmemFull, abort_flag) &&
+                                               !*abort_flag && nkb > 0);
   tc_fence_after();
   uint32_t r[32];
   tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(warp * 32) << 16), r);

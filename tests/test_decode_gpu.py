@@ -38,7 +38,7 @@ def test_decode_attention(hd, G):
     v = torch.randn(B, Hkv, cap, hd, device="cuda", generator=g).to(torch.bfloat16)
     lens = torch.tensor([1, 333, 700], dtype=torch.int32, device="cuda")
     for softcap in (0.0, 5.0):
-        for nsplit in (1, 3, 8):
+        for nsplit in (1, 3, 8, None):
             out = ops.decode_attn(q, k, v, lens, 1 / math.sqrt(hd), softcap, nsplit=nsplit)
             ref = _ref_decode(q.cpu(), k.cpu(), v.cpu(), lens.cpu(), 1 / math.sqrt(hd), softcap)
             assert (out.float().cpu() - ref).abs().max() < 2e-2
