@@ -122,6 +122,17 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = F
     return c
 
 
+_SMS = {}
+
+
+def _sm_count(device) -> int:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    n = _SMS.get(idx)
+    if n is None:
+        n = _SMS[idx] = torch.cuda.get_device_properties(idx).multi_processor_count
+    return n
+
+
 SKINNY_MAX_ROWS = 32 if os.environ.get("PCB_SKINNY", "1") != "0" else 0   # PCB_SKINNY=0: regular GEMM only
 
 
@@ -140,8 +151,9 @@ def linear(x: torch.Tensor, w_kn: torch.Tensor, out: Optional[torch.Tensor] = No
     if out is None:
         out = torch.empty(x2.shape[0], N, device=x.device, dtype=torch.float32 if fp32 else torch.bfloat16)
     y = out.view(x2.shape[0], N)
-    skinny_ok = (bias is None and x2.shape[0] <= SKINNY_MAX_ROWS and N <= 1024 * 128 and w_kn.is_contiguous()
-                 and y.is_contiguous() and x2.shape[1] % 8 == 0 and N % 8 == 0)
+    # one 128-column tile per SM at most: wider products (an LM head) stream better on the regular GEMM
+    skinny_ok = (bias is None and x2.shape[0] <= SKINNY_MAX_ROWS and N <= 128 * _sm_count(x.device)
+                 and w_kn.is_contiguous() and y.is_contiguous() and x2.shape[1] % 8 == 0 and N % 8 == 0)
     if skinny_ok:
         ext().skinny_gemm(x2, w_kn, y, None)
     else:

@@ -17,7 +17,8 @@ from . import (ext, gemm, gemm_pc, attn_fwd, attn_bwd, EPI_BF16, EPI_F32, EPI_RE
                EPI_RED_F32, EPI_PC_PRED, EPI_PC_STATE)
 
 CASES = ("gemm_swiglu", "gemm_lmhead", "gemm_dw", "pc_pred", "pc_state", "attn_fwd", "attn_fwd_mma", "attn_bwd",
-         "attn_fwd_d128", "attn_fwd_mma_d128", "attn_bwd_d128", "moe_fwd", "moe_layer")
+         "attn_fwd_d128", "attn_fwd_mma_d128", "attn_bwd_d128", "moe_fwd", "moe_layer", "skinny_qkv",
+         "decode_attn_b32")
 
 
 def build(which: str, dev: str = "cuda"):
@@ -99,6 +100,18 @@ def build(which: str, dev: str = "cuda"):
             moe.forward(x, res, out, router, w1, b1, w2, b2, k, buf)
             moe.backward(dx, x, dn, router, w1, w2, k, buf, scr, *grads, 0.01)
         return layer, 3 * flops
+    if which == "skinny_qkv":           # decode projection of the 1.3B decoder: 32 rows, K 2048, N 6144
+        x, w = rn(32, 2048).to(bf), rn(2048, 6144, scale=0.02).to(bf)
+        y = torch.empty(32, 6144, device=dev, dtype=bf)
+        from . import linear
+        return (lambda: linear(x, w, out=y)), 2 * 32 * 2048 * 6144
+    if which == "decode_attn_b32":      # decode attention: batch 32, 16 heads of 128, 640 cached keys
+        from . import decode_attn
+        B, H, hd, L, cap = 32, 16, 128, 640, 768
+        q = rn(B, H, hd).to(bf)
+        kc, vc = rn(B, H, cap, hd).to(bf), rn(B, H, cap, hd).to(bf)
+        lens = torch.full((B,), L, dtype=torch.int32, device=dev)
+        return (lambda: decode_attn(q, kc, vc, lens, hd ** -0.5)), 4 * B * H * L * hd
     raise ValueError(f"unknown case {which!r}; one of {CASES}")
 
 
@@ -178,6 +191,59 @@ def decoder_gemm_table(iters: int = 20) -> list:
     return rows
 
 
+def decode_linear_table(iters: int = 50) -> list:
+    """Decode-sized projections (<= 32 rows) of the 1.3B decoder on the skinny tcgen05 kernel, on the
+    regular tcgen05 GEMM, through ops.linear (which picks one of the two) and on torch.matmul (cuBLAS,
+    for reference): device time per launch from CUDA
+    events around one replay of a CUDA graph of `iters` launches (launch overhead out, programmatic
+    launch overlap in)."""
+    from . import linear
+    import predicitivecoding_b200.ops as ops_mod
+    dev = "cuda"
+
+    def graph_us(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        g, s = torch.cuda.CUDAGraph(), torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                for _ in range(iters):
+                    fn()
+        torch.cuda.current_stream().wait_stream(s)
+        g.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) * 1e3 / iters
+
+    rows = []
+    for name, (M, K, N) in (("qkv", (32, 2048, 6144)), ("o", (32, 2048, 2048)), ("w13", (32, 2048, 11008)),
+                            ("w2", (32, 5504, 2048)), ("lm head", (32, 2048, 32000)), ("qkv, 8 rows", (8, 2048, 6144)),
+                            ("124M qkv", (32, 768, 2304))):
+        x = torch.randn(M, K, device=dev).to(torch.bfloat16)
+        w = (torch.randn(K, N, device=dev) * 0.02).to(torch.bfloat16)
+        y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+        sk = graph_us(lambda: ext().skinny_gemm(x, w, y))
+        keep = ops_mod.SKINNY_MAX_ROWS
+        try:
+            ops_mod.SKINNY_MAX_ROWS = 0
+            reg = graph_us(lambda: linear(x, w, out=y))
+            ops_mod.SKINNY_MAX_ROWS = 32
+            routed = graph_us(lambda: linear(x, w, out=y))
+        finally:
+            ops_mod.SKINNY_MAX_ROWS = keep
+        tm = graph_us(lambda: torch.matmul(x, w, out=y))
+        rows.append({"shape": name, "M": M, "K": K, "N": N, "skinny_us": round(sk, 2), "tcgen05_gemm_us": round(reg, 2),
+                     "ops_linear_us": round(routed, 2), "torch_matmul_us": round(tm, 2),
+                     "skinny_weight_TBps": round(K * N * 2 / sk / 1e6, 2)})
+    return rows
+
+
 def step_breakdown(steps: int = 2) -> list:
     """Device time per kernel of one step of the 124M decoder trainer (micro-batch 16 x 1024), from the
     CUDA activity records of torch.profiler over `steps` steps after 3 warm-up steps; eager launches
@@ -210,12 +276,16 @@ def step_breakdown(steps: int = 2) -> list:
 
 def main() -> None:
     p = argparse.ArgumentParser()
-    p.add_argument("case", choices=CASES + ("all", "decoder_gemms", "step_breakdown"))
+    p.add_argument("case", choices=CASES + ("all", "decoder_gemms", "decode_linears", "step_breakdown"))
     p.add_argument("--time", type=int, default=0, help="time N launches after warm-up")
     a = p.parse_args()
     ext()
     if a.case == "decoder_gemms":
         for row in decoder_gemm_table():
+            print(json.dumps(row))
+        return
+    if a.case == "decode_linears":
+        for row in decode_linear_table():
             print(json.dumps(row))
         return
     if a.case == "step_breakdown":
