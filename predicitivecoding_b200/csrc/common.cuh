@@ -7,6 +7,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cstdlib>
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -427,4 +428,42 @@ PCB_DEVICE void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, uint64_
       : "memory");
 }
 
+}  // namespace pcb
+
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch.  A kernel launched with pdl_launch may be scheduled while the kernel
+// before it in the stream is still running; it must call pdl_begin() before its first global-memory
+// access (that waits for the previous grid to complete and its writes to be visible) and lets the next
+// kernel be scheduled from then on.  Both are no-ops for an ordinary launch.  PCB_PDL=0 turns the
+// programmatic attribute off everywhere.
+// ---------------------------------------------------------------------------
+namespace pcb {
+PCB_DEVICE void pdl_begin() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+inline bool pdl_env_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("PCB_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t pdl_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = pdl_env_enabled() ? 1 : 0;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
 }  // namespace pcb

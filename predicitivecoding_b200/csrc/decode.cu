@@ -35,6 +35,7 @@ decode_attn_split_kernel(const __nv_bfloat16* __restrict__ q,      // [B, H, HD]
                          float* __restrict__ part_acc,             // [B, H, nsplit, HD]
                          float* __restrict__ part_ml,              // [B, H, nsplit, 2]
                          int Hkv, int cap, int nsplit, float scale, float softcap) {
+  pdl_begin();
   const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
   const int H = Hkv * G;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -176,6 +177,7 @@ decode_attn_split_kernel(const __nv_bfloat16* __restrict__ q,      // [B, H, HD]
 template <int HD>
 __global__ void decode_attn_combine_kernel(const float* __restrict__ part_acc, const float* __restrict__ part_ml,
                                            __nv_bfloat16* __restrict__ out, int nsplit) {
+  pdl_begin();
   const long long bh = blockIdx.x;                 // b * H + h
   const int d = threadIdx.x;
   float mm = -INFINITY;
@@ -333,14 +335,14 @@ int launch_decode(const __nv_bfloat16* q, const __nv_bfloat16* kc, const __nv_bf
   switch (G) {
 #define PCB_DEC_CASE(GG)                                                                                       \
   case GG:                                                                                                     \
-    decode_attn_split_kernel<HD, GG><<<grid, kDecWarps * 32, 0, s>>>(q, kc, vc, lens, pacc, pml, Hkv, cap,     \
-                                                                     nsplit, scale, softcap);                  \
+    pdl_launch(decode_attn_split_kernel<HD, GG>, grid, dim3(kDecWarps * 32), 0, s, q, kc, vc, lens, pacc, pml, \
+               Hkv, cap, nsplit, scale, softcap);                                                              \
     break;
     PCB_DEC_CASE(1) PCB_DEC_CASE(2) PCB_DEC_CASE(4) PCB_DEC_CASE(8)
 #undef PCB_DEC_CASE
     default: return -2;
   }
-  decode_attn_combine_kernel<HD><<<B * Hkv * G, HD, 0, s>>>(pacc, pml, out, nsplit);
+  pdl_launch(decode_attn_combine_kernel<HD>, dim3(B * Hkv * G), dim3(HD), 0, s, pacc, pml, out, nsplit);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
@@ -350,6 +352,7 @@ __global__ void rope_append_kernel(const __nv_bfloat16* __restrict__ qkv, const 
                                    const long long* __restrict__ pos, __nv_bfloat16* __restrict__ qo,
                                    __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ vc, int H, int HD,
                                    int cap) {
+  pdl_begin();
   const int b = blockIdx.x;
   const long long p = *pos;
   const int D = H * HD;
@@ -371,6 +374,7 @@ __global__ void rope_append_kernel(const __nv_bfloat16* __restrict__ qkv, const 
 // a[r, j] = silu(gu[r, j]) * gu[r, F + j] for gu [rows, 2F] bf16 (gate | up), a [rows, F] bf16
 __global__ void swiglu_rows_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* __restrict__ a, int rows,
                                    int F) {
+  pdl_begin();
   const long long n = (long long)rows * F;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     const long long r = i / F;
@@ -450,10 +454,9 @@ int pcb_linear_scan_bwd(const float* a, const float* st, const float* ds, float*
 int pcb_rope_append(const void* qkv, const float* cs_table, const long long* pos, void* qo, void* kc, void* vc, int B,
                     int H, int HD, int cap, cudaStream_t s) {
   if (HD % 2 || B <= 0) return -2;
-  rope_append_kernel<<<B, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(qkv),
-                                       reinterpret_cast<const float2*>(cs_table), pos,
-                                       reinterpret_cast<__nv_bfloat16*>(qo), reinterpret_cast<__nv_bfloat16*>(kc),
-                                       reinterpret_cast<__nv_bfloat16*>(vc), H, HD, cap);
+  pdl_launch(rope_append_kernel, dim3(B), dim3(256), 0, s, reinterpret_cast<const __nv_bfloat16*>(qkv),
+             reinterpret_cast<const float2*>(cs_table), pos, reinterpret_cast<__nv_bfloat16*>(qo),
+             reinterpret_cast<__nv_bfloat16*>(kc), reinterpret_cast<__nv_bfloat16*>(vc), H, HD, cap);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
@@ -461,7 +464,7 @@ int pcb_swiglu_rows(const void* gu, void* a, int rows, int F, cudaStream_t s) {
   const long long n = (long long)rows * F;
   long long blocks = (n + 255) / 256;
   if (blocks > 148 * 8) blocks = 148 * 8;
-  swiglu_rows_kernel<<<(unsigned)blocks, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(gu),
-                                                      reinterpret_cast<__nv_bfloat16*>(a), rows, F);
+  pdl_launch(swiglu_rows_kernel, dim3((unsigned)blocks), dim3(256), 0, s, reinterpret_cast<const __nv_bfloat16*>(gu),
+             reinterpret_cast<__nv_bfloat16*>(a), rows, F);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }

@@ -108,6 +108,7 @@ namespace {
 __global__ void __launch_bounds__(kTpThreads)
 tp_allreduce_norm_kernel(const __nv_bfloat16* const* __restrict__ peers, int world, int D, float* __restrict__ x,
                          const __nv_bfloat16* __restrict__ gamma, __nv_bfloat16* __restrict__ y, float eps) {
+  pdl_begin();
   const int r = blockIdx.x;
   float ss = 0.f;
   for (int i = threadIdx.x * 8; i < D; i += kTpThreads * 8) {
@@ -162,8 +163,8 @@ tp_allreduce_norm_kernel(const __nv_bfloat16* const* __restrict__ peers, int wor
 int pcb_tp_allreduce_norm(const void* peers, int world, int rows, int D, float* x, const void* gamma, void* y,
                           float eps, cudaStream_t s) {
   if (D % 8 || rows <= 0 || world <= 0) return -2;
-  tp_allreduce_norm_kernel<<<rows, kTpThreads, 0, s>>>(reinterpret_cast<const __nv_bfloat16* const*>(peers), world,
-                                                         D, x, reinterpret_cast<const __nv_bfloat16*>(gamma),
-                                                         reinterpret_cast<__nv_bfloat16*>(y), eps);
+  pdl_launch(tp_allreduce_norm_kernel, dim3(rows), dim3(kTpThreads), 0, s,
+             reinterpret_cast<const __nv_bfloat16* const*>(peers), world, D, x,
+             reinterpret_cast<const __nv_bfloat16*>(gamma), reinterpret_cast<__nv_bfloat16*>(y), eps);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
