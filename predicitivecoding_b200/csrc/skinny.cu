@@ -9,7 +9,7 @@
 // and the matching [32 m x 64 k] activation tile into a 9-stage ring (the bytes in flight per SM bound a
 // weight stream), one thread issues tcgen05.mma (M 128, N 32, K 16 x 4) into 32 TMEM columns, and the
 // four warps read the accumulator back (thread = weight column, registers = the 32 rows).  With S = 1 the
-// rows are stored directly.  Otherwise CTA c of the cluster owns rows [c R, (c + 1) R), R = 32 / S:
+// rows are stored directly.  Otherwise CTA c of the cluster owns rows [c R, (c + 1) R), R = ceil(32 / S):
 // every CTA pushes each owner its R rows with vector stores into the owner's shared memory (fire and
 // forget), one cluster barrier makes them visible, and each owner sums its S partials in a fixed order
 // and stores its rows -- no global workspace, no atomics, the same bits on every run, one barrier.
@@ -39,14 +39,21 @@ constexpr int kMaxSplits = 16;           // cluster size (above 8 where the GPU 
 constexpr int W_BYTES = kBK * kBN * 2;   // two [64 n x 64 k] boxes, 128B swizzle
 constexpr int X_BYTES = kBM * kBK * 2;   // [32 m x 64 k], 128B swizzle
 constexpr int STAGE = W_BYTES + X_BYTES;
-// receive buffer of an owner: [S sources][128 columns][stride] fp32, stride = R padded so that the
-// vector accesses of eight consecutive columns hit disjoint banks
-__host__ __device__ constexpr int recv_stride(int S) { return (kBM / S) <= 4 ? kBM / S : kBM / S + 4; }
+// receive buffer of an owner: [S sources][128 columns][stride] fp32 holding its R = ceil(32 / S) rows;
+// stride = R padded so that the accesses of consecutive columns hit disjoint banks (16-byte vectors of
+// eight columns when R is a multiple of 4, single words of 32 columns otherwise)
+__host__ __device__ constexpr int rows_per_owner(int S) { return (kBM + S - 1) / S; }
+__host__ __device__ constexpr bool vec_rows(int S) { return rows_per_owner(S) % 4 == 0; }
+__host__ __device__ constexpr int recv_stride(int S) {
+  return vec_rows(S) ? (rows_per_owner(S) % 8 == 0 ? rows_per_owner(S) + 4 : rows_per_owner(S))
+                     : (rows_per_owner(S) | 1);
+}
 __host__ __device__ constexpr int recv_bytes(int S) { return S == 1 ? 0 : S * kBN * recv_stride(S) * 4; }
+__host__ __device__ constexpr int max_recv_bytes(int S = 2) {
+  return S > kMaxSplits ? 0 : (recv_bytes(S) > max_recv_bytes(S + 1) ? recv_bytes(S) : max_recv_bytes(S + 1));
+}
 constexpr int RECV_OFF = kStages * STAGE;
-constexpr int RECV_MAX = 4 * kBN * 12 * 4;   // the largest of recv_bytes(2, 4, 8, 16)
-static_assert(recv_bytes(2) <= RECV_MAX && recv_bytes(4) <= RECV_MAX && recv_bytes(8) <= RECV_MAX &&
-                  recv_bytes(16) <= RECV_MAX, "receive buffer");
+constexpr int RECV_MAX = max_recv_bytes();
 constexpr int BAR_OFF = RECV_OFF + RECV_MAX;
 constexpr int SMEM = BAR_OFF + 256 + 1024;
 constexpr int kThreads = 128;
@@ -71,8 +78,8 @@ PCB_DEVICE void st_dsmem_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, u
   asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
                : "memory");
 }
-PCB_DEVICE void st_dsmem_v2(uint32_t addr, uint32_t a, uint32_t b) {
-  asm volatile("st.shared::cluster.v2.b32 [%0], {%1, %2};" ::"r"(addr), "r"(a), "r"(b) : "memory");
+PCB_DEVICE void st_dsmem_b32(uint32_t addr, uint32_t a) {
+  asm volatile("st.shared::cluster.b32 [%0], %1;" ::"r"(addr), "r"(a) : "memory");
 }
 
 PCB_DEVICE void store_out(const Args& a, int m, int n, float v) {
@@ -83,7 +90,7 @@ PCB_DEVICE void store_out(const Args& a, int m, int n, float v) {
 template <int S>
 __global__ void __launch_bounds__(kThreads, 1)
     skinny_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, const Args a) {
-  constexpr int R = kBM / S;                 // rows each CTA of the cluster stores
+  constexpr int R = rows_per_owner(S);       // rows each CTA of the cluster stores (the last ones may have fewer)
   constexpr int STRIDE = recv_stride(S);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -192,12 +199,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t mine = smem_u32(recv) + (uint32_t)((split * kBN + threadIdx.x) * STRIDE * 4);
 #pragma unroll
     for (int c = 0; c < S; ++c) {
-      if (c * R < a.M) {
+      if (c * R < kBM && c * R < a.M) {
         const uint32_t dst = mapa_shared(mine, (uint32_t)c);
+        if constexpr (vec_rows(S)) {
 #pragma unroll
-        for (int j = 0; j < R; j += (R >= 4 ? 4 : 2)) {
-          if constexpr (R >= 4) st_dsmem_v4(dst + j * 4, r[c * R + j], r[c * R + j + 1], r[c * R + j + 2], r[c * R + j + 3]);
-          else st_dsmem_v2(dst + j * 4, r[c * R + j], r[c * R + j + 1]);
+          for (int j = 0; j < R; j += 4)
+            if (c * R + j < kBM)
+              st_dsmem_v4(dst + j * 4, r[c * R + j], r[c * R + j + 1], r[c * R + j + 2], r[c * R + j + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < R; ++j)
+            if (c * R + j < kBM) st_dsmem_b32(dst + j * 4, r[c * R + j]);
         }
       }
     }
@@ -210,24 +222,23 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int q = 0; q < S; ++q) {                            // source CTAs in order: deterministic
         const float* src = recv + (q * kBN + threadIdx.x) * STRIDE;
+        if constexpr (vec_rows(S)) {
 #pragma unroll
-        for (int j = 0; j < R; j += (R >= 4 ? 4 : 2)) {
-          if constexpr (R >= 4) {
+          for (int j = 0; j < R; j += 4) {
             const float4 v = *reinterpret_cast<const float4*>(src + j);
             acc[j] += v.x;
             acc[j + 1] += v.y;
             acc[j + 2] += v.z;
             acc[j + 3] += v.w;
-          } else {
-            const float2 v = *reinterpret_cast<const float2*>(src + j);
-            acc[j] += v.x;
-            acc[j + 1] += v.y;
           }
+        } else {
+#pragma unroll
+          for (int j = 0; j < R; ++j) acc[j] += src[j];
         }
       }
 #pragma unroll
       for (int j = 0; j < R; ++j)
-        if (split * R + j < a.M) store_out(a, split * R + j, n, acc[j]);
+        if (split * R + j < a.M && split * R + j < kBM) store_out(a, split * R + j, n, acc[j]);
     }
     if (tr && threadIdx.x == 0) tr[6] = global_ns();
   }
@@ -324,7 +335,9 @@ static int skinny_max_clusters(int S) {
 
 // Split count (cluster size) for a skinny product: a power of two up to 16 so that column tiles x splits
 // fill about one wave of one CTA per SM, each split has at least two k-blocks, and all the clusters (one
-// per column tile) are resident together.
+// per column tile) are resident together.  (Clusters of 3, 6 or 9 CTAs, which fill more SMs for some
+// shapes, measured slower on B200: 9.2 against 4.0 us for a [32 x 768] x [768 x 2304] product with 6
+// against 4, 10.1 against 5.3 us for [32 x 2048] x [2048 x 2048] with 9 against 4.)
 int pcb_skinny_splits(int N, int K, int num_sms) {
   const int ntiles = (N + skinny::kBN - 1) / skinny::kBN;
   const int total_kb = (K + skinny::kBK - 1) / skinny::kBK;
