@@ -10,11 +10,13 @@
 // slice of the cache for all G query heads that share that kv head (GQA), keeps an online-softmax
 // state per warp, merges its 4 warps in shared memory and writes (m, l, acc) for the split; a
 // second launch merges the splits.  Keys are scored lane-per-key (no shuffles in the dot product),
-// values are accumulated lane-per-dimension (coalesced 2*HD-byte rows), so K and V are each read
-// once from HBM.
+// values are accumulated lane-per-dimension (coalesced 2*HD-byte rows) and requested early (half of a
+// tile's value rows together with its keys, the other half right after the key math), so K and V are
+// each read once from HBM in little more than one memory round trip per tile.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <cstdint>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -64,19 +66,43 @@ decode_attn_split_kernel(const __nv_bfloat16* __restrict__ q,      // [B, H, HD]
   }
 
   __shared__ float ssc[kDecWarps][G][32];
+  constexpr int LPK = HD / 8;                     // lanes per key row (16 for HD 128, 8 for HD 64)
+  constexpr int KPS = 32 / LPK;                   // keys per warp step
+  constexpr int STEPS = 32 / KPS;
+  const int sub = lane / LPK, c = lane % LPK;
+  // this lane's 8 query dims (c * 8 ..) stay in registers for one or two heads
+  constexpr bool QREG = G <= 2;
+  float qr[QREG ? G : 1][8];
+  if constexpr (QREG) {
+#pragma unroll
+    for (int hh = 0; hh < G; ++hh)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) qr[hh][e] = sq[hh][c * 8 + e];
+  }
+  using VRaw = typename std::conditional<DPL == 4, uint2, uint32_t>::type;
   for (int tile = t0 + warp * 32; tile < t1; tile += kDecWarps * 32) {
     // scores: half-warps take one key row each (HD/8 lanes x 16 bytes, coalesced), two rows per step;
-    // the partial dot products are reduced across the half-warp and parked in shared memory
-    constexpr int LPK = HD / 8;                   // lanes per key row (16 for HD 128, 8 for HD 64)
-    constexpr int KPS = 32 / LPK;                 // keys per warp step
-    const int sub = lane / LPK, c = lane % LPK;
-    constexpr int STEPS = 32 / KPS;
-    uint4 raw_all[STEPS];                         // every load of the tile in flight before any math
+    // the partial dot products are reduced across the half-warp and parked in shared memory.  The first
+    // 16 value rows are requested together with the keys and the other 16 right after the key math, so a
+    // tile costs little more than one memory round trip; rows past the slice repeat its last row
+    // (weight 0).
+    const int nk = min(32, t1 - tile);
+    uint4 raw_all[STEPS];
 #pragma unroll
     for (int it = 0; it < STEPS; ++it) {
       const int t = tile + it * KPS + sub;
       raw_all[it] = t < t1 ? __ldg(reinterpret_cast<const uint4*>(kc + kvbase + (long long)t * HD) + c)
                            : make_uint4(0u, 0u, 0u, 0u);
+    }
+    // (with four or eight heads per kv head the registers go to the per-head state: values follow the
+    // softmax in batches of eight rows instead)
+    constexpr bool EARLY_V = G <= 2;
+    VRaw va[EARLY_V ? 16 : 1], vb[EARLY_V ? 16 : 1];
+    if constexpr (EARLY_V) {
+#pragma unroll
+      for (int u = 0; u < 16; ++u)
+        va[u] = __ldg(reinterpret_cast<const VRaw*>(vc + kvbase + (long long)(tile + min(u, nk - 1)) * HD +
+                                                    lane * DPL));
     }
 #pragma unroll
     for (int it = 0; it < STEPS; ++it) {
@@ -91,7 +117,10 @@ decode_attn_split_kernel(const __nv_bfloat16* __restrict__ q,      // [B, H, HD]
         for (int e = 0; e < 4; ++e) {
           const float2 kv = __bfloat1622float2(p2[e]);
 #pragma unroll
-          for (int hh = 0; hh < G; ++hh) part[hh] += sq[hh][c * 8 + 2 * e] * kv.x + sq[hh][c * 8 + 2 * e + 1] * kv.y;
+          for (int hh = 0; hh < G; ++hh) {
+            if constexpr (QREG) part[hh] += qr[hh][2 * e] * kv.x + qr[hh][2 * e + 1] * kv.y;
+            else part[hh] += sq[hh][c * 8 + 2 * e] * kv.x + sq[hh][c * 8 + 2 * e + 1] * kv.y;
+          }
         }
       }
 #pragma unroll
@@ -100,6 +129,12 @@ decode_attn_split_kernel(const __nv_bfloat16* __restrict__ q,      // [B, H, HD]
         for (int o = LPK / 2; o > 0; o >>= 1) part[hh] += __shfl_xor_sync(0xffffffffu, part[hh], o);
         if (c == 0) ssc[warp][hh][kk + sub] = part[hh];
       }
+    }
+    if constexpr (EARLY_V) {
+#pragma unroll
+      for (int u = 0; u < 16; ++u)
+        vb[u] = __ldg(reinterpret_cast<const VRaw*>(vc + kvbase + (long long)(tile + min(16 + u, nk - 1)) * HD +
+                                                    lane * DPL));
     }
     __syncwarp();
     const int t = tile + lane;
@@ -123,28 +158,37 @@ decode_attn_split_kernel(const __nv_bfloat16* __restrict__ q,      // [B, H, HD]
 #pragma unroll
       for (int j = 0; j < DPL; ++j) acc[hh][j] *= corr;
     }
-    const int nk = min(32, t1 - tile);
-    for (int k0 = 0; k0 < nk; k0 += 8) {         // eight value rows in flight at a time
-      float vv[8][DPL];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int kk = min(k0 + u, nk - 1);       // rows past nk get weight 0 below
-        const __nv_bfloat16* vrow = vc + kvbase + (long long)(tile + kk) * HD + lane * DPL;
-#pragma unroll
-        for (int j = 0; j < DPL; j += 2) {
-          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(vrow + j));
-          vv[u][j] = f.x;
-          vv[u][j + 1] = f.y;
-        }
+    auto pv = [&](const VRaw& raw, int u) {
+      float vv[DPL];
+      if constexpr (DPL == 4) {
+        const float2 a0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
+        const float2 a1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+        vv[0] = a0.x; vv[1] = a0.y; vv[2] = a1.x; vv[3] = a1.y;
+      } else {
+        const float2 a0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw));
+        vv[0] = a0.x; vv[1] = a0.y;
       }
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
+      for (int hh = 0; hh < G; ++hh) {
+        const float pk = __shfl_sync(0xffffffffu, p[hh], u);   // 0 for keys past the slice
 #pragma unroll
-        for (int hh = 0; hh < G; ++hh) {
-          const float pk = k0 + u < nk ? __shfl_sync(0xffffffffu, p[hh], k0 + u) : 0.f;
+        for (int j = 0; j < DPL; ++j) acc[hh][j] += pk * vv[j];
+      }
+    };
+    if constexpr (EARLY_V) {
 #pragma unroll
-          for (int j = 0; j < DPL; ++j) acc[hh][j] += pk * vv[u][j];
-        }
+      for (int u = 0; u < 16; ++u) pv(va[u], u);
+#pragma unroll
+      for (int u = 0; u < 16; ++u) pv(vb[u], 16 + u);
+    } else {
+      for (int k0 = 0; k0 < nk; k0 += 8) {       // eight value rows in flight at a time
+        VRaw vr[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          vr[u] = __ldg(reinterpret_cast<const VRaw*>(vc + kvbase + (long long)(tile + min(k0 + u, nk - 1)) * HD +
+                                                      lane * DPL));
+#pragma unroll
+        for (int u = 0; u < 8; ++u) pv(vr[u], k0 + u);
       }
     }
   }

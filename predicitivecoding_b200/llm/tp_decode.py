@@ -73,9 +73,10 @@ class TensorParallelDecoder:
         self.rope_cs = torch.stack((cos, sin), dim=-1).contiguous()          # [cap, hd/2, 2]
         self.scale = 1.0 / math.sqrt(hd)
         # decode-step state (static buffers so the step can be captured)
-        # key splits per (sequence, head): 3 measured best on B200 for 256-512 (sequence, head) pairs at
-        # 640 cached keys (53 / 24 us against 55 / 27 us with 2 and 61 / 29 us with 4)
-        nsplit = max(1, min(3, self.cap // 64))
+        # key splits per (sequence, head): one split while the (sequence, head) pairs fit in one wave of the
+        # attention kernel (3 CTAs per SM), two beyond; measured on B200 at 640 cached keys: 256 pairs
+        # 13.9 us with 1 split (16.8 with 2), 512 pairs 35.1 us with 2 (38.5 with 1, 35.7 with 3)
+        nsplit = max(1, min(1 if batch * self.Hl <= 3 * 148 else 2, self.cap // 64))
         self.nsplit = nsplit
         self.pacc = torch.empty(batch * self.Hl * nsplit * hd, device=dev)
         self.pml = torch.empty(batch * self.Hl * nsplit * 2, device=dev)
