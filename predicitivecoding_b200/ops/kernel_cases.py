@@ -244,6 +244,45 @@ def decode_linear_table(iters: int = 50) -> list:
     return rows
 
 
+def decode_attn_split_table(iters: int = 20) -> list:
+    """Split-KV decode attention of the 1.3B decoder's decode step (batch 32, 640 cached keys of hd 128;
+    16 heads at TP=1, 8 at TP=2) for each key-split count: device time per call from CUDA events around
+    one replay of a CUDA graph of `iters` calls, and the K/V stream rate."""
+    from . import decode_attn
+    dev = "cuda"
+    rows = []
+    for (B, H, hd, L, cap) in ((32, 16, 128, 640, 768), (32, 8, 128, 640, 768)):
+        q = torch.randn(B, H, hd, device=dev).to(torch.bfloat16)
+        kc = torch.randn(B, H, cap, hd, device=dev).to(torch.bfloat16)
+        vc = torch.randn(B, H, cap, hd, device=dev).to(torch.bfloat16)
+        lens = torch.full((B,), L, dtype=torch.int32, device=dev)
+        out = torch.empty_like(q)
+        for ns in (1, 2, 3, 4, 8):
+            scratch = (torch.empty(B * H * ns * hd, device=dev), torch.empty(B * H * ns * 2, device=dev))
+            fn = lambda: decode_attn(q, kc, vc, lens, hd ** -0.5, nsplit=ns, out=out, scratch=scratch)
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            g, st = torch.cuda.CUDAGraph(), torch.cuda.Stream()
+            st.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(st):
+                with torch.cuda.graph(g, stream=st):
+                    for _ in range(iters):
+                        fn()
+            torch.cuda.current_stream().wait_stream(st)
+            g.replay()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            g.replay()
+            b.record()
+            torch.cuda.synchronize()
+            us = a.elapsed_time(b) * 1e3 / iters
+            rows.append({"batch": B, "heads": H, "hd": hd, "keys": L, "nsplit": ns, "us": round(us, 2),
+                         "kv_TBps": round(2 * B * H * L * hd * 2 / us / 1e6, 2)})
+    return rows
+
+
 def step_breakdown(steps: int = 2) -> list:
     """Device time per kernel of one step of the 124M decoder trainer (micro-batch 16 x 1024), from the
     CUDA activity records of torch.profiler over `steps` steps after 3 warm-up steps; eager launches
@@ -276,12 +315,17 @@ def step_breakdown(steps: int = 2) -> list:
 
 def main() -> None:
     p = argparse.ArgumentParser()
-    p.add_argument("case", choices=CASES + ("all", "decoder_gemms", "decode_linears", "step_breakdown"))
+    p.add_argument("case", choices=CASES + ("all", "decoder_gemms", "decode_linears", "decode_attn_splits",
+                                            "step_breakdown"))
     p.add_argument("--time", type=int, default=0, help="time N launches after warm-up")
     a = p.parse_args()
     ext()
     if a.case == "decoder_gemms":
         for row in decoder_gemm_table():
+            print(json.dumps(row))
+        return
+    if a.case == "decode_attn_splits":
+        for row in decode_attn_split_table():
             print(json.dumps(row))
         return
     if a.case == "decode_linears":
