@@ -7,7 +7,7 @@
 // thread-block cluster (S = 1, 2, 4, 8 or 16) until about one CTA per SM streams a disjoint weight slab.
 // Each CTA: one TMA producer thread loads [64 k x 128 n] weight tiles (MN-major, two 64-column boxes)
 // and the matching [32 m x 64 k] activation tile into a 9-stage ring (the bytes in flight per SM bound a
-// weight stream), one thread issues tcgen05.mma (M 128, N 32, K 16 x 4) into 32 TMEM columns, and the
+// weight stream; a 4-stage ring with two CTAs per SM when that allows more CTAs), one thread issues tcgen05.mma (M 128, N 32, K 16 x 4) into 32 TMEM columns, and the
 // four warps read the accumulator back (thread = weight column, registers = the 32 rows).  With S = 1 the
 // rows are stored directly.  Otherwise CTA c of the cluster owns rows [c R, (c + 1) R), R = ceil(32 / S):
 // every CTA pushes each owner its R rows with vector stores into the owner's shared memory (fire and
@@ -34,7 +34,8 @@ namespace skinny {
 constexpr int kBN = 128;                 // weight columns per CTA (MMA M)
 constexpr int kBM = 32;                  // activation rows (MMA N)
 constexpr int kBK = 64;
-constexpr int kStages = 9;               // 144 KB of weights in flight per CTA, one CTA per SM
+constexpr int kStagesWide = 9;           // 144 KB of weights in flight per CTA, one CTA per SM
+constexpr int kStagesPair = 4;           // 64 KB per CTA, two CTAs per SM (twice the CTAs resident)
 constexpr int kMaxSplits = 16;           // cluster size (above 8 where the GPU allows it)
 constexpr int W_BYTES = kBK * kBN * 2;   // two [64 n x 64 k] boxes, 128B swizzle
 constexpr int X_BYTES = kBM * kBK * 2;   // [32 m x 64 k], 128B swizzle
@@ -52,12 +53,16 @@ __host__ __device__ constexpr int recv_bytes(int S) { return S == 1 ? 0 : S * kB
 __host__ __device__ constexpr int max_recv_bytes(int S = 2) {
   return S > kMaxSplits ? 0 : (recv_bytes(S) > max_recv_bytes(S + 1) ? recv_bytes(S) : max_recv_bytes(S + 1));
 }
-constexpr int RECV_OFF = kStages * STAGE;
 constexpr int RECV_MAX = max_recv_bytes();
-constexpr int BAR_OFF = RECV_OFF + RECV_MAX;
-constexpr int SMEM = BAR_OFF + 256 + 1024;
+template <int STAGES>
+struct Layout {
+  static constexpr int RECV_OFF = STAGES * STAGE;
+  static constexpr int BAR_OFF = RECV_OFF + RECV_MAX;
+  static constexpr int SMEM = BAR_OFF + 256 + 1024;
+};
 constexpr int kThreads = 128;
-static_assert(SMEM <= 232448, "shared memory budget");
+static_assert(Layout<kStagesWide>::SMEM <= 232448, "shared memory budget");
+static_assert(2 * (Layout<kStagesPair>::SMEM + 1024) <= 233472, "two CTAs per SM");
 
 struct Args {
   void* y;                 // [M, N] bf16 or fp32
@@ -87,19 +92,20 @@ PCB_DEVICE void store_out(const Args& a, int m, int n, float v) {
   else reinterpret_cast<__nv_bfloat16*>(a.y)[(long long)m * a.ldy + n] = __float2bfloat16_rn(v);
 }
 
-template <int S>
+template <int S, int kStages>
 __global__ void __launch_bounds__(kThreads, 1)
     skinny_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, const Args a) {
   constexpr int R = rows_per_owner(S);       // rows each CTA of the cluster stores (the last ones may have fewer)
   constexpr int STRIDE = recv_stride(S);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + BAR_OFF);
+  using L = Layout<kStages>;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
   uint64_t* empty = full + kStages;
   uint64_t* done = empty + kStages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* recv = reinterpret_cast<float*>(smem + RECV_OFF);
+  float* recv = reinterpret_cast<float*>(smem + L::RECV_OFF);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ntile = blockIdx.x, split = blockIdx.y;   // the cluster spans blockIdx.y: rank == split
@@ -282,40 +288,46 @@ using namespace pcb;
 
 using KernelFn = void (*)(const CUtensorMap, const CUtensorMap, const skinny::Args);
 
-static KernelFn skinny_fn(int S) {
+// kernel for cluster size S (1, 2, 4, 8, 16) and ring depth (pair: 4 stages, two CTAs per SM)
+static KernelFn skinny_fn(int S, bool pair) {
   switch (S) {
-    case 1: return skinny::skinny_kernel<1>;
-    case 2: return skinny::skinny_kernel<2>;
-    case 4: return skinny::skinny_kernel<4>;
-    case 8: return skinny::skinny_kernel<8>;
-    default: return skinny::skinny_kernel<16>;
+    case 1: return pair ? skinny::skinny_kernel<1, skinny::kStagesPair> : skinny::skinny_kernel<1, skinny::kStagesWide>;
+    case 2: return pair ? skinny::skinny_kernel<2, skinny::kStagesPair> : skinny::skinny_kernel<2, skinny::kStagesWide>;
+    case 4: return pair ? skinny::skinny_kernel<4, skinny::kStagesPair> : skinny::skinny_kernel<4, skinny::kStagesWide>;
+    case 8: return pair ? skinny::skinny_kernel<8, skinny::kStagesPair> : skinny::skinny_kernel<8, skinny::kStagesWide>;
+    default:
+      return pair ? skinny::skinny_kernel<16, skinny::kStagesPair> : skinny::skinny_kernel<16, skinny::kStagesWide>;
   }
+}
+static int skinny_smem(bool pair) {
+  return pair ? skinny::Layout<skinny::kStagesPair>::SMEM : skinny::Layout<skinny::kStagesWide>::SMEM;
 }
 
 static void skinny_attrs() {
   static std::once_flag once;
   std::call_once(once, [] {
-    for (int S = 1; S <= skinny::kMaxSplits; S *= 2) {
-      cudaFuncSetAttribute(skinny_fn(S), cudaFuncAttributeMaxDynamicSharedMemorySize, skinny::SMEM);
-      cudaFuncSetAttribute(skinny_fn(S), cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    }
+    for (int S = 1; S <= skinny::kMaxSplits; S *= 2)
+      for (int pair = 0; pair < 2; ++pair) {
+        cudaFuncSetAttribute(skinny_fn(S, pair), cudaFuncAttributeMaxDynamicSharedMemorySize, skinny_smem(pair));
+        cudaFuncSetAttribute(skinny_fn(S, pair), cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+      }
     cudaGetLastError();
   });
 }
 
-// Clusters of `S` CTAs (with this kernel's shared memory) the GPU can hold at once; cached per device.
-static int skinny_max_clusters(int S) {
-  static int cache[64][skinny::kMaxSplits + 1] = {};
+// Clusters of `S` CTAs the GPU can hold at once for a ring depth; cached per device.
+static int skinny_max_clusters(int S, bool pair) {
+  static int cache[64][2][skinny::kMaxSplits + 1] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return 0;
-  int& c = cache[dev][S];
+  int& c = cache[dev][pair ? 1 : 0][S];
   if (c == 0) {
     skinny_attrs();
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(1, S, 1);
     cfg.blockDim = dim3(skinny::kThreads, 1, 1);
-    cfg.dynamicSmemBytes = skinny::SMEM;
+    cfg.dynamicSmemBytes = skinny_smem(pair);
     cudaLaunchAttribute at[1];
     at[0].id = cudaLaunchAttributeClusterDimension;
     at[0].val.clusterDim.x = 1;
@@ -324,7 +336,7 @@ static int skinny_max_clusters(int S) {
     cfg.attrs = at;
     cfg.numAttrs = 1;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, skinny_fn(S), &cfg) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&n, skinny_fn(S, pair), &cfg) != cudaSuccess) {
       cudaGetLastError();
       n = 0;
     }
@@ -333,19 +345,34 @@ static int skinny_max_clusters(int S) {
   return c;
 }
 
-// Split count (cluster size) for a skinny product: a power of two up to 16 so that column tiles x splits
-// fill about one wave of one CTA per SM, each split has at least two k-blocks, and all the clusters (one
-// per column tile) are resident together.  (Clusters of 3, 6 or 9 CTAs, which fill more SMs for some
-// shapes, measured slower on B200: 9.2 against 4.0 us for a [32 x 768] x [768 x 2304] product with 6
-// against 4, 10.1 against 5.3 us for [32 x 2048] x [2048 x 2048] with 9 against 4.)
-int pcb_skinny_splits(int N, int K, int num_sms) {
+// Split count (cluster size) and ring depth for a skinny product: a power of two up to 16 so that column
+// tiles x splits fill about one wave (one CTA per SM with the deep ring, two with the shallow one), each
+// split has at least two k-blocks, and all the clusters (one per column tile) are resident together; the
+// shallow ring is taken when it allows a larger cluster.  (Clusters of 3, 6 or 9 CTAs, which fill more
+// SMs for some shapes, measured slower on B200: 9.2 against 4.0 us for a [32 x 768] x [768 x 2304]
+// product with 6 against 4, 10.1 against 5.3 us for [32 x 2048] x [2048 x 2048] with 9 against 4.)
+// Returns splits, negated when the shallow ring is chosen.
+static int skinny_pick(int N, int K, int num_sms, bool pair) {
   const int ntiles = (N + skinny::kBN - 1) / skinny::kBN;
   const int total_kb = (K + skinny::kBK - 1) / skinny::kBK;
-  const int cap = min(min(max(1, num_sms / ntiles), max(1, total_kb / 2)), skinny::kMaxSplits);
+  const int slots = pair ? 2 * num_sms : num_sms;
+  const int cap = min(min(max(1, slots / ntiles), max(1, total_kb / 2)), skinny::kMaxSplits);
   int s = 1;
   while (s * 2 <= cap) s *= 2;
-  while (s > 1 && skinny_max_clusters(s) < ntiles) s /= 2;
+  while (s > 1 && skinny_max_clusters(s, pair) < ntiles) s /= 2;
   return s;
+}
+
+int pcb_skinny_splits(int N, int K, int num_sms) {
+  const char* e = getenv("PCB_SKINNY_RING");           // "wide" / "pair" force one ring depth
+  const bool only_wide = e && e[0] == 'w', only_pair = e && e[0] == 'p';
+  const int wide = skinny_pick(N, K, num_sms, false);
+  if (only_wide) return wide;
+  const int pair = skinny_pick(N, K, num_sms, true);
+  // more column tiles than SMs (an LM head): the shallow ring keeps them in one wave
+  // (32 x 2048 x 32000: 23.0 us against 31.3 us on the deep ring and 29.0 us on the regular GEMM)
+  const bool many_tiles = (N + skinny::kBN - 1) / skinny::kBN > num_sms;
+  return (only_pair || many_tiles || pair > wide) ? -pair : wide;
 }
 
 // Programmatic dependent launch (PCB_PDL=0 turns it off).
@@ -358,11 +385,14 @@ static bool skinny_pdl() {
 }
 
 // y [M, N] (bf16, or fp32 with y_f32) = x [M, K] bf16 @ W [K, N] bf16 (row-major), M <= 32, K split over
-// `splits` CTAs of a cluster (1, 2, 4, 8 or 16); `trace` (optional) receives 8 timestamps per CTA.
+// `splits` CTAs of a cluster (1, 2, 4, 8 or 16; negative: the same count on the shallow two-CTAs-per-SM
+// ring); `trace` (optional) receives 8 timestamps per CTA.
 // Returns 0, -1 bad arguments, -5 tensor-map encode, -(1000 + cudaError) launch.
 int pcb_skinny_gemm(const void* x, long long ldx, const void* w, long long ldw, void* y, long long ldy, int y_f32,
                     int M, int N, int K, int splits, int* err, unsigned long long* trace, cudaStream_t stream) {
   if (M < 1 || M > skinny::kBM || N < 1 || K < 1) return -1;
+  const bool pair = splits < 0;
+  if (pair) splits = -splits;
   if (splits != 1 && splits != 2 && splits != 4 && splits != 8 && splits != 16) return -1;
   if (ldx % 8 || ldw % 8 || ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15)) return -1;
   CUtensorMap tw, tx;
@@ -381,7 +411,7 @@ int pcb_skinny_gemm(const void* x, long long ldx, const void* w, long long ldw, 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((N + skinny::kBN - 1) / skinny::kBN, splits, 1);
   cfg.blockDim = dim3(skinny::kThreads, 1, 1);
-  cfg.dynamicSmemBytes = skinny::SMEM;
+  cfg.dynamicSmemBytes = skinny_smem(pair);
   cfg.stream = stream;
   cudaLaunchAttribute attr_v[2];
   attr_v[0].id = cudaLaunchAttributeClusterDimension;
@@ -392,6 +422,6 @@ int pcb_skinny_gemm(const void* x, long long ldx, const void* w, long long ldw, 
   attr_v[1].val.programmaticStreamSerializationAllowed = skinny_pdl() ? 1 : 0;
   cfg.attrs = attr_v;
   cfg.numAttrs = 2;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, skinny_fn(splits), tw, tx, a);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, skinny_fn(splits, pair), tw, tx, a);
   return e == cudaSuccess ? 0 : -(1000 + (int)e);
 }

@@ -151,8 +151,8 @@ def linear(x: torch.Tensor, w_kn: torch.Tensor, out: Optional[torch.Tensor] = No
     if out is None:
         out = torch.empty(x2.shape[0], N, device=x.device, dtype=torch.float32 if fp32 else torch.bfloat16)
     y = out.view(x2.shape[0], N)
-    # one 128-column tile per SM at most: wider products (an LM head) stream better on the regular GEMM
-    skinny_ok = (bias is None and x2.shape[0] <= SKINNY_MAX_ROWS and N <= 128 * _sm_count(x.device)
+    # up to two 128-column tiles per SM (one wave of the shallow ring); wider products take the regular GEMM
+    skinny_ok = (bias is None and x2.shape[0] <= SKINNY_MAX_ROWS and N <= 2 * 128 * _sm_count(x.device)
                  and w_kn.is_contiguous() and y.is_contiguous() and x2.shape[1] % 8 == 0 and N % 8 == 0)
     if skinny_ok:
         ext().skinny_gemm(x2, w_kn, y, None)
