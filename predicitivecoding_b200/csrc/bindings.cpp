@@ -701,7 +701,7 @@ void decode_attn(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& vc
   check(pcb_decode_attn(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), lens.data_ptr<int>(), pacc.data_ptr<float>(),
                         pml.data_ptr<float>(), out.data_ptr(), B, H, Hkv, HD, cap, nsplit, (float)scale,
                         (float)softcap, cur_stream()),
-        "decode_attn", 2);
+        "decode_attn", nsplit > 1 ? 2 : 1);
 }
 void wq_gemv(const at::Tensor& x, const at::Tensor& w, const at::Tensor& scale, at::Tensor& y, int64_t bits) {
   reqc(x, at::kFloat, "x");

@@ -9,7 +9,7 @@
 // decode attention: flash-decoding.  One CTA per (split, kv-head, sequence) walks a contiguous
 // slice of the cache for all G query heads that share that kv head (GQA), keeps an online-softmax
 // state per warp, merges its 4 warps in shared memory and writes (m, l, acc) for the split; a
-// second launch merges the splits.  Keys are scored lane-per-key (no shuffles in the dot product),
+// second launch merges the splits (with one split the CTA writes the output itself).  Keys are scored lane-per-key (no shuffles in the dot product),
 // values are accumulated lane-per-dimension (coalesced 2*HD-byte rows) and requested early (half of a
 // tile's value rows together with its keys, the other half right after the key math), so K and V are
 // each read once from HBM in little more than one memory round trip per tile.
@@ -36,6 +36,7 @@ decode_attn_split_kernel(const __nv_bfloat16* __restrict__ q,      // [B, H, HD]
                          const int* __restrict__ lens,             // [B]
                          float* __restrict__ part_acc,             // [B, H, nsplit, HD]
                          float* __restrict__ part_ml,              // [B, H, nsplit, 2]
+                         __nv_bfloat16* __restrict__ out,          // [B, H, HD], written when nsplit == 1
                          int Hkv, int cap, int nsplit, float scale, float softcap) {
   pdl_begin();
   const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
@@ -212,9 +213,14 @@ decode_attn_split_kernel(const __nv_bfloat16* __restrict__ q,      // [B, H, HD]
       ll += sm_l[w][hh] * c;
       a += sacc[w][hh][d] * c;
     }
-    const long long row = ((long long)b * H + g * G + hh) * nsplit + split;
-    part_acc[row * HD + d] = a;
-    if (d == 0) { part_ml[row * 2] = mm; part_ml[row * 2 + 1] = ll; }
+    if (nsplit == 1) {
+      // one split: this CTA has the whole row, so it writes the output (no merge launch)
+      out[((long long)b * H + g * G + hh) * HD + d] = __float2bfloat16(ll > 0.f ? a / ll : 0.f);
+    } else {
+      const long long row = ((long long)b * H + g * G + hh) * nsplit + split;
+      part_acc[row * HD + d] = a;
+      if (d == 0) { part_ml[row * 2] = mm; part_ml[row * 2 + 1] = ll; }
+    }
   }
 }
 
@@ -380,13 +386,14 @@ int launch_decode(const __nv_bfloat16* q, const __nv_bfloat16* kc, const __nv_bf
 #define PCB_DEC_CASE(GG)                                                                                       \
   case GG:                                                                                                     \
     pdl_launch(decode_attn_split_kernel<HD, GG>, grid, dim3(kDecWarps * 32), 0, s, q, kc, vc, lens, pacc, pml, \
-               Hkv, cap, nsplit, scale, softcap);                                                              \
+               out, Hkv, cap, nsplit, scale, softcap);                                                         \
     break;
     PCB_DEC_CASE(1) PCB_DEC_CASE(2) PCB_DEC_CASE(4) PCB_DEC_CASE(8)
 #undef PCB_DEC_CASE
     default: return -2;
   }
-  pdl_launch(decode_attn_combine_kernel<HD>, dim3(B * Hkv * G), dim3(HD), 0, s, pacc, pml, out, nsplit);
+  if (nsplit > 1)
+    pdl_launch(decode_attn_combine_kernel<HD>, dim3(B * Hkv * G), dim3(HD), 0, s, pacc, pml, out, nsplit);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 

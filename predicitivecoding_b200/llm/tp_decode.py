@@ -73,9 +73,10 @@ class TensorParallelDecoder:
         self.rope_cs = torch.stack((cos, sin), dim=-1).contiguous()          # [cap, hd/2, 2]
         self.scale = 1.0 / math.sqrt(hd)
         # decode-step state (static buffers so the step can be captured)
-        # key splits per (sequence, head): one split while the (sequence, head) pairs fit in one wave of the
-        # attention kernel (3 CTAs per SM), two beyond; measured on B200 at 640 cached keys: 256 pairs
-        # 13.9 us with 1 split (16.8 with 2), 512 pairs 35.1 us with 2 (38.5 with 1, 35.7 with 3)
+        # key splits per (sequence, head): one split (the attention kernel then writes the output itself, no
+        # merge launch) while the (sequence, head) pairs fit one wave of the kernel (3 CTAs per SM), two
+        # beyond; measured on B200 at 640 cached keys: 256 pairs 13.9 us with 1 split (16.8 + merge with 2);
+        # 512 pairs 35.1 us + merge with 2 against 38.5 us with 1 (decode step 2.09 against 2.15 ms)
         nsplit = max(1, min(1 if batch * self.Hl <= 3 * 148 else 2, self.cap // 64))
         self.nsplit = nsplit
         self.pacc = torch.empty(batch * self.Hl * nsplit * hd, device=dev)
