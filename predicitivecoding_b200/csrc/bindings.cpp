@@ -64,7 +64,7 @@ int pcb_coll_gather(const void* const* src_peers, void* out, long long chunk, lo
                     int dtype, int num_sms, cudaStream_t s);
 int pcb_rope_append(const void* qkv, const float* cs_table, const long long* pos, void* qo, void* kc, void* vc, int B,
                     int H, int HD, int cap, cudaStream_t s);
-int pcb_swiglu_rows(const void* gu, void* a, int rows, int F, cudaStream_t s);
+int pcb_swiglu_rows(const void* gu, void* a, int rows, int F, int il16, cudaStream_t s);
 long long pcb_checked_violations();
 int pcb_attn_bwd_stats(unsigned long long* out);
 int pcb_attn_fwd_stats(unsigned long long* out);
@@ -129,7 +129,8 @@ int pcb_moe_seg_colsum(const void* x, const int* seg, int E, int N, int cap, flo
 
 int pcb_skinny_splits(int N, int K, int num_sms);
 int pcb_skinny_gemm(const void* x, long long ldx, const void* w, long long ldw, void* y, long long ldy, int y_f32,
-                    int M, int N, int K, int splits, int* err, unsigned long long* trace, cudaStream_t stream);
+                    int M, int N, int K, int splits, int* err, unsigned long long* trace, int swiglu,
+                    cudaStream_t stream);
 
 extern "C" void pcb_set_gemm_mode(int mode);
 
@@ -300,21 +301,23 @@ void gemm_grouped(const at::Tensor& a, const at::Tensor& b, bool b_mn, int64_t e
 // `trace` (int64, optional) receives 8 globaltimer stamps per CTA: start, weights requested, dependency
 // wait over, first tile landed, accumulator read, partials visible, rows stored, end.
 void skinny_gemm(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, const c10::optional<at::Tensor>& err,
-                 const c10::optional<at::Tensor>& trace) {
+                 const c10::optional<at::Tensor>& trace, bool swiglu) {
   req(x, at::kBFloat16, "x");
   req(w, at::kBFloat16, "w");
   PCB_CHECK(y.scalar_type() == at::kBFloat16 || y.scalar_type() == at::kFloat, "skinny_gemm: y bf16 or fp32");
   PCB_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(0), "skinny_gemm: x [M, K], w [K, N]");
-  PCB_CHECK(x.size(0) <= 32 && y.size(0) == x.size(0) && y.size(1) == w.size(1), "skinny_gemm: M <= 32, y [M, N]");
+  PCB_CHECK(x.size(0) <= 32 && y.size(0) == x.size(0) && y.size(1) == (swiglu ? w.size(1) / 2 : w.size(1)),
+            "skinny_gemm: M <= 32, y [M, N] ([M, N / 2] with the SwiGLU epilogue)");
   const int M = x.size(0), K = x.size(1), N = w.size(1);
   PCB_CHECK(K % 8 == 0 && N % 8 == 0, "skinny_gemm: K and N must be multiples of 8 (16-byte rows)");
+  PCB_CHECK(!swiglu || N % 32 == 0, "skinny_gemm: the SwiGLU epilogue needs N a multiple of 32");
   const at::cuda::CUDAGuard guard(x.device());
   const int splits = pcb_skinny_splits(N, K, num_sms());
   check(pcb_skinny_gemm(x.data_ptr(), row_stride(x, "x"), w.data_ptr(), row_stride(w, "w"), y.data_ptr(),
                         row_stride(y, "y"), y.scalar_type() == at::kFloat ? 1 : 0, M, N, K, splits,
                         err ? err->data_ptr<int>() : nullptr,
                         trace ? reinterpret_cast<unsigned long long*>(trace->data_ptr<int64_t>()) : nullptr,
-                        cur_stream()),
+                        swiglu ? 1 : 0, cur_stream()),
         "skinny_gemm");
 }
 
@@ -845,12 +848,12 @@ int64_t rope_append(const at::Tensor& qkv, const at::Tensor& cs_table, const at:
                          kc.data_ptr(), vc.data_ptr(), (int)kc.size(0), (int)kc.size(1), (int)kc.size(3),
                          (int)kc.size(2), cur_stream());
 }
-int64_t swiglu_rows(const at::Tensor& gu, at::Tensor& a) {
+int64_t swiglu_rows(const at::Tensor& gu, at::Tensor& a, bool interleave16) {
   reqc(gu, at::kBFloat16, "gu");
   reqc(a, at::kBFloat16, "a");
-  const int F = a.size(-1);
+  const int64_t F = a.size(-1);
   PCB_CHECK(gu.size(-1) == 2 * F, "swiglu_rows: gu must be [rows, 2F]");
-  return pcb_swiglu_rows(gu.data_ptr(), a.data_ptr(), (int)(a.numel() / F), F, cur_stream());
+  return pcb_swiglu_rows(gu.data_ptr(), a.data_ptr(), (int)(a.numel() / F), F, interleave16 ? 1 : 0, cur_stream());
 }
 
 
@@ -926,7 +929,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_pc", &gemm_pc);
   m.def("gemm_grouped", &gemm_grouped);
   m.def("skinny_gemm", &skinny_gemm, py::arg("x"), py::arg("w"), py::arg("y"), py::arg("err") = py::none(),
-        py::arg("trace") = py::none());
+        py::arg("trace") = py::none(), py::arg("swiglu") = false);
   m.def("moe_route", &moe_route);
   m.def("moe_dispatch", &moe_dispatch);
   m.def("moe_gather", &moe_gather);
@@ -984,7 +987,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       for (int i = 0; i < 12; ++i) out.push_back((int64_t)v[i]);
     return out;
   });
-  m.def("swiglu_rows", &swiglu_rows);
+  m.def("swiglu_rows", &swiglu_rows, py::arg("gu"), py::arg("a"), py::arg("interleave16") = false);
   m.def("annotate", &annotate);
   m.def("coll_reduce", &coll_reduce);
   m.def("coll_reduce_push", &coll_reduce_push);

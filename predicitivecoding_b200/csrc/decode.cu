@@ -424,14 +424,16 @@ __global__ void rope_append_kernel(const __nv_bfloat16* __restrict__ qkv, const 
 
 // a[r, j] = silu(gu[r, j]) * gu[r, F + j] for gu [rows, 2F] bf16 (gate | up), a [rows, F] bf16
 __global__ void swiglu_rows_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* __restrict__ a, int rows,
-                                   int F) {
+                                   int F, int il16) {
   pdl_begin();
   const long long n = (long long)rows * F;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     const long long r = i / F;
     const int j = (int)(i % F);
-    const float g = __bfloat162float(gu[r * 2 * F + j]);
-    const float u = __bfloat162float(gu[r * 2 * F + F + j]);
+    // gate | up halves, or alternating blocks of 16 gate and 16 up columns
+    const long long gi = r * 2 * F + (il16 ? (j >> 4) * 32 + (j & 15) : j);
+    const float g = __bfloat162float(gu[gi]);
+    const float u = __bfloat162float(gu[gi + (il16 ? 16 : F)]);
     a[i] = __float2bfloat16(g / (1.f + __expf(-g)) * u);
   }
 }
@@ -511,11 +513,12 @@ int pcb_rope_append(const void* qkv, const float* cs_table, const long long* pos
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
-int pcb_swiglu_rows(const void* gu, void* a, int rows, int F, cudaStream_t s) {
+int pcb_swiglu_rows(const void* gu, void* a, int rows, int F, int il16, cudaStream_t s) {
+  if (il16 && F % 16) return -2;
   const long long n = (long long)rows * F;
   long long blocks = (n + 255) / 256;
   if (blocks > 148 * 8) blocks = 148 * 8;
   pdl_launch(swiglu_rows_kernel, dim3((unsigned)blocks), dim3(256), 0, s, reinterpret_cast<const __nv_bfloat16*>(gu),
-             reinterpret_cast<__nv_bfloat16*>(a), rows, F);
+             reinterpret_cast<__nv_bfloat16*>(a), rows, F, il16);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }

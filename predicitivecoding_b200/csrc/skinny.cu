@@ -14,6 +14,9 @@
 // forget), one cluster barrier makes them visible, and each owner sums its S partials in a fixed order
 // and stores its rows -- no global workspace, no atomics, the same bits on every run, one barrier.
 //
+// A SwiGLU epilogue (W's columns in alternating blocks of 16 gate and 16 up columns, so each warp holds
+// both halves of its 16 features) writes silu(gate) * up instead of the product.
+//
 // Launched as a programmatic dependent: the weights are not written by the kernels before it, so the
 // first ring of weight tiles is requested (right after the barriers are initialised, while TMEM is being
 // allocated) before griddepcontrol.wait and streams in while the previous kernel drains; activations
@@ -71,6 +74,7 @@ struct Args {
   int y_f32;
   int* err;
   unsigned long long* trace;  // optional: 8 globaltimer stamps (ns) per CTA at the phase boundaries
+  int swiglu;                 // 1: W's columns alternate 16 gate / 16 up columns; y [M, N / 2] = silu(g) * u
 };
 
 PCB_DEVICE unsigned long long global_ns() {
@@ -90,6 +94,20 @@ PCB_DEVICE void st_dsmem_b32(uint32_t addr, uint32_t a) {
 PCB_DEVICE void store_out(const Args& a, int m, int n, float v) {
   if (a.y_f32) reinterpret_cast<float*>(a.y)[(long long)m * a.ldy + n] = v;
   else reinterpret_cast<__nv_bfloat16*>(a.y)[(long long)m * a.ldy + n] = __float2bfloat16_rn(v);
+}
+
+// Store of row m's value v in column n (thread = column, a warp = 32 aligned columns).  With the SwiGLU
+// epilogue a warp's columns are 16 gate columns then the 16 matching up columns: lanes 0-15 take the up
+// value from lane + 16 and store silu(gate) * up as feature (n / 32) * 16 + lane.  Every lane of the warp
+// must call it (the shuffle); `ok` guards the store.
+PCB_DEVICE void store_act(const Args& a, int m, int n, float v, bool ok) {
+  if (!a.swiglu) {
+    if (ok) store_out(a, m, n, v);
+    return;
+  }
+  const float up = __shfl_down_sync(0xffffffffu, v, 16);
+  const int lane = threadIdx.x & 31;
+  if (ok && lane < 16) store_out(a, m, (n >> 5) * 16 + lane, v / (1.f + __expf(-v)) * up);
 }
 
 template <int S, int kStages>
@@ -195,11 +213,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (tr && threadIdx.x == 0) tr[4] = global_ns();
   const int n = n0 + threadIdx.x;
   if constexpr (S == 1) {
-    if (n < a.N) {
 #pragma unroll
-      for (int m = 0; m < kBM; ++m)
-        if (m < a.M) store_out(a, m, n, __uint_as_float(r[m]));
-    }
+    for (int m = 0; m < kBM; ++m)
+      if (m < a.M) store_act(a, m, n, __uint_as_float(r[m]), n < a.N);   // m < M is warp-uniform
   } else {
     // push rows [c R, (c + 1) R) to owner c, at [split][column][row - c R] of its receive buffer
     const uint32_t mine = smem_u32(recv) + (uint32_t)((split * kBN + threadIdx.x) * STRIDE * 4);
@@ -221,7 +237,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     cluster_sync_all();   // release the pushes / acquire the partials addressed to this CTA
     if (tr && threadIdx.x == 0) tr[5] = global_ns();
-    if (split * R < a.M && n < a.N) {
+    if (split * R < a.M) {                                      // uniform over the CTA
       float acc[R];
 #pragma unroll
       for (int j = 0; j < R; ++j) acc[j] = 0.f;
@@ -244,7 +260,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
 #pragma unroll
       for (int j = 0; j < R; ++j)
-        if (split * R + j < a.M && split * R + j < kBM) store_out(a, split * R + j, n, acc[j]);
+        if (split * R + j < a.M && split * R + j < kBM) store_act(a, split * R + j, n, acc[j], n < a.N);
     }
     if (tr && threadIdx.x == 0) tr[6] = global_ns();
   }
@@ -386,10 +402,12 @@ static bool skinny_pdl() {
 
 // y [M, N] (bf16, or fp32 with y_f32) = x [M, K] bf16 @ W [K, N] bf16 (row-major), M <= 32, K split over
 // `splits` CTAs of a cluster (1, 2, 4, 8 or 16; negative: the same count on the shallow two-CTAs-per-SM
-// ring); `trace` (optional) receives 8 timestamps per CTA.
+// ring); `trace` (optional) receives 8 timestamps per CTA; `swiglu`: W's columns alternate 16 gate and 16
+// up columns (N a multiple of 32) and y [M, N / 2] receives silu(gate) * up.
 // Returns 0, -1 bad arguments, -5 tensor-map encode, -(1000 + cudaError) launch.
 int pcb_skinny_gemm(const void* x, long long ldx, const void* w, long long ldw, void* y, long long ldy, int y_f32,
-                    int M, int N, int K, int splits, int* err, unsigned long long* trace, cudaStream_t stream) {
+                    int M, int N, int K, int splits, int* err, unsigned long long* trace, int swiglu,
+                    cudaStream_t stream) {
   if (M < 1 || M > skinny::kBM || N < 1 || K < 1) return -1;
   const bool pair = splits < 0;
   if (pair) splits = -splits;
@@ -407,6 +425,8 @@ int pcb_skinny_gemm(const void* x, long long ldx, const void* w, long long ldw, 
   a.y_f32 = y_f32;
   a.err = err;
   a.trace = trace;
+  if (swiglu && N % 32) return -1;
+  a.swiglu = swiglu ? 1 : 0;
   skinny_attrs();
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((N + skinny::kBN - 1) / skinny::kBN, splits, 1);

@@ -34,7 +34,7 @@ from ..models.decoder_lm import DecoderLM, rope_tables
 def tp_decode_supports(cfg: DecoderLmConfig, world: int) -> bool:
     return (cfg.use_rms_norm and cfg.use_rope and cfg.ffn == "swiglu" and cfg.num_experts == 0
             and cfg.block_pattern is None and cfg.num_loops == 1 and not cfg.use_plan
-            and cfg.num_heads % world == 0 and cfg.ff_dim % world == 0 and cfg.vocab % world == 0
+            and cfg.num_heads % world == 0 and cfg.ff_dim % (16 * world) == 0 and cfg.vocab % world == 0
             and cfg.head_dim in (64, 128))
 
 
@@ -109,7 +109,9 @@ class TensorParallelDecoder:
                 self._shard(f"b{l}.ln2", blk.ln2_g)
                 self._shard(f"b{l}.wqkv", torch.cat((blk.wq[:, hs], blk.wk[:, hs], blk.wv[:, hs]), 1))
                 self._shard(f"b{l}.wo", blk.wo[hs, :])
-                self._shard(f"b{l}.w13", torch.cat((blk.w1[:, fs], blk.w3[:, fs]), 1))
+                # gate and up in alternating 16-column blocks: the decode projection applies SwiGLU in its
+                # epilogue (each warp of the skinny kernel holds both halves of 16 features)
+                self._shard(f"b{l}.w13", ops.interleave16(blk.w1[:, fs], blk.w3[:, fs]))
                 self._shard(f"b{l}.w2", blk.w2[fs, :])
 
     def _random(self, seed: int) -> None:
@@ -130,7 +132,7 @@ class TensorParallelDecoder:
             self.W[f"b{l}.ln2"] = torch.ones(D, device=dev, dtype=torch.bfloat16)
             self.W[f"b{l}.wqkv"] = rn(own, D, 3 * self.Dl)
             self.W[f"b{l}.wo"] = rn(own, self.Dl, D)
-            self.W[f"b{l}.w13"] = rn(own, D, 2 * self.Fl)
+            self.W[f"b{l}.w13"] = rn(own, D, 2 * self.Fl)   # random: already "interleaved"
             self.W[f"b{l}.w2"] = rn(own, self.Fl, D)
 
     # ------------------------------------------------------------------ pieces
@@ -159,9 +161,7 @@ class TensorParallelDecoder:
         W, L = self.W, self.cfg.num_blocks
         o = attn(ops.linear(h, W[f"b{l}.wqkv"]), l)
         h2 = self._row_parallel(o, W[f"b{l}.wo"], x, W[f"b{l}.ln2"], bufs)
-        gu = ops.linear(h2, W[f"b{l}.w13"])
-        a = torch.empty(gu.shape[0], self.Fl, device=self.device, dtype=torch.bfloat16)
-        ops.ext().swiglu_rows(gu, a)
+        a = ops.linear_swiglu(h2, W[f"b{l}.w13"])
         nxt = W[f"b{l + 1}.ln1"] if l + 1 < L else W["lnf"]
         return self._row_parallel(a, W[f"b{l}.w2"], x, nxt, bufs)
 

@@ -161,6 +161,39 @@ def linear(x: torch.Tensor, w_kn: torch.Tensor, out: Optional[torch.Tensor] = No
     return out.view(*shape[:-1], N)
 
 
+FUSED_SWIGLU = os.environ.get("PCB_FUSED_SWIGLU", "1") != "0"   # 0: GEMM + SwiGLU pass for every row count
+
+
+def interleave16(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """[K, F] gate and up weights -> [K, 2F] with alternating blocks of 16 gate and 16 up columns, the
+    layout linear_swiglu reads (F a multiple of 16)."""
+    K, F_ = gate.shape
+    if F_ % 16 or up.shape != gate.shape:
+        raise ValueError("interleave16 needs equal [K, F] gate and up with F a multiple of 16")
+    return torch.stack((gate.reshape(K, F_ // 16, 16), up.reshape(K, F_ // 16, 16)), 2).reshape(K, 2 * F_)
+
+
+def linear_swiglu(x: torch.Tensor, w_il: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """silu(x @ W_gate) * (x @ W_up) for W in the interleave16 layout: bf16 [..., F].  Up to 32 rows run
+    the skinny kernel with the SwiGLU epilogue (one launch); more rows run the GEMM and a SwiGLU pass."""
+    shape = x.shape
+    x2 = x.reshape(-1, shape[-1])
+    if not x2.is_contiguous():
+        x2 = x2.contiguous()
+    F_ = w_il.shape[1] // 2
+    if out is None:
+        out = torch.empty(x2.shape[0], F_, device=x.device, dtype=torch.bfloat16)
+    a = out.view(x2.shape[0], F_)
+    if (FUSED_SWIGLU and x2.shape[0] <= SKINNY_MAX_ROWS and w_il.shape[1] <= 2 * 128 * _sm_count(x.device)
+            and w_il.is_contiguous()
+            and a.is_contiguous() and x2.shape[1] % 8 == 0 and w_il.shape[1] % 32 == 0):
+        ext().skinny_gemm(x2, w_il, a, None, None, True)
+    else:
+        gu = linear(x2, w_il)
+        ext().swiglu_rows(gu, a, True)
+    return out.view(*shape[:-1], F_)
+
+
 def linear_ok(x: torch.Tensor, w_kn: torch.Tensor) -> bool:
     """Shapes and dtypes the tcgen05 projection path takes (16-byte rows)."""
     return (x.is_cuda and x.dtype == torch.bfloat16 and w_kn.dtype == torch.bfloat16 and w_kn.dim() == 2

@@ -445,3 +445,18 @@ def test_profiling_cases_run(case):
         fn()
     torch.cuda.synchronize()
     assert flops > 0
+
+
+@pytest.mark.parametrize("M,K,F", [(1, 2048, 2752), (32, 2048, 5504), (7, 512, 688), (64, 512, 688)])
+def test_linear_swiglu_matches_fp32(M, K, F):
+    """silu(x W_gate) * (x W_up) from the interleaved [K, 2F] weight: the skinny kernel's SwiGLU epilogue
+    (<= 32 rows) and the GEMM + SwiGLU-pass fallback (64 rows) against fp32."""
+    g = torch.Generator(device=DEV).manual_seed(M + K + F)
+    x = torch.randn(M, K, device=DEV, generator=g).to(torch.bfloat16)
+    wg = (torch.randn(K, F, device=DEV, generator=g) * K ** -0.5).to(torch.bfloat16)
+    wu = (torch.randn(K, F, device=DEV, generator=g) * K ** -0.5).to(torch.bfloat16)
+    ref = torch.nn.functional.silu(x.float() @ wg.float()) * (x.float() @ wu.float())
+    a = ops.linear_swiglu(x, ops.interleave16(wg, wu))
+    torch.cuda.synchronize()
+    assert a.shape == (M, F) and a.dtype == torch.bfloat16
+    assert rel_err(a, ref) < 2e-2
