@@ -22,6 +22,7 @@
   } while (0)
 
 #include "gemm_api.h"
+#include "skinny_api.h"
 
 // launchers defined in the .cu files
 int pcb_embed_fwd(const int* tok, const void* W, float* x, int M, int D, int V, cudaStream_t s);
@@ -130,7 +131,7 @@ int pcb_moe_seg_colsum(const void* x, const int* seg, int E, int N, int cap, flo
 int pcb_skinny_splits(int N, int K, int num_sms);
 int pcb_skinny_gemm(const void* x, long long ldx, const void* w, long long ldw, void* y, long long ldy, int y_f32,
                     int M, int N, int K, int splits, int* err, unsigned long long* trace, int swiglu,
-                    cudaStream_t stream);
+                    const SkinnyRope* rope, cudaStream_t stream);
 
 extern "C" void pcb_set_gemm_mode(int mode);
 
@@ -317,8 +318,36 @@ void skinny_gemm(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, const 
                         row_stride(y, "y"), y.scalar_type() == at::kFloat ? 1 : 0, M, N, K, splits,
                         err ? err->data_ptr<int>() : nullptr,
                         trace ? reinterpret_cast<unsigned long long*>(trace->data_ptr<int64_t>()) : nullptr,
-                        swiglu ? 1 : 0, cur_stream()),
+                        swiglu ? 1 : 0, nullptr, cur_stream()),
         "skinny_gemm");
+}
+
+// One decode token per row: qkv = x @ w on the skinny kernel with the RoPE + KV-append epilogue
+// (q rotated into qo [M, H * hd]; k rotated and v appended at row *pos of kc / vc [M, H, cap, hd]).
+void skinny_qkv_rope(const at::Tensor& x, const at::Tensor& w, const at::Tensor& cs_table, const at::Tensor& pos,
+                     at::Tensor& qo, at::Tensor& kc, at::Tensor& vc) {
+  req(x, at::kBFloat16, "x");
+  req(w, at::kBFloat16, "w");
+  reqc(cs_table, at::kFloat, "cs_table");
+  reqc(qo, at::kBFloat16, "qo");
+  reqc(kc, at::kBFloat16, "kc");
+  reqc(vc, at::kBFloat16, "vc");
+  PCB_CHECK(pos.dtype() == at::kLong && pos.is_cuda(), "skinny_qkv_rope: pos must be a cuda int64 scalar tensor");
+  PCB_CHECK(kc.dim() == 4 && vc.sizes() == kc.sizes(), "skinny_qkv_rope: caches are [B, H, cap, hd]");
+  const int M = x.size(0), K = x.size(1), N = w.size(1);
+  const int H = kc.size(1), hd = kc.size(3), cap = kc.size(2);
+  PCB_CHECK(x.dim() == 2 && w.dim() == 2 && w.size(0) == K && M <= 32 && kc.size(0) == M && N == 3 * H * hd &&
+                qo.numel() == (int64_t)M * H * hd,
+            "skinny_qkv_rope: x [M <= 32, K], w [K, 3 H hd], qo [M, H hd], caches [M, H, cap, hd]");
+  PCB_CHECK(K % 8 == 0 && N % 8 == 0, "skinny_qkv_rope: K and N must be multiples of 8");
+  const at::cuda::CUDAGuard guard(x.device());
+  SkinnyRope r{reinterpret_cast<__nv_bfloat16*>(qo.data_ptr()), reinterpret_cast<__nv_bfloat16*>(kc.data_ptr()),
+               reinterpret_cast<__nv_bfloat16*>(vc.data_ptr()), cs_table.data_ptr<float>(),
+               reinterpret_cast<const long long*>(pos.data_ptr<int64_t>()), H, hd, cap};
+  const int splits = pcb_skinny_splits(N, K, num_sms());
+  check(pcb_skinny_gemm(x.data_ptr(), row_stride(x, "x"), w.data_ptr(), row_stride(w, "w"), qo.data_ptr(), 0, 0, M,
+                        N, K, splits, nullptr, nullptr, 0, &r, cur_stream()),
+        "skinny_qkv_rope");
 }
 
 // ---------------------------------------------------------------- mixture of experts
@@ -930,6 +959,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_grouped", &gemm_grouped);
   m.def("skinny_gemm", &skinny_gemm, py::arg("x"), py::arg("w"), py::arg("y"), py::arg("err") = py::none(),
         py::arg("trace") = py::none(), py::arg("swiglu") = false);
+  m.def("skinny_qkv_rope", &skinny_qkv_rope);
   m.def("moe_route", &moe_route);
   m.def("moe_dispatch", &moe_dispatch);
   m.def("moe_gather", &moe_gather);

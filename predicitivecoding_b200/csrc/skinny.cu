@@ -15,7 +15,9 @@
 // and stores its rows -- no global workspace, no atomics, the same bits on every run, one barrier.
 //
 // A SwiGLU epilogue (W's columns in alternating blocks of 16 gate and 16 up columns, so each warp holds
-// both halves of its 16 features) writes silu(gate) * up instead of the product.
+// both halves of its 16 features) writes silu(gate) * up instead of the product; a RoPE epilogue takes a
+// token's q | k | v, rotates q and k (partner column from the neighbouring lane) and appends k and v to
+// the KV cache, so a decode step's qkv projection, RoPE and cache append are one launch.
 //
 // Launched as a programmatic dependent: the weights are not written by the kernels before it, so the
 // first ring of weight tiles is requested (right after the barriers are initialised, while TMEM is being
@@ -75,6 +77,15 @@ struct Args {
   int* err;
   unsigned long long* trace;  // optional: 8 globaltimer stamps (ns) per CTA at the phase boundaries
   int swiglu;                 // 1: W's columns alternate 16 gate / 16 up columns; y [M, N / 2] = silu(g) * u
+  // RoPE + KV-cache append epilogue (rope_q != nullptr): the product is one token's q | k | v per row
+  // (N = 3 H hd); q and k are rotated at position *pos (cs [cap, hd / 2] cos/sin pairs), q goes to
+  // rope_q [M, H hd], k and v to row *pos of the caches [M, H, cap, hd]
+  __nv_bfloat16* rope_q;
+  __nv_bfloat16* rope_k;
+  __nv_bfloat16* rope_v;
+  const float2* rope_cs;
+  const long long* pos;
+  int heads, hd, cap;
 };
 
 PCB_DEVICE unsigned long long global_ns() {
@@ -101,6 +112,23 @@ PCB_DEVICE void store_out(const Args& a, int m, int n, float v) {
 // value from lane + 16 and store silu(gate) * up as feature (n / 32) * 16 + lane.  Every lane of the warp
 // must call it (the shuffle); `ok` guards the store.
 PCB_DEVICE void store_act(const Args& a, int m, int n, float v, bool ok) {
+  if (a.rope_q != nullptr) {
+    // adjacent columns (lanes 2j, 2j + 1) are the pair (x_2j, x_2j+1) that RoPE rotates together
+    const float partner = __shfl_xor_sync(0xffffffffu, v, 1);
+    if (!ok) return;
+    const int D = a.heads * a.hd, part = n / D, within = n - part * D;
+    const int h = within / a.hd, d = within - h * a.hd;
+    const long long p = *a.pos;
+    if (part == 2) {
+      a.rope_v[(((long long)m * a.heads + h) * a.cap + p) * a.hd + d] = __float2bfloat16_rn(v);
+      return;
+    }
+    const float2 c = a.rope_cs[p * (a.hd / 2) + d / 2];
+    const float r = (d & 1) ? partner * c.y + v * c.x : v * c.x - partner * c.y;
+    if (part == 0) a.rope_q[(long long)m * D + within] = __float2bfloat16_rn(r);
+    else a.rope_k[(((long long)m * a.heads + h) * a.cap + p) * a.hd + d] = __float2bfloat16_rn(r);
+    return;
+  }
   if (!a.swiglu) {
     if (ok) store_out(a, m, n, v);
     return;
@@ -302,6 +330,8 @@ static bool make_map(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t o
 
 using namespace pcb;
 
+#include "skinny_api.h"
+
 using KernelFn = void (*)(const CUtensorMap, const CUtensorMap, const skinny::Args);
 
 // kernel for cluster size S (1, 2, 4, 8, 16) and ring depth (pair: 4 stages, two CTAs per SM)
@@ -403,11 +433,12 @@ static bool skinny_pdl() {
 // y [M, N] (bf16, or fp32 with y_f32) = x [M, K] bf16 @ W [K, N] bf16 (row-major), M <= 32, K split over
 // `splits` CTAs of a cluster (1, 2, 4, 8 or 16; negative: the same count on the shallow two-CTAs-per-SM
 // ring); `trace` (optional) receives 8 timestamps per CTA; `swiglu`: W's columns alternate 16 gate and 16
-// up columns (N a multiple of 32) and y [M, N / 2] receives silu(gate) * up.
+// up columns (N a multiple of 32) and y [M, N / 2] receives silu(gate) * up; `rope` (optional): the
+// product is q | k | v of one token per row, rotated and written to rope->q and the caches (y unused).
 // Returns 0, -1 bad arguments, -5 tensor-map encode, -(1000 + cudaError) launch.
 int pcb_skinny_gemm(const void* x, long long ldx, const void* w, long long ldw, void* y, long long ldy, int y_f32,
                     int M, int N, int K, int splits, int* err, unsigned long long* trace, int swiglu,
-                    cudaStream_t stream) {
+                    const SkinnyRope* rope, cudaStream_t stream) {
   if (M < 1 || M > skinny::kBM || N < 1 || K < 1) return -1;
   const bool pair = splits < 0;
   if (pair) splits = -splits;
@@ -427,6 +458,17 @@ int pcb_skinny_gemm(const void* x, long long ldx, const void* w, long long ldw, 
   a.trace = trace;
   if (swiglu && N % 32) return -1;
   a.swiglu = swiglu ? 1 : 0;
+  if (rope != nullptr) {
+    if (swiglu || N != 3 * rope->heads * rope->hd || rope->hd % 2) return -1;
+    a.rope_q = rope->q;
+    a.rope_k = rope->k;
+    a.rope_v = rope->v;
+    a.rope_cs = reinterpret_cast<const float2*>(rope->cs);
+    a.pos = rope->pos;
+    a.heads = rope->heads;
+    a.hd = rope->hd;
+    a.cap = rope->cap;
+  }
   skinny_attrs();
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((N + skinny::kBN - 1) / skinny::kBN, splits, 1);

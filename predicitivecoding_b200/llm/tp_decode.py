@@ -159,7 +159,7 @@ class TensorParallelDecoder:
     def _layer(self, x: torch.Tensor, h: torch.Tensor, l: int, attn, bufs) -> torch.Tensor:
         """One block on normalised input h (residual x updated in place); returns the next norm's output."""
         W, L = self.W, self.cfg.num_blocks
-        o = attn(ops.linear(h, W[f"b{l}.wqkv"]), l)
+        o = attn(h, W[f"b{l}.wqkv"], l)
         h2 = self._row_parallel(o, W[f"b{l}.wo"], x, W[f"b{l}.ln2"], bufs)
         a = ops.linear_swiglu(h2, W[f"b{l}.w13"])
         nxt = W[f"b{l + 1}.ln1"] if l + 1 < L else W["lnf"]
@@ -198,7 +198,8 @@ class TensorParallelDecoder:
         lse = torch.empty(B * Hl, P, device=self.device)
         cs = self.rope_cs[:P].contiguous()
 
-        def attn(qkv, l):                                      # qkv [M, 3*Dl] = q | k | v column blocks
+        def attn(h, w_qkv, l):
+            qkv = ops.linear(h, w_qkv)                         # [M, 3*Dl] = q | k | v column blocks
             ops.rope(qkv, cs, P, Dl, hd, 2, 1.0)
             kv = qkv.view(B, P, 3, Hl, hd)
             self.kc[l][:, :, :P].copy_(kv[:, :, 1].transpose(1, 2))
@@ -227,9 +228,9 @@ class TensorParallelDecoder:
         x = self.W["wemb"].index_select(0, self.tok).float()   # [B, D]
         self.lens.add_(1)
 
-        def attn(qkv, l):                                      # qkv [B, 3*Dl]
-            # RoPE on q and k at self.pos, q -> self.qbuf, k / v appended to the caches (one kernel)
-            ops.ext().rope_append(qkv, self.rope_cs, self.pos, self.qbuf, self.kc[l], self.vc[l])
+        def attn(h, w_qkv, l):
+            # projection, RoPE on q and k at self.pos, q -> self.qbuf, k / v appended to the caches (one launch)
+            ops.qkv_rope_append(h, w_qkv, self.rope_cs, self.pos, self.qbuf, self.kc[l], self.vc[l])
             o = ops.decode_attn(self.qbuf, self.kc[l], self.vc[l], self.lens, self.scale, nsplit=self.nsplit,
                                 scratch=(self.pacc, self.pml))
             return o.view(B, Dl)

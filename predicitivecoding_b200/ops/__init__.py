@@ -162,6 +162,7 @@ def linear(x: torch.Tensor, w_kn: torch.Tensor, out: Optional[torch.Tensor] = No
 
 
 FUSED_SWIGLU = os.environ.get("PCB_FUSED_SWIGLU", "1") != "0"   # 0: GEMM + SwiGLU pass for every row count
+FUSED_ROPE = os.environ.get("PCB_FUSED_ROPE", "1") != "0"       # 0: GEMM + RoPE/append kernel for every row count
 
 
 def interleave16(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
@@ -192,6 +193,19 @@ def linear_swiglu(x: torch.Tensor, w_il: torch.Tensor, out: Optional[torch.Tenso
         gu = linear(x2, w_il)
         ext().swiglu_rows(gu, a, True)
     return out.view(*shape[:-1], F_)
+
+
+def qkv_rope_append(x: torch.Tensor, w_qkv: torch.Tensor, rope_cs: torch.Tensor, pos: torch.Tensor,
+                    q_out: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor) -> None:
+    """One decode token per row: q | k | v = x @ w_qkv, RoPE on q and k at position ``pos`` (device int64
+    scalar), q -> q_out [B, H, hd], k and v appended to row ``pos`` of the caches [B, H, cap, hd].  Up to
+    32 rows this is one launch of the skinny kernel with the RoPE epilogue; otherwise the GEMM and the
+    RoPE/append kernel."""
+    if (FUSED_ROPE and x.shape[0] <= SKINNY_MAX_ROWS and w_qkv.shape[1] <= 2 * 128 * _sm_count(x.device)
+            and x.is_contiguous() and w_qkv.is_contiguous() and x.shape[1] % 8 == 0 and w_qkv.shape[1] % 8 == 0):
+        ext().skinny_qkv_rope(x, w_qkv, rope_cs, pos, q_out, k_cache, v_cache)
+    else:
+        ext().rope_append(linear(x, w_qkv), rope_cs, pos, q_out, k_cache, v_cache)
 
 
 def linear_ok(x: torch.Tensor, w_kn: torch.Tensor) -> bool:

@@ -460,3 +460,46 @@ def test_linear_swiglu_matches_fp32(M, K, F):
     torch.cuda.synchronize()
     assert a.shape == (M, F) and a.dtype == torch.bfloat16
     assert rel_err(a, ref) < 2e-2
+
+
+@pytest.mark.parametrize("B,H,hd", [(4, 4, 64), (32, 16, 128), (3, 2, 128)])
+@pytest.mark.parametrize("fused", [True, False])
+def test_qkv_rope_append_matches_fp32(B, H, hd, fused):
+    """Decode qkv projection + RoPE at position pos + KV-cache append: the skinny kernel's RoPE epilogue and
+    the GEMM + RoPE/append kernel against fp32 (adjacent-pair rotation), other cache rows untouched."""
+    D, K, cap, p = H * hd, 256, 64, 37
+    g = torch.Generator(device=DEV).manual_seed(B * H + hd)
+    x = torch.randn(B, K, device=DEV, generator=g).to(torch.bfloat16)
+    w = (torch.randn(K, 3 * D, device=DEV, generator=g) * K ** -0.5).to(torch.bfloat16)
+    ang = torch.arange(cap, device=DEV, dtype=torch.float32)[:, None] * \
+        (10000.0 ** (-torch.arange(0, hd, 2, device=DEV, dtype=torch.float32) / hd))[None]
+    cs = torch.stack((ang.cos(), ang.sin()), -1).contiguous()            # [cap, hd/2, 2]
+    pos = torch.tensor(p, device=DEV, dtype=torch.int64)
+    q = torch.zeros(B, H, hd, device=DEV, dtype=torch.bfloat16)
+    kc = torch.full((B, H, cap, hd), 7.0, device=DEV, dtype=torch.bfloat16)
+    vc = torch.full((B, H, cap, hd), 7.0, device=DEV, dtype=torch.bfloat16)
+    keep = ops.FUSED_ROPE
+    try:
+        ops.FUSED_ROPE = fused
+        ops.qkv_rope_append(x, w, cs, pos, q, kc, vc)
+    finally:
+        ops.FUSED_ROPE = keep
+    torch.cuda.synchronize()
+    y = x.float() @ w.float()
+    c, s = cs[p, :, 0], cs[p, :, 1]
+
+    def rot(t):                                                           # [B, H, hd]
+        a, b = t[..., 0::2], t[..., 1::2]
+        out = torch.empty_like(t)
+        out[..., 0::2] = a * c - b * s
+        out[..., 1::2] = a * s + b * c
+        return out
+    qr = rot(y[:, :D].view(B, H, hd))
+    kr = rot(y[:, D:2 * D].view(B, H, hd))
+    vr = y[:, 2 * D:].view(B, H, hd)
+    assert rel_err(q, qr) < 1e-2
+    assert rel_err(kc[:, :, p], kr) < 1e-2
+    assert rel_err(vc[:, :, p], vr) < 1e-2
+    others = torch.ones(cap, dtype=torch.bool)
+    others[p] = False
+    assert bool((kc[:, :, others] == 7.0).all()) and bool((vc[:, :, others] == 7.0).all())
