@@ -70,7 +70,7 @@ long long pcb_checked_violations();
 int pcb_attn_bwd_stats(unsigned long long* out);
 int pcb_attn_fwd_stats(unsigned long long* out);
 int pcb_tp_allreduce_norm(const void* peers, int world, int rows, int D, float* x, const void* gamma, void* y,
-                          float eps, cudaStream_t s);
+                          float eps, void* const* flags, unsigned int* ctr, int rank, int* err, cudaStream_t s);
 int pcb_tp_reduce_norm(const void* slots, int world, int rows, int D, const float* resid, float* x_out,
                        int accumulate, const void* gamma, void* y, long long ldy, float* inv, float eps,
                        cudaStream_t s);
@@ -887,15 +887,29 @@ int64_t swiglu_rows(const at::Tensor& gu, at::Tensor& a, bool interleave16) {
 
 
 // fused all-reduce (peer loads) + residual add + RMSNorm of replicated rows; returns the status
+// flags (int64 [world] pointers to [rows, world] int32 flag arrays), ctr (int32 [rows]), rank, err: the
+// in-kernel per-row handshake that replaces a device barrier before the reads (all optional together).
 int64_t tp_allreduce_norm(const at::Tensor& peers, int64_t world, at::Tensor& x, const at::Tensor& gamma, at::Tensor& y,
-                          double eps) {
+                          double eps, const c10::optional<at::Tensor>& flags, const c10::optional<at::Tensor>& ctr,
+                          int64_t rank, const c10::optional<at::Tensor>& err) {
   reqc(x, at::kFloat, "x");
   reqc(y, at::kBFloat16, "y");
   req(gamma, at::kBFloat16, "gamma");
   PCB_CHECK(peers.dtype() == at::kLong && peers.numel() >= world, "tp_allreduce_norm: pointer table");
   const int D = x.size(-1);
-  return pcb_tp_allreduce_norm(peers.data_ptr(), (int)world, (int)(x.numel() / D), D, x.data_ptr<float>(),
-                               gamma.data_ptr(), y.data_ptr(), (float)eps, cur_stream());
+  const int rows = (int)(x.numel() / D);
+  void* const* fl = nullptr;
+  unsigned int* c = nullptr;
+  if (flags) {
+    PCB_CHECK(flags->dtype() == at::kLong && flags->numel() >= world && ctr && ctr->dtype() == at::kInt &&
+                  ctr->numel() >= rows && rank >= 0 && rank < world,
+              "tp_allreduce_norm: flag pointers [world], epoch counters [rows] int32 and a rank");
+    fl = reinterpret_cast<void* const*>(flags->data_ptr<int64_t>());
+    c = reinterpret_cast<unsigned int*>(ctr->data_ptr<int>());
+  }
+  return pcb_tp_allreduce_norm(peers.data_ptr(), (int)world, rows, D, x.data_ptr<float>(), gamma.data_ptr(),
+                               y.data_ptr(), (float)eps, fl, c, (int)rank, err ? err->data_ptr<int>() : nullptr,
+                               cur_stream());
 }
 
 
@@ -993,7 +1007,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("linear_scan", &linear_scan);
   m.def("linear_scan_bwd", &linear_scan_bwd);
   m.def("tp_reduce_norm", &tp_reduce_norm);
-  m.def("tp_allreduce_norm", &tp_allreduce_norm);
+  m.def("tp_allreduce_norm", &tp_allreduce_norm, py::arg("peers"), py::arg("world"), py::arg("x"), py::arg("gamma"),
+        py::arg("y"), py::arg("eps"), py::arg("flags") = py::none(), py::arg("ctr") = py::none(),
+        py::arg("rank") = 0, py::arg("err") = py::none());
   m.def("rope_append", &rope_append);
   m.def("checked_violations", []() { return (int64_t)pcb_checked_violations(); });
   m.def("attn_bwd_stats", []() {

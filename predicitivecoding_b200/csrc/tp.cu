@@ -105,11 +105,52 @@ namespace {
 // x[r] += sum_s peers[s][r] (bf16 partial products read from every rank's buffer over NVLink, summed
 // in rank order), then y[r] = x[r] * gamma / rms(x[r]) in bf16: the all-reduce of a row-parallel
 // product fused with the residual add and the next RMSNorm.  Rows are replicated on every rank.
+//
+// With `flags` (sync variant) the kernel also replaces the device barrier that must precede it: CTA r
+// (row r) bumps its own epoch counter ctr[r], stores it into slot [r][rank] of every rank's flag array
+// (release, system scope) and waits until slot [r][p] of its own array holds that epoch for every p
+// (acquire; bounded, error code on timeout).  A peer reaches the store only after its row-parallel
+// product (the kernel before it in its stream) has completed, and each row only reads row r of the
+// peers' partials, so a per-row handshake is all the ordering the reads need; the partial buffers are
+// double-buffered, so a buffer is rewritten only after every rank has passed the next handshake.
+__device__ __forceinline__ void st_release_sys_u32(unsigned int* p, unsigned int v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned int ld_acquire_sys_u32(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 __global__ void __launch_bounds__(kTpThreads)
 tp_allreduce_norm_kernel(const __nv_bfloat16* const* __restrict__ peers, int world, int D, float* __restrict__ x,
-                         const __nv_bfloat16* __restrict__ gamma, __nv_bfloat16* __restrict__ y, float eps) {
+                         const __nv_bfloat16* __restrict__ gamma, __nv_bfloat16* __restrict__ y, float eps,
+                         unsigned int* const* __restrict__ flags, unsigned int* __restrict__ ctr, int rank,
+                         int* __restrict__ err) {
   pdl_begin();
   const int r = blockIdx.x;
+  if (flags != nullptr) {
+    __shared__ unsigned int epoch;
+    if (threadIdx.x == 0) {
+      epoch = ctr[r] + 1;
+      ctr[r] = epoch;
+    }
+    __syncthreads();
+    const unsigned int e = epoch;
+    const int p = threadIdx.x;
+    if (p < world) {
+      st_release_sys_u32(flags[p] + (long long)r * world + rank, e);
+      const unsigned int* mine = flags[rank] + (long long)r * world + p;
+      const long long t0 = clock64();
+      while (ld_acquire_sys_u32(mine) < e) {
+        if (clock64() - t0 > kSpinBudgetCycles) {
+          record_error(err, kErrTimeoutPeer);
+          break;
+        }
+      }
+    }
+    __syncthreads();
+  }
   float ss = 0.f;
   for (int i = threadIdx.x * 8; i < D; i += kTpThreads * 8) {
     const long long o = (long long)r * D + i;
@@ -158,13 +199,17 @@ tp_allreduce_norm_kernel(const __nv_bfloat16* const* __restrict__ peers, int wor
 }
 }  // namespace
 
-// peers: device array of `world` pointers to [rows, D] bf16 partials (this rank's included); the
-// caller orders it after a barrier that follows every rank's write of its partial.
+// peers: device array of `world` pointers to [rows, D] bf16 partials (this rank's included).  Without
+// `flags` the caller orders it after a barrier that follows every rank's write of its partial; with
+// `flags` (device array of `world` pointers to [rows, world] uint32 flag arrays, one per rank, zero at
+// first) and `ctr` ([rows] uint32 epochs, this rank's) the kernel does the per-row handshake itself.
 int pcb_tp_allreduce_norm(const void* peers, int world, int rows, int D, float* x, const void* gamma, void* y,
-                          float eps, cudaStream_t s) {
-  if (D % 8 || rows <= 0 || world <= 0) return -2;
+                          float eps, void* const* flags, unsigned int* ctr, int rank, int* err, cudaStream_t s) {
+  if (D % 8 || rows <= 0 || world <= 0 || world > kTpThreads) return -2;
+  if (flags != nullptr && ctr == nullptr) return -2;
   pdl_launch(tp_allreduce_norm_kernel, dim3(rows), dim3(kTpThreads), 0, s,
              reinterpret_cast<const __nv_bfloat16* const*>(peers), world, D, x,
-             reinterpret_cast<const __nv_bfloat16*>(gamma), reinterpret_cast<__nv_bfloat16*>(y), eps);
+             reinterpret_cast<const __nv_bfloat16*>(gamma), reinterpret_cast<__nv_bfloat16*>(y), eps,
+             reinterpret_cast<unsigned int* const*>(flags), ctr, rank, err);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }

@@ -21,6 +21,7 @@ layout runs on T GPUs:
 from __future__ import annotations
 
 import math
+import os
 from typing import Optional
 
 import torch
@@ -29,6 +30,9 @@ import torch.distributed as dist
 from .. import ops
 from ..models.config import DecoderLmConfig
 from ..models.decoder_lm import DecoderLM, rope_tables
+
+
+_ROW_SYNC = os.environ.get("PCB_TP_ROW_SYNC", "1") != "0"   # 0: device barrier + all-reduce kernel
 
 
 def tp_decode_supports(cfg: DecoderLmConfig, world: int) -> bool:
@@ -65,6 +69,9 @@ class TensorParallelDecoder:
         self.comm = Communicator(self.pg, backend="peer", device=dev, capacity_bytes=1 << 20) if T > 1 else None
         self.peer = PeerGroup(self.pg, dev)
         self.pbuf = [self.peer.symmetric(batch * D, bf16) for _ in range(2)]   # decode partials
+        # per-row handshake of the decode all-reduce (replaces a device barrier before each one)
+        self.row_flags = self.peer.symmetric(batch * T, torch.int32) if T > 1 else None
+        self.row_epoch = torch.zeros(batch, device=dev, dtype=torch.int32) if T > 1 else None
         self.pbuf_prefill = None
         self._flip = 0
         self.kc = [torch.zeros(batch, self.Hl, self.cap, hd, device=dev, dtype=bf16) for _ in range(L)]
@@ -148,10 +155,15 @@ class TensorParallelDecoder:
         self._flip ^= 1
         rows = a.shape[0]
         ops.linear(a, w, out=buf.local[:rows * self.cfg.dim].view(rows, self.cfg.dim))
-        if self.T > 1:
-            self.peer.barrier()
         y = torch.empty(x.shape, device=self.device, dtype=torch.bfloat16)
-        rc = ops.ext().tp_allreduce_norm(buf.ptrs, self.T, x, gamma, y, self.cfg.eps)
+        if self.T > 1 and rows == self.B and _ROW_SYNC:
+            # decode: the kernel does a per-row handshake with the peers before reading their partials
+            rc = ops.ext().tp_allreduce_norm(buf.ptrs, self.T, x, gamma, y, self.cfg.eps, self.row_flags.ptrs,
+                                             self.row_epoch, self.t, self.peer.err)
+        else:
+            if self.T > 1:
+                self.peer.barrier()
+            rc = ops.ext().tp_allreduce_norm(buf.ptrs, self.T, x, gamma, y, self.cfg.eps)
         if rc != 0:
             raise RuntimeError(f"tp_allreduce_norm failed with status {rc}")
         return y
