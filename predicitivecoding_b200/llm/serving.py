@@ -77,6 +77,10 @@ class InferenceModel:
             for name, p in b.named_parameters():
                 blk[name] = cast(p)
             blk["_ref"] = b
+            if (self._tc and cfg.ffn == "swiglu" and cfg.num_experts == 0 and "w1" in blk and "w3" in blk
+                    and blk["w1"].shape[1] % 16 == 0 and blk["w1"].shape[0] % 8 == 0):
+                # gate and up in alternating 16-column blocks: one projection launch with SwiGLU in its epilogue
+                blk["w13"] = ops.interleave16(blk.pop("w1"), blk.pop("w3")).contiguous()
             self.blocks.append(blk)
 
     # ------------------------------------------------------------ pieces
@@ -94,6 +98,8 @@ class InferenceModel:
             return blk["_ref"].moe_ffn(h.float(), None).to(h.dtype)
         if c.ffn == "gelu":
             return self._mm(gelu_tanh(self._mm(h, blk["w1"]) + blk["b1"]), blk["w2"]) + blk["b2"]
+        if "w13" in blk:
+            return self._mm(ops.linear_swiglu(h.contiguous(), blk["w13"]), blk["w2"])
         return self._mm(F.silu(self._mm(h, blk["w1"])) * self._mm(h, blk["w3"]), blk["w2"])
 
     def new_cache(self, batch: int, max_len: Optional[int] = None, window: Optional[int] = None,

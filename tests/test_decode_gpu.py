@@ -121,3 +121,24 @@ def test_serving_decode_kernel_matches_sdpa_path():
             assert ops.launch_count() >= before + 6 * cfg.num_blocks * 2
         logits[fast] = torch.stack(outs)
     assert (logits[True] - logits[False]).abs().max() < 5e-2 * logits[False].abs().max()
+
+
+def test_serving_swiglu_projection_matches_autograd_model():
+    """The exported bf16 model (w1/w3 interleaved for the fused SwiGLU projection) against the fp32 autograd
+    model: prefill logits of a prompt and the logits of decode steps."""
+    from predicitivecoding_b200.llm.serving import export
+    from predicitivecoding_b200.models.config import DecoderLmConfig
+    from predicitivecoding_b200.models.decoder_lm import DecoderLM
+    cfg = DecoderLmConfig(256, 256, 2, 4, 512, 128, use_rms_norm=True, use_rope=True, ffn="swiglu")
+    m = DecoderLM(cfg, seed=6).eval()
+    inf = export(m, "cuda", torch.bfloat16)
+    assert all("w13" in blk for blk in inf.blocks)
+    toks = torch.randint(0, 256, (2, 9), generator=torch.Generator().manual_seed(3))
+    with torch.no_grad():
+        ref = m(toks).float()                                   # [2, 9, V] fp32 on the CPU
+    c = inf.new_cache(2)
+    pre = inf.prefill(toks[:, :5].cuda(), c).float().cpu()
+    steps = [inf.step(toks[:, i].cuda(), c).float().cpu() for i in range(5, 9)]
+    got = torch.cat([pre, torch.stack(steps, 1)], 1)
+    err = float((got - ref).norm() / ref.norm())
+    assert err < 3e-2, err
