@@ -178,6 +178,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // programmatic dependent launch: barrier set-up and the TMEM allocation above overlap the previous
+  // kernel's tail; no global memory is touched before it has completed
+  pdl_wait();
 
   if (warp >= 12) {
    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsCtl));
@@ -511,10 +514,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == kMmaWarp) tmem_dealloc(tmem, 512);
 }
 
-// delta[b*H + h][i] = sum_d dO[row, h, d] * O[row, h, d]: 8 lanes per (row, head), 16-byte loads
+// delta[b*H + h][i] = sum_d dO[row, h, d] * O[row, h, d]: 8 lanes per (row, head), 16-byte loads;
+// and zeroes the fp32 dQ accumulator (n4 float4s) in the same pass, which the backward kernel adds into
 __global__ void bwd_delta_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout,
-                                 long long ld_o, float* __restrict__ dvec, long long rows_h, int S, int H) {
+                                 long long ld_o, float* __restrict__ dvec, long long rows_h, int S, int H,
+                                 float4* __restrict__ dq_zero, long long n4) {
+  pdl_wait();
   const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride)
+    dq_zero[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   for (long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x; t < rows_h * 8; t += stride) {
     const long long hr = t >> 3;
     const int part = (int)(t & 7);
@@ -540,6 +548,7 @@ __global__ void bwd_delta_kernel(const __nv_bfloat16* __restrict__ o, const __nv
 __global__ void bwd_dq_convert_kernel(const float* __restrict__ dq_acc, __nv_bfloat16* __restrict__ dqkv,
                                       long long ld_d, long long rows, int D, int S,
                                       const float2* __restrict__ rope_cs) {
+  pdl_wait();
   const long long per_row = D / 8;
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x; t < rows * per_row; t += stride) {
@@ -639,10 +648,9 @@ int pcb_attn_bwd_tc(const void* qkv, long long ld, const void* out, const void* 
       return -5;
   }
   const long long rows = (long long)B * S;
-  if (cudaMemsetAsync(dq_acc, 0, rows * H * HD * sizeof(float), s) != cudaSuccess) return -1003;
-  fab::bwd_delta_kernel<<<148 * 8, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(out),
-                                                reinterpret_cast<const __nv_bfloat16*>(dout), ld_o, dvec, rows * H,
-                                                S, H);
+  step_launch(fab::bwd_delta_kernel, dim3(148 * 8), dim3(256), 0, s, reinterpret_cast<const __nv_bfloat16*>(out),
+             reinterpret_cast<const __nv_bfloat16*>(dout), ld_o, dvec, rows * H, S, H,
+             reinterpret_cast<float4*>(dq_acc), rows * H * HD / 4);
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(fab::attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fab::SMEM);
@@ -657,14 +665,13 @@ int pcb_attn_bwd_tc(const void* qkv, long long ld, const void* out, const void* 
   }
   const int n_items = B * H * (S / fab::kT);
   const int grid = n_items < num_sms ? n_items : num_sms;  // persistent: one CTA per SM
-  fab::attn_bwd_tc_kernel<<<grid, fab::kThreads, fab::SMEM, s>>>(tq, td, tdq, lse, dvec,
-                                                                  reinterpret_cast<__nv_bfloat16*>(dqkv), ld_d, S, H,
-                                                                  scale, reinterpret_cast<const float2*>(rope_cs),
-                                                                  B * H, err);
+  step_launch(fab::attn_bwd_tc_kernel, dim3(grid), dim3(fab::kThreads), fab::SMEM, s, tq, td, tdq, lse, dvec,
+             reinterpret_cast<__nv_bfloat16*>(dqkv), ld_d, S, H, scale, reinterpret_cast<const float2*>(rope_cs),
+             B * H, err);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return -(1000 + static_cast<int>(e));
-  fab::bwd_dq_convert_kernel<<<148 * 8, 256, 0, s>>>(dq_acc, reinterpret_cast<__nv_bfloat16*>(dqkv), ld_d, rows,
-                                                     H * HD, S, reinterpret_cast<const float2*>(rope_cs));
+  step_launch(fab::bwd_dq_convert_kernel, dim3(148 * 8), dim3(256), 0, s, dq_acc, reinterpret_cast<__nv_bfloat16*>(dqkv),
+             ld_d, rows, H * HD, S, reinterpret_cast<const float2*>(rope_cs));
   const cudaError_t e2 = cudaGetLastError();
   return e2 == cudaSuccess ? 0 : -(1000 + static_cast<int>(e2));
 }

@@ -170,6 +170,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // programmatic dependent launch: barrier set-up and the TMEM allocation above overlap the previous
+  // kernel's tail; no global memory is touched before it has completed
+  pdl_wait();
   if (warp >= 8) {
     // control warpgroup: registers down, then the TMA warp and the MMA warp
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsCtl));
@@ -520,8 +523,8 @@ static int fa_launch(const void* qkv, long long ld, void* out, long long ld_o, f
   }
   const int n_items = B * H * (S / (2 * fa::kBQ));
   const int grid = n_items < num_sms ? n_items : num_sms;  // persistent: one CTA per SM
-  fa::attn_fwd_tc_kernel<HD><<<grid, fa::kThreads, C::SMEM, s>>>(tm, reinterpret_cast<__nv_bfloat16*>(out), ld_o,
-                                                                   lse, S, H, B * H, scale, err);
+  step_launch(fa::attn_fwd_tc_kernel<HD>, dim3(grid), dim3(fa::kThreads), C::SMEM, s, tm,
+             reinterpret_cast<__nv_bfloat16*>(out), ld_o, lse, S, H, B * H, scale, err);
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : -(1000 + static_cast<int>(e));
 }

@@ -442,6 +442,10 @@ PCB_DEVICE void pdl_begin() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
+// Wait only: the next kernel is scheduled when this grid exits (the implicit trigger), so its CTAs never
+// sit waiting on SMs this grid still computes on.  For the kernels of the training step, whose
+// successors would otherwise occupy warp slots for the whole of a long kernel.
+PCB_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 inline bool pdl_env_enabled() {
   static const bool on = [] {
@@ -451,9 +455,21 @@ inline bool pdl_env_enabled() {
   return on;
 }
 
+// Training-step kernels (norms, attention, cross-entropy, AdamW, embedding) launch programmatically
+// only with PCB_PDL_STEP=1.  They wait (pdl_wait) before touching memory either way.  On the 124M
+// decoder step the programmatic attribute on these kernels cost 0.13-0.25 ms per step in alternating
+// same-box runs, so it is off by default; the pair GEMM and the decode kernels keep it (PCB_PDL).
+inline bool pdl_step_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("PCB_PDL_STEP");
+    return e && e[0] == '1';
+  }();
+  return on;
+}
+
 template <typename... KArgs, typename... Args>
-inline cudaError_t pdl_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
-                              Args&&... args) {
+inline cudaError_t launch_ex(bool programmatic, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                             cudaStream_t s, Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -461,9 +477,22 @@ inline cudaError_t pdl_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
   cfg.stream = s;
   cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  at[0].val.programmaticStreamSerializationAllowed = pdl_env_enabled() ? 1 : 0;
+  at[0].val.programmaticStreamSerializationAllowed = programmatic ? 1 : 0;
   cfg.attrs = at;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t pdl_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args&&... args) {
+  return launch_ex(pdl_env_enabled(), kernel, grid, block, smem, s, static_cast<Args&&>(args)...);
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t step_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                               Args&&... args) {
+  return launch_ex(pdl_env_enabled() && pdl_step_enabled(), kernel, grid, block, smem, s,
+                   static_cast<Args&&>(args)...);
 }
 }  // namespace pcb

@@ -25,6 +25,7 @@ __device__ unsigned long long g_checked_violations = 0;
 
 __global__ void embed_fwd_kernel(const int* __restrict__ tok, const __nv_bfloat16* __restrict__ W,
                                  float* __restrict__ x, int M, int D, int V) {
+  pdl_wait();
   const int t = blockIdx.x;
   if (t >= M) return;
   int id = tok[t];
@@ -41,6 +42,7 @@ __global__ void embed_fwd_kernel(const int* __restrict__ tok, const __nv_bfloat1
 // dW[tok[t],:] += dx[t,:]
 __global__ void embed_bwd_kernel(const int* __restrict__ tok, const float* __restrict__ dx, float* __restrict__ dW,
                                  int M, int D, int V) {
+  pdl_wait();
   const int t = blockIdx.x;
   if (t >= M) return;
   int id = tok[t];
@@ -64,6 +66,7 @@ template <int VPT>  // float4 vectors per lane
 __global__ void rmsnorm_fwd_kernel(const float* __restrict__ x, const __nv_bfloat16* __restrict__ g,
                                    __nv_bfloat16* __restrict__ y, float* __restrict__ inv_out, int M, int D,
                                    float eps) {
+  pdl_wait();
   const int warps = blockDim.x >> 5;
   const int row = blockIdx.x * warps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -103,6 +106,7 @@ __global__ void rmsnorm_bwd_kernel(const float* __restrict__ dy, const float* __
                                    const __nv_bfloat16* __restrict__ g, const float* __restrict__ inv_in,
                                    float* __restrict__ dx, __nv_bfloat16* __restrict__ dx16, float* __restrict__ dg,
                                    int M, int D, int accumulate) {
+  pdl_wait();
   extern __shared__ float sdg[];  // [D] per-block dgamma partial
   for (int i = threadIdx.x; i < D; i += blockDim.x) sdg[i] = 0.f;
   __syncthreads();
@@ -216,6 +220,7 @@ __global__ void rope_kernel(__nv_bfloat16* __restrict__ buf, long long ld, const
 // PredictiveCoding.Device/Kernels/DeviceTrainKernels.cs:503-537.
 __global__ void ce_fwd_bwd_kernel(__nv_bfloat16* __restrict__ logits, long long ld, const int* __restrict__ tgt,
                                   float* __restrict__ loss, int M, int V, float scale, int write_grad) {
+  pdl_wait();
   const int r = blockIdx.x;
   if (r >= M) return;
   __nv_bfloat16* row = logits + (long long)r * ld;
@@ -316,6 +321,7 @@ template <int RV>
 __global__ void __launch_bounds__(512, 1)
     ce_rows_kernel(__nv_bfloat16* __restrict__ logits, long long ld, const int* __restrict__ tgt,
                    float* __restrict__ loss, int M, int V, float scale, int write_grad) {
+  pdl_wait();
   __shared__ float red_m[2][16], red_s[2][16];
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int nvec = V >> 3;
@@ -401,6 +407,7 @@ __global__ void __launch_bounds__(512, 1)
 // ------------------------------------------------------------------ reductions
 // out[0] += sum(x^2) over n elements (global-norm clipping).
 __global__ void sumsq_kernel(const float* __restrict__ x, long long n, float* __restrict__ out, int square) {
+  pdl_wait();
   float s = 0.f;
   const long long n4 = n / 4;
   const float4* x4 = reinterpret_cast<const float4*>(x);
@@ -433,6 +440,7 @@ PCB_DEVICE float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
 // out[n] (+)= sum over rows of x[m, n]   (bf16 or fp32 input)
 template <typename T>
 __global__ void colsum_kernel(const T* __restrict__ x, long long ld, float* __restrict__ out, int M, int N, float scale) {
+  pdl_wait();
   const int n = blockIdx.x * blockDim.x + threadIdx.x;
   if (n >= N) return;
   const int rows_per = (M + gridDim.y - 1) / gridDim.y;
@@ -466,6 +474,7 @@ __global__ void adamw_kernel(float* __restrict__ w, const float* __restrict__ g,
                              float* __restrict__ v, __nv_bfloat16* __restrict__ w16, long long n,
                              long long n_decay, const float* __restrict__ hyper, float b1, float b2, float eps,
                              const float* __restrict__ clip_sumsq, float max_norm) {
+  pdl_wait();
   const float lr = hyper[0], wd = hyper[1], bc1 = hyper[2], bc2 = hyper[3];
   float s = hyper[4];
   const float grad_scale = s;
@@ -541,7 +550,7 @@ static int grid_for(long long n, int threads, int cap = 148 * 16) {
 
 int pcb_embed_fwd(const int* tok, const void* W, float* x, int M, int D, int V, cudaStream_t s) {
   if (D % 4) return -1;
-  embed_fwd_kernel<<<M, 128, 0, s>>>(tok, reinterpret_cast<const __nv_bfloat16*>(W), x, M, D, V);
+  step_launch(embed_fwd_kernel, dim3(M), dim3(128), 0, s, tok, reinterpret_cast<const __nv_bfloat16*>(W), x, M, D, V);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
@@ -559,7 +568,7 @@ long long pcb_checked_violations() {
 
 int pcb_embed_bwd(const int* tok, const float* dx, float* dW, int M, int D, int V, cudaStream_t s) {
   if (D % 4) return -1;
-  embed_bwd_kernel<<<M, 128, 0, s>>>(tok, dx, dW, M, D, V);
+  step_launch(embed_bwd_kernel, dim3(M), dim3(128), 0, s, tok, dx, dW, M, D, V);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
@@ -569,10 +578,10 @@ int pcb_rmsnorm_fwd(const float* x, const void* gv, void* y, float* inv, int M, 
   const int grid = (M + rows_per_block - 1) / rows_per_block;
   __nv_bfloat16* yb = reinterpret_cast<__nv_bfloat16*>(y);
   const __nv_bfloat16* g = reinterpret_cast<const __nv_bfloat16*>(gv);
-  if (D <= 512) rmsnorm_fwd_kernel<4><<<grid, 256, 0, s>>>(x, g, yb, inv, M, D, eps);
-  else if (D <= 1024) rmsnorm_fwd_kernel<8><<<grid, 256, 0, s>>>(x, g, yb, inv, M, D, eps);
-  else if (D <= 2048) rmsnorm_fwd_kernel<16><<<grid, 256, 0, s>>>(x, g, yb, inv, M, D, eps);
-  else rmsnorm_fwd_kernel<32><<<grid, 256, 0, s>>>(x, g, yb, inv, M, D, eps);
+  if (D <= 512) step_launch(rmsnorm_fwd_kernel<4>, dim3(grid), dim3(256), 0, s, x, g, yb, inv, M, D, eps);
+  else if (D <= 1024) step_launch(rmsnorm_fwd_kernel<8>, dim3(grid), dim3(256), 0, s, x, g, yb, inv, M, D, eps);
+  else if (D <= 2048) step_launch(rmsnorm_fwd_kernel<16>, dim3(grid), dim3(256), 0, s, x, g, yb, inv, M, D, eps);
+  else step_launch(rmsnorm_fwd_kernel<32>, dim3(grid), dim3(256), 0, s, x, g, yb, inv, M, D, eps);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
@@ -591,7 +600,7 @@ static int launch_rmsnorm_bwd(const float* dy, const float* x, const __nv_bfloat
   int grid = (M + 7) / 8;
   const int cap = (num_sms > 0 ? num_sms : 148) * per_sm;
   if (grid > cap) grid = cap;
-  rmsnorm_bwd_kernel<VPT><<<grid, 256, (size_t)D * sizeof(float), s>>>(dy, x, g, inv, dx, dx16, dg, M, D, accumulate);
+  step_launch(rmsnorm_bwd_kernel<VPT>, dim3(grid), dim3(256), (size_t)D * sizeof(float), s, dy, x, g, inv, dx, dx16, dg, M, D, accumulate);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
@@ -640,35 +649,35 @@ int pcb_ce(void* logits, long long ld, const int* tgt, float* loss, int M, int V
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int grid = M < sms ? M : sms;
     auto* lg = reinterpret_cast<__nv_bfloat16*>(logits);
-    if (nvec <= 512) ce_rows_kernel<1><<<grid, 512, 0, s>>>(lg, ld, tgt, loss, M, V, scale, write_grad);
-    else if (nvec <= 1024) ce_rows_kernel<2><<<grid, 512, 0, s>>>(lg, ld, tgt, loss, M, V, scale, write_grad);
-    else if (nvec <= 2048) ce_rows_kernel<4><<<grid, 512, 0, s>>>(lg, ld, tgt, loss, M, V, scale, write_grad);
-    else ce_rows_kernel<8><<<grid, 512, 0, s>>>(lg, ld, tgt, loss, M, V, scale, write_grad);
+    if (nvec <= 512) step_launch(ce_rows_kernel<1>, dim3(grid), dim3(512), 0, s, lg, ld, tgt, loss, M, V, scale, write_grad);
+    else if (nvec <= 1024) step_launch(ce_rows_kernel<2>, dim3(grid), dim3(512), 0, s, lg, ld, tgt, loss, M, V, scale, write_grad);
+    else if (nvec <= 2048) step_launch(ce_rows_kernel<4>, dim3(grid), dim3(512), 0, s, lg, ld, tgt, loss, M, V, scale, write_grad);
+    else step_launch(ce_rows_kernel<8>, dim3(grid), dim3(512), 0, s, lg, ld, tgt, loss, M, V, scale, write_grad);
     return cudaGetLastError() == cudaSuccess ? 0 : -3;
   }
-  ce_fwd_bwd_kernel<<<M, 512, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(logits), ld, tgt, loss, M, V, scale,
+  step_launch(ce_fwd_bwd_kernel, dim3(M), dim3(512), 0, s, reinterpret_cast<__nv_bfloat16*>(logits), ld, tgt, loss, M, V, scale,
                                        write_grad);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
 int pcb_sumsq(const float* x, long long n, float* out, int square, cudaStream_t s) {
-  sumsq_kernel<<<grid_for(n / 4 + 1, 512, 148 * 4), 512, 0, s>>>(x, n, out, square);
+  step_launch(sumsq_kernel, dim3(grid_for(n / 4 + 1, 512, 148 * 4)), dim3(512), 0, s, x, n, out, square);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
 int pcb_colsum(const void* x, int is_bf16, long long ld, float* out, int M, int N, float scale, cudaStream_t s) {
   dim3 grid((N + 255) / 256, 64);
   if (is_bf16)
-    colsum_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), ld, out, M, N, scale);
+    step_launch(colsum_kernel<__nv_bfloat16>, dim3(grid), dim3(256), 0, s, reinterpret_cast<const __nv_bfloat16*>(x), ld, out, M, N, scale);
   else
-    colsum_kernel<float><<<grid, 256, 0, s>>>(reinterpret_cast<const float*>(x), ld, out, M, N, scale);
+    step_launch(colsum_kernel<float>, dim3(grid), dim3(256), 0, s, reinterpret_cast<const float*>(x), ld, out, M, N, scale);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
 int pcb_adamw(float* w, const float* g, float* m, float* v, void* w16, long long n, long long n_decay,
               const float* hyper, float b1, float b2, float eps, const float* clip_sumsq, float max_norm,
               cudaStream_t s) {
-  adamw_kernel<<<grid_for(n, 256, 148 * 8), 256, 0, s>>>(w, g, m, v, reinterpret_cast<__nv_bfloat16*>(w16), n,
+  step_launch(adamw_kernel, dim3(grid_for(n, 256, 148 * 8)), dim3(256), 0, s, w, g, m, v, reinterpret_cast<__nv_bfloat16*>(w16), n,
                                                            n_decay, hyper, b1, b2, eps, clip_sumsq, max_norm);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }

@@ -24,6 +24,7 @@ plus the SwiGLU extension.
 from __future__ import annotations
 
 import math
+import os
 import time
 from typing import Dict, List, Optional, Sequence
 
@@ -223,6 +224,19 @@ class FusedDecoderTrainer:
         self.rope_cs = torch.stack((cos, sin), dim=-1).contiguous()  # [S, hd/2, 2]
         self.attn_scale = 1.0 / math.sqrt(hd)
         self.launches_per_step = None
+        # Weight-gradient GEMMs on a second stream (SwiGLU dense blocks): they feed only the optimizer, so
+        # they fill the SMs that the chain of input gradients, norms and attention leaves idle (tails of
+        # persistent grids, memory-bound kernels).  The bf16 gradient buffers they read come in two
+        # copies, so the chain writes one while a weight-gradient GEMM still reads the other.
+        # PCB_WGRAD_STREAM=0 keeps every GEMM on one stream.
+        self._wg_stream = None
+        self._wg_read: Dict[tuple, torch.cuda.Event] = {}
+        if (torch.device(dev).type == "cuda" and os.environ.get("PCB_WGRAD_STREAM", "1") != "0"
+                and cfg.num_experts == 0 and cfg.ffn == "swiglu"):
+            self._wg_stream = torch.cuda.Stream(dev)
+            self.dx16_pp = [self.dx16, z(M, D)]
+            self.dpre_pp = [self.dpre, z(M, fpre)]
+            self.dqkv_pp = [self.dqkv, z(M, 3 * D)]
 
     def _bucket_names(self) -> List[List[str]]:
         """Tensor groups in the order the backward finishes their gradients: LM head + final norm,
@@ -266,6 +280,8 @@ class FusedDecoderTrainer:
         ev.record(torch.cuda.current_stream(self.device))
         s = self._push_stream
         s.wait_event(ev)
+        if self._wg_stream is not None:
+            s.wait_stream(self._wg_stream)   # the bucket's weight gradients come from the side stream
         base = self.grad.data_ptr()
         with torch.cuda.stream(s):
             for q, dst, src, n in self._plans[b]:
@@ -436,6 +452,9 @@ class FusedDecoderTrainer:
             ops.sumsq(self.moe_aux, self.loss_sum, square=False)
 
     def _backward(self) -> None:
+        if self._wg_stream is not None:
+            self._backward_two_streams()
+            return
         cfg = self.cfg
         W, G = self.W, self.G
         B, S, D, H, hd = self.B, self.S, cfg.dim, cfg.num_heads, cfg.head_dim
@@ -478,6 +497,70 @@ class FusedDecoderTrainer:
             self._bucket_done(L - l)
         ops.embed_bwd(self.tok, self.dx, G["wemb"])
         self._bucket_done(L + 1)
+
+    def _backward_two_streams(self) -> None:
+        """The SwiGLU backward of ``_backward`` with every weight-gradient GEMM (dW += dY^T X, fp32
+        reduce epilogue) on the side stream.  Each one forks from the main stream after its inputs are
+        written; before the main stream rewrites a bf16 gradient copy it waits for the weight-gradient
+        GEMM that last read it; the main stream joins the side stream at the end."""
+        cfg = self.cfg
+        W, G = self.W, self.G
+        B, S, D, H, hd = self.B, self.S, cfg.dim, cfg.num_heads, cfg.head_dim
+        L = cfg.num_blocks
+        RED = ops.EPI_RED_F32
+        main = torch.cuda.current_stream(self.device)
+        side = self._wg_stream
+        read = self._wg_read
+
+        def wgrad(dy, x, g, key):
+            side.wait_stream(main)
+            with torch.cuda.stream(side):
+                ops.gemm(dy, x, a_mn=True, b_mn=True, epi=RED, c=g)
+            if key is not None:
+                ev = torch.cuda.Event()
+                ev.record(side)
+                read[key] = ev
+
+        def claim(key):
+            ev = read.pop(key, None)
+            if ev is not None:
+                main.wait_event(ev)
+
+        dx16, dpre, dqkv = self.dx16_pp, self.dpre_pp, self.dqkv_pp
+        dl = self.logits  # holds dlogits after the fused CE (not rewritten during the backward)
+        wgrad(dl, self.nf, G["wout"], None)                                           # dWout = dL^T nf
+        ops.gemm(dl, W["wout"], b_mn=True, epi=ops.EPI_F32, c=self.dn)                # dnf = dL Wout
+        k = 0
+        claim(("dx16", k))
+        ops.rmsnorm_bwd(self.dn, self.x[L], W["lnf"], self.invf, self.dx, G["lnf"], False, dx16[k])
+        self._bucket_done(0)
+        for l in reversed(range(L)):
+            p = l & 1
+            wgrad(dx16[k], self.act[l], G[f"b{l}.w2"], ("dx16", k))
+            claim(("dpre", p))
+            ops.gemm(dx16[k], W[f"b{l}.w2"], b_mn=True, epi=ops.EPI_SWIGLU_BWD, c=dpre[p], aux=self.pre[l])
+            wgrad(dpre[p], self.n2[l], G[f"b{l}.w13"], ("dpre", p))
+            ops.gemm(dpre[p], W[f"b{l}.w13"], b_mn=True, epi=ops.EPI_F32, c=self.dn)
+            k ^= 1
+            claim(("dx16", k))
+            ops.rmsnorm_bwd(self.dn, self.xmid[l], W[f"b{l}.ln2"], self.inv2[l], self.dx, G[f"b{l}.ln2"], True,
+                            dx16[k])
+            wgrad(dx16[k], self.ao[l], G[f"b{l}.wo"], ("dx16", k))
+            ops.gemm(dx16[k], W[f"b{l}.wo"], b_mn=True, epi=ops.EPI_BF16, c=self.dao)
+            claim(("dqkv", p))
+            ops.attn_bwd(self.qkv[l], self.ao[l], self.dao, self.lse[l], self.dvec, self.dq_acc, dqkv[p],
+                         B, S, H, hd, self.attn_scale, self.rope_cs)
+            wgrad(dqkv[p], self.n1[l], G[f"b{l}.wqkv"], ("dqkv", p))
+            ops.gemm(dqkv[p], W[f"b{l}.wqkv"], b_mn=True, epi=ops.EPI_F32, c=self.dn)
+            k ^= 1
+            claim(("dx16", k))
+            ops.rmsnorm_bwd(self.dn, self.x[l], W[f"b{l}.ln1"], self.inv1[l], self.dx, G[f"b{l}.ln1"], True,
+                            dx16[k])
+            self._bucket_done(L - l)
+        ops.embed_bwd(self.tok, self.dx, G["wemb"])
+        self._bucket_done(L + 1)
+        main.wait_stream(side)   # every weight gradient is complete before the optimizer
+        read.clear()
 
     def _optimizer(self) -> None:
         """Gradient sync (data parallel) + AdamW on this rank's shard + bf16 weight refresh."""
