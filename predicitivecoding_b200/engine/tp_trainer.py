@@ -27,6 +27,7 @@ All cross-rank ordering is by the bounded device barrier; nothing waits on the h
 from __future__ import annotations
 
 import math
+import os
 from typing import Optional
 
 import torch
@@ -159,6 +160,20 @@ class TensorParallelTrainer:
         self.rope_cs = torch.stack((cos, sin), dim=-1).contiguous()
         self.attn_scale = 1.0 / math.sqrt(hd)
         self.launches_per_step = None
+        # Weight-gradient GEMMs on a second stream: at tensor-parallel widths the per-rank products are
+        # narrow, and the dW GEMMs (which only feed the optimizer) fill the SMs the gather/reduce-scatter
+        # chain leaves idle.  The buffers they read that the backward rewrites (the gathered output
+        # gradient, dpre, dqkv) come in two copies; every rank alternates them in the same order, so the
+        # symmetric gather buffer a peer reads is always the one this rank wrote for that use.
+        # PCB_WGRAD_STREAM=0 keeps one stream (and one copy of each buffer).
+        self._wg_stream = None
+        self._wg_read = {}
+        self.GD_pp, self.dpre_pp, self.dqkv_pp = [self.GD, self.GD], [self.dpre, self.dpre], [self.dqkv, self.dqkv]
+        if self.device.type == "cuda" and os.environ.get("PCB_WGRAD_STREAM", "1") != "0":
+            self._wg_stream = torch.cuda.Stream(dev)
+            self.GD_pp[1] = self.peer.symmetric(M * D, bf16)
+            self.dpre_pp[1] = z(M, 2 * Fl)
+            self.dqkv_pp[1] = z(M, 3 * Dl)
 
     # ------------------------------------------------------------------ weights
     def _shard_full(self, model: DecoderLM):
@@ -262,37 +277,69 @@ class TensorParallelTrainer:
         L = cfg.num_blocks
         RED = ops.EPI_RED_F32
         sl = slice(self.t * R, (self.t + 1) * R)
-        GDfull = self.GD.local.view(self.M, cfg.dim)
+        main = torch.cuda.current_stream(self.device)
+        side, read = self._wg_stream, self._wg_read
+
+        def wgrad(dy, x, g, key):
+            """dW += dy^T x (fp32 reduce epilogue), on the side stream when there is one."""
+            if side is None:
+                ops.gemm(dy, x, a_mn=True, b_mn=True, epi=RED, c=g)
+                return
+            side.wait_stream(main)
+            with torch.cuda.stream(side):
+                ops.gemm(dy, x, a_mn=True, b_mn=True, epi=RED, c=g)
+            if key is not None:
+                ev = torch.cuda.Event()
+                ev.record(side)
+                read[key] = ev
+
+        def claim(key):
+            """The main stream is about to rewrite buffer ``key``: wait for the dW GEMM that read it."""
+            ev = read.pop(key, None)
+            if ev is not None:
+                main.wait_event(ev)
+
+        GD, dpre, dqkv = self.GD_pp, self.dpre_pp, self.dqkv_pp
         dl = self.logits
-        ops.gemm(dl, self.nf, a_mn=True, b_mn=True, epi=RED, c=G["wout"])
+        wgrad(dl, self.nf, G["wout"], None)
         ops.gemm(dl, W["wout"], b_mn=True, epi=ops.EPI_F32, c=self.dn)
-        ops.rmsnorm_bwd(self.dn, self.x[L], W["lnf"], self.invf, self.dx, G["lnf"], False, self._own(self.GD))
+        k = 0
+        claim(("GD", k))
+        ops.rmsnorm_bwd(self.dn, self.x[L], W["lnf"], self.invf, self.dx, G["lnf"], False, self._own(GD[k]))
         for l in reversed(range(L)):
+            p = l & 1
             # ---- FFN (row-parallel W2, column-parallel W13)
             self._barrier()
-            self._ag_gemm(self.GD, W[f"b{l}.w2"], b_mn=True, epi=ops.EPI_SWIGLU_BWD, c=self.dpre, aux=self.pre[l])
-            ops.gemm(GDfull, self.act[l], a_mn=True, b_mn=True, epi=RED, c=G[f"b{l}.w2"])
-            ops.gemm(self.dpre, self.G2[l].local.view(self.M, cfg.dim), a_mn=True, b_mn=True, epi=RED,
-                     c=G[f"b{l}.w13"])
-            self._rs_gemm(self.dpre, W[f"b{l}.w13"], b_mn=True)
+            claim(("dpre", p))
+            self._ag_gemm(GD[k], W[f"b{l}.w2"], b_mn=True, epi=ops.EPI_SWIGLU_BWD, c=dpre[p], aux=self.pre[l])
+            wgrad(GD[k].local.view(self.M, cfg.dim), self.act[l], G[f"b{l}.w2"], ("GD", k))
+            wgrad(dpre[p], self.G2[l].local.view(self.M, cfg.dim), G[f"b{l}.w13"], ("dpre", p))
+            self._rs_gemm(dpre[p], W[f"b{l}.w13"], b_mn=True)
             self._barrier()
             ops.ext().tp_reduce_norm(self.slots.local, T, None, self.dn, False, None, None, None, cfg.eps)
+            k ^= 1
+            claim(("GD", k))
             ops.rmsnorm_bwd(self.dn, self.xmid[l], W[f"b{l}.ln2"], self.inv2[l], self.dx, G[f"b{l}.ln2"], True,
-                            self._own(self.GD))
+                            self._own(GD[k]))
             # ---- attention (row-parallel Wo, column-parallel Wqkv)
             self._barrier()
-            self._ag_gemm(self.GD, W[f"b{l}.wo"], b_mn=True, epi=ops.EPI_BF16, c=self.dao)
-            ops.gemm(GDfull, self.ao[l], a_mn=True, b_mn=True, epi=RED, c=G[f"b{l}.wo"])
-            ops.attn_bwd(self.qkv[l], self.ao[l], self.dao, self.lse[l], self.dvec, self.dq_acc, self.dqkv,
+            self._ag_gemm(GD[k], W[f"b{l}.wo"], b_mn=True, epi=ops.EPI_BF16, c=self.dao)
+            wgrad(GD[k].local.view(self.M, cfg.dim), self.ao[l], G[f"b{l}.wo"], ("GD", k))
+            claim(("dqkv", p))
+            ops.attn_bwd(self.qkv[l], self.ao[l], self.dao, self.lse[l], self.dvec, self.dq_acc, dqkv[p],
                          B, S, self.Hl, hd, self.attn_scale, self.rope_cs)
-            ops.gemm(self.dqkv, self.G1[l].local.view(self.M, cfg.dim), a_mn=True, b_mn=True, epi=RED,
-                     c=G[f"b{l}.wqkv"])
-            self._rs_gemm(self.dqkv, W[f"b{l}.wqkv"], b_mn=True)
+            wgrad(dqkv[p], self.G1[l].local.view(self.M, cfg.dim), G[f"b{l}.wqkv"], ("dqkv", p))
+            self._rs_gemm(dqkv[p], W[f"b{l}.wqkv"], b_mn=True)
             self._barrier()
             ops.ext().tp_reduce_norm(self.slots.local, T, None, self.dn, False, None, None, None, cfg.eps)
+            k ^= 1
+            claim(("GD", k))
             ops.rmsnorm_bwd(self.dn, self.x[l], W[f"b{l}.ln1"], self.inv1[l], self.dx, G[f"b{l}.ln1"], True,
-                            self._own(self.GD))
+                            self._own(GD[k]))
         ops.embed_bwd(self.tok[sl], self.dx, G["wemb"])
+        if side is not None:
+            main.wait_stream(side)   # every weight gradient is complete before the optimizer
+            read.clear()
 
     def _optimizer(self) -> None:
         if self.comm is not None:
