@@ -186,6 +186,11 @@ class FusedDecoderTrainer:
         self.tok_pin = torch.zeros(M, dtype=torch.int32).pin_memory()
         self.tgt_pin = torch.zeros(M, dtype=torch.int32).pin_memory()
         self.loss_pin = torch.zeros(1, dtype=f32).pin_memory()
+        # step_pipelined: each step's loss leaves through one of two pinned slots, read one step later
+        self._loss_slots = [torch.zeros(1, dtype=f32).pin_memory() for _ in range(2)]
+        self._loss_ev = [torch.cuda.Event() for _ in range(2)] if torch.device(dev).type == "cuda" else None
+        self._pipe_pending: Optional[int] = None
+        self._pipe_n = 0
         self.x = [z(M, D, dt=f32) for _ in range(L + 1)]
         self.xmid = [z(M, D, dt=f32) for _ in range(L)]
         self.n1 = [z(M, D) for _ in range(L)]
@@ -688,6 +693,34 @@ class FusedDecoderTrainer:
         self.stage(tokens, targets)
         self.launch(lr)
         return self.read_loss()
+
+    def step_pipelined(self, tokens: torch.Tensor, targets: torch.Tensor,
+                       lr: Optional[float] = None) -> Optional[float]:
+        """Public API for a training loop that never leaves the GPU waiting on the host: stage and launch
+        this step, then return the mean loss of the previous one (None on the first call; ``flush()``
+        returns the last).  The host prepares step i+1 while step i runs.  Every step still copies its
+        tokens and targets from pinned memory to the device, and its loss comes back to the host: a
+        4-byte copy, ordered after the step, into one of two pinned slots that alternate, so the slot
+        read for step i is not rewritten before step i+2 is launched."""
+        self.stage(tokens, targets)
+        self.launch(lr)
+        slot = self._pipe_n & 1
+        self._pipe_n += 1
+        self._loss_slots[slot].copy_(self.loss_sum, non_blocking=True)
+        self._loss_ev[slot].record(torch.cuda.current_stream(self.device))
+        prev, self._pipe_pending = self._pipe_pending, slot
+        if prev is None:
+            return None
+        self._loss_ev[prev].synchronize()
+        return float(self._loss_slots[prev][0]) / self.M
+
+    def flush(self) -> Optional[float]:
+        """Mean loss of the last step launched by ``step_pipelined`` (waits for that step only)."""
+        prev, self._pipe_pending = self._pipe_pending, None
+        if prev is None:
+            return None
+        self._loss_ev[prev].synchronize()
+        return float(self._loss_slots[prev][0]) / self.M
 
     @torch.no_grad()
     def evaluate_loss(self, tokens: torch.Tensor, targets: torch.Tensor) -> float:

@@ -156,3 +156,20 @@ def test_web_pretrain_demo_trains_on_the_device_and_resumes(tmp_path):
     assert "fresh" in first and "4 steps" in first
     second = demos.web_pretrain(str(tmp_path), max_steps=4)
     assert "resumed" in second
+
+
+@pytest.mark.parametrize("use_graph", [False, True])
+def test_pipelined_steps_return_the_same_losses_one_step_later(use_graph):
+    """step_pipelined(i) returns step i-1's loss and flush() the last one; the sequence equals step()'s."""
+    cfg = small_cfg("swiglu")
+    data = [batch(cfg, 4, seed=s) for s in range(5)]
+    a = FusedDecoderTrainer(cfg, 4, device="cuda", model=DecoderLM(cfg, seed=2), use_graph=use_graph)
+    ref = [a.step(tok, tgt) for tok, tgt in data]
+    b = FusedDecoderTrainer(cfg, 4, device="cuda", model=DecoderLM(cfg, seed=2), use_graph=use_graph)
+    got = [b.step_pipelined(tok, tgt) for tok, tgt in data]
+    assert got[0] is None
+    got = got[1:] + [b.flush()]
+    assert b.flush() is None
+    for x, y in zip(got, ref):
+        assert x == pytest.approx(y, rel=2e-3)
+    assert rel(b.w32, a.w32) < 1e-3
