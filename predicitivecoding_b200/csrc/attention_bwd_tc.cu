@@ -325,6 +325,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const float* sl = lse + (long long)it.bh * S + qi * kT;   // read through L1 / L2
         const float* sd = dvec + (long long)it.bh * S + qi * kT;
+        {   // pull the next tile's lse / delta lines (this warpgroup's 64 queries: two 128-byte lines each)
+            // into L1 now, so the next tile's quarter loads hit L1 instead of waiting on L2
+          int nbh = it.bh, nq = qi + 1;
+          if (nq >= T) {
+            const int ni = snake_item(ic + 1);
+            nbh = ni < n_items ? ni % BH : -1;
+            nq = ni < n_items ? ni / BH : 0;
+          }
+          if (nbh >= 0 && (warp & 3) == 0 && lane < 4)
+            prefetch_l1(((lane & 2) ? dvec : lse) + (long long)nbh * S + nq * kT + 64 * gw + 32 * (lane & 1));
+        }
         const bool diag = qi == it.kb;
         uint8_t* ds_buf = sDS + (tcount & 1) * 2 * kAtom;
 #pragma unroll 1
